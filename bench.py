@@ -1,0 +1,537 @@
+#!/usr/bin/env python3
+"""Encoder non-GEMM throughput on B200: frames/s and achieved HBM GB/s.
+
+Workload (the one the metric is quoted on at 1/2/4/8 GPUs):
+per GPU, a batch of 256 independent utterances of T = 375 frames run through
+the 24-block non-GEMM op sequence of the FastConformer encoder
+(pkcu_encoder_nongemm: LayerNorms, bias+Swish, residuals, QKV head split with
+pos_bias_u/v, positional head split, rel-shift + score combine + softmax, head
+concat, GLU, depthwise conv + Swish, conv transpose-add). GEMM outputs are
+seeded N(0,1) stand-ins resident in HBM (the GEMMs are outside this path);
+block parameters are random (LN gamma ~ N(1,0.1), others ~ 0.1 N(0,1)).
+Each step reads > 10 GB per GPU, far above the 126 MB L2.
+
+Multi-GPU: one process per GPU (torchrun), every rank runs its own batch, no
+collective on the data path (weak scaling); time = max over ranks of the
+device time (CUDA events), value = all ranks' frames / that time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W]          # this library
+  python bench.py --impl reference [--steps K] [--warmup W]    # reference CPU code
+
+Output: one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime as dt
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "parakeet-unified-en-0.6b-c_b200")
+sys.path.insert(0, os.path.join(PKG, "python"))
+
+METRIC = "encoder non-GEMM frames/s and achieved HBM GB/s (% of peak) at 1/2/4/8 B200"
+D, H, DH, FF = 1024, 8, 128, 4096
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--utts", type=int, default=256, help="utterances per GPU")
+    ap.add_argument("--T", type=int, default=375, help="frames per utterance")
+    ap.add_argument("--blocks", type=int, default=24)
+    ap.add_argument("--groups", type=int, default=8, help="pipeline groups of the host-buffer run")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ── algorithmic bytes (read each input once, write each output once) ─────────
+
+def kernel_table(F, T, n_items):
+    """(name, bytes per launch over the batch, launches per block)."""
+    L = 2 * T - 1
+    S = n_items * H * T * T
+    return [
+        ("bias_swish_rows", 8 * F * FF, 2),
+        ("residual_layer_norm", 16 * F * D, 1),
+        ("qkv_split_uv", 28 * F * D, 1),
+        ("pos_head_split", 8 * n_items * L * D, 1),
+        ("relpos_combine_softmax", 12 * S, 1),
+        ("head_concat", 8 * F * D, 1),
+        ("residual_layer_norm_transpose", 16 * F * D, 1),
+        ("glu", 12 * F * D, 1),
+        ("dwconv_bn_swish", 8 * F * D, 1),
+        ("transpose_add_layer_norm", 16 * F * D, 1),
+        ("residual_layer_norm2", 16 * F * D, 1),
+    ]
+
+
+def step_bytes(F, T, n_items, n_blocks):
+    per_block = sum(b * n for _, b, n in kernel_table(F, T, n_items))
+    # + the first block's LN_ff1 (8FD); the last block's residual_layer_norm2 writes no LN_next
+    return n_blocks * per_block + 8 * F * D - 4 * F * D
+
+
+# ── clocks during the timed region ───────────────────────────────────────────
+
+class ClockSampler:
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_index):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ident = str(local_index)
+        if vis:
+            parts = [p.strip() for p in vis.split(",") if p.strip()]
+            if local_index < len(parts):
+                ident = parts[local_index]
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", ident], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self, t0, t1):
+        if self.proc is None:
+            return {"unavailable": "nvidia-smi not found"}
+        self.proc.terminate()
+        try:
+            out = self.proc.communicate(timeout=10)[0]
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out = ""
+        rows = []
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                ts = dt.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[1]), float(f[2]), f[3], f[4:8]))
+            except ValueError:
+                continue
+        inside = [r for r in rows if t0 <= r[0] <= t1] or rows
+        if not inside:
+            return {"unavailable": "no samples"}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v == "Active"})
+        sm = sorted(r[1] for r in inside)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[2] for r in inside),
+                "samples": len(inside), "reasons": reasons}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel):
+    """DRAM bytes per launch from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    except (OSError, ValueError):
+        return None
+
+
+# ── CPU reference path (the reference's own compiled code) ────────────────────
+
+class RefRunner:
+    """The reference's conformer_block (csrc/encoder.c:482-491) from
+    oracle/_ref/libpkref.so, GEMM calls replaced by no-ops, so that only the
+    reference's non-GEMM code runs; one utterance of T frames per call, rows
+    spread over PK_THREADS pool threads as in the reference."""
+
+    def __init__(self, T, n_blocks, threads=None):
+        import numpy as np
+        cores = os.cpu_count() or 1
+        self.threads_req = threads or min(cores, 16)   # the reference clamps to 16 (csrc/threadpool.c:10)
+        os.environ["PK_THREADS"] = str(self.threads_req)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import pyoracle as po
+        self.po = po
+        self.ref = po.Reference()
+        rng = np.random.default_rng(4)
+        blocks = [po.random_block_inputs(rng, 1)[0] for _ in range(min(n_blocks, 4))]
+        self.flat = (po.FP * (22 * n_blocks))()
+        self.keep = []
+        for b in range(n_blocks):
+            p = blocks[b % len(blocks)]
+            for j, role in enumerate(po.PARAM_ROLES):
+                a = po.f32(p[role])
+                self.keep.append(a)
+                self.flat[22 * b + j] = a.ctypes.data_as(po.FP)
+        self.ws = rng.standard_normal(self.ref.L.pkref_ws_floats(T)).astype(np.float32)
+        self.x = rng.standard_normal((T, D)).astype(np.float32)
+        self.T, self.n_blocks = T, n_blocks
+        self.run_one()   # warm-up; creates the thread pool
+        self.threads = self.ref.L.pkref_pool_threads()
+
+    def run_one(self):
+        po = self.po
+        rc = self.ref.L.pkref_conformer_blocks(self.x.ctypes.data_as(po.FP), self.T, self.n_blocks,
+                                               self.flat, None, None, 0, self.ws.ctypes.data_as(po.FP))
+        assert rc == 0
+
+    def sample(self, seconds, min_utts=1, max_utts=64):
+        n, t0 = 0, time.perf_counter()
+        while n < min_utts or (time.perf_counter() - t0 < seconds and n < max_utts):
+            self.run_one()
+            n += 1
+        secs = time.perf_counter() - t0
+        return n * self.T / secs, n, secs
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: rank 0 times the reference CPU implementation."""
+    if rank != 0:
+        return
+    r = RefRunner(args.T, args.blocks)
+    for _ in range(args.warmup):
+        r.run_one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r.run_one()
+    secs = time.perf_counter() - t0
+    threads = r.threads
+    frames = args.steps * args.T
+    value = frames / secs
+    sample = (f"{args.steps} steps x 1 utterance x T={args.T} x {args.blocks} blocks through the "
+              f"reference's conformer_block with GEMMs as no-ops, PK_THREADS={threads}")
+    line = {
+        "metric": METRIC, "value": value, "unit": "frames/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * secs / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, world):
+    return {"workload": f"config 4: {args.utts} utterances x T={args.T} per GPU, "
+                        f"{args.blocks}-block non-GEMM op sequence (fused kernels), fp32",
+            "model": "parakeet-unified-en-0.6b FastConformer (D=1024, 8x128 heads, FF=4096, conv k=9)",
+            "utterances_per_gpu": args.utts, "global_batch": args.utts * world, "seq_len": args.T,
+            "blocks": args.blocks, "parallelism": f"dp{world} (utterances sharded, no collectives)",
+            "l2": "inputs larger than L2 (GEMM stand-ins > 10 GB per GPU per step)"}
+
+
+# ── this library ──────────────────────────────────────────────────────────────
+
+def setup_device(args, rank):
+    import torch
+    import pkcuda
+    seq = pkcuda.Seq([args.T] * args.utts)
+    ws = pkcuda.EncoderWorkspace(seq, args.groups)
+    x_addr, gout, gin = ws.device()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234 + rank)
+    F = seq.frames
+    # Fill x and the stand-in GEMM outputs with N(0,1) (views of the workspace).
+    total = ws.device_bytes // 4
+    base = torch.empty(0, device="cuda")
+    del base
+    fills = [(x_addr, F * D)]
+    ext = {"ff1_h": F * FF, "ff1_out": F * D, "qkv": 3 * F * D, "P": seq.pos_rows * D,
+           "ac": seq.score_elems, "bd": seq.bd_elems, "attn_h": F * D, "att_out": F * D,
+           "pw1": 2 * F * D, "pw2": F * D, "ff2_h": F * FF, "ff2_out": F * D}
+    for f in pkcuda.GEMM_OUT_FIELDS:
+        fills.append((getattr(gout, f), ext[f]))
+    for addr, n in fills:
+        t = tensor_at(addr, n)
+        t.normal_(generator=gen)
+    blocks = []
+    for _ in range(args.blocks):
+        p = {}
+        for f in pkcuda.BLOCK_PARAM_FIELDS:
+            n = {"ff1_b1": FF, "ff2_b1": FF, "qkv_b": 3 * D, "pw1_b": 2 * D, "dw_w": 9 * D,
+                 "pos_u": D, "pos_v": D}.get(f, D)
+            t = torch.randn(n, device="cuda", generator=gen)
+            if f.startswith("norm") and f.endswith("_w"):
+                t = 1.0 + 0.1 * t
+            elif f == "dw_w":
+                t = 0.3 * t
+            else:
+                t = 0.1 * t
+            p[f] = t.contiguous()
+        blocks.append(p)
+    arr = pkcuda.block_params_array(blocks)
+    del total
+    return seq, ws, x_addr, gout, gin, blocks, arr
+
+
+def tensor_at(addr, n):
+    """A float32 torch view of n elements of device memory owned by the C library."""
+    import torch
+
+    class _Holder:
+        pass
+
+    h = _Holder()
+    h.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (addr, False),
+                                  "version": 3, "strides": None}
+    return torch.as_tensor(h, device="cuda")
+
+
+def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
+    """Average device time of each kernel of the sequence, launched alone on
+    the bench stream over the full batch (CUDA events on that stream)."""
+    import torch
+    import pkcuda
+    F, T, n = seq.frames, args.T, args.utts
+    p = blocks[0]
+    sh = stream.cuda_stream
+    P = lambda k: pkcuda.ptr(p[k])
+    scale = 1.0 / (128.0 ** 0.5)
+    calls = {
+        "bias_swish_rows": lambda: pkcuda.call("pkcu_bias_swish_rows", gout.ff1_h, P("ff1_b1"), gin.h1, F, FF, sh),
+        "residual_layer_norm": lambda: pkcuda.call("pkcu_residual_layer_norm", x_addr, gout.ff1_out, P("ff1_b2"), 0.5,
+                                                   P("norm_sa_w"), P("norm_sa_b"), gin.ln_sa, F, sh),
+        "qkv_split_uv": lambda: pkcuda.call("pkcu_qkv_split_uv", gout.qkv, P("qkv_b"), P("pos_u"), P("pos_v"),
+                                            gin.Qu, gin.Qv, gin.K, gin.V, seq.handle, sh),
+        "pos_head_split": lambda: pkcuda.call("pkcu_pos_head_split", gout.P, gin.P_h, seq.handle, sh),
+        "relpos_combine_softmax": lambda: pkcuda.call("pkcu_relpos_combine_softmax", gout.ac, gout.bd, gin.S,
+                                                      scale, seq.handle, sh),
+        "head_concat": lambda: pkcuda.call("pkcu_head_concat", gout.attn_h, gin.attn, seq.handle, sh),
+        "residual_layer_norm_transpose": lambda: pkcuda.call(
+            "pkcu_residual_layer_norm_transpose", x_addr, gout.att_out, P("out_b"), 1.0, P("norm_conv_w"),
+            P("norm_conv_b"), gin.cf, seq.handle, sh),
+        "glu": lambda: pkcuda.call("pkcu_glu", gout.pw1, P("pw1_b"), gin.gated, D, 0, seq.handle, sh),
+        "dwconv_bn_swish": lambda: pkcuda.call("pkcu_dwconv_bn_swish", gin.gated, P("dw_w"), P("dw_b"), None, 0.0,
+                                               1, gin.dw, D, 9, seq.handle, sh),
+        "transpose_add_layer_norm": lambda: pkcuda.call(
+            "pkcu_transpose_add_layer_norm", x_addr, gout.pw2, P("pw2_b"), P("norm_ff2_w"), P("norm_ff2_b"),
+            gin.ln_ff2, seq.handle, sh),
+        "residual_layer_norm2": lambda: pkcuda.call(
+            "pkcu_residual_layer_norm2", x_addr, gout.ff2_out, P("ff2_b2"), 0.5, P("norm_out_w"), P("norm_out_b"),
+            P("norm_ff1_w"), P("norm_ff1_b"), gin.ln_ff1, F, sh),
+    }
+    table = {}
+    for name, nbytes, per_block in kernel_table(F, T, n):
+        fn = calls[name]
+        fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        table[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                       "launches_per_step": per_block * args.blocks}
+    return table
+
+
+def ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import pkcuda
+
+    torch.cuda.set_device(local_rank)
+    pkcuda.lib()
+    stream = torch.cuda.Stream()        # graphs cannot be captured on the legacy stream
+    with torch.cuda.stream(stream):
+        _ours(args, rank, world, local_rank, stream)
+
+
+def _ours(args, rank, world, local_rank, stream):
+    import torch
+    import torch.distributed as dist
+    import pkcuda
+    seq, ws, x_addr, gout, gin, blocks, arr = setup_device(args, rank)
+    F = seq.frames
+
+    def step():
+        pkcuda.call("pkcu_encoder_nongemm", x_addr, C.cast(arr, pkcuda.VP), args.blocks,
+                    C.byref(gout), C.byref(gin), seq.handle, None, None, stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        run()
+    e1.record(stream)
+    e1.synchronize()
+    t1 = time.time()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t0, t1)
+    ms = e0.elapsed_time(e1)
+    ms_t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    frames_all = F * args.steps * world
+    value = frames_all / (ms_max / 1e3)
+    bytes_step = step_bytes(F, args.T, args.utts, args.blocks)
+    hbm_gbs = bytes_step * args.steps / (ms / 1e3) / 1e9
+
+    # Per-kernel device times (each kernel alone over the full batch).
+    table = time_kernels(args, seq, x_addr, gout, gin, blocks, stream)
+
+    # End to end through the host-buffer C entry point (pinned host memory).
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, ws, arr, gout, x_addr, stream, world)
+
+    if graph is not None:
+        del graph
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = RefRunner(args.T, args.blocks)
+        fps, n_utts, secs = r.sample(args.cpu_seconds)
+        cpu = {"value": fps, "unit": "frames/s", "cores": r.threads, "kind": "reference",
+               "sample": f"{n_utts} utterance(s) x T={args.T} x {args.blocks} blocks through the "
+                         f"reference's own conformer_block (GEMMs as no-ops), "
+                         f"PK_THREADS={r.threads}, {secs:.1f} s"}
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    dom = max(table, key=lambda k: table[k]["ms"] * table[k]["launches_per_step"])
+    d = table[dom]
+    traffic = ncu_traffic(dom)
+    line = {
+        "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) GEMM outputs and inputs, random block parameters)",
+        "config": config_dict(args, world),
+        "hbm": {"algorithmic_bytes_per_step": bytes_step, "achieved_gbs_per_gpu": hbm_gbs,
+                "peak_gbs": peak, "frac": hbm_gbs / peak, "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": d["gbs"] / peak, "traffic": traffic,
+                     "peak_kind": peak_kind},
+        "kernels": {k: {"ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
+                        "frac": round(v["gbs"] / peak, 3), "launches_per_step": v["launches_per_step"]}
+                    for k, v in table.items()},
+        "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
+        "graph": graph is not None or not args.no_graph,
+        "clocks": clocks,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, ws, arr, gout, x_addr, stream, world):
+    """frames/s through pkcu_encoder_nongemm_host: every step copies x and the
+    GEMM outputs from pinned host memory and x back (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    import pkcuda
+    seq = ws.seq
+    F = seq.frames
+    # Pinned host copies of x and the GEMM outputs: skip the run (and say so)
+    # unless every local rank's copy fits well inside the host's free memory.
+    need = (ws.h2d_bytes + ws.d2h_bytes) * int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    avail = 0
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    avail = int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    if need > 0.4 * avail:
+        return {"unavailable": f"pinned host buffers need {need / 1e9:.1f} GB, "
+                               f"host has {avail / 1e9:.1f} GB available"}
+    host = {}
+    for f in pkcuda.GEMM_OUT_FIELDS:
+        addr = getattr(gout, f)
+        n = {"ff1_h": F * FF, "ff2_h": F * FF, "qkv": 3 * F * D, "P": seq.pos_rows * D,
+             "ac": seq.score_elems, "bd": seq.bd_elems, "pw1": 2 * F * D}.get(f, F * D)
+        h = torch.empty(n, dtype=torch.float32, pin_memory=True)
+        h.copy_(tensor_at(addr, n))
+        host[f] = h
+    xh = torch.empty(F * D, dtype=torch.float32, pin_memory=True)
+    xh.copy_(tensor_at(x_addr, F * D))
+    gh = pkcuda.gemm_outputs(host)
+    steps = max(2, min(args.steps, 5))
+    ws.run_host(xh.data_ptr(), gh, arr, args.blocks, stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ws.run_host(xh.data_ptr(), gh, arr, args.blocks, stream)
+    secs = time.perf_counter() - t0
+    s_t = torch.tensor([secs], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(s_t, op=dist.ReduceOp.MAX)
+    secs = float(s_t.item())
+    return {"value": F * steps * world / secs, "unit": "frames/s", "steps": steps,
+            "h2d_bytes_per_step": ws.h2d_bytes, "d2h_bytes_per_step": ws.d2h_bytes,
+            "pipeline_groups": args.groups,
+            "note": "pkcu_encoder_nongemm_host: H2D of x + GEMM outputs, 24 blocks, D2H of x, "
+                    "host wall clock per call (synchronous API), max over ranks"}
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if world > 1 and rank != 0:
+            return
+        reference_arm(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=dt.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,323 @@
+/* pkcuda.h -- C ABI of libpk_tensor_ops_cuda.so: B200 (sm_100a) kernels for the
+ * non-GEMM work of the Parakeet FastConformer encoder and RNN-T joint.
+ *
+ * Reference: eschmidbauer/parakeet-unified-en-0.6b-c, a pure-C CPU engine.
+ * Citations below are file:line within that project.
+ *
+ * Three layers, all plain C:
+ *
+ *  1. Drop-in host API -- the exact prototypes of csrc/parakeet.h:231-262
+ *     (pk_layer_norm ... pk_depthwise_conv1d). Host pointers in and out,
+ *     synchronous, no return value, like the functions they replace. Each call
+ *     copies its operands to the GPU, runs the kernel and copies the result
+ *     back. pk_cuda_status() reports the outcome of the calling thread's last
+ *     drop-in call (the reference itself reports no errors).
+ *
+ *  2. Device API -- pkcu_*: device pointers, asynchronous on the given stream,
+ *     int status (PKCU_OK or an error code). Covers the reference's tensor_ops
+ *     (csrc/tensor_ops.c), the inline loops of csrc/encoder.c and
+ *     csrc/decoder.c, and the dequantisation of csrc/blas.c / csrc/weights.c,
+ *     plus producer/consumer fusions of adjacent ops. Unless stated otherwise
+ *     every float pointer must be 16-byte aligned (cudaMalloc memory is) and
+ *     in/out buffers of one call must not overlap.
+ *
+ *  3. Sequence driver -- pkcu_encoder_nongemm: the whole per-block non-GEMM op
+ *     sequence of csrc/encoder.c:482-491 for a batch of utterances or chunks,
+ *     with a hook at every GEMM.
+ *
+ * Model constants follow csrc/parakeet.h:15-30: D = 1024, 8 heads of 128,
+ * FF = 4096, conv kernel 9, joint width 640, 1025 logits.
+ */
+#ifndef PKCUDA_H
+#define PKCUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same underlying type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *pkcu_stream_t;
+
+/* ── status ──────────────────────────────────────────────────────────────── */
+
+#define PKCU_OK          0
+#define PKCU_ERR_ARG     1   /* NULL pointer, size out of range, misaligned pointer */
+#define PKCU_ERR_CUDA    2   /* a CUDA runtime call or kernel launch failed */
+#define PKCU_ERR_NOMEM   3   /* device or host allocation failed */
+
+const char *pkcu_status_string(int status);
+/* Detail of the calling thread's most recent failure ("" if none). */
+const char *pkcu_last_error(void);
+/* Library version, e.g. "0.1.0". */
+const char *pkcu_version(void);
+
+/* ── batches of items (utterances / chunks) ─────────────────────────────────
+ * Ops that know about sequence structure take a pkcu_seq: n_items items of
+ * T_b frames each, concatenated. Per-item tensor layouts, item after item:
+ *   frames [T_b, D] (time-first rows)         -> offset Σ T       * D
+ *   heads  [H, T_b, 128]                       -> offset Σ T       * D
+ *   channel-first [C, T_b]                     -> offset Σ T       * C
+ *   scores [H, T_b, T_b]                       -> offset Σ H T^2
+ *   bd     [H, T_b, 2T_b-1]                    -> offset Σ H T(2T-1)
+ *   pos    [2T_b-1, D]                         -> offset Σ (2T-1)  * D
+ * The edge chunks of the reference's chunked encoder have fewer frames than
+ * the interior ones (csrc/encoder.c:531-543); a ragged batch keeps them
+ * unpadded. pkcu_seq_create allocates on the current device (ragged batches
+ * only) and synchronises; a pkcu_seq is read-only afterwards and may be shared
+ * by concurrent calls. */
+typedef struct pkcu_seq pkcu_seq;
+
+int  pkcu_seq_create(const int *lengths, int n_items, pkcu_seq **out);
+void pkcu_seq_destroy(pkcu_seq *seq);
+int       pkcu_seq_n_items(const pkcu_seq *seq);
+long long pkcu_seq_frames(const pkcu_seq *seq);       /* Σ T_b            */
+long long pkcu_seq_score_elems(const pkcu_seq *seq);  /* Σ H T_b^2        */
+long long pkcu_seq_bd_elems(const pkcu_seq *seq);     /* Σ H T_b(2T_b-1)  */
+long long pkcu_seq_pos_rows(const pkcu_seq *seq);     /* Σ (2T_b-1)       */
+
+/* ── 1. drop-in host API (csrc/parakeet.h:231-262) ────────────────────────── */
+
+/* csrc/tensor_ops.c:151 */
+void pk_layer_norm(const float *x, const float *gamma, const float *beta_, float *out, int len);
+/* csrc/tensor_ops.c:249 */
+void pk_layer_norm_rows(const float *x, const float *gamma, const float *beta_, float *out,
+                        int n_rows, int D);
+/* csrc/tensor_ops.c:275 */
+void pk_layer_norm_rows_inplace(float *x, const float *gamma, const float *beta_, int n_rows,
+                                int D);
+/* csrc/tensor_ops.c:367 */
+void pk_swish(float *x, int len);
+/* csrc/tensor_ops.c:401 */
+void pk_relu(float *x, int len);
+/* csrc/tensor_ops.c:284 */
+void pk_softmax(float *x, int len);
+/* csrc/tensor_ops.c:359 */
+void pk_softmax_rows(float *x, int n_rows, int len);
+/* csrc/tensor_ops.c:420 */
+void pk_bias_add(float *x, const float *b, int len);
+/* csrc/tensor_ops.c:570; b may be NULL (:561) */
+void pk_depthwise_conv1d(const float *x, const float *w, const float *b, float *out, int C,
+                         int T, int K);
+/* Status of the calling thread's last drop-in call: PKCU_OK or an error code
+ * (the message is in pkcu_last_error()). A failing drop-in also prints one
+ * line to stderr. */
+int pk_cuda_status(void);
+
+/* ── 2. device API ──────────────────────────────────────────────────────────
+ * The reference's tensor_ops. Any alignment is accepted here; the 16-byte
+ * aligned, D % 4 == 0 case takes the vectorised kernels. */
+
+/* pk_layer_norm_rows (csrc/tensor_ops.c:151-254): out = (x-mean)/sqrt(var+1e-5)
+ * * gamma + beta per row of D. out may equal x (pk_layer_norm_rows_inplace,
+ * :256-280). */
+int pkcu_layer_norm_rows(const float *x, const float *gamma, const float *beta, float *out,
+                         int n_rows, int D, pkcu_stream_t stream);
+/* pk_softmax_rows (csrc/tensor_ops.c:284-363), in place, rows of len. */
+int pkcu_softmax_rows(float *x, int n_rows, int len, pkcu_stream_t stream);
+/* pk_swish (csrc/tensor_ops.c:367-397) over a flat array, in place. */
+int pkcu_swish(float *x, long long n, pkcu_stream_t stream);
+/* pk_relu (csrc/tensor_ops.c:401-416), in place. */
+int pkcu_relu(float *x, long long n, pkcu_stream_t stream);
+/* pk_bias_add (csrc/tensor_ops.c:420-435) applied to each of n_rows rows. */
+int pkcu_bias_add_rows(float *x, const float *b, int n_rows, int len, pkcu_stream_t stream);
+/* pk_depthwise_conv1d (csrc/tensor_ops.c:477-575): x, out [C, T]; w [C, K];
+ * b [C] or NULL; symmetric zero padding (K-1)/2. */
+int pkcu_depthwise_conv1d(const float *x, const float *w, const float *b, float *out, int C,
+                          int T, int K, pkcu_stream_t stream);
+
+/* Feed-forward bias + Swish (csrc/encoder.c:193-196): out = swish(in + b)
+ * row-wise over [n_rows, len]; out may equal in. */
+int pkcu_bias_swish_rows(const float *in, const float *b, float *out, int n_rows, int len,
+                         pkcu_stream_t stream);
+/* Residual (csrc/encoder.c:199-216 macaron alpha=0.5, :420-434 attention
+ * alpha=1): x += alpha * (y + bias) over [n_rows, D]; bias may be NULL. */
+int pkcu_residual_add(float *x, const float *y, const float *bias, float alpha, int n_rows,
+                      int D, pkcu_stream_t stream);
+/* Residual then the next module's LayerNorm in one pass (D = 1024):
+ * x += alpha*(y + bias); ln = LN(x; gamma, beta). */
+int pkcu_residual_layer_norm(float *x, const float *y, const float *bias, float alpha,
+                             const float *gamma, const float *beta, float *ln, int n_rows,
+                             pkcu_stream_t stream);
+/* End of a block and start of the next (csrc/encoder.c:489-490 then :191):
+ * x = LN_out(x + alpha*(y + bias)) in place; when g_next != NULL also
+ * ln_next = LN_next(x). D = 1024. */
+int pkcu_residual_layer_norm2(float *x, const float *y, const float *bias, float alpha,
+                              const float *g_out, const float *b_out, const float *g_next,
+                              const float *b_next, float *ln_next, int n_rows,
+                              pkcu_stream_t stream);
+
+/* Attention head gather (csrc/encoder.c:313-356): qkv [frames, 3D] (+ bqkv
+ * [3D]) -> Qu = Q + u[h], Qv = Q + v[h], K, V, each per item [H, T_b, 128];
+ * u, v [H, 128]. */
+int pkcu_qkv_split_uv(const float *qkv, const float *bqkv, const float *u, const float *v,
+                      float *Qu, float *Qv, float *K, float *V, const pkcu_seq *seq,
+                      pkcu_stream_t stream);
+/* Positional head split (csrc/encoder.c:362-368): P per item [2T_b-1, D] ->
+ * P_h per item [H, 2T_b-1, 128]. */
+int pkcu_pos_head_split(const float *P, float *P_h, const pkcu_seq *seq, pkcu_stream_t stream);
+/* relative_shift (csrc/encoder.c:230-254): out[h,i,j] = bd[h,i,T-1-i+j]
+ * (bd per item [H,T,2T-1], out per item [H,T,T]). */
+int pkcu_relative_shift(const float *bd, float *out, const pkcu_seq *seq, pkcu_stream_t stream);
+/* Score combine (csrc/encoder.c:380-400): S = (ac + rel_shift(bd)) * scale. */
+int pkcu_relpos_combine(const float *ac, const float *bd, float *S, float scale,
+                        const pkcu_seq *seq, pkcu_stream_t stream);
+/* Score combine fused with the row softmax of csrc/encoder.c:403. S may equal ac. */
+int pkcu_relpos_combine_softmax(const float *ac, const float *bd, float *S, float scale,
+                                const pkcu_seq *seq, pkcu_stream_t stream);
+/* Head concat (csrc/encoder.c:410-415): per item [H, T_b, 128] -> [T_b, D]. */
+int pkcu_head_concat(const float *attn_h, float *attn, const pkcu_seq *seq,
+                     pkcu_stream_t stream);
+/* Conv-module LayerNorm + channel-first copy (csrc/encoder.c:446-452):
+ * x [frames, D] -> cf per item [D, T_b]. */
+int pkcu_layer_norm_transpose(const float *x, const float *gamma, const float *beta, float *cf,
+                              const pkcu_seq *seq, pkcu_stream_t stream);
+/* Attention residual (csrc/encoder.c:420-434) fused with the above:
+ * x += alpha*(y + bias); cf = channel-first LN(x). */
+int pkcu_residual_layer_norm_transpose(float *x, const float *y, const float *bias,
+                                       float alpha, const float *gamma, const float *beta,
+                                       float *cf, const pkcu_seq *seq, pkcu_stream_t stream);
+
+#define PKCU_CHANNEL_FIRST 0   /* per item [2C, T_b] -> [C, T_b] (csrc/encoder.c:457-465) */
+#define PKCU_TIME_FIRST    1   /* [frames, 2C] -> [frames, C] */
+/* GLU with the pointwise-conv bias (csrc/tensor_ops.c:585-589) folded in:
+ * a = in[c] + bias[c], g = in[C+c] + bias[C+c], out = a / (1 + exp(-g)).
+ * bias may be NULL. */
+int pkcu_glu(const float *in, const float *bias, float *out, int C, int layout,
+             const pkcu_seq *seq, pkcu_stream_t stream);
+/* Depthwise conv (csrc/tensor_ops.c:477-575) + bias, optional inference
+ * BatchNorm (bn = [mean C | var C | gamma C | beta C], or NULL: the reference
+ * folds BN into w/b offline), optional Swish (csrc/encoder.c:470), on
+ * channel-first per item [C, T_b]; w [C, K], b [C] or NULL. */
+int pkcu_dwconv_bn_swish(const float *x, const float *w, const float *b, const float *bn,
+                         float bn_eps, int apply_swish, float *out, int C, int K,
+                         const pkcu_seq *seq, pkcu_stream_t stream);
+/* Conv residual (csrc/encoder.c:475-477): x[t,d] += y[d,t] + bias[d], y per
+ * item [D, T_b] (bias: the pw2 bias, csrc/tensor_ops.c:585-589; may be NULL). */
+int pkcu_transpose_add(float *x, const float *y, const float *bias, const pkcu_seq *seq,
+                       pkcu_stream_t stream);
+/* The same fused with the FF2 LayerNorm (csrc/encoder.c:489 -> :191):
+ * x[t,d] += y[d,t] + bias[d]; ln = LN(x). */
+int pkcu_transpose_add_layer_norm(float *x, const float *y, const float *bias,
+                                  const float *gamma, const float *beta, float *ln,
+                                  const pkcu_seq *seq, pkcu_stream_t stream);
+
+/* int8 per-tensor dequant (csrc/blas.c:526-558): out = (float)q * scale. */
+int pkcu_dequant_i8(const int8_t *q, float scale, float *out, long long n, pkcu_stream_t stream);
+/* Fused-QKV int8 build (csrc/weights.c:437-487): ms = max(sq, sk, sv); each of
+ * q, k, v [K, D] requantised to ms (clamp(roundf(x * s/ms), +-127), copied
+ * when s == ms) into fused [K, 3D]. *ms_out (host) receives ms. */
+int pkcu_requant_qkv_i8(const int8_t *q, const int8_t *k, const int8_t *v, float sq, float sk,
+                        float sv, int8_t *fused, float *ms_out, int K, int D,
+                        pkcu_stream_t stream);
+#define PKCU_GROUP_ALONG_K 0   /* scales [K/G, N] */
+#define PKCU_GROUP_ALONG_N 1   /* scales [K, N/G]: the reference layout, G = 32 */
+/* int4 group dequant (csrc/blas.c:780-843, csrc/weights.c:505-515, format
+ * extract_weights.py:589-594): packed [K, N/2] bytes, low nibble = even
+ * column, signed 4-bit; out [K, N] = (float)q * scale. */
+int pkcu_dequant_i4(const uint8_t *packed, const float *scales, float *out, int K, int N,
+                    int group, int axis, pkcu_stream_t stream);
+/* Fused-QKV int4 path (csrc/weights.c:488-544): three int4 [K, D] with
+ * [K, D/G] scales -> fp32 fused [K, 3D]. */
+int pkcu_dequant_i4_qkv(const uint8_t *pq, const uint8_t *pk, const uint8_t *pv,
+                        const float *sq, const float *sk, const float *sv, float *fused, int K,
+                        int D, int group, pkcu_stream_t stream);
+
+#define PKCU_ACT_RELU 0   /* csrc/decoder.c:62-67 */
+#define PKCU_ACT_TANH 1
+/* Joint add + activation: out[b,t,j] = act(enc[b,t,j] + pred[b,j]). */
+int pkcu_joint_add_act(const float *enc, const float *pred, float *out, int B, int T, int J,
+                       int act, pkcu_stream_t stream);
+/* Greedy argmax (csrc/decoder.c:106-114): first maximum of each row of V
+ * logits, NaN never selected after index 0. out int32 [n_rows]. */
+int pkcu_argmax_rows(const float *logits, int32_t *out, long long n_rows, int V,
+                     pkcu_stream_t stream);
+
+/* ── 3. sequence driver ──────────────────────────────────────────────────── */
+
+/* Non-GEMM parameters of one conformer block (csrc/parakeet.h:78-125). */
+typedef struct {
+    const float *norm_ff1_w, *norm_ff1_b, *ff1_b1, *ff1_b2;
+    const float *norm_sa_w, *norm_sa_b, *qkv_b, *pos_u, *pos_v, *out_b;
+    const float *norm_conv_w, *norm_conv_b, *pw1_b, *dw_w, *dw_b, *pw2_b;
+    const float *norm_ff2_w, *norm_ff2_b, *ff2_b1, *ff2_b2;
+    const float *norm_out_w, *norm_out_b;
+} pkcu_block_params;
+
+/* GEMM outputs the non-GEMM ops consume (bias not yet added). */
+typedef struct {
+    const float *ff1_h;    /* [frames, 4096]     */
+    const float *ff1_out;  /* [frames, 1024]     */
+    const float *qkv;      /* [frames, 3072]     */
+    const float *P;        /* pos [2T-1, 1024]   */
+    const float *ac;       /* scores [H, T, T]   */
+    const float *bd;       /* bd [H, T, 2T-1]    */
+    const float *attn_h;   /* heads [H, T, 128]  */
+    const float *att_out;  /* [frames, 1024]     */
+    const float *pw1;      /* channel-first [2048, T] */
+    const float *pw2;      /* channel-first [1024, T] */
+    const float *ff2_h;    /* [frames, 4096]     */
+    const float *ff2_out;  /* [frames, 1024]     */
+} pkcu_gemm_outputs;
+
+/* GEMM inputs the non-GEMM ops produce (per-item layouts as above). Buffers
+ * whose consumers run one after another may alias (e.g. the four LN outputs). */
+typedef struct {
+    float *ln_ff1, *h1, *ln_sa, *Qu, *K, *Qv, *P_h, *S, *V, *attn, *cf, *dw, *ln_ff2, *h2;
+    float *gated;   /* GLU output, the depthwise conv's input [D, T] per item */
+} pkcu_gemm_inputs;
+
+/* GEMM points, in the order they occur in one block. */
+enum {
+    PKCU_GEMM_FF1_1 = 0, PKCU_GEMM_FF1_2, PKCU_GEMM_QKV, PKCU_GEMM_POS, PKCU_GEMM_AC,
+    PKCU_GEMM_BD, PKCU_GEMM_AV, PKCU_GEMM_OUT, PKCU_GEMM_PW1, PKCU_GEMM_PW2,
+    PKCU_GEMM_FF2_1, PKCU_GEMM_FF2_2
+};
+/* Called (on the host, in stream order) where a GEMM runs: it must enqueue on
+ * `stream` the product that fills the matching pkcu_gemm_outputs buffer from
+ * the pkcu_gemm_inputs buffers of block `block`. Return PKCU_OK to continue.
+ * With no hook the pkcu_gemm_outputs buffers are consumed as they are. */
+typedef int (*pkcu_gemm_hook)(void *user, int block, int gemm, pkcu_stream_t stream);
+
+/* Runs n_blocks conformer blocks' non-GEMM ops (csrc/encoder.c:482-491) on x
+ * [frames, D] in place, fused at producer/consumer boundaries:
+ *   LN_ff1 | bias+Swish | res+LN_sa | QKV split | pos split | combine+softmax |
+ *   head concat | res+LN_conv+transpose | GLU | dwconv+bias+Swish |
+ *   transpose-add+LN_ff2 | bias+Swish | res+LN_out(+LN_ff1 of the next block)
+ * All pointers are device pointers; blocks[] is a host array. */
+int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks,
+                         const pkcu_gemm_outputs *gemm_out, const pkcu_gemm_inputs *gemm_in,
+                         const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
+                         pkcu_stream_t stream);
+
+/* Number of kernel launches pkcu_encoder_nongemm makes for n_blocks blocks. */
+int pkcu_encoder_nongemm_launches(int n_blocks);
+
+/* Host-buffer form (the reference's pk_encoder takes and returns host
+ * buffers, csrc/encoder.c:612-633). A workspace owns the device copies of x,
+ * the GEMM outputs and the GEMM inputs for one batch shape, split into
+ * n_groups groups of consecutive items. pkcu_encoder_nongemm_host copies x
+ * and the GEMM outputs (host arrays in the batch layouts above) to the device,
+ * runs the sequence and copies x back, pipelining the copies of one group
+ * against the compute of the next; it returns when x_host holds the result.
+ * Host arrays should be page-locked for the copies to overlap. */
+typedef struct pkcu_encoder_ws pkcu_encoder_ws;
+int  pkcu_encoder_ws_create(const pkcu_seq *seq, int n_groups, pkcu_encoder_ws **out);
+void pkcu_encoder_ws_destroy(pkcu_encoder_ws *ws);
+/* Device views of the workspace's whole-batch buffers. */
+int  pkcu_encoder_ws_device(pkcu_encoder_ws *ws, float **x, pkcu_gemm_outputs *gemm_out,
+                            pkcu_gemm_inputs *gemm_in);
+long long pkcu_encoder_ws_device_bytes(const pkcu_encoder_ws *ws);
+long long pkcu_encoder_ws_h2d_bytes(const pkcu_encoder_ws *ws);   /* per host call */
+long long pkcu_encoder_ws_d2h_bytes(const pkcu_encoder_ws *ws);   /* per host call */
+int  pkcu_encoder_nongemm_host(pkcu_encoder_ws *ws, float *x_host,
+                               const pkcu_gemm_outputs *gemm_out_host,
+                               const pkcu_block_params *blocks, int n_blocks,
+                               pkcu_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKCUDA_H */

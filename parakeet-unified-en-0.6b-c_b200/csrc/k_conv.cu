@@ -1,0 +1,226 @@
+// k_conv.cu -- convolution-module ops: GLU and the depthwise conv with its
+// bias, optional BatchNorm and Swish.
+//
+// GLU (csrc/encoder.c:454-465): the pointwise-conv output pw1 [2C, T] gets its
+// bias (csrc/tensor_ops.c:585-589), then out[c,t] = a * 1/(1 + expf(-g)) with
+// a = pw1[c,t], g = pw1[C+c,t]. Per item the [C, T] halves are contiguous, so
+// the kernel streams both halves as flat float4 arrays (12 bytes per output).
+// The gate uses CUDA's expf; the reference's -ffast-math build uses glibc's
+// vectorised expf, so GLU is compared within tolerance.
+//
+// Depthwise conv (csrc/tensor_ops.c:477-575): out[c,t] = b[c] + sum_k
+// x[c, t-pad+k] * w[c,k], pad = (K-1)/2, taps outside [0, T) skipped, the sum
+// accumulated in k order as a fused multiply-add chain from the bias (the
+// reference's vectorised interior). Then optional inference BatchNorm
+// ((y - mean)/sqrtf(var + eps))*gamma + beta and optional Swish (the pk_swish
+// call of csrc/encoder.c:470, polynomial on the first 8*floor(C*T/8) entries of
+// the item). One warp per channel row; 128-output chunks of the row plus the
+// K-1 halo are staged in shared memory so every input element is read from HBM
+// once (8 bytes per output).
+#include <math.h>
+
+#include "pk_common.cuh"
+
+namespace pk {
+
+constexpr int GLU_THREADS = 256;
+constexpr int DW_WARPS = 8;
+constexpr int DW_CHUNK = 128;
+constexpr int DW_MAX_K = PK_DW_MAX_K;
+constexpr int DW_SMEM_PER_WARP = DW_CHUNK + DW_MAX_K - 1;
+
+__device__ __forceinline__ float glu1(float a, float g) { return a * sigmoid_libm(g); }
+
+// Channel-first GLU over each item's [2C, T] block.
+__global__ void __launch_bounds__(GLU_THREADS)
+glu_cf_kernel(const float *__restrict__ in, const float *__restrict__ bias, float *__restrict__ out,
+              int C, SeqDev seq, int vec) {
+  const int item = blockIdx.y;
+  const int T = seq_T(seq, item);
+  const long long f0 = seq_frame_off(seq, item);
+  const long long n = (long long)C * T;
+  const float *A = in + 2 * f0 * C;
+  const float *G = A + n;
+  float *O = out + f0 * C;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    for (; i < (n >> 2); i += stride) {
+      const long long e = 4 * i;
+      float4 a = ldg4_stream(A + e), g = ldg4_stream(G + e);
+      if (bias) {
+        int d = (int)(e / T), r = (int)(e - (long long)d * T);
+        float av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          av[k] = av[k] + __ldg(bias + d);
+          gv[k] = gv[k] + __ldg(bias + C + d);
+          if (++r == T) { r = 0; d++; }
+        }
+        a = make_float4(av[0], av[1], av[2], av[3]);
+        g = make_float4(gv[0], gv[1], gv[2], gv[3]);
+      }
+      st4(O + e, make_float4(glu1(a.x, g.x), glu1(a.y, g.y), glu1(a.z, g.z), glu1(a.w, g.w)));
+    }
+  } else {
+    for (; i < n; i += stride) {
+      float a = A[i], g = G[i];
+      if (bias) {
+        const int d = (int)(i / T);
+        a = a + bias[d];
+        g = g + bias[C + d];
+      }
+      O[i] = glu1(a, g);
+    }
+  }
+}
+
+// Time-first GLU: rows [2C] -> [C], split along the channel axis.
+__global__ void __launch_bounds__(GLU_THREADS)
+glu_tf_kernel(const float *__restrict__ in, const float *__restrict__ bias, float *__restrict__ out,
+              int C, long long n) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long row = e / C;
+    const int c = (int)(e - row * C);
+    float a = in[row * 2 * C + c], g = in[row * 2 * C + C + c];
+    if (bias) { a = a + bias[c]; g = g + bias[C + c]; }
+    out[e] = glu1(a, g);
+  }
+}
+
+// KC > 0: compile-time kernel width (taps in registers); KC == 0: runtime K.
+template <int KC>
+__global__ void __launch_bounds__(32 * DW_WARPS)
+dwconv_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
+              const float *__restrict__ bn, float bn_eps, int apply_swish, float *__restrict__ out,
+              int C, int Kr, SeqDev seq) {
+  __shared__ float stage[DW_WARPS][DW_SMEM_PER_WARP];
+  const int K = KC > 0 ? KC : Kr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * DW_WARPS + warp;
+  if (c >= C) return;
+  const int item = blockIdx.y;
+  const int T = seq_T(seq, item);
+  const long long base = seq_frame_off(seq, item) * C + (long long)c * T;
+  const int pad = (K - 1) / 2;
+  const long long n8 = ((long long)C * T) & ~7LL;
+  float wk[KC > 0 ? KC : 1];
+  if (KC > 0) {
+#pragma unroll
+    for (int k = 0; k < (KC > 0 ? KC : 1); k++) wk[k] = __ldg(w + (long long)c * K + k);
+  }
+  const float bias = b ? __ldg(b + c) : 0.0f;
+  float mean = 0.0f, den = 1.0f, gam = 1.0f, bet = 0.0f;
+  if (bn) {
+    mean = __ldg(bn + c);
+    den = sqrtf(__ldg(bn + C + c) + bn_eps);
+    gam = __ldg(bn + 2 * C + c);
+    bet = __ldg(bn + 3 * C + c);
+  }
+  float *s = stage[warp];
+  for (int t0 = 0; t0 < T; t0 += DW_CHUNK) {
+    for (int k = lane; k < DW_CHUNK + K - 1; k += 32) {
+      const int tt = t0 - pad + k;
+      s[k] = (tt >= 0 && tt < T) ? x[base + tt] : 0.0f;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < DW_CHUNK / 32; j++) {
+      const int o = lane + 32 * j;
+      const int t = t0 + o;
+      if (t >= T) break;
+      float val = bias;
+      if (KC > 0) {
+#pragma unroll
+        for (int k = 0; k < (KC > 0 ? KC : 1); k++) {
+          const int tt = t - pad + k;
+          if (tt >= 0 && tt < T) val = fmaf(s[o + k], wk[k], val);
+        }
+      } else {
+        for (int k = 0; k < K; k++) {
+          const int tt = t - pad + k;
+          if (tt >= 0 && tt < T) val = fmaf(s[o + k], __ldg(w + (long long)c * K + k), val);
+        }
+      }
+      if (bn) val = ((val - mean) / den) * gam + bet;
+      if (apply_swish) {
+        const long long flat = (long long)c * T + t;
+        val = (flat < n8) ? swish_poly(val) : swish_tail(val);
+      }
+      out[base + t] = val;
+    }
+    __syncwarp();
+  }
+}
+
+static unsigned per_item_grid(long long work, int n_items) {
+  long long g = (work + GLU_THREADS - 1) / GLU_THREADS;
+  long long cap = ((long long)pkcu_sm_count() * 16 + n_items - 1) / n_items;
+  if (cap < 1) cap = 1;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
+static int launch_dwconv(const float *x, const float *w, const float *b, const float *bn,
+                         float bn_eps, int apply_swish, float *out, int C, int K, SeqDev sd,
+                         cudaStream_t s) {
+  dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
+  if (K == 9)
+    dwconv_kernel<9><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
+  else
+    dwconv_kernel<0><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
+  return PKCU_OK;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" int pkcu_glu(const float *in, const float *bias, float *out, int C, int layout,
+                        const pkcu_seq *seq, pkcu_stream_t stream) {
+  if (!in || !out || !seq || C <= 0 ||
+      (layout != PKCU_CHANNEL_FIRST && layout != PKCU_TIME_FIRST))
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_glu: bad argument");
+  if (seq->dev.n_items > 65535)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_glu: at most 65535 items per call");
+  if (seq->frames == 0) return PKCU_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (layout == PKCU_CHANNEL_FIRST) {
+    const int vec = (C % 4 == 0) && PK_ALIGNED16(in) && PK_ALIGNED16(out);
+    const long long per = (long long)C * seq->dev.max_T;
+    dim3 grid(per_item_grid(vec ? per / 4 : per, seq->dev.n_items), (unsigned)seq->dev.n_items);
+    glu_cf_kernel<<<grid, GLU_THREADS, 0, s>>>(in, bias, out, C, seq->dev, vec);
+  } else {
+    const long long n = seq->frames * C;
+    long long g = (n + GLU_THREADS * 4 - 1) / (GLU_THREADS * 4);
+    if (g > (long long)pkcu_sm_count() * 32) g = (long long)pkcu_sm_count() * 32;
+    glu_tf_kernel<<<(unsigned)g, GLU_THREADS, 0, s>>>(in, bias, out, C, n);
+  }
+  return pkcu_launch_status("pkcu_glu");
+}
+
+extern "C" int pkcu_dwconv_bn_swish(const float *x, const float *w, const float *b,
+                                    const float *bn, float bn_eps, int apply_swish, float *out,
+                                    int C, int K, const pkcu_seq *seq, pkcu_stream_t stream) {
+  if (!x || !w || !out || !seq || C <= 0 || K <= 0 || K > DW_MAX_K)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_dwconv_bn_swish: bad argument (K must be 1..%d)",
+                     DW_MAX_K);
+  if (seq->dev.n_items > 65535)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_dwconv_bn_swish: at most 65535 items per call");
+  if (seq->frames == 0) return PKCU_OK;
+  launch_dwconv(x, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, (cudaStream_t)stream);
+  return pkcu_launch_status("pkcu_dwconv_bn_swish");
+}
+
+extern "C" int pkcu_depthwise_conv1d(const float *x, const float *w, const float *b, float *out,
+                                     int C, int T, int K, pkcu_stream_t stream) {
+  if (!x || !w || !out || C < 0 || T < 0 || K <= 0 || K > DW_MAX_K)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_depthwise_conv1d: bad argument (K must be 1..%d)",
+                     DW_MAX_K);
+  if (C == 0 || T == 0) return PKCU_OK;
+  pkcu_seq_dev sd = {1, T, T, nullptr, nullptr, nullptr, nullptr, nullptr};
+  launch_dwconv(x, w, b, nullptr, 0.0f, 0, out, C, K, sd, (cudaStream_t)stream);
+  return pkcu_launch_status("pkcu_depthwise_conv1d");
+}

@@ -1,0 +1,155 @@
+// pk_common.cuh -- device helpers shared by the sm_100a kernels of the
+// non-GEMM encoder ops (LayerNorm, softmax, rel-pos scores, Swish, GLU,
+// depthwise conv, residuals, dequant, joint, argmax).
+//
+// All kernel translation units are compiled with --fmad=false: a multiply and
+// an add round separately unless the code calls fmaf(), which is where the
+// reference's AVX2 path (csrc/tensor_ops.c, csrc/encoder.c) fuses them.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "pkcuda_internal.h"
+
+#define PK_FULL_MASK 0xffffffffu
+
+namespace pk {
+
+// ── reductions ───────────────────────────────────────────────────────────────
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(PK_FULL_MASK, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(PK_FULL_MASK, v, o));
+  return v;
+}
+
+// Sum over a CTA whose size is a multiple of 32; every thread gets the result.
+// red must hold 33 floats of shared memory.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < nw ? red[lane] : 0.0f;
+    t = warp_sum(t);
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < nw ? red[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// ── the reference's polynomial exp ───────────────────────────────────────────
+//
+// Restates pk_exp_avx2 (csrc/tensor_ops.c:97-121) operation by operation so the
+// GPU result is bit-identical to it: clamp to [-87, 87] (max first, so NaN
+// becomes -87 as with _mm256_max_ps), k = round-half-even(x * log2 e),
+// r = x - k ln2 as one fused multiply-add (the reference build contracts it),
+// Horner evaluation of the degree-5 Taylor polynomial with FMAs, and 2^k built
+// directly in the exponent field.
+__device__ __forceinline__ float exp_poly(float x) {
+  x = (x > -87.0f) ? x : -87.0f;
+  x = (x < 87.0f) ? x : 87.0f;
+  const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+  const int ki = __float2int_rn(kf);
+  const float r = fmaf(-kf, 0.69314718055994529f, x);
+  float y = 1.0f / 120.0f;
+  y = fmaf(y, r, 1.0f / 24.0f);
+  y = fmaf(y, r, 1.0f / 6.0f);
+  y = fmaf(y, r, 0.5f);
+  y = fmaf(y, r, 1.0f);
+  y = fmaf(y, r, 1.0f);
+  return __fmul_rn(y, __int_as_float((ki + 127) << 23));
+}
+
+// Swish of the vector body of pk_swish (csrc/tensor_ops.c:383-388):
+// v * (1 / (1 + exp(0 - v))) with an IEEE division.
+__device__ __forceinline__ float swish_poly(float v) {
+  const float e = exp_poly(__fsub_rn(0.0f, v));
+  return __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+}
+
+// Swish of the scalar tail of pk_swish (csrc/tensor_ops.c:389): x / (1 + expf(-x)).
+__device__ __forceinline__ float swish_tail(float v) {
+  return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+}
+
+// Sigmoid gate of the GLU (csrc/encoder.c:462): 1 / (1 + expf(-b)).
+__device__ __forceinline__ float sigmoid_libm(float b) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)));
+}
+
+// ── ragged batches ───────────────────────────────────────────────────────────
+//
+// A batch of independent utterances / chunks with per-item frame counts T_b.
+// Per-item tensors are concatenated item after item. Uniform batches carry
+// no device arrays: every offset is computed from uniform_T.
+using SeqDev = pkcu_seq_dev;
+
+__device__ __forceinline__ int seq_T(const SeqDev &s, int b) {
+  return s.uniform_T > 0 ? s.uniform_T : __ldg(s.T + b);
+}
+__device__ __forceinline__ long long seq_frame_off(const SeqDev &s, int b) {
+  return s.uniform_T > 0 ? (long long)b * s.uniform_T : __ldg(s.frame_off + b);
+}
+__device__ __forceinline__ long long seq_score_off(const SeqDev &s, int b) {
+  return s.uniform_T > 0 ? (long long)b * PK_H * s.uniform_T * s.uniform_T
+                         : __ldg(s.score_off + b);
+}
+__device__ __forceinline__ long long seq_bd_off(const SeqDev &s, int b) {
+  return s.uniform_T > 0 ? (long long)b * PK_H * s.uniform_T * (2LL * s.uniform_T - 1)
+                         : __ldg(s.bd_off + b);
+}
+__device__ __forceinline__ long long seq_pos_off(const SeqDev &s, int b) {
+  return s.uniform_T > 0 ? (long long)b * (2LL * s.uniform_T - 1) : __ldg(s.pos_off + b);
+}
+
+// ── memory helpers ───────────────────────────────────────────────────────────
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+// Read once: cache-streaming load (evict-first).
+__device__ __forceinline__ float4 ldg4_stream(const float *p) {
+  return __ldcs(reinterpret_cast<const float4 *>(p));
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                     __fadd_rn(a.w, b.w));
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device (the first
+// launch on each device; later launches, including ones under stream
+// capture, make no attribute call). `flags` is a per-kernel static array.
+template <typename K>
+inline void smem_optin(K kernel, size_t bytes, int *flags) {
+  const int dev = pkcu_device();
+  if (dev < 64 && flags[dev] >= (int)bytes) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (dev < 64) flags[dev] = (int)bytes;
+}
+
+}  // namespace pk

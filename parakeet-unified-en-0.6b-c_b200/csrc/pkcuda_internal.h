@@ -1,0 +1,58 @@
+/* pkcuda_internal.h -- definitions shared by the C host code and the CUDA
+ * kernels of libpk_tensor_ops_cuda.so. Not installed; the public interface is
+ * include/pkcuda.h. */
+#ifndef PKCUDA_INTERNAL_H
+#define PKCUDA_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include "pkcuda.h"
+
+#define PK_D   1024   /* model width (csrc/parakeet.h:15) */
+#define PK_H   8      /* attention heads (:16) */
+#define PK_DH  128    /* head width (:17) */
+#define PK_FF  4096   /* feed-forward width (:18) */
+#define PK_DW_MAX_K 129  /* widest depthwise kernel the conv kernels stage */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Device view of a batch of items (utterances or chunks) of T_b frames each,
+ * concatenated item after item. uniform_T > 0: all items share that length and
+ * the array pointers are NULL. */
+typedef struct {
+    int n_items;
+    int uniform_T;
+    int max_T;
+    const int *T;
+    const long long *frame_off;
+    const long long *score_off;
+    const long long *bd_off;
+    const long long *pos_off;
+} pkcu_seq_dev;
+
+struct pkcu_seq {
+    pkcu_seq_dev dev;
+    int *lengths;            /* host copy [n_items] */
+    long long frames, score_elems, bd_elems, pos_rows;
+    void *dev_block;         /* one cudaMalloc holding the device arrays (ragged only) */
+    int device;
+};
+
+/* Records a failure message for pkcu_last_error() and returns status. */
+int pkcu_fail(int status, const char *fmt, ...);
+/* Maps the last launch error (cudaGetLastError) to a status. */
+int pkcu_launch_status(const char *what);
+/* Streaming multiprocessor count of the current device (cached). */
+int pkcu_sm_count(void);
+/* Current device index, or 0. */
+int pkcu_device(void);
+
+#define PK_ALIGNED16(p) ((((uintptr_t)(p)) & 15u) == 0)
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

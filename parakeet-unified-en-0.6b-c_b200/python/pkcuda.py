@@ -1,0 +1,313 @@
+"""ctypes binding of libpk_tensor_ops_cuda.so for Python callers (tests, bench).
+
+The library is plain C (include/pkcuda.h); this module only marshals
+arguments. Device buffers are torch CUDA tensors (torch is used for device
+memory and streams only); every call goes through the C ABI and raises
+PkCudaError on a non-zero status. There is no CPU fallback: if the shared
+library is missing, loading fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libpk_tensor_ops_cuda.so")
+CSRC_DIR = os.path.join(PKG_DIR, "csrc")
+
+D, H, DH, FF = 1024, 8, 128, 4096
+PKCU_CHANNEL_FIRST, PKCU_TIME_FIRST = 0, 1
+PKCU_GROUP_ALONG_K, PKCU_GROUP_ALONG_N = 0, 1
+PKCU_ACT_RELU, PKCU_ACT_TANH = 0, 1
+
+# Symbols declared by include/pkcuda.h (checked by the CPU test suite).
+EXPORTED = (
+    "pkcu_status_string", "pkcu_last_error", "pkcu_version",
+    "pkcu_seq_create", "pkcu_seq_destroy", "pkcu_seq_n_items", "pkcu_seq_frames",
+    "pkcu_seq_score_elems", "pkcu_seq_bd_elems", "pkcu_seq_pos_rows",
+    "pk_layer_norm", "pk_layer_norm_rows", "pk_layer_norm_rows_inplace", "pk_swish", "pk_relu",
+    "pk_softmax", "pk_softmax_rows", "pk_bias_add", "pk_depthwise_conv1d", "pk_cuda_status",
+    "pkcu_layer_norm_rows", "pkcu_softmax_rows", "pkcu_swish", "pkcu_relu", "pkcu_bias_add_rows",
+    "pkcu_depthwise_conv1d", "pkcu_bias_swish_rows", "pkcu_residual_add",
+    "pkcu_residual_layer_norm", "pkcu_residual_layer_norm2", "pkcu_qkv_split_uv",
+    "pkcu_pos_head_split", "pkcu_relative_shift", "pkcu_relpos_combine",
+    "pkcu_relpos_combine_softmax", "pkcu_head_concat", "pkcu_layer_norm_transpose",
+    "pkcu_residual_layer_norm_transpose", "pkcu_glu", "pkcu_dwconv_bn_swish",
+    "pkcu_transpose_add", "pkcu_transpose_add_layer_norm", "pkcu_dequant_i8",
+    "pkcu_requant_qkv_i8", "pkcu_dequant_i4", "pkcu_dequant_i4_qkv", "pkcu_joint_add_act",
+    "pkcu_argmax_rows", "pkcu_encoder_nongemm", "pkcu_encoder_nongemm_launches",
+    "pkcu_encoder_ws_create", "pkcu_encoder_ws_destroy", "pkcu_encoder_ws_device",
+    "pkcu_encoder_ws_device_bytes", "pkcu_encoder_ws_h2d_bytes", "pkcu_encoder_ws_d2h_bytes",
+    "pkcu_encoder_nongemm_host",
+)
+
+
+class PkCudaError(RuntimeError):
+    pass
+
+
+VP, I, LL, F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
+
+_SIGS = {
+    "pkcu_status_string": (C.c_char_p, [I]),
+    "pkcu_last_error": (C.c_char_p, []),
+    "pkcu_version": (C.c_char_p, []),
+    "pkcu_seq_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
+    "pkcu_seq_destroy": (None, [VP]),
+    "pkcu_seq_n_items": (I, [VP]),
+    "pkcu_seq_frames": (LL, [VP]),
+    "pkcu_seq_score_elems": (LL, [VP]),
+    "pkcu_seq_bd_elems": (LL, [VP]),
+    "pkcu_seq_pos_rows": (LL, [VP]),
+    "pk_layer_norm": (None, [VP, VP, VP, VP, I]),
+    "pk_layer_norm_rows": (None, [VP, VP, VP, VP, I, I]),
+    "pk_layer_norm_rows_inplace": (None, [VP, VP, VP, I, I]),
+    "pk_swish": (None, [VP, I]),
+    "pk_relu": (None, [VP, I]),
+    "pk_softmax": (None, [VP, I]),
+    "pk_softmax_rows": (None, [VP, I, I]),
+    "pk_bias_add": (None, [VP, VP, I]),
+    "pk_depthwise_conv1d": (None, [VP, VP, VP, VP, I, I, I]),
+    "pk_cuda_status": (I, []),
+    "pkcu_layer_norm_rows": (I, [VP, VP, VP, VP, I, I, VP]),
+    "pkcu_softmax_rows": (I, [VP, I, I, VP]),
+    "pkcu_swish": (I, [VP, LL, VP]),
+    "pkcu_relu": (I, [VP, LL, VP]),
+    "pkcu_bias_add_rows": (I, [VP, VP, I, I, VP]),
+    "pkcu_depthwise_conv1d": (I, [VP, VP, VP, VP, I, I, I, VP]),
+    "pkcu_bias_swish_rows": (I, [VP, VP, VP, I, I, VP]),
+    "pkcu_residual_add": (I, [VP, VP, VP, F, I, I, VP]),
+    "pkcu_residual_layer_norm": (I, [VP, VP, VP, F, VP, VP, VP, I, VP]),
+    "pkcu_residual_layer_norm2": (I, [VP, VP, VP, F, VP, VP, VP, VP, VP, I, VP]),
+    "pkcu_qkv_split_uv": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP, VP]),
+    "pkcu_pos_head_split": (I, [VP, VP, VP, VP]),
+    "pkcu_relative_shift": (I, [VP, VP, VP, VP]),
+    "pkcu_relpos_combine": (I, [VP, VP, VP, F, VP, VP]),
+    "pkcu_relpos_combine_softmax": (I, [VP, VP, VP, F, VP, VP]),
+    "pkcu_head_concat": (I, [VP, VP, VP, VP]),
+    "pkcu_layer_norm_transpose": (I, [VP, VP, VP, VP, VP, VP]),
+    "pkcu_residual_layer_norm_transpose": (I, [VP, VP, VP, F, VP, VP, VP, VP, VP]),
+    "pkcu_glu": (I, [VP, VP, VP, I, I, VP, VP]),
+    "pkcu_dwconv_bn_swish": (I, [VP, VP, VP, VP, F, I, VP, I, I, VP, VP]),
+    "pkcu_transpose_add": (I, [VP, VP, VP, VP, VP]),
+    "pkcu_transpose_add_layer_norm": (I, [VP, VP, VP, VP, VP, VP, VP, VP]),
+    "pkcu_dequant_i8": (I, [VP, F, VP, LL, VP]),
+    "pkcu_requant_qkv_i8": (I, [VP, VP, VP, F, F, F, VP, C.POINTER(F), I, I, VP]),
+    "pkcu_dequant_i4": (I, [VP, VP, VP, I, I, I, I, VP]),
+    "pkcu_dequant_i4_qkv": (I, [VP, VP, VP, VP, VP, VP, VP, I, I, I, VP]),
+    "pkcu_joint_add_act": (I, [VP, VP, VP, I, I, I, I, VP]),
+    "pkcu_argmax_rows": (I, [VP, VP, LL, I, VP]),
+    "pkcu_encoder_nongemm": (I, [VP, VP, I, VP, VP, VP, VP, VP, VP]),
+    "pkcu_encoder_nongemm_launches": (I, [I]),
+    "pkcu_encoder_ws_create": (I, [VP, I, C.POINTER(VP)]),
+    "pkcu_encoder_ws_destroy": (None, [VP]),
+    "pkcu_encoder_ws_device": (I, [VP, C.POINTER(VP), VP, VP]),
+    "pkcu_encoder_ws_device_bytes": (LL, [VP]),
+    "pkcu_encoder_ws_h2d_bytes": (LL, [VP]),
+    "pkcu_encoder_ws_d2h_bytes": (LL, [VP]),
+    "pkcu_encoder_nongemm_host": (I, [VP, VP, VP, VP, I, VP]),
+}
+
+_lib = None
+
+
+def build(verbose: bool = False) -> str:
+    """Compile the library in-tree (make in csrc/); returns the .so path."""
+    out = subprocess.run(["make", "-C", CSRC_DIR, "-j8"], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("libpk_tensor_ops_cuda build failed:\n" + out.stdout + out.stderr)
+    if verbose:
+        print(out.stdout)
+    return LIB_PATH
+
+
+def lib():
+    """The loaded shared library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise PkCudaError(f"{LIB_PATH} is missing: run __graft_entry__.build() "
+                              "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().pkcu_last_error().decode()
+
+
+def check(status: int, what: str = "") -> None:
+    if status != 0:
+        L = lib()
+        raise PkCudaError(f"{what}: {L.pkcu_status_string(status).decode()}: "
+                          f"{L.pkcu_last_error().decode()}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+# ── torch plumbing ────────────────────────────────────────────────────────────
+
+def ptr(t) -> int | None:
+    """Device address of a torch tensor (None for None)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_handle(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class Seq:
+    """A pkcu_seq batch descriptor (items of T_b frames)."""
+
+    def __init__(self, lengths):
+        self.lengths = [int(t) for t in lengths]
+        arr = (I * len(self.lengths))(*self.lengths)
+        h = VP()
+        check(lib().pkcu_seq_create(arr, len(self.lengths), C.byref(h)), "pkcu_seq_create")
+        self.handle = h
+
+    @property
+    def frames(self) -> int:
+        return lib().pkcu_seq_frames(self.handle)
+
+    @property
+    def score_elems(self) -> int:
+        return lib().pkcu_seq_score_elems(self.handle)
+
+    @property
+    def bd_elems(self) -> int:
+        return lib().pkcu_seq_bd_elems(self.handle)
+
+    @property
+    def pos_rows(self) -> int:
+        return lib().pkcu_seq_pos_rows(self.handle)
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_seq_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ── sequence driver structs ───────────────────────────────────────────────────
+
+BLOCK_PARAM_FIELDS = ("norm_ff1_w", "norm_ff1_b", "ff1_b1", "ff1_b2", "norm_sa_w", "norm_sa_b",
+                      "qkv_b", "pos_u", "pos_v", "out_b", "norm_conv_w", "norm_conv_b", "pw1_b",
+                      "dw_w", "dw_b", "pw2_b", "norm_ff2_w", "norm_ff2_b", "ff2_b1", "ff2_b2",
+                      "norm_out_w", "norm_out_b")
+GEMM_OUT_FIELDS = ("ff1_h", "ff1_out", "qkv", "P", "ac", "bd", "attn_h", "att_out", "pw1", "pw2",
+                   "ff2_h", "ff2_out")
+GEMM_IN_FIELDS = ("ln_ff1", "h1", "ln_sa", "Qu", "K", "Qv", "P_h", "S", "V", "attn", "cf", "dw",
+                  "ln_ff2", "h2", "gated")
+
+
+class BlockParams(C.Structure):
+    _fields_ = [(f, VP) for f in BLOCK_PARAM_FIELDS]
+
+
+class GemmOutputs(C.Structure):
+    _fields_ = [(f, VP) for f in GEMM_OUT_FIELDS]
+
+
+class GemmInputs(C.Structure):
+    _fields_ = [(f, VP) for f in GEMM_IN_FIELDS]
+
+
+def block_params_array(blocks):
+    """blocks: list of {field: tensor} -> ctypes array of pkcu_block_params."""
+    arr = (BlockParams * len(blocks))()
+    for i, b in enumerate(blocks):
+        for f in BLOCK_PARAM_FIELDS:
+            setattr(arr[i], f, ptr(b[f]))
+    return arr
+
+
+def gemm_outputs(d) -> GemmOutputs:
+    g = GemmOutputs()
+    for f in GEMM_OUT_FIELDS:
+        setattr(g, f, ptr(d[f]))
+    return g
+
+
+def gemm_inputs(d) -> GemmInputs:
+    g = GemmInputs()
+    for f in GEMM_IN_FIELDS:
+        setattr(g, f, ptr(d[f]))
+    return g
+
+
+class EncoderWorkspace:
+    """pkcu_encoder_ws: device buffers of one batch shape, n_groups pipeline groups."""
+
+    def __init__(self, seq: Seq, n_groups: int):
+        h = VP()
+        check(lib().pkcu_encoder_ws_create(seq.handle, n_groups, C.byref(h)),
+              "pkcu_encoder_ws_create")
+        self.handle = h
+        self.seq = seq
+
+    def device(self):
+        """(x address, GemmOutputs, GemmInputs) of the device buffers."""
+        x = VP()
+        go, gi = GemmOutputs(), GemmInputs()
+        check(lib().pkcu_encoder_ws_device(self.handle, C.byref(x), C.byref(go), C.byref(gi)),
+              "pkcu_encoder_ws_device")
+        return x.value, go, gi
+
+    @property
+    def device_bytes(self) -> int:
+        return lib().pkcu_encoder_ws_device_bytes(self.handle)
+
+    @property
+    def h2d_bytes(self) -> int:
+        return lib().pkcu_encoder_ws_h2d_bytes(self.handle)
+
+    @property
+    def d2h_bytes(self) -> int:
+        return lib().pkcu_encoder_ws_d2h_bytes(self.handle)
+
+    def run_host(self, x_host_addr: int, gout_host: GemmOutputs, blocks_arr, n_blocks: int,
+                 stream=None) -> None:
+        call("pkcu_encoder_nongemm_host", self.handle, x_host_addr, C.cast(C.pointer(gout_host), VP),
+             C.cast(blocks_arr, VP), n_blocks, stream_handle(stream))
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_encoder_ws_destroy(self.handle)
+            self.handle = VP()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def encoder_nongemm(x, blocks_arr, n_blocks, gout: GemmOutputs, gin: GemmInputs, seq: Seq,
+                    stream=None) -> None:
+    call("pkcu_encoder_nongemm", x if isinstance(x, int) else ptr(x), C.cast(blocks_arr, VP), n_blocks,
+         C.cast(C.pointer(gout), VP), C.cast(C.pointer(gin), VP), seq.handle, None, None,
+         stream_handle(stream))

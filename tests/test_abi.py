@@ -1,0 +1,109 @@
+"""CPU: the C ABI of libpk_tensor_ops_cuda.so (no kernel launches).
+
+Checks that the built library loads, exports every function include/pkcuda.h
+declares, and rejects bad arguments with PKCU_ERR_ARG before touching a GPU.
+"""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+import pkcuda
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "pkcuda.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(pk(?:cu)?_\w+)\s*\(", src, flags=re.M)
+    return sorted(set(n for n in names if not n.endswith("_t")))
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not os.path.exists(pkcuda.LIB_PATH):
+        pkcuda.build()
+    return pkcuda.lib()
+
+
+def test_header_declares_expected_surface():
+    names = header_functions()
+    assert set(names) == set(pkcuda.EXPORTED), set(names) ^ set(pkcuda.EXPORTED)
+
+
+def test_library_exports_every_header_symbol(L):
+    out = subprocess.run(["nm", "-D", "--defined-only", pkcuda.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [n for n in header_functions() if n not in exported]
+    assert not missing, missing
+
+
+def test_dropin_prototypes_match_reference_header():
+    """The drop-in block repeats csrc/parakeet.h:231-262 prototype for prototype."""
+    src = open(HEADER).read()
+    for proto in (
+        "void pk_layer_norm(const float *x, const float *gamma, const float *beta_, float *out, int len);",
+        "void pk_swish(float *x, int len);",
+        "void pk_relu(float *x, int len);",
+        "void pk_softmax(float *x, int len);",
+        "void pk_softmax_rows(float *x, int n_rows, int len);",
+        "void pk_bias_add(float *x, const float *b, int len);",
+    ):
+        assert proto in src, proto
+
+
+def test_status_strings(L):
+    assert L.pkcu_status_string(0) == b"ok"
+    assert L.pkcu_status_string(1) == b"invalid argument"
+    assert L.pkcu_status_string(2) == b"CUDA error"
+    assert L.pkcu_version().decode().count(".") == 2
+    assert L.pkcu_encoder_nongemm_launches(24) == 1 + 13 * 24
+
+
+def test_argument_validation_without_gpu(L):
+    ERR_ARG = 1
+    assert L.pkcu_layer_norm_rows(None, None, None, None, 4, 1024, None) == ERR_ARG
+    assert b"pkcu_layer_norm_rows" in L.pkcu_last_error()
+    assert L.pkcu_softmax_rows(None, 1, 5, None) == ERR_ARG
+    assert L.pkcu_swish(None, 5, None) == ERR_ARG
+    assert L.pkcu_relu(None, 5, None) == ERR_ARG
+    assert L.pkcu_depthwise_conv1d(None, None, None, None, 4, 4, 9, None) == ERR_ARG
+    assert L.pkcu_dequant_i4(None, None, None, 4, 7, 32, 1, None) == ERR_ARG  # odd N
+    assert L.pkcu_argmax_rows(None, None, 3, 1025, None) == ERR_ARG
+    assert L.pkcu_joint_add_act(None, None, None, 1, 1, 640, 7, None) == ERR_ARG
+    # misaligned pointer where 16-byte alignment is required
+    assert L.pkcu_residual_layer_norm(3, 16, None, C.c_float(1.0), 16, 16, 16, 4, None) == ERR_ARG
+    assert b"aligned" in L.pkcu_last_error()
+    # NULL batch descriptor
+    assert L.pkcu_qkv_split_uv(16, None, 16, 16, 16, 16, 16, 16, None, None) == ERR_ARG
+    assert L.pkcu_encoder_nongemm(None, None, 1, None, None, None, None, None, None) == ERR_ARG
+
+
+def test_requant_rejects_bad_scales(L):
+    ms = C.c_float()
+    assert L.pkcu_requant_qkv_i8(16, 16, 16, 0.0, 1.0, 1.0, 16, C.byref(ms), 4, 16, None) == 1
+
+
+def test_seq_rejects_bad_lengths(L):
+    h = C.c_void_p()
+    arr = (C.c_int * 3)(5, 0, 7)
+    assert L.pkcu_seq_create(arr, 3, C.byref(h)) == 1
+    assert not h.value
+    assert L.pkcu_seq_create(arr, 0, C.byref(h)) == 1
+
+
+def test_uniform_seq_needs_no_device(L):
+    """A uniform batch keeps no device arrays: its offsets are arithmetic."""
+    h = C.c_void_p()
+    arr = (C.c_int * 4)(375, 375, 375, 375)
+    assert L.pkcu_seq_create(arr, 4, C.byref(h)) == 0
+    assert L.pkcu_seq_frames(h) == 1500
+    assert L.pkcu_seq_score_elems(h) == 4 * 8 * 375 * 375
+    assert L.pkcu_seq_bd_elems(h) == 4 * 8 * 375 * 749
+    assert L.pkcu_seq_pos_rows(h) == 4 * 749
+    L.pkcu_seq_destroy(h)

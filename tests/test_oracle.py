@@ -1,0 +1,203 @@
+"""CPU: the restatement (oracle/) pinned against the reference.
+
+Three kinds of evidence:
+  * golden vectors produced by the reference's own compiled code
+    (tests/golden/reference_vectors.npz, tests/golden/make_golden.py);
+  * the reference library itself at the BASELINE shapes (T = 32, 375, 416),
+    when oracle/_ref/libpkref.so was built;
+  * known answers that follow from the reference code: the closed form of
+    relative_shift, first-maximum argmax, int4 nibble order, requant rounding.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_bitexact, assert_close
+
+import pyoracle as po
+
+
+# ── golden vectors ───────────────────────────────────────────────────────────
+
+def test_golden_layer_norm(oracle, golden):
+    assert_close(oracle.layer_norm_rows(golden["ln_x"], golden["ln_g"], golden["ln_b"]),
+                 golden["ln_out"], "ln")
+    assert_close(oracle.layer_norm_rows(golden["ln37_x"], golden["ln37_g"], golden["ln37_b"]),
+                 golden["ln37_out"], "ln D=37")
+
+
+@pytest.mark.parametrize("name", ["sm7", "sm375", "sm32"])
+def test_golden_softmax(oracle, golden, name):
+    assert_close(oracle.softmax_rows(golden[name + "_x"]), golden[name + "_out"], name)
+
+
+def test_golden_swish_relu(oracle, golden):
+    assert_close(oracle.swish(golden["swish_x"]), golden["swish_out"], "swish")
+    assert_bitexact(oracle.relu(golden["relu_x"]), golden["relu_out"], "relu")
+
+
+def test_golden_dwconv(oracle, golden):
+    assert_close(oracle.depthwise_conv1d(golden["dw_x"], golden["dw_w"], golden["dw_b"]),
+                 golden["dw_out"], "dwconv k=9")
+    assert_close(oracle.depthwise_conv1d(golden["dw5_x"], golden["dw5_w"], None),
+                 golden["dw5_out"], "dwconv k=3 no bias")
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 7])
+def test_golden_relative_shift(oracle, golden, T):
+    assert_bitexact(oracle.relative_shift(golden[f"rs{T}_bd"]), golden[f"rs{T}_out"], "rel_shift")
+
+
+def test_golden_dequant(oracle, golden):
+    assert_bitexact(oracle.dequant_i8(golden["i8_q"], float(golden["i8_scale"][0])),
+                    golden["i8_out"], "int8")
+    K, N = golden["i4_out"].shape
+    assert_bitexact(oracle.dequant_i4(golden["i4_packed"], golden["i4_scales"], K, N, 32, 1),
+                    golden["i4_out"], "int4")
+
+
+def test_golden_requant(oracle, golden):
+    sq, sk, sv, ms = (float(v) for v in golden["rq_scales"])
+    fused, oms = oracle.requant_qkv_i8(golden["rq_q"], golden["rq_k"], golden["rq_v"], sq, sk, sv)
+    assert np.float32(oms) == np.float32(ms)
+    assert_bitexact(fused, golden["rq_fused"], "requant")
+
+
+def test_int4_pack_roundtrip(oracle):
+    """Exporter packing (extract_weights.py:589-594) then dequant gives q * scale."""
+    rng = np.random.default_rng(5)
+    for K, N, G, axis in ((8, 64, 32, 1), (256, 32, 128, 0), (3, 16, 2, 1)):
+        q = rng.integers(-8, 8, size=(K, N)).astype(np.int8)
+        packed = ((q[:, 0::2] & 0x0F) | ((q[:, 1::2] & 0x0F) << 4)).astype(np.uint8)
+        if axis == 1:
+            sc = rng.uniform(1e-3, 2e-2, size=(K, N // G)).astype(np.float32)
+            full = np.repeat(sc, G, axis=1)
+        else:
+            sc = rng.uniform(1e-3, 2e-2, size=(K // G, N)).astype(np.float32)
+            full = np.repeat(sc, G, axis=0)
+        assert_bitexact(oracle.dequant_i4(packed, sc, K, N, G, axis),
+                        (q.astype(np.float32) * full).astype(np.float32), f"G={G} axis={axis}")
+
+
+def _golden_block(golden):
+    ps = {k: golden["blk_p_" + k] for k in po.PARAM_ROLES}
+    si = {k: golden["blk_si_" + k] for k in po.STANDIN_ROLES}
+    return ps, si, golden["blk_x"]
+
+
+def test_golden_block(oracle, golden):
+    ps, si, x = _golden_block(golden)
+    xo, caps = oracle.conformer_block(x, ps, si)
+    assert_close(xo, golden["blk_x_out"], "block x")
+    for k in po.CAPTURE_ROLES:
+        assert_close(caps[k], golden["blk_cap_" + k], "block " + k)
+
+
+# ── the reference library at BASELINE shapes ─────────────────────────────────
+
+def test_ref_layer_norm_T375(oracle, reference):
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((375, 1024)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(1024)).astype(np.float32)
+    assert_close(oracle.layer_norm_rows(x, g, b), reference.layer_norm_rows(x, g, b), "ln")
+    assert_close(oracle.layer_norm_rows(x, g, b), reference.layer_norm_rows_inplace(x, g, b),
+                 "ln inplace")
+
+
+@pytest.mark.parametrize("T", [32, 375, 416])
+def test_ref_softmax(oracle, reference, T):
+    rng = np.random.default_rng(T)
+    s = (3 * rng.standard_normal((8 * 16, T))).astype(np.float32)
+    assert_close(oracle.softmax_rows(s), reference.softmax_rows(s), f"softmax T={T}")
+
+
+def test_ref_requant_loader(oracle, reference):
+    """Fused-QKV requant against the reference loader (csrc/weights.c:437-487)."""
+    rng = np.random.default_rng(11)
+    q, k, v = (rng.integers(-127, 128, size=(1024, 1024), dtype=np.int8) for _ in range(3))
+    fused, scales = reference.load_fused_qkv_i8(q, k, v, 0.0031, 0.0092, 0.0092)
+    mine, ms = oracle.requant_qkv_i8(q, k, v, *(float(s) for s in scales[:3]))
+    assert np.float32(ms) == scales[3]
+    assert_bitexact(mine, fused, "requant")
+
+
+def test_ref_swish(oracle, reference):
+    rng = np.random.default_rng(8)
+    h = (4 * rng.standard_normal((375, 4096))).astype(np.float32)
+    assert_close(oracle.swish(h), reference.swish(h), "swish")
+
+
+def test_ref_dwconv(oracle, reference):
+    rng = np.random.default_rng(9)
+    for T in (1, 4, 8, 9, 375):
+        x = rng.standard_normal((64, T)).astype(np.float32)
+        w = (0.3 * rng.standard_normal((64, 9))).astype(np.float32)
+        b = (0.1 * rng.standard_normal(64)).astype(np.float32)
+        assert_close(oracle.depthwise_conv1d(x, w, b), reference.depthwise_conv1d(x, w, b),
+                     f"dwconv T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 2, 32, 41])
+def test_ref_block(oracle, reference, T):
+    """The whole block: the reference's own conformer_block (GEMMs replaced by
+    the same stand-ins) against the restatement, every GEMM input compared."""
+    ps, si, x = po.random_block_inputs(np.random.default_rng(100 + T), T)
+    xo, co = oracle.conformer_block(x, ps, si)
+    xr, cr = reference.conformer_block(x, ps, si)
+    assert_close(xo, xr, "x")
+    for k in po.CAPTURE_ROLES:
+        if k in ("Qu", "K", "Qv", "V", "P_h", "attn"):
+            assert_bitexact(co[k], cr[k], k)
+        else:
+            assert_close(co[k], cr[k], k)
+
+
+# ── known answers ────────────────────────────────────────────────────────────
+
+@pytest.mark.parametrize("T", list(range(1, 71)))
+def test_kat_relative_shift_closed_form(oracle, T):
+    rng = np.random.default_rng(T)
+    bd = rng.standard_normal((8, T, 2 * T - 1)).astype(np.float32)
+    i, j = np.meshgrid(np.arange(T), np.arange(T), indexing="ij")
+    assert_bitexact(oracle.relative_shift(bd), bd[:, i, T - 1 - i + j], f"T={T}")
+
+
+def test_kat_argmax(oracle):
+    nan = np.nan
+    rows = np.array([
+        [1, 3, 3, 2],          # tie -> first
+        [nan, 5, 6, 7],        # NaN at 0 -> 0 (strict '>' against NaN)
+        [1, nan, 0, 2],        # later NaN skipped
+        [-np.inf, -np.inf, -np.inf, -np.inf],
+        [0.0, -0.0, 0.0, -1],  # +0 == -0 -> first
+        [-5, -4, -4, -9],
+    ], np.float32)
+    assert list(oracle.argmax_rows(rows)) == [1, 0, 3, 0, 0, 1]
+
+
+def test_kat_int4_nibbles(oracle):
+    # byte 0x8F: low nibble 0xF = -1 (column 0), high nibble 0x8 = -8 (column 1)
+    packed = np.array([[0x8F, 0x71, 0x00, 0x07]], np.uint8)
+    out = oracle.dequant_i4(packed, np.ones((1, 1), np.float32), 1, 8, 8, 1)
+    assert list(out[0]) == [-1, -8, 1, 7, 0, 0, 7, 0]
+
+
+def test_kat_requant(oracle):
+    q = np.array([[127, -127, 3, -3, 1, 2, 0, 50]], np.int8)
+    k = np.array([[127, -127, 3, -3, 1, 2, 0, 50]], np.int8)
+    v = np.array([[127, -127, 3, -3, 1, 2, 0, 50]], np.int8)
+    fused, ms = oracle.requant_qkv_i8(q, k, v, 0.5, 1.0, 0.25)
+    assert ms == 1.0
+    assert list(fused[0, 8:16]) == list(k[0])                      # s == ms: copied
+    assert list(fused[0, :8]) == [64, -64, 2, -2, 1, 1, 0, 25]     # roundf half away from zero
+    assert list(fused[0, 16:]) == [32, -32, 1, -1, 0, 1, 0, 13]
+
+
+def test_kat_exp_poly_exact_points(oracle):
+    # exp(0) = 1 exactly; the clamp saturates at +-87.
+    assert oracle.exp_poly(0.0) == 1.0
+    assert oracle.exp_poly(-1000.0) == oracle.exp_poly(-87.0)
+    assert oracle.exp_poly(1000.0) == oracle.exp_poly(87.0)
+    # degree-5 Taylor on |r| <= ln2/2: relative error below 2e-6 (r^6/720 at the edge)
+    for x in (1.0, -3.5, 10.0, -20.25):
+        assert abs(oracle.exp_poly(x) / np.exp(np.float64(x)) - 1) < 2e-6
