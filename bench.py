@@ -417,8 +417,8 @@ def _ours(args, rank, world, local_rank, stream):
     if not args.no_e2e:
         e2e = run_e2e(args, ws, arr, gout, x_addr, stream, world)
 
-    if graph is not None:
-        del graph
+    used_graph = graph is not None
+    del graph
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = RefRunner(args.T, args.blocks)
@@ -448,7 +448,7 @@ def _ours(args, rank, world, local_rank, stream):
                         "frac": round(v["gbs"] / peak, 3), "launches_per_step": v["launches_per_step"]}
                     for k, v in table.items()},
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
-        "graph": graph is not None or not args.no_graph,
+        "graph": used_graph,
         "clocks": clocks,
         "e2e": e2e,
         "cpu_baseline": cpu,

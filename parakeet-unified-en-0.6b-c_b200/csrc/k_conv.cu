@@ -154,6 +154,101 @@ dwconv_kernel(const float *__restrict__ x, const float *__restrict__ w, const fl
   }
 }
 
+// K = 9 rows up to DW_ROW_MAX - 12 frames: the whole row plus its zero halo is
+// staged in shared memory in one pass (every lane issues its loads back to
+// back). Each lane then produces 4 consecutive outputs t = 4g..4g+3 from the 12
+// staged values s[4g .. 4g+11] read as three 16-byte shared loads. Groups whose
+// every tap lies inside [0, T) run without per-tap predicates; edge groups skip
+// the out-of-range taps exactly as the reference does.
+constexpr int DW_ROW_MAX = 640;
+
+// Swish after the conv: none, polynomial only (C*T_b a multiple of 8, e.g.
+// C = 1024), or with the scalar-tail rule for the last C*T_b % 8 entries.
+enum { DW_SWISH_NONE = 0, DW_SWISH_POLY = 1, DW_SWISH_TAIL = 2 };
+
+template <int SW>
+__device__ __forceinline__ float dw_finish(float val, float mean, float den, float gam, float bet,
+                                           const float *bn, long long flat, long long n8) {
+  if (bn) val = ((val - mean) / den) * gam + bet;
+  if (SW == DW_SWISH_POLY) val = swish_poly(val);
+  if (SW == DW_SWISH_TAIL) val = (flat < n8) ? swish_poly(val) : swish_tail(val);
+  return val;
+}
+
+template <int KC, int SW>
+__global__ void __launch_bounds__(32 * DW_WARPS)
+dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                  const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
+                  float *__restrict__ out, int C, SeqDev seq) {
+  static_assert(KC == 9, "the 4-output register window assumes K = 9");
+  __shared__ __align__(16) float stage[DW_WARPS][DW_ROW_MAX];
+  constexpr int K = KC;
+  constexpr int pad = (K - 1) / 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * DW_WARPS + warp;
+  if (c >= C) return;
+  const int item = blockIdx.y;
+  const int T = seq_T(seq, item);
+  const long long base = seq_frame_off(seq, item) * C + (long long)c * T;
+  float *s = stage[warp];
+  const int n_groups = (T + 3) >> 2;
+  const int n_stage = 4 * n_groups + 8;   // s[0 .. 4*n_groups + 7] are read
+  // s[k] = x[k - pad], zero outside [0, T)
+#pragma unroll 4
+  for (int k = lane; k < n_stage; k += 32) {
+    const int tt = k - pad;
+    s[k] = (tt >= 0 && tt < T) ? __ldcs(x + base + tt) : 0.0f;
+  }
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; k++) wk[k] = __ldg(w + (long long)c * K + k);
+  const float bias = b ? __ldg(b + c) : 0.0f;
+  float mean = 0.0f, den = 1.0f, gam = 1.0f, bet = 0.0f;
+  if (bn) {
+    mean = __ldg(bn + c);
+    den = sqrtf(__ldg(bn + C + c) + bn_eps);
+    gam = __ldg(bn + 2 * C + c);
+    bet = __ldg(bn + 3 * C + c);
+  }
+  const long long n8 = ((long long)C * T) & ~7LL;
+  const long long flat0 = (long long)c * T;
+  __syncwarp();
+  for (int g = lane; g < n_groups; g += 32) {
+    const int t0 = 4 * g;
+    const float4 a0 = *reinterpret_cast<const float4 *>(s + t0);
+    const float4 a1 = *reinterpret_cast<const float4 *>(s + t0 + 4);
+    const float4 a2 = *reinterpret_cast<const float4 *>(s + t0 + 8);
+    const float win[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                           a2.x, a2.y, a2.z, a2.w};
+    float v[4];
+    if (t0 >= pad && t0 + 3 + pad < T) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        float val = bias;
+#pragma unroll
+        for (int k = 0; k < K; k++) val = fmaf(win[q + k], wk[k], val);
+        v[q] = val;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        float val = bias;
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+          const int tt = t0 + q - pad + k;
+          if (tt >= 0 && tt < T) val = fmaf(win[q + k], wk[k], val);
+        }
+        v[q] = val;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int t = t0 + q;
+      if (t < T) out[base + t] = dw_finish<SW>(v[q], mean, den, gam, bet, bn, flat0 + t, n8);
+    }
+  }
+}
+
 static unsigned per_item_grid(long long work, int n_items) {
   long long g = (work + GLU_THREADS - 1) / GLU_THREADS;
   long long cap = ((long long)pkcu_sm_count() * 16 + n_items - 1) / n_items;
@@ -167,7 +262,14 @@ static int launch_dwconv(const float *x, const float *w, const float *b, const f
                          float bn_eps, int apply_swish, float *out, int C, int K, SeqDev sd,
                          cudaStream_t s) {
   dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
-  if (K == 9)
+  if (K == 9 && 4 * ((sd.max_T + 3) / 4) + 8 <= DW_ROW_MAX) {
+    if (!apply_swish)
+      dwconv_row_kernel<9, DW_SWISH_NONE><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
+    else if (C % 8 == 0)   // every item's C*T_b is a multiple of 8: no scalar tail
+      dwconv_row_kernel<9, DW_SWISH_POLY><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
+    else
+      dwconv_row_kernel<9, DW_SWISH_TAIL><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
+  } else if (K == 9)
     dwconv_kernel<9><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
   else
     dwconv_kernel<0><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);

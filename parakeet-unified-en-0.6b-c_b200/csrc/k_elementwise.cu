@@ -76,8 +76,9 @@ enum { ROW_BIAS = 0, ROW_BIAS_SWISH = 1, ROW_RESID = 2 };
 // ROW_BIAS      : x[r,c] += b[c]                    (pk_bias_add per row)
 // ROW_BIAS_SWISH: out[r,c] = swish(in[r,c] + b[c])  (csrc/encoder.c:194-196)
 // ROW_RESID     : x[r,c] = fma(y[r,c] + b[c], alpha, x[r,c])
-// Vector path: len % 4 == 0 and 16-byte aligned pointers.
-template <int OP>
+// Vector path: len % 4 == 0 and 16-byte aligned pointers. TAIL: the flat
+// length is not a multiple of 8, so the last elements take Swish's scalar form.
+template <int OP, bool TAIL>
 __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
 row_vec_kernel(const float *in, const float *__restrict__ b, const float *__restrict__ y,
                float alpha, float *out, long long n_rows, int len, long long n8) {
@@ -86,7 +87,7 @@ row_vec_kernel(const float *in, const float *__restrict__ b, const float *__rest
   if (row >= n_rows) return;
   const long long base = row * len;
   const int len4 = len >> 2;
-  constexpr int U = 4;
+  constexpr int U = 8;
   for (int c0 = lane; c0 < len4; c0 += 32 * U) {
     float4 v[U], t[U];
 #pragma unroll
@@ -108,11 +109,14 @@ row_vec_kernel(const float *in, const float *__restrict__ b, const float *__rest
       } else if (OP == ROW_BIAS_SWISH) {
         r = add4(v[u], bb);
         const long long e = base + 4 * c;
-        if (e + 4 <= n8) r = swish4(r);
-        else r = make_float4(e < n8 ? swish_poly(r.x) : swish_tail(r.x),
-                             e + 1 < n8 ? swish_poly(r.y) : swish_tail(r.y),
-                             e + 2 < n8 ? swish_poly(r.z) : swish_tail(r.z),
-                             e + 3 < n8 ? swish_poly(r.w) : swish_tail(r.w));
+        if (!TAIL || e + 4 <= n8) {
+          r = swish4(r);
+        } else {   // only the last float4s of a flat array whose length is not a multiple of 8
+          r = make_float4(e < n8 ? swish_poly(r.x) : swish_tail(r.x),
+                          e + 1 < n8 ? swish_poly(r.y) : swish_tail(r.y),
+                          e + 2 < n8 ? swish_poly(r.z) : swish_tail(r.z),
+                          e + 3 < n8 ? swish_poly(r.w) : swish_tail(r.w));
+        }
       } else {
         const float4 yy = b ? add4(t[u], bb) : t[u];
         r = make_float4(fmaf(yy.x, alpha, v[u].x), fmaf(yy.y, alpha, v[u].y),
@@ -197,8 +201,11 @@ static int launch_rows(const float *in, const float *b, const float *y, float al
   const bool vec = (len % 4 == 0) && PK_ALIGNED16(in) && PK_ALIGNED16(out) &&
                    (!b || PK_ALIGNED16(b)) && (!y || PK_ALIGNED16(y));
   if (vec) {
-    row_vec_kernel<OP><<<(unsigned)((n_rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA),
-                         32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8);
+    const unsigned grid = (unsigned)((n_rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA);
+    if (n8 == n)
+      row_vec_kernel<OP, false><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8);
+    else
+      row_vec_kernel<OP, true><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8);
   } else {
     row_scalar_kernel<OP><<<flat_grid(n, EW_THREADS * 4), EW_THREADS, 0, s>>>(
         in, b, y, alpha, out, n, len, n8);

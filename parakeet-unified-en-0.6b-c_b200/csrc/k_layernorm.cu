@@ -151,7 +151,7 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // (csrc/encoder.c:447-452). The normalised rows are staged in shared memory
 // and leave as 64-byte runs of 16 consecutive frames per channel.
 template <bool RESID>
-__global__ void __launch_bounds__(LT_THREADS)
+__global__ void __launch_bounds__(LT_THREADS, 2)
 ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                     float alpha, const float *__restrict__ g, const float *__restrict__ b,
                     float *__restrict__ cf, SeqDev seq) {
@@ -183,7 +183,7 @@ ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restri
   if (t < nrows) {
     float *dst = cf + f0 * PK_D + t0 + t;
     const float *src = tile + t * LT_STRIDE;
-#pragma unroll 4
+#pragma unroll 8
     for (int d = dsub; d < PK_D; d += LT_THREADS / LT_TT) dst[(long long)d * T] = src[d];
   }
 }
@@ -192,7 +192,7 @@ ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restri
 // y per item [D, T_b] with the pointwise bias of csrc/tensor_ops.c:585-589),
 // optionally followed by the FF2 LayerNorm of the updated rows.
 template <bool WITH_LN>
-__global__ void __launch_bounds__(LT_THREADS)
+__global__ void __launch_bounds__(LT_THREADS, 2)
 transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                      const float *__restrict__ g, const float *__restrict__ b,
                      float *__restrict__ ln, SeqDev seq) {
@@ -210,7 +210,7 @@ transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restr
     if (t < nrows) {
       const float *src = y + f0 * PK_D + t0 + t;
       float *dst = tile + t * LT_STRIDE;
-#pragma unroll 4
+#pragma unroll 8
       for (int d = dsub; d < PK_D; d += LT_THREADS / LT_TT) dst[d] = __ldcs(src + (long long)d * T);
     }
   }

@@ -39,12 +39,14 @@ __device__ __forceinline__ void softmax_regs(float (&v)[NPL], int len, int lane)
   mx = warp_max(mx);
   const int len8 = len & ~7;
   float s = 0.0f;
+  // Polynomial everywhere, then libm expf for the len % 8 tail entries only
+  // (a warp-uniform branch: the tail lies in one or two register slots).
 #pragma unroll
   for (int k = 0; k < NPL; k++) {
     const int j = lane + 32 * k;
     if (j < len) {
-      const float d = v[k] - mx;
-      const float e = (j < len8) ? exp_poly(d) : expf(d);
+      float e = exp_poly(v[k] - mx);
+      if (32 * k + 31 >= len8 && j >= len8) e = expf(v[k] - mx);
       v[k] = e;
       s += e;
     }
@@ -182,6 +184,101 @@ relpos_scores_cta_kernel(const float *ac, const float *__restrict__ bd, float *S
   for (int j = threadIdx.x; j < len; j += blockDim.x) S[rw.s + j] = sm_row[j] * inv;
 }
 
+// ── pipelined score rows ─────────────────────────────────────────────────────
+// Persistent warps walk the flat list of score rows of every item. Each warp
+// double-buffers in shared memory: while it computes row n (registers), the
+// async copies of row n+1's ac row and bd band are in flight, so the HBM
+// stream never waits on the softmax arithmetic. Rows of up to 32*NPL entries.
+constexpr int PIPE_WARPS = 8;
+
+struct RowLoc {
+  long long ac, bd;   // first element of the ac row / of the used bd band
+  int T, valid;
+};
+
+__device__ __forceinline__ RowLoc locate_row(const SeqDev &seq, long long row, long long total_rows) {
+  RowLoc o;
+  o.valid = row < total_rows;
+  if (!o.valid) { o.ac = o.bd = 0; o.T = 0; return o; }
+  int item;
+  long long r;
+  if (seq.uniform_T > 0) {
+    const long long per = (long long)PK_H * seq.uniform_T;
+    item = (int)(row / per);
+    r = row - (long long)item * per;
+  } else {   // rows of item b: [H*frame_off[b], H*frame_off[b+1])
+    int lo = 0, hi = seq.n_items;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if ((long long)PK_H * __ldg(seq.frame_off + mid) <= row) lo = mid; else hi = mid;
+    }
+    item = lo;
+    r = row - (long long)PK_H * __ldg(seq.frame_off + lo);
+  }
+  const int T = seq_T(seq, item);
+  const int i = (int)(r % T);
+  o.ac = seq_score_off(seq, item) + r * T;
+  o.bd = seq_bd_off(seq, item) + r * (2 * T - 1) + (T - 1 - i);
+  o.T = T;
+  return o;
+}
+
+template <int NPL, bool SOFTMAX>
+__global__ void __launch_bounds__(32 * PIPE_WARPS)
+relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *S, float scale,
+                          SeqDev seq, long long total_rows, long long ac_total, long long bd_total,
+                          int stage) {
+  extern __shared__ float4 pipe_smem4[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // per warp: [buf0 ac | buf0 bd | buf1 ac | buf1 bd], `stage` floats each
+  float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * 4 * stage;
+  const long long nw = (long long)gridDim.x * PIPE_WARPS;
+  long long row = (long long)blockIdx.x * PIPE_WARPS + warp;
+  RowLoc cur = locate_row(seq, row, total_rows);
+  int off_ac = 0, off_bd = 0;
+  if (cur.valid) {
+    off_ac = cp_async_span(wb, ac, cur.ac, cur.T, ac_total, lane);
+    off_bd = cp_async_span(wb + stage, bd, cur.bd, cur.T, bd_total, lane);
+  }
+  cp_async_commit();
+  int buf = 0;
+  for (; cur.valid; row += nw) {
+    // prefetch the next row into the other buffer
+    const RowLoc nxt = locate_row(seq, row + nw, total_rows);
+    int noff_ac = 0, noff_bd = 0;
+    float *nb = wb + (buf ^ 1) * 2 * stage;
+    if (nxt.valid) {
+      noff_ac = cp_async_span(nb, ac, nxt.ac, nxt.T, ac_total, lane);
+      noff_bd = cp_async_span(nb + stage, bd, nxt.bd, nxt.T, bd_total, lane);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();   // this lane's copies of the current row have landed
+    __syncwarp();         // ... and every other lane's
+    const float *sa = wb + buf * 2 * stage + off_ac;
+    const float *sb = wb + buf * 2 * stage + stage + off_bd;
+    const int len = cur.T;
+    float v[NPL];
+#pragma unroll
+    for (int k = 0; k < NPL; k++) {
+      const int j = lane + 32 * k;
+      v[k] = (j < len) ? (sa[j] + sb[j]) * scale : 0.0f;
+    }
+    if (SOFTMAX) softmax_regs<NPL>(v, len, lane);
+    float *dst = S + cur.ac;
+#pragma unroll
+    for (int k = 0; k < NPL; k++) {
+      const int j = lane + 32 * k;
+      if (j < len) dst[j] = v[k];
+    }
+    __syncwarp();         // the buffer is refilled two rows from now
+    cur = nxt;
+    off_ac = noff_ac;
+    off_bd = noff_bd;
+    buf ^= 1;
+  }
+  cp_async_wait<0>();
+}
+
 // relative_shift alone: out[h,i,j] = bd[h,i,T-1-i+j] (exact gather).
 __global__ void __launch_bounds__(256)
 relative_shift_kernel(const float *__restrict__ bd, float *__restrict__ out, SeqDev seq) {
@@ -207,11 +304,37 @@ static void launch_scores_warp(const float *ac, const float *bd, float *S, float
                                                                               seq->dev);
 }
 
+template <int NPL, bool SOFTMAX>
+static void launch_scores_pipe(const float *ac, const float *bd, float *S, float scale,
+                               const pkcu_seq *seq, cudaStream_t s) {
+  const int stage = ((seq->dev.max_T + 8 + 3) / 4) * 4;
+  const size_t smem = sizeof(float) * 4 * (size_t)stage * PIPE_WARPS;
+  static int flags[64];
+  smem_optin(relpos_scores_pipe_kernel<NPL, SOFTMAX>, smem, flags);
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, relpos_scores_pipe_kernel<NPL, SOFTMAX>,
+                                                32 * PIPE_WARPS, smem);
+  if (per_sm < 1) per_sm = 1;
+  const long long rows = (long long)PK_H * seq->frames;
+  long long grid = (rows + PIPE_WARPS - 1) / PIPE_WARPS;
+  const long long cap = (long long)pkcu_sm_count() * per_sm;
+  if (grid > cap) grid = cap;
+  relpos_scores_pipe_kernel<NPL, SOFTMAX><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
+      ac, bd, S, scale, seq->dev, rows, seq->score_elems, seq->bd_elems, stage);
+}
+
 template <bool SOFTMAX>
 static int launch_scores(const float *ac, const float *bd, float *S, float scale,
                          const pkcu_seq *seq, cudaStream_t s) {
   const int T = seq->dev.max_T;
   const int npl = (T + 31) / 32;
+  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && npl <= 16) {
+    if (npl <= 4) launch_scores_pipe<4, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (npl <= 8) launch_scores_pipe<8, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (npl <= 12) launch_scores_pipe<12, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else launch_scores_pipe<16, SOFTMAX>(ac, bd, S, scale, seq, s);
+    return PKCU_OK;
+  }
   if (npl <= 4) launch_scores_warp<4, SOFTMAX>(ac, bd, S, scale, seq, s);
   else if (npl <= 8) launch_scores_warp<8, SOFTMAX>(ac, bd, S, scale, seq, s);
   else if (npl <= 12) launch_scores_warp<12, SOFTMAX>(ac, bd, S, scale, seq, s);

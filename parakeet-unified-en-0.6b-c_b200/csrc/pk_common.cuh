@@ -70,11 +70,20 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 // r = x - k ln2 as one fused multiply-add (the reference build contracts it),
 // Horner evaluation of the degree-5 Taylor polynomial with FMAs, and 2^k built
 // directly in the exponent field.
+//
+// The rounding uses the 1.5 * 2^23 shifter: for |t| < 2^22, t + 1.5*2^23 lands
+// in [2^23, 2^24), where the float spacing is 1, so the add itself rounds t to
+// the nearest integer, ties to even (the reference's _MM_FROUND_TO_NEAREST_INT),
+// and the subtraction back is exact. The integer k sits in the low mantissa
+// bits of the shifted value, so no float-to-int conversion is needed either:
+// the whole function runs on the FMA/ALU pipes.
 __device__ __forceinline__ float exp_poly(float x) {
-  x = (x > -87.0f) ? x : -87.0f;
-  x = (x < 87.0f) ? x : 87.0f;
-  const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
-  const int ki = __float2int_rn(kf);
+  constexpr float kShift = 12582912.0f;   // 1.5 * 2^23, bit pattern 0x4B400000
+  // fmaxf returns -87 for a NaN x, like _mm256_max_ps(x, -87); the result is
+  // then never NaN, so fminf is the plain upper clamp.
+  x = fminf(fmaxf(x, -87.0f), 87.0f);
+  const float shifted = __fadd_rn(__fmul_rn(x, 1.44269504088896341f), kShift);
+  const float kf = __fsub_rn(shifted, kShift);
   const float r = fmaf(-kf, 0.69314718055994529f, x);
   float y = 1.0f / 120.0f;
   y = fmaf(y, r, 1.0f / 24.0f);
@@ -82,14 +91,17 @@ __device__ __forceinline__ float exp_poly(float x) {
   y = fmaf(y, r, 0.5f);
   y = fmaf(y, r, 1.0f);
   y = fmaf(y, r, 1.0f);
-  return __fmul_rn(y, __int_as_float((ki + 127) << 23));
+  // (k + 127) << 23 with k = bits(shifted) - 0x4B400000
+  const int pow2k = (__float_as_int(shifted) - (0x4B400000 - 127)) << 23;
+  return __fmul_rn(y, __int_as_float(pow2k));
 }
 
 // Swish of the vector body of pk_swish (csrc/tensor_ops.c:383-388):
-// v * (1 / (1 + exp(0 - v))) with an IEEE division.
+// v * (1 / (1 + exp(0 - v))). __frcp_rn is the correctly rounded reciprocal,
+// i.e. the IEEE quotient 1/d.
 __device__ __forceinline__ float swish_poly(float v) {
   const float e = exp_poly(__fsub_rn(0.0f, v));
-  return __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+  return __fmul_rn(v, __frcp_rn(__fadd_rn(1.0f, e)));
 }
 
 // Swish of the scalar tail of pk_swish (csrc/tensor_ops.c:389): x / (1 + expf(-x)).
@@ -99,7 +111,7 @@ __device__ __forceinline__ float swish_tail(float v) {
 
 // Sigmoid gate of the GLU (csrc/encoder.c:462): 1 / (1 + expf(-b)).
 __device__ __forceinline__ float sigmoid_libm(float b) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-b)));
+  return __frcp_rn(__fadd_rn(1.0f, expf(-b)));
 }
 
 // ── ragged batches ───────────────────────────────────────────────────────────
@@ -139,6 +151,41 @@ __device__ __forceinline__ float4 ldg4_stream(const float *p) {
 __device__ __forceinline__ float4 add4(float4 a, float4 b) {
   return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
                      __fadd_rn(a.w, b.w));
+}
+
+// ── asynchronous global -> shared copies (cp.async) ─────────────────────────
+// Completion is tracked per thread by commit groups; a warp that reads data
+// copied by other lanes waits for its own groups and then __syncwarp()s.
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Copies floats [start, start + n) of a 16-byte aligned array of `total`
+// floats into dst (16-byte aligned) as 16-byte chunks of the aligned superset
+// [start & ~3, ...): dst[k] holds src[(start & ~3) + k]. Chunks that would run
+// past the end of the array fall back to 4-byte copies. Returns start & 3,
+// the offset of src[start] in dst. Warp-cooperative.
+__device__ __forceinline__ int cp_async_span(float *dst, const float *src, long long start, int n,
+                                             long long total, int lane) {
+  const long long a0 = start & ~3LL;
+  long long a1 = (start + n + 3) & ~3LL;
+  const long long lim = total & ~3LL;
+  if (a1 > lim) a1 = lim > a0 ? lim : a0;
+  const int n16 = (int)((a1 - a0) >> 2);
+  for (int q = lane; q < n16; q += 32) cp_async16(dst + 4 * q, src + a0 + 4 * q);
+  for (long long e = a1 + lane; e < start + n; e += 32) cp_async4(dst + (e - a0), src + e);
+  return (int)(start - a0);
 }
 
 // Raises a kernel's dynamic shared-memory limit once per device (the first

@@ -7,14 +7,25 @@ import numpy as np
 D, H, DH, FF = 1024, 8, 128, 4096
 
 
+# Device tensors made by dev()/empty() stay referenced until the end of the
+# test (conftest clears this list): an expression like dev(a).data_ptr()
+# would otherwise free the block at once and torch's caching allocator would
+# hand the same memory to the next operand.
+ALIVE = []
+
+
 def dev(a):
     import torch
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ALIVE.append(t)
+    return t
 
 
 def empty(shape, dtype=None):
     import torch
-    return torch.empty(shape, dtype=dtype or torch.float32, device="cuda")
+    t = torch.empty(shape, dtype=dtype or torch.float32, device="cuda")
+    ALIVE.append(t)
+    return t
 
 
 def host(t):

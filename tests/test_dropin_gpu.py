@@ -1,8 +1,6 @@
 """GPU: the drop-in host API (the prototypes of csrc/parakeet.h:231-262) with
 host buffers, against the reference's own compiled functions and the
 restatement."""
-import ctypes as C
-
 import numpy as np
 import pytest
 
@@ -78,4 +76,3 @@ def test_dropin_reports_errors(cuda):
     L.pk_depthwise_conv1d(p(x), p(x), None, p(x), 1, 8, 500)   # K above the limit
     assert L.pk_cuda_status() == 1
     assert b"K must be" in L.pkcu_last_error()
-    del C

@@ -143,7 +143,7 @@ def test_softmax_rows(cuda, oracle, R, n):
     assert_close(host(xd), oracle.softmax_rows(x), f"softmax {R}x{n}")
 
 
-@pytest.mark.parametrize("lengths", RAGGED + [[1100, 33]])
+@pytest.mark.parametrize("lengths", RAGGED + [[1100, 33], [600, 7], [512, 1]])
 def test_relpos_scores(cuda, oracle, lengths):
     r = rng(11 + sum(lengths))
     L = Layout(lengths)
