@@ -166,16 +166,16 @@ constexpr int DW_ROW_MAX = 640;
 // C = 1024), or with the scalar-tail rule for the last C*T_b % 8 entries.
 enum { DW_SWISH_NONE = 0, DW_SWISH_POLY = 1, DW_SWISH_TAIL = 2 };
 
-template <int SW>
+template <int SW, bool BN>
 __device__ __forceinline__ float dw_finish(float val, float mean, float den, float gam, float bet,
-                                           const float *bn, long long flat, long long n8) {
-  if (bn) val = ((val - mean) / den) * gam + bet;
+                                           long long flat, long long n8) {
+  if (BN) val = ((val - mean) / den) * gam + bet;
   if (SW == DW_SWISH_POLY) val = swish_poly(val);
   if (SW == DW_SWISH_TAIL) val = (flat < n8) ? swish_poly(val) : swish_tail(val);
   return val;
 }
 
-template <int KC, int SW>
+template <int KC, int SW, bool BN>
 __global__ void __launch_bounds__(32 * DW_WARPS)
 dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
                   const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
@@ -204,7 +204,7 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
   for (int k = 0; k < K; k++) wk[k] = __ldg(w + (long long)c * K + k);
   const float bias = b ? __ldg(b + c) : 0.0f;
   float mean = 0.0f, den = 1.0f, gam = 1.0f, bet = 0.0f;
-  if (bn) {
+  if (BN) {
     mean = __ldg(bn + c);
     den = sqrtf(__ldg(bn + C + c) + bn_eps);
     gam = __ldg(bn + 2 * C + c);
@@ -222,13 +222,18 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
                            a2.x, a2.y, a2.z, a2.w};
     float v[4];
     if (t0 >= pad && t0 + 3 + pad < T) {
+      // outputs (t0, t0+1) and (t0+2, t0+3) as packed pairs; each output's
+      // multiply-add chain runs in the same k order as the scalar form
+      float2 v01 = splat2(bias), v23 = splat2(bias);
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        float val = bias;
-#pragma unroll
-        for (int k = 0; k < K; k++) val = fmaf(win[q + k], wk[k], val);
-        v[q] = val;
+      for (int k = 0; k < K; k++) {
+        v01 = fma2(make_float2(win[k], win[k + 1]), splat2(wk[k]), v01);
+        v23 = fma2(make_float2(win[k + 2], win[k + 3]), splat2(wk[k]), v23);
       }
+      v[0] = v01.x;
+      v[1] = v01.y;
+      v[2] = v23.x;
+      v[3] = v23.y;
     } else {
 #pragma unroll
       for (int q = 0; q < 4; q++) {
@@ -241,10 +246,27 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
         v[q] = val;
       }
     }
+    if (SW == DW_SWISH_POLY) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int t = t0 + q;
-      if (t < T) out[base + t] = dw_finish<SW>(v[q], mean, den, gam, bet, bn, flat0 + t, n8);
+      for (int q = 0; q < 4; q += 2) {
+        float2 p = make_float2(v[q], v[q + 1]);
+        if (BN) {
+          p.x = ((p.x - mean) / den) * gam + bet;
+          p.y = ((p.y - mean) / den) * gam + bet;
+        }
+        p = swish_poly2(p);
+        v[q] = p.x;
+        v[q + 1] = p.y;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if (t0 + q < T) out[base + t0 + q] = v[q];
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int t = t0 + q;
+        if (t < T) out[base + t] = dw_finish<SW, BN>(v[q], mean, den, gam, bet, flat0 + t, n8);
+      }
     }
   }
 }
@@ -263,12 +285,20 @@ static int launch_dwconv(const float *x, const float *w, const float *b, const f
                          cudaStream_t s) {
   dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
   if (K == 9 && 4 * ((sd.max_T + 3) / 4) + 8 <= DW_ROW_MAX) {
-    if (!apply_swish)
-      dwconv_row_kernel<9, DW_SWISH_NONE><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
-    else if (C % 8 == 0)   // every item's C*T_b is a multiple of 8: no scalar tail
-      dwconv_row_kernel<9, DW_SWISH_POLY><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
-    else
-      dwconv_row_kernel<9, DW_SWISH_TAIL><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd);
+    // every item's C*T_b is a multiple of 8 when C is: no scalar Swish tail
+    const int sw = !apply_swish ? DW_SWISH_NONE : (C % 8 == 0 ? DW_SWISH_POLY : DW_SWISH_TAIL);
+#define PK_DW_ROW(SWV, BNV) \
+  dwconv_row_kernel<9, SWV, BNV><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd)
+    if (bn) {
+      if (sw == DW_SWISH_NONE) PK_DW_ROW(DW_SWISH_NONE, true);
+      else if (sw == DW_SWISH_POLY) PK_DW_ROW(DW_SWISH_POLY, true);
+      else PK_DW_ROW(DW_SWISH_TAIL, true);
+    } else {
+      if (sw == DW_SWISH_NONE) PK_DW_ROW(DW_SWISH_NONE, false);
+      else if (sw == DW_SWISH_POLY) PK_DW_ROW(DW_SWISH_POLY, false);
+      else PK_DW_ROW(DW_SWISH_TAIL, false);
+    }
+#undef PK_DW_ROW
   } else if (K == 9)
     dwconv_kernel<9><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
   else

@@ -19,7 +19,8 @@ constexpr int EW_THREADS = 256;
 constexpr int ROWS_PER_CTA = 8;
 
 __device__ __forceinline__ float4 swish4(float4 v) {
-  return make_float4(swish_poly(v.x), swish_poly(v.y), swish_poly(v.z), swish_poly(v.w));
+  const float2 a = swish_poly2(make_float2(v.x, v.y)), b = swish_poly2(make_float2(v.z, v.w));
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 // ── flat Swish ───────────────────────────────────────────────────────────────

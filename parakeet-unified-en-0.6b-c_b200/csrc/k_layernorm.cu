@@ -146,7 +146,7 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
   }
 }
 
-// LayerNorm of frames [t0, t0+16) of one item, optionally after the attention
+// LayerNorm of frames [t0, t0 + LT_TT) of one item, optionally after the attention
 // residual, written channel-first: cf[d, t] per item [D, T_b]
 // (csrc/encoder.c:447-452). The normalised rows are staged in shared memory
 // and leave as 64-byte runs of 16 consecutive frames per channel.

@@ -41,20 +41,44 @@ __device__ __forceinline__ void softmax_regs(float (&v)[NPL], int len, int lane)
   float s = 0.0f;
   // Polynomial everywhere, then libm expf for the len % 8 tail entries only
   // (a warp-uniform branch: the tail lies in one or two register slots).
+  if constexpr (NPL == 1) {
+    if (lane < len) {
+      float e = exp_poly_nonpos(v[0] - mx);
+      if (lane >= len8) e = expf(v[0] - mx);
+      v[0] = e;
+      s = e;
+    }
+    s = warp_sum(s);
+    v[0] *= 1.0f / s;
+  } else {
+    static_assert(NPL % 2 == 0, "register slots are processed in pairs");
+    float2 s2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int k = 0; k < NPL; k++) {
-    const int j = lane + 32 * k;
-    if (j < len) {
-      float e = exp_poly(v[k] - mx);
-      if (32 * k + 31 >= len8 && j >= len8) e = expf(v[k] - mx);
-      v[k] = e;
-      s += e;
+    for (int k = 0; k < NPL; k += 2) {
+      const int j0 = lane + 32 * k, j1 = j0 + 32;
+      float2 d = sub2(make_float2(v[k], v[k + 1]), splat2(mx));
+      d.x = fmaxf(d.x, -87.0f);   // exp_poly_nonpos: arguments are <= 0 or NaN
+      d.y = fmaxf(d.y, -87.0f);
+      float2 e = exp_poly2_clamped(d);
+      if (32 * k + 63 >= len8) {
+        if (j0 >= len8 && j0 < len) e.x = expf(v[k] - mx);
+        if (j1 >= len8 && j1 < len) e.y = expf(v[k + 1] - mx);
+      }
+      e.x = (j0 < len) ? e.x : 0.0f;
+      e.y = (j1 < len) ? e.y : 0.0f;
+      v[k] = e.x;
+      v[k + 1] = e.y;
+      s2 = add2(s2, e);
+    }
+    s = warp_sum(s2.x + s2.y);
+    const float2 inv = splat2(1.0f / s);
+#pragma unroll
+    for (int k = 0; k < NPL; k += 2) {
+      const float2 o = mul2(make_float2(v[k], v[k + 1]), inv);
+      v[k] = o.x;
+      v[k + 1] = o.y;
     }
   }
-  s = warp_sum(s);
-  const float inv = 1.0f / s;
-#pragma unroll
-  for (int k = 0; k < NPL; k++) v[k] *= inv;
 }
 
 // In-place softmax of rows of len <= 32*NPL (pk_softmax_rows).
@@ -98,7 +122,7 @@ softmax_rows_cta_kernel(float *x, int len, int use_smem) {
   float s = 0.0f;
   for (int j = threadIdx.x; j < len; j += blockDim.x) {
     const float d = buf[j] - mx;
-    const float e = (j < len8) ? exp_poly(d) : expf(d);
+    const float e = (j < len8) ? exp_poly_nonpos(d) : expf(d);
     buf[j] = e;
     s += e;
   }
@@ -175,7 +199,7 @@ relpos_scores_cta_kernel(const float *ac, const float *__restrict__ bd, float *S
   float s = 0.0f;
   for (int j = threadIdx.x; j < len; j += blockDim.x) {
     const float d = sm_row[j] - mx;
-    const float e = (j < len8) ? exp_poly(d) : expf(d);
+    const float e = (j < len8) ? exp_poly_nonpos(d) : expf(d);
     sm_row[j] = e;
     s += e;
   }
@@ -196,29 +220,32 @@ struct RowLoc {
   int T, valid;
 };
 
-__device__ __forceinline__ RowLoc locate_row(const SeqDev &seq, long long row, long long total_rows) {
+// Row indices fit in 32 bits (the launcher checks H * frames < 2^31), so the
+// decomposition row -> (item, head-row r, query i) uses 32-bit unsigned
+// division; only the element offsets are 64-bit.
+__device__ __forceinline__ RowLoc locate_row(const SeqDev &seq, unsigned row, unsigned total_rows) {
   RowLoc o;
   o.valid = row < total_rows;
   if (!o.valid) { o.ac = o.bd = 0; o.T = 0; return o; }
   int item;
-  long long r;
+  unsigned r;
   if (seq.uniform_T > 0) {
-    const long long per = (long long)PK_H * seq.uniform_T;
+    const unsigned per = (unsigned)(PK_H * seq.uniform_T);
     item = (int)(row / per);
-    r = row - (long long)item * per;
+    r = row - (unsigned)item * per;
   } else {   // rows of item b: [H*frame_off[b], H*frame_off[b+1])
     int lo = 0, hi = seq.n_items;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if ((long long)PK_H * __ldg(seq.frame_off + mid) <= row) lo = mid; else hi = mid;
+      if ((unsigned)(PK_H * __ldg(seq.frame_off + mid)) <= row) lo = mid; else hi = mid;
     }
     item = lo;
-    r = row - (long long)PK_H * __ldg(seq.frame_off + lo);
+    r = row - (unsigned)(PK_H * __ldg(seq.frame_off + lo));
   }
   const int T = seq_T(seq, item);
-  const int i = (int)(r % T);
-  o.ac = seq_score_off(seq, item) + r * T;
-  o.bd = seq_bd_off(seq, item) + r * (2 * T - 1) + (T - 1 - i);
+  const int i = (int)(r % (unsigned)T);
+  o.ac = seq_score_off(seq, item) + (long long)r * T;
+  o.bd = seq_bd_off(seq, item) + (long long)r * (2 * T - 1) + (T - 1 - i);
   o.T = T;
   return o;
 }
@@ -226,14 +253,14 @@ __device__ __forceinline__ RowLoc locate_row(const SeqDev &seq, long long row, l
 template <int NPL, bool SOFTMAX>
 __global__ void __launch_bounds__(32 * PIPE_WARPS)
 relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *S, float scale,
-                          SeqDev seq, long long total_rows, long long ac_total, long long bd_total,
+                          SeqDev seq, unsigned total_rows, long long ac_total, long long bd_total,
                           int stage) {
   extern __shared__ float4 pipe_smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // per warp: [buf0 ac | buf0 bd | buf1 ac | buf1 bd], `stage` floats each
   float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * 4 * stage;
-  const long long nw = (long long)gridDim.x * PIPE_WARPS;
-  long long row = (long long)blockIdx.x * PIPE_WARPS + warp;
+  const unsigned nw = gridDim.x * PIPE_WARPS;
+  unsigned row = blockIdx.x * PIPE_WARPS + warp;
   RowLoc cur = locate_row(seq, row, total_rows);
   int off_ac = 0, off_bd = 0;
   if (cur.valid) {
@@ -259,9 +286,13 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
     const int len = cur.T;
     float v[NPL];
 #pragma unroll
-    for (int k = 0; k < NPL; k++) {
-      const int j = lane + 32 * k;
-      v[k] = (j < len) ? (sa[j] + sb[j]) * scale : 0.0f;
+    for (int k = 0; k < NPL; k += 2) {
+      const int j0 = lane + 32 * k, j1 = j0 + 32;
+      const float2 a = make_float2(j0 < len ? sa[j0] : 0.0f, j1 < len ? sa[j1] : 0.0f);
+      const float2 b = make_float2(j0 < len ? sb[j0] : 0.0f, j1 < len ? sb[j1] : 0.0f);
+      const float2 c = mul2(add2(a, b), splat2(scale));   // (ac + bd) * scale, each rounded
+      v[k] = j0 < len ? c.x : 0.0f;
+      v[k + 1] = j1 < len ? c.y : 0.0f;
     }
     if (SOFTMAX) softmax_regs<NPL>(v, len, lane);
     float *dst = S + cur.ac;
@@ -320,7 +351,12 @@ static void launch_scores_pipe(const float *ac, const float *bd, float *S, float
   const long long cap = (long long)pkcu_sm_count() * per_sm;
   if (grid > cap) grid = cap;
   relpos_scores_pipe_kernel<NPL, SOFTMAX><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
-      ac, bd, S, scale, seq->dev, rows, seq->score_elems, seq->bd_elems, stage);
+      ac, bd, S, scale, seq->dev, (unsigned)rows, seq->score_elems, seq->bd_elems, stage);
+}
+
+// The pipelined kernel indexes rows in 32 bits (and nw + row must not wrap).
+static bool pipe_rows_fit(const pkcu_seq *seq) {
+  return (long long)PK_H * seq->frames < (1LL << 31);
 }
 
 template <bool SOFTMAX>
@@ -328,7 +364,7 @@ static int launch_scores(const float *ac, const float *bd, float *S, float scale
                          const pkcu_seq *seq, cudaStream_t s) {
   const int T = seq->dev.max_T;
   const int npl = (T + 31) / 32;
-  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && npl <= 16) {
+  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && npl <= 16 && pipe_rows_fit(seq)) {
     if (npl <= 4) launch_scores_pipe<4, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (npl <= 8) launch_scores_pipe<8, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (npl <= 12) launch_scores_pipe<12, SOFTMAX>(ac, bd, S, scale, seq, s);

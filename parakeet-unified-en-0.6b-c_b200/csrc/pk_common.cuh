@@ -77,11 +77,8 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 // and the subtraction back is exact. The integer k sits in the low mantissa
 // bits of the shifted value, so no float-to-int conversion is needed either:
 // the whole function runs on the FMA/ALU pipes.
-__device__ __forceinline__ float exp_poly(float x) {
+__device__ __forceinline__ float exp_poly_clamped(float x) {   // x in [-87, 87]
   constexpr float kShift = 12582912.0f;   // 1.5 * 2^23, bit pattern 0x4B400000
-  // fmaxf returns -87 for a NaN x, like _mm256_max_ps(x, -87); the result is
-  // then never NaN, so fminf is the plain upper clamp.
-  x = fminf(fmaxf(x, -87.0f), 87.0f);
   const float shifted = __fadd_rn(__fmul_rn(x, 1.44269504088896341f), kShift);
   const float kf = __fsub_rn(shifted, kShift);
   const float r = fmaf(-kf, 0.69314718055994529f, x);
@@ -94,6 +91,82 @@ __device__ __forceinline__ float exp_poly(float x) {
   // (k + 127) << 23 with k = bits(shifted) - 0x4B400000
   const int pow2k = (__float_as_int(shifted) - (0x4B400000 - 127)) << 23;
   return __fmul_rn(y, __int_as_float(pow2k));
+}
+
+__device__ __forceinline__ float exp_poly(float x) {
+  // fmaxf returns -87 for a NaN x, like _mm256_max_ps(x, -87); the result is
+  // then never NaN, so fminf is the plain upper clamp.
+  return exp_poly_clamped(fminf(fmaxf(x, -87.0f), 87.0f));
+}
+
+// exp_poly for arguments that are <= 0 or NaN (softmax's x - max): the upper
+// clamp cannot change them.
+__device__ __forceinline__ float exp_poly_nonpos(float x) {
+  return exp_poly_clamped(fmaxf(x, -87.0f));
+}
+
+// ── packed fp32 pairs (sm_100 f32x2 arithmetic) ──────────────────────────────
+// add/sub/mul/fma.rn.f32x2 apply one IEEE fp32 operation, round to nearest,
+// to each half of a register pair: the results are those of the scalar
+// instructions, at half the issue slots. Used where the kernels are bound by
+// instruction issue (polynomial exp, Swish, depthwise taps, score combine).
+
+__device__ __forceinline__ unsigned long long pk2(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 unpk2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
+  return unpk2(r);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
+  return unpk2(r);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
+  return unpk2(r);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return unpk2(r);
+}
+__device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
+
+// exp_poly_clamped on a pair (inputs already in [-87, 87]); per element the
+// same operations as the scalar form. -kf*ln2 + x == kf*(-ln2) + x exactly.
+__device__ __forceinline__ float2 exp_poly2_clamped(float2 x) {
+  constexpr float kShift = 12582912.0f;
+  const float2 shifted = add2(mul2(x, splat2(1.44269504088896341f)), splat2(kShift));
+  const float2 kf = sub2(shifted, splat2(kShift));
+  const float2 r = fma2(kf, splat2(-0.69314718055994529f), x);
+  float2 y = splat2(1.0f / 120.0f);
+  y = fma2(y, r, splat2(1.0f / 24.0f));
+  y = fma2(y, r, splat2(1.0f / 6.0f));
+  y = fma2(y, r, splat2(0.5f));
+  y = fma2(y, r, splat2(1.0f));
+  y = fma2(y, r, splat2(1.0f));
+  const int px = (__float_as_int(shifted.x) - (0x4B400000 - 127)) << 23;
+  const int py = (__float_as_int(shifted.y) - (0x4B400000 - 127)) << 23;
+  return mul2(y, make_float2(__int_as_float(px), __int_as_float(py)));
+}
+
+__device__ __forceinline__ float2 swish_poly2(float2 v) {
+  float2 m = sub2(splat2(0.0f), v);
+  m.x = fminf(fmaxf(m.x, -87.0f), 87.0f);
+  m.y = fminf(fmaxf(m.y, -87.0f), 87.0f);
+  const float2 d = add2(splat2(1.0f), exp_poly2_clamped(m));
+  return mul2(v, make_float2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
 
 // Swish of the vector body of pk_swish (csrc/tensor_ops.c:383-388):
