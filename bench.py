@@ -71,8 +71,7 @@ def kernel_table(F, T, n_items):
         ("relpos_combine_softmax", 12 * S, 1),
         ("head_concat", 8 * F * D, 1),
         ("residual_layer_norm_transpose", 16 * F * D, 1),
-        ("glu", 12 * F * D, 1),
-        ("dwconv_bn_swish", 8 * F * D, 1),
+        ("glu_dwconv_bn_swish", 12 * F * D, 1),
         ("transpose_add_layer_norm", 16 * F * D, 1),
         ("residual_layer_norm2", 16 * F * D, 1),
     ]
@@ -320,9 +319,8 @@ def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
         "residual_layer_norm_transpose": lambda: pkcuda.call(
             "pkcu_residual_layer_norm_transpose", x_addr, gout.att_out, P("out_b"), 1.0, P("norm_conv_w"),
             P("norm_conv_b"), gin.cf, seq.handle, sh),
-        "glu": lambda: pkcuda.call("pkcu_glu", gout.pw1, P("pw1_b"), gin.gated, D, 0, seq.handle, sh),
-        "dwconv_bn_swish": lambda: pkcuda.call("pkcu_dwconv_bn_swish", gin.gated, P("dw_w"), P("dw_b"), None, 0.0,
-                                               1, gin.dw, D, 9, seq.handle, sh),
+        "glu_dwconv_bn_swish": lambda: pkcuda.call("pkcu_glu_dwconv_bn_swish", gout.pw1, P("pw1_b"), P("dw_w"),
+                                                   P("dw_b"), None, 0.0, 1, gin.dw, D, 9, seq.handle, sh),
         "transpose_add_layer_norm": lambda: pkcuda.call(
             "pkcu_transpose_add_layer_norm", x_addr, gout.pw2, P("pw2_b"), P("norm_ff2_w"), P("norm_ff2_b"),
             gin.ln_ff2, seq.handle, sh),

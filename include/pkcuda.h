@@ -52,6 +52,11 @@ const char *pkcu_status_string(int status);
 const char *pkcu_last_error(void);
 /* Library version, e.g. "0.1.0". */
 const char *pkcu_version(void);
+/* Device self-test (no counterpart in the reference): checks, for every float
+ * d in [1, 2^126), that the fast reciprocal the Swish kernels use equals the
+ * correctly rounded IEEE reciprocal on the current device. *mismatches
+ * receives the number of differing inputs (0 expected). Synchronous, ~1 ms. */
+int pkcu_selftest(unsigned long long *mismatches);
 
 /* ── batches of items (utterances / chunks) ─────────────────────────────────
  * Ops that know about sequence structure take a pkcu_seq: n_items items of
@@ -193,6 +198,14 @@ int pkcu_glu(const float *in, const float *bias, float *out, int C, int layout,
 int pkcu_dwconv_bn_swish(const float *x, const float *w, const float *b, const float *bn,
                          float bn_eps, int apply_swish, float *out, int C, int K,
                          const pkcu_seq *seq, pkcu_stream_t stream);
+/* The GLU (csrc/encoder.c:457-465, as pkcu_glu with PKCU_CHANNEL_FIRST) fused
+ * into the depthwise conv's input: reads the pointwise-conv output pw1 per
+ * item [2C, T_b] (+ pw1_bias [2C], may be NULL) and never materialises the
+ * GLU output. Bit-identical to pkcu_glu followed by pkcu_dwconv_bn_swish. */
+int pkcu_glu_dwconv_bn_swish(const float *pw1, const float *pw1_bias, const float *w,
+                             const float *b, const float *bn, float bn_eps, int apply_swish,
+                             float *out, int C, int K, const pkcu_seq *seq,
+                             pkcu_stream_t stream);
 /* Conv residual (csrc/encoder.c:475-477): x[t,d] += y[d,t] + bias[d], y per
  * item [D, T_b] (bias: the pw2 bias, csrc/tensor_ops.c:585-589; may be NULL). */
 int pkcu_transpose_add(float *x, const float *y, const float *bias, const pkcu_seq *seq,
@@ -265,7 +278,7 @@ typedef struct {
  * whose consumers run one after another may alias (e.g. the four LN outputs). */
 typedef struct {
     float *ln_ff1, *h1, *ln_sa, *Qu, *K, *Qv, *P_h, *S, *V, *attn, *cf, *dw, *ln_ff2, *h2;
-    float *gated;   /* GLU output, the depthwise conv's input [D, T] per item */
+    float *gated;   /* GLU output [D, T] per item: not written by the fused sequence (may be NULL) */
 } pkcu_gemm_inputs;
 
 /* GEMM points, in the order they occur in one block. */
@@ -283,7 +296,7 @@ typedef int (*pkcu_gemm_hook)(void *user, int block, int gemm, pkcu_stream_t str
 /* Runs n_blocks conformer blocks' non-GEMM ops (csrc/encoder.c:482-491) on x
  * [frames, D] in place, fused at producer/consumer boundaries:
  *   LN_ff1 | bias+Swish | res+LN_sa | QKV split | pos split | combine+softmax |
- *   head concat | res+LN_conv+transpose | GLU | dwconv+bias+Swish |
+ *   head concat | res+LN_conv+transpose | GLU+dwconv+bias+Swish |
  *   transpose-add+LN_ff2 | bias+Swish | res+LN_out(+LN_ff1 of the next block)
  * All pointers are device pointers; blocks[] is a host array. */
 int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks,

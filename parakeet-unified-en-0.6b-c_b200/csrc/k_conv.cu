@@ -89,12 +89,49 @@ glu_tf_kernel(const float *__restrict__ in, const float *__restrict__ bias, floa
   }
 }
 
+// The depthwise conv's input row c of an item, read either plainly (x per
+// item [C, T]) or, with the GLU folded in, from the pointwise-conv output
+// pw1 per item [2C, T]: in[c, t] = a * sigmoid(g), a = pw1[c, t] (+ bias[c]),
+// g = pw1[C + c, t] (+ bias[C + c]) -- the same operations as glu_cf_kernel,
+// so the fused result is bit-identical to GLU followed by the conv.
+struct DwIn {
+  const float *src;
+  long long base;      // element offset of row c (or of the a-row with GLU)
+  long long gate;      // offset from the a-row to the g-row (C * T)
+  float ba, bg;
+  bool bias;
+};
+
+__device__ __forceinline__ DwIn dw_in_row(const float *src, const float *glu_bias, bool glu,
+                                          const SeqDev &seq, int item, int c, int C, int T) {
+  DwIn r;
+  r.src = src;
+  const long long f0 = seq_frame_off(seq, item);
+  r.base = (glu ? 2 * f0 * C : f0 * C) + (long long)c * T;
+  r.gate = (long long)C * T;
+  r.bias = glu && glu_bias != nullptr;
+  r.ba = r.bias ? __ldg(glu_bias + c) : 0.0f;
+  r.bg = r.bias ? __ldg(glu_bias + C + c) : 0.0f;
+  return r;
+}
+
+template <bool GLU>
+__device__ __forceinline__ float dw_in(const DwIn &in, int tt) {
+  if (!GLU) return __ldcs(in.src + in.base + tt);
+  float a = __ldcs(in.src + in.base + tt), g = __ldcs(in.src + in.base + in.gate + tt);
+  if (in.bias) {
+    a = a + in.ba;
+    g = g + in.bg;
+  }
+  return glu1(a, g);
+}
+
 // KC > 0: compile-time kernel width (taps in registers); KC == 0: runtime K.
 template <int KC>
 __global__ void __launch_bounds__(32 * DW_WARPS)
 dwconv_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
               const float *__restrict__ bn, float bn_eps, int apply_swish, float *__restrict__ out,
-              int C, int Kr, SeqDev seq) {
+              int C, int Kr, SeqDev seq, int glu, const float *__restrict__ glu_bias) {
   __shared__ float stage[DW_WARPS][DW_SMEM_PER_WARP];
   const int K = KC > 0 ? KC : Kr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,6 +140,7 @@ dwconv_kernel(const float *__restrict__ x, const float *__restrict__ w, const fl
   const int item = blockIdx.y;
   const int T = seq_T(seq, item);
   const long long base = seq_frame_off(seq, item) * C + (long long)c * T;
+  const DwIn in = dw_in_row(x, glu_bias, glu != 0, seq, item, c, C, T);
   const int pad = (K - 1) / 2;
   const long long n8 = ((long long)C * T) & ~7LL;
   float wk[KC > 0 ? KC : 1];
@@ -122,7 +160,7 @@ dwconv_kernel(const float *__restrict__ x, const float *__restrict__ w, const fl
   for (int t0 = 0; t0 < T; t0 += DW_CHUNK) {
     for (int k = lane; k < DW_CHUNK + K - 1; k += 32) {
       const int tt = t0 - pad + k;
-      s[k] = (tt >= 0 && tt < T) ? x[base + tt] : 0.0f;
+      s[k] = (tt >= 0 && tt < T) ? (glu ? dw_in<true>(in, tt) : dw_in<false>(in, tt)) : 0.0f;
     }
     __syncwarp();
 #pragma unroll
@@ -175,11 +213,11 @@ __device__ __forceinline__ float dw_finish(float val, float mean, float den, flo
   return val;
 }
 
-template <int KC, int SW, bool BN>
+template <int KC, int SW, bool BN, bool GLU>
 __global__ void __launch_bounds__(32 * DW_WARPS)
 dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
                   const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
-                  float *__restrict__ out, int C, SeqDev seq) {
+                  float *__restrict__ out, int C, SeqDev seq, const float *__restrict__ glu_bias) {
   static_assert(KC == 9, "the 4-output register window assumes K = 9");
   __shared__ __align__(16) float stage[DW_WARPS][DW_ROW_MAX];
   constexpr int K = KC;
@@ -190,14 +228,44 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
   const int item = blockIdx.y;
   const int T = seq_T(seq, item);
   const long long base = seq_frame_off(seq, item) * C + (long long)c * T;
+  const DwIn in = dw_in_row(x, glu_bias, GLU, seq, item, c, C, T);
   float *s = stage[warp];
   const int n_groups = (T + 3) >> 2;
   const int n_stage = 4 * n_groups + 8;   // s[0 .. 4*n_groups + 7] are read
-  // s[k] = x[k - pad], zero outside [0, T)
+  // s[k] = in[k - pad], zero outside [0, T)
+  if constexpr (GLU) {
+    // Both GLU halves land in shared memory through async copies (every load
+    // of the row in flight at once), then the gate is applied in place.
+    __shared__ float stage_g[DW_WARPS][DW_ROW_MAX];
+    float *sg = stage_g[warp];
+    for (int k = lane; k < n_stage; k += 32) {
+      const int tt = k - pad;
+      if (tt >= 0 && tt < T) {
+        cp_async4(s + k, in.src + in.base + tt);
+        cp_async4(sg + k, in.src + in.base + in.gate + tt);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    for (int k = lane; k < n_stage; k += 32) {   // the same k as this lane copied
+      const int tt = k - pad;
+      float val = 0.0f;
+      if (tt >= 0 && tt < T) {
+        float a = s[k], g = sg[k];
+        if (in.bias) {
+          a = a + in.ba;
+          g = g + in.bg;
+        }
+        val = glu1(a, g);
+      }
+      s[k] = val;
+    }
+  } else {
 #pragma unroll 4
-  for (int k = lane; k < n_stage; k += 32) {
-    const int tt = k - pad;
-    s[k] = (tt >= 0 && tt < T) ? __ldcs(x + base + tt) : 0.0f;
+    for (int k = lane; k < n_stage; k += 32) {
+      const int tt = k - pad;
+      s[k] = (tt >= 0 && tt < T) ? dw_in<false>(in, tt) : 0.0f;
+    }
   }
   float wk[K];
 #pragma unroll
@@ -280,29 +348,38 @@ static unsigned per_item_grid(long long work, int n_items) {
   return (unsigned)g;
 }
 
+// glu != 0: x is the pointwise-conv output per item [2C, T] and the GLU (with
+// glu_bias, may be NULL) is applied while staging.
 static int launch_dwconv(const float *x, const float *w, const float *b, const float *bn,
                          float bn_eps, int apply_swish, float *out, int C, int K, SeqDev sd,
-                         cudaStream_t s) {
+                         cudaStream_t s, int glu = 0, const float *glu_bias = nullptr) {
   dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
   if (K == 9 && 4 * ((sd.max_T + 3) / 4) + 8 <= DW_ROW_MAX) {
     // every item's C*T_b is a multiple of 8 when C is: no scalar Swish tail
     const int sw = !apply_swish ? DW_SWISH_NONE : (C % 8 == 0 ? DW_SWISH_POLY : DW_SWISH_TAIL);
-#define PK_DW_ROW(SWV, BNV) \
-  dwconv_row_kernel<9, SWV, BNV><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, sd)
+#define PK_DW_ROW(SWV, BNV, GLUV)                                                        \
+  dwconv_row_kernel<9, SWV, BNV, GLUV><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, \
+                                                                      out, C, sd, glu_bias)
+#define PK_DW_ROW_SW(BNV, GLUV)                               \
+  do {                                                        \
+    if (sw == DW_SWISH_NONE) PK_DW_ROW(DW_SWISH_NONE, BNV, GLUV); \
+    else if (sw == DW_SWISH_POLY) PK_DW_ROW(DW_SWISH_POLY, BNV, GLUV); \
+    else PK_DW_ROW(DW_SWISH_TAIL, BNV, GLUV);                 \
+  } while (0)
     if (bn) {
-      if (sw == DW_SWISH_NONE) PK_DW_ROW(DW_SWISH_NONE, true);
-      else if (sw == DW_SWISH_POLY) PK_DW_ROW(DW_SWISH_POLY, true);
-      else PK_DW_ROW(DW_SWISH_TAIL, true);
+      if (glu) PK_DW_ROW_SW(true, true); else PK_DW_ROW_SW(true, false);
     } else {
-      if (sw == DW_SWISH_NONE) PK_DW_ROW(DW_SWISH_NONE, false);
-      else if (sw == DW_SWISH_POLY) PK_DW_ROW(DW_SWISH_POLY, false);
-      else PK_DW_ROW(DW_SWISH_TAIL, false);
+      if (glu) PK_DW_ROW_SW(false, true); else PK_DW_ROW_SW(false, false);
     }
+#undef PK_DW_ROW_SW
 #undef PK_DW_ROW
-  } else if (K == 9)
-    dwconv_kernel<9><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
-  else
-    dwconv_kernel<0><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd);
+  } else if (K == 9) {
+    dwconv_kernel<9><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd,
+                                                     glu, glu_bias);
+  } else {
+    dwconv_kernel<0><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, apply_swish, out, C, K, sd,
+                                                     glu, glu_bias);
+  }
   return PKCU_OK;
 }
 
@@ -344,6 +421,21 @@ extern "C" int pkcu_dwconv_bn_swish(const float *x, const float *w, const float 
   if (seq->frames == 0) return PKCU_OK;
   launch_dwconv(x, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, (cudaStream_t)stream);
   return pkcu_launch_status("pkcu_dwconv_bn_swish");
+}
+
+extern "C" int pkcu_glu_dwconv_bn_swish(const float *pw1, const float *pw1_bias, const float *w,
+                                        const float *b, const float *bn, float bn_eps,
+                                        int apply_swish, float *out, int C, int K,
+                                        const pkcu_seq *seq, pkcu_stream_t stream) {
+  if (!pw1 || !w || !out || !seq || C <= 0 || K <= 0 || K > DW_MAX_K)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_glu_dwconv_bn_swish: bad argument (K must be 1..%d)",
+                     DW_MAX_K);
+  if (seq->dev.n_items > 65535)
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_glu_dwconv_bn_swish: at most 65535 items per call");
+  if (seq->frames == 0) return PKCU_OK;
+  launch_dwconv(pw1, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, (cudaStream_t)stream, 1,
+                pw1_bias);
+  return pkcu_launch_status("pkcu_glu_dwconv_bn_swish");
 }
 
 extern "C" int pkcu_depthwise_conv1d(const float *x, const float *w, const float *b, float *out,

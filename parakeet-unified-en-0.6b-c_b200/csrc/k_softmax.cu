@@ -60,7 +60,13 @@ __device__ __forceinline__ void softmax_regs(float (&v)[NPL], int len, int lane)
       d.x = fmaxf(d.x, -87.0f);   // exp_poly_nonpos: arguments are <= 0 or NaN
       d.y = fmaxf(d.y, -87.0f);
       float2 e = exp_poly2_clamped(d);
-      if (32 * k + 63 >= len8) {
+      if (32 * k + 63 < len8) {   // warp-uniform: both slots valid, both polynomial
+        v[k] = e.x;
+        v[k + 1] = e.y;
+        s2 = add2(s2, e);
+        continue;
+      }
+      {
         if (j0 >= len8 && j0 < len) e.x = expf(v[k] - mx);
         if (j1 >= len8 && j1 < len) e.y = expf(v[k + 1] - mx);
       }
@@ -288,9 +294,16 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
 #pragma unroll
     for (int k = 0; k < NPL; k += 2) {
       const int j0 = lane + 32 * k, j1 = j0 + 32;
+      if (32 * k + 63 < len) {   // warp-uniform: both slots inside the row
+        const float2 c = mul2(add2(make_float2(sa[j0], sa[j1]), make_float2(sb[j0], sb[j1])),
+                              splat2(scale));   // (ac + bd) * scale, each rounded
+        v[k] = c.x;
+        v[k + 1] = c.y;
+        continue;
+      }
       const float2 a = make_float2(j0 < len ? sa[j0] : 0.0f, j1 < len ? sa[j1] : 0.0f);
       const float2 b = make_float2(j0 < len ? sb[j0] : 0.0f, j1 < len ? sb[j1] : 0.0f);
-      const float2 c = mul2(add2(a, b), splat2(scale));   // (ac + bd) * scale, each rounded
+      const float2 c = mul2(add2(a, b), splat2(scale));
       v[k] = j0 < len ? c.x : 0.0f;
       v[k + 1] = j1 < len ? c.y : 0.0f;
     }
@@ -299,7 +312,7 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
 #pragma unroll
     for (int k = 0; k < NPL; k++) {
       const int j = lane + 32 * k;
-      if (j < len) dst[j] = v[k];
+      if (32 * k + 31 < len || j < len) dst[j] = v[k];
     }
     __syncwarp();         // the buffer is refilled two rows from now
     cur = nxt;

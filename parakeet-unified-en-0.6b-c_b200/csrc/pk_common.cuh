@@ -161,12 +161,32 @@ __device__ __forceinline__ float2 exp_poly2_clamped(float2 x) {
   return mul2(y, make_float2(__int_as_float(px), __int_as_float(py)));
 }
 
+// Correctly rounded 1/d for d in [1, 2^126): the hardware approximation
+// followed by one fused Newton step, r = r0 + r0*(1 - d*r0). Over that range
+// it equals the IEEE quotient (__frcp_rn) for every float: the library's
+// self-test pkcu_selftest() checks all 1,056,964,608 inputs on the device.
+// Swish's denominators 1 + exp_poly(-v) lie in [1, 6.1e37].
+__device__ __forceinline__ float rcp_approx(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+__device__ __forceinline__ float rcp_1_2e126(float d) {
+  const float r0 = rcp_approx(d);
+  return fmaf(fmaf(-d, r0, 1.0f), r0, r0);
+}
+__device__ __forceinline__ float2 rcp2_1_2e126(float2 d) {
+  const float2 r0 = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  const float2 e = fma2(make_float2(-d.x, -d.y), r0, splat2(1.0f));
+  return fma2(e, r0, r0);
+}
+
 __device__ __forceinline__ float2 swish_poly2(float2 v) {
   float2 m = sub2(splat2(0.0f), v);
   m.x = fminf(fmaxf(m.x, -87.0f), 87.0f);
   m.y = fminf(fmaxf(m.y, -87.0f), 87.0f);
   const float2 d = add2(splat2(1.0f), exp_poly2_clamped(m));
-  return mul2(v, make_float2(__frcp_rn(d.x), __frcp_rn(d.y)));
+  return mul2(v, rcp2_1_2e126(d));
 }
 
 // Swish of the vector body of pk_swish (csrc/tensor_ops.c:383-388):
@@ -174,7 +194,7 @@ __device__ __forceinline__ float2 swish_poly2(float2 v) {
 // i.e. the IEEE quotient 1/d.
 __device__ __forceinline__ float swish_poly(float v) {
   const float e = exp_poly(__fsub_rn(0.0f, v));
-  return __fmul_rn(v, __frcp_rn(__fadd_rn(1.0f, e)));
+  return __fmul_rn(v, rcp_1_2e126(__fadd_rn(1.0f, e)));
 }
 
 // Swish of the scalar tail of pk_swish (csrc/tensor_ops.c:389): x / (1 + expf(-x)).
@@ -184,7 +204,8 @@ __device__ __forceinline__ float swish_tail(float v) {
 
 // Sigmoid gate of the GLU (csrc/encoder.c:462): 1 / (1 + expf(-b)).
 __device__ __forceinline__ float sigmoid_libm(float b) {
-  return __frcp_rn(__fadd_rn(1.0f, expf(-b)));
+  const float d = __fadd_rn(1.0f, expf(-b));   // in [1, inf]
+  return d < 0x1p126f ? rcp_1_2e126(d) : __frcp_rn(d);
 }
 
 // ── ragged batches ───────────────────────────────────────────────────────────

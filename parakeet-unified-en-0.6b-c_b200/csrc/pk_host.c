@@ -381,7 +381,7 @@ void pk_depthwise_conv1d(const float *x, const float *w, const float *b, float *
 
 /* ── sequence driver ─────────────────────────────────────────────────────── */
 
-int pkcu_encoder_nongemm_launches(int n_blocks) { return n_blocks > 0 ? 1 + 13 * n_blocks : 0; }
+int pkcu_encoder_nongemm_launches(int n_blocks) { return n_blocks > 0 ? 1 + 12 * n_blocks : 0; }
 
 #define PK_TRY(call) do { int st_ = (call); if (st_) return st_; } while (0)
 #define PK_HOOK(blk, g) do { if (hook) PK_TRY(hook(hook_user, (blk), (g), stream)); } while (0)
@@ -427,9 +427,8 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
                                                   p->norm_conv_b, gi->cf, seq, stream));
         /* conv module (csrc/encoder.c:439-478) */
         PK_HOOK(b, PKCU_GEMM_PW1);
-        PK_TRY(pkcu_glu(go->pw1, p->pw1_b, gi->gated, PK_D, PKCU_CHANNEL_FIRST, seq, stream));
-        PK_TRY(pkcu_dwconv_bn_swish(gi->gated, p->dw_w, p->dw_b, NULL, 0.0f, 1, gi->dw, PK_D, 9, seq,
-                                    stream));
+        PK_TRY(pkcu_glu_dwconv_bn_swish(go->pw1, p->pw1_b, p->dw_w, p->dw_b, NULL, 0.0f, 1, gi->dw,
+                                        PK_D, 9, seq, stream));
         PK_HOOK(b, PKCU_GEMM_PW2);
         PK_TRY(pkcu_transpose_add_layer_norm(x, go->pw2, p->pw2_b, p->norm_ff2_w, p->norm_ff2_b,
                                              gi->ln_ff2, seq, stream));

@@ -23,7 +23,7 @@ PKCU_ACT_RELU, PKCU_ACT_TANH = 0, 1
 
 # Symbols declared by include/pkcuda.h (checked by the CPU test suite).
 EXPORTED = (
-    "pkcu_status_string", "pkcu_last_error", "pkcu_version",
+    "pkcu_status_string", "pkcu_last_error", "pkcu_version", "pkcu_selftest",
     "pkcu_seq_create", "pkcu_seq_destroy", "pkcu_seq_n_items", "pkcu_seq_frames",
     "pkcu_seq_score_elems", "pkcu_seq_bd_elems", "pkcu_seq_pos_rows",
     "pk_layer_norm", "pk_layer_norm_rows", "pk_layer_norm_rows_inplace", "pk_swish", "pk_relu",
@@ -34,6 +34,7 @@ EXPORTED = (
     "pkcu_pos_head_split", "pkcu_relative_shift", "pkcu_relpos_combine",
     "pkcu_relpos_combine_softmax", "pkcu_head_concat", "pkcu_layer_norm_transpose",
     "pkcu_residual_layer_norm_transpose", "pkcu_glu", "pkcu_dwconv_bn_swish",
+    "pkcu_glu_dwconv_bn_swish",
     "pkcu_transpose_add", "pkcu_transpose_add_layer_norm", "pkcu_dequant_i8",
     "pkcu_requant_qkv_i8", "pkcu_dequant_i4", "pkcu_dequant_i4_qkv", "pkcu_joint_add_act",
     "pkcu_argmax_rows", "pkcu_encoder_nongemm", "pkcu_encoder_nongemm_launches",
@@ -53,6 +54,7 @@ _SIGS = {
     "pkcu_status_string": (C.c_char_p, [I]),
     "pkcu_last_error": (C.c_char_p, []),
     "pkcu_version": (C.c_char_p, []),
+    "pkcu_selftest": (I, [C.POINTER(C.c_ulonglong)]),
     "pkcu_seq_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
     "pkcu_seq_destroy": (None, [VP]),
     "pkcu_seq_n_items": (I, [VP]),
@@ -90,6 +92,7 @@ _SIGS = {
     "pkcu_residual_layer_norm_transpose": (I, [VP, VP, VP, F, VP, VP, VP, VP, VP]),
     "pkcu_glu": (I, [VP, VP, VP, I, I, VP, VP]),
     "pkcu_dwconv_bn_swish": (I, [VP, VP, VP, VP, F, I, VP, I, I, VP, VP]),
+    "pkcu_glu_dwconv_bn_swish": (I, [VP, VP, VP, VP, VP, F, I, VP, I, I, VP, VP]),
     "pkcu_transpose_add": (I, [VP, VP, VP, VP, VP]),
     "pkcu_transpose_add_layer_norm": (I, [VP, VP, VP, VP, VP, VP, VP, VP]),
     "pkcu_dequant_i8": (I, [VP, F, VP, LL, VP]),

@@ -19,6 +19,26 @@ def rng(seed):
     return np.random.default_rng(seed)
 
 
+def test_selftest_reciprocal(cuda):
+    """Every float d in [1, 2^126): fast reciprocal == correctly rounded 1/d."""
+    import ctypes as C
+    bad = C.c_ulonglong(12345)
+    cuda.call("pkcu_selftest", C.byref(bad))
+    assert bad.value == 0
+
+
+def test_swish_dense_sweep(cuda, oracle):
+    """Swish body bit-exact against the restatement on a dense sweep of
+    [-100, 100] (every 509th float of that range)."""
+    u = np.arange(0, 0x42C80000, 509, dtype=np.uint32)     # [+0, 100)
+    pos = u.view(np.float32)
+    x = np.concatenate([pos, -pos]).astype(np.float32)
+    x = x[: x.size & ~7]
+    xd = dev(x)
+    cuda.call("pkcu_swish", xd.data_ptr(), x.size, cuda.stream_handle())
+    assert_bitexact(host(xd), oracle.swish(x), "swish sweep")
+
+
 # ── LayerNorm family ──────────────────────────────────────────────────────────
 
 @pytest.mark.parametrize("R,Dd,offset", [(1, 1024, 0), (7, 1024, 0), (375, 1024, 0),
@@ -325,6 +345,37 @@ def test_dwconv_bn_swish(cuda, oracle, lengths, with_bn):
             if with_bn:
                 y = oracle.batch_norm(y, bn[:D], bn[D:2 * D], bn[2 * D:3 * D], bn[3 * D:], 1e-5)
             assert_bitexact(L.chunk(got, i, D, (D, T)), oracle.swish(y), f"item {i}")
+
+
+@pytest.mark.parametrize("lengths,K", [([408, 416, 416, 408], 9), ([9, 1, 4], 9), ([700], 9),
+                                       ([33, 20], 5)])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_glu_dwconv_fused(cuda, oracle, lengths, K, with_bias):
+    """GLU folded into the depthwise conv: bit-identical to GLU then conv."""
+    r = rng(23 + sum(lengths) + K)
+    L = Layout(lengths)
+    F = L.frames
+    pw1 = (3 * r.standard_normal(2 * F * D)).astype(np.float32)
+    gb = (0.1 * r.standard_normal(2 * D)).astype(np.float32)
+    w = (0.3 * r.standard_normal((D, K))).astype(np.float32)
+    b = (0.1 * r.standard_normal(D)).astype(np.float32)
+    with cuda.Seq(lengths) as seq:
+        gated, two, fused = empty(F * D), empty(F * D), empty(F * D)
+        gbd = dev(gb).data_ptr() if with_bias else None
+        cuda.call("pkcu_glu", dev(pw1).data_ptr(), gbd, gated.data_ptr(), D, cuda.PKCU_CHANNEL_FIRST,
+                  seq.handle, cuda.stream_handle())
+        cuda.call("pkcu_dwconv_bn_swish", gated.data_ptr(), dev(w).data_ptr(), dev(b).data_ptr(), None,
+                  0.0, 1, two.data_ptr(), D, K, seq.handle, cuda.stream_handle())
+        cuda.call("pkcu_glu_dwconv_bn_swish", dev(pw1).data_ptr(), gbd, dev(w).data_ptr(),
+                  dev(b).data_ptr(), None, 0.0, 1, fused.data_ptr(), D, K, seq.handle,
+                  cuda.stream_handle())
+        got = host(fused)
+        assert_bitexact(got, host(two), "fused == GLU then conv")
+        for i, T in enumerate(lengths):
+            item = L.chunk(pw1, i, 2 * D, (2 * D, T))
+            g = oracle.glu_channel_first(oracle.pointwise_bias(item, gb) if with_bias else item)
+            want = oracle.swish(oracle.depthwise_conv1d(g, w, b))
+            assert_close(L.chunk(got, i, D, (D, T)), want, f"item {i}")
 
 
 # ── weights ───────────────────────────────────────────────────────────────────
