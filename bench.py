@@ -83,6 +83,25 @@ def step_bytes(F, T, n_items, n_blocks):
     return n_blocks * per_block + 8 * F * D - 4 * F * D
 
 
+# ── multi-GPU plumbing (one process per GPU, no data-path collective) ────────
+
+def shard(rank: int, world: int, per_rank: int) -> range:
+    """Global indices of the utterances one rank processes. Weak scaling: each
+    rank owns its own per_rank independent utterances; nothing is exchanged."""
+    assert 0 <= rank < world and per_rank > 0
+    return range(rank * per_rank, (rank + 1) * per_rank)
+
+
+def max_over_ranks(x: float, world: int, device=None) -> float:
+    """Max of a per-rank timing over all ranks (the slowest rank sets the pace)."""
+    import torch
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ── clocks during the timed region ───────────────────────────────────────────
 
 class ClockSampler:
@@ -241,14 +260,15 @@ def config_dict(args, world):
 
 # ── this library ──────────────────────────────────────────────────────────────
 
-def setup_device(args, rank):
+def setup_device(args, rank, world):
     import torch
     import pkcuda
-    seq = pkcuda.Seq([args.T] * args.utts)
+    mine = shard(rank, world, args.utts)
+    seq = pkcuda.Seq([args.T] * len(mine))
     ws = pkcuda.EncoderWorkspace(seq, args.groups)
     x_addr, gout, gin = ws.device()
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234 + mine.start)   # this rank's own utterances
     F = seq.frames
     # Fill x and the stand-in GEMM outputs with N(0,1) (views of the workspace).
     total = ws.device_bytes // 4
@@ -361,7 +381,7 @@ def _ours(args, rank, world, local_rank, stream):
     import torch
     import torch.distributed as dist
     import pkcuda
-    seq, ws, x_addr, gout, gin, blocks, arr = setup_device(args, rank)
+    seq, ws, x_addr, gout, gin, blocks, arr = setup_device(args, rank, world)
     F = seq.frames
 
     def step():
@@ -398,10 +418,7 @@ def _ours(args, rank, world, local_rank, stream):
         dist.barrier()
     clocks = sampler.stop(t0, t1)
     ms = e0.elapsed_time(e1)
-    ms_t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    ms_max = max_over_ranks(ms, world, device="cuda")
     frames_all = F * args.steps * world
     value = frames_all / (ms_max / 1e3)
     bytes_step = step_bytes(F, args.T, args.utts, args.blocks)
@@ -495,11 +512,7 @@ def run_e2e(args, ws, arr, gout, x_addr, stream, world):
     t0 = time.perf_counter()
     for _ in range(steps):
         ws.run_host(xh.data_ptr(), gh, arr, args.blocks, stream)
-    secs = time.perf_counter() - t0
-    s_t = torch.tensor([secs], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(s_t, op=dist.ReduceOp.MAX)
-    secs = float(s_t.item())
+    secs = max_over_ranks(time.perf_counter() - t0, world, device="cuda")
     return {"value": F * steps * world / secs, "unit": "frames/s", "steps": steps,
             "h2d_bytes_per_step": ws.h2d_bytes, "d2h_bytes_per_step": ws.d2h_bytes,
             "pipeline_groups": args.groups,
