@@ -105,6 +105,16 @@ void pk_bias_add(float *x, const float *b, int len);
 /* csrc/tensor_ops.c:570; b may be NULL (:561) */
 void pk_depthwise_conv1d(const float *x, const float *w, const float *b, float *out, int C,
                          int T, int K);
+/* No counterpart in the reference. pk_softmax_rows for callers that cannot let
+ * the library allocate device memory (a real-time callback that must not wait
+ * on the allocator, a process that pre-assigns all device memory to its own
+ * pool, code running during CUDA graph capture): the rows are staged in a
+ * fixed 16 MiB array that every device loading the library holds until exit,
+ * so n_rows * len may be at most 4,194,304 (larger sizes return
+ * PKCU_ERR_ARG). The first call on a device looks up the array's address --
+ * make it before any stream capture. Calls share the array; calls whose GPU
+ * work overlaps race on it. Returns PKCU_OK or an error code. */
+int pk_softmax_rows_noalloc(float *x, int n_rows, int len);
 /* Status of the calling thread's last drop-in call: PKCU_OK or an error code
  * (the message is in pkcu_last_error()). A failing drop-in also prints one
  * line to stderr. */

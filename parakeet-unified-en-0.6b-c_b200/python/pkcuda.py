@@ -28,6 +28,7 @@ EXPORTED = (
     "pkcu_seq_score_elems", "pkcu_seq_bd_elems", "pkcu_seq_pos_rows",
     "pk_layer_norm", "pk_layer_norm_rows", "pk_layer_norm_rows_inplace", "pk_swish", "pk_relu",
     "pk_softmax", "pk_softmax_rows", "pk_bias_add", "pk_depthwise_conv1d", "pk_cuda_status",
+    "pk_softmax_rows_noalloc",
     "pkcu_layer_norm_rows", "pkcu_softmax_rows", "pkcu_swish", "pkcu_relu", "pkcu_bias_add_rows",
     "pkcu_depthwise_conv1d", "pkcu_bias_swish_rows", "pkcu_residual_add",
     "pkcu_residual_layer_norm", "pkcu_residual_layer_norm2", "pkcu_qkv_split_uv",
@@ -72,6 +73,7 @@ _SIGS = {
     "pk_bias_add": (None, [VP, VP, I]),
     "pk_depthwise_conv1d": (None, [VP, VP, VP, VP, I, I, I]),
     "pk_cuda_status": (I, []),
+    "pk_softmax_rows_noalloc": (I, [VP, I, I]),
     "pkcu_layer_norm_rows": (I, [VP, VP, VP, VP, I, I, VP]),
     "pkcu_softmax_rows": (I, [VP, I, I, VP]),
     "pkcu_swish": (I, [VP, LL, VP]),
