@@ -57,6 +57,15 @@ const char *pkcu_version(void);
  * correctly rounded IEEE reciprocal on the current device. *mismatches
  * receives the number of differing inputs (0 expected). Synchronous, ~1 ms. */
 int pkcu_selftest(unsigned long long *mismatches);
+/* Device-side wait check (no counterpart in the reference): kernels that stage
+ * rows with bulk asynchronous copies wait for them at most 1 s; a wait that
+ * runs out makes the kernel abandon that part of its output and is counted.
+ * *count receives the number of such waits on the current device since the
+ * last reset (0 in correct operation); reset != 0 clears it. Synchronous. */
+int pkcu_wait_timeouts(unsigned *count, int reset);
+/* Self-test of that bound: one warp waits 20 ms on a barrier whose copy never
+ * comes; *timed_out receives 1 when the wait gave up as designed. */
+int pkcu_selftest_wait(int *timed_out);
 
 /* ── batches of items (utterances / chunks) ─────────────────────────────────
  * Ops that know about sequence structure take a pkcu_seq: n_items items of

@@ -339,6 +339,177 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
   }
 }
 
+// ── aligned-chunk form (K = 9, C % 8 == 0, 16-byte aligned arrays) ──────────
+// With C a multiple of 4 an item's input row c (x or either GLU half) and its
+// output row start at the same offset mod 4 floats (off), so the work is cut
+// into the 4-float chunks of that common alignment. Lane 0 of each warp copies
+// the row (both GLU halves) into shared memory as the 16-byte aligned superset
+// with one bulk copy per half, completion on the warp's mbarrier:
+// s[4 + k] = row[(start & ~3) + k], so row entry t sits at s[4 + off + t] and
+// chunk q (entries t = 4q + e - off) at s[4 + 4q + e].
+//
+// The GLU gate runs 4 entries at a time on the chunks wholly inside the row
+// and one entry per lane on the at most 6 entries outside them. The conv runs
+// 4 outputs at a time on the chunks whose 9-tap windows s[4q .. 4q + 11] lie
+// wholly inside the row -- packed tap chains, packed Swish, one 16-byte store
+// -- and one output per lane, with the out-of-row taps skipped, on the at most
+// 15 outputs near the row's ends. No lane runs an edge path inside the loops.
+constexpr int DWA_ROW = 656;
+
+__host__ __device__ constexpr int dwa_row_need(int T) { return 4 * ((T + 6) / 4) + 8; }
+
+// GLU of 4 values: a * sigmoid(g), the pair reciprocal when both denominators
+// are below 2^126 (bit-identical to glu1 on each value).
+__device__ __forceinline__ float4 glu4(float4 a, float4 g, float ba, float bg, bool bias) {
+  if (bias) {
+    const float2 a01 = add2(make_float2(a.x, a.y), splat2(ba));
+    const float2 a23 = add2(make_float2(a.z, a.w), splat2(ba));
+    const float2 g01 = add2(make_float2(g.x, g.y), splat2(bg));
+    const float2 g23 = add2(make_float2(g.z, g.w), splat2(bg));
+    a = make_float4(a01.x, a01.y, a23.x, a23.y);
+    g = make_float4(g01.x, g01.y, g23.x, g23.y);
+  }
+  const float2 d01 = add2(splat2(1.0f), make_float2(expf(-g.x), expf(-g.y)));
+  const float2 d23 = add2(splat2(1.0f), make_float2(expf(-g.z), expf(-g.w)));
+  float2 r01, r23;
+  if (fmaxf(fmaxf(d01.x, d01.y), fmaxf(d23.x, d23.y)) < 0x1p126f) {
+    r01 = rcp2_1_2e126(d01);
+    r23 = rcp2_1_2e126(d23);
+  } else {
+    r01 = make_float2(sigmoid_libm(g.x), sigmoid_libm(g.y));
+    r23 = make_float2(sigmoid_libm(g.z), sigmoid_libm(g.w));
+  }
+  const float2 o01 = mul2(make_float2(a.x, a.y), r01);
+  const float2 o23 = mul2(make_float2(a.z, a.w), r23);
+  return make_float4(o01.x, o01.y, o23.x, o23.y);
+}
+
+template <int SW, bool BN>
+__device__ __forceinline__ float dwa_finish(float val, float mean, float den, float gam, float bet) {
+  if (BN) val = ((val - mean) / den) * gam + bet;
+  if (SW == DW_SWISH_POLY) val = swish_poly(val);
+  return val;
+}
+
+template <int SW, bool BN, bool GLU>
+__global__ void __launch_bounds__(32 * DW_WARPS)
+dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                 const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
+                 float *__restrict__ out, int C, SeqDev seq, const float *__restrict__ glu_bias,
+                 long long x_total) {
+  static_assert(SW == DW_SWISH_NONE || SW == DW_SWISH_POLY, "no scalar Swish tail here");
+  constexpr int K = 9;
+  __shared__ __align__(16) float stage[DW_WARPS][DWA_ROW];
+  __shared__ __align__(16) float stage_g[GLU ? DW_WARPS : 1][GLU ? DWA_ROW : 4];
+  __shared__ unsigned long long bars[DW_WARPS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * DW_WARPS + warp;
+  if (c >= C) return;
+  const int item = blockIdx.y;
+  const int T = seq_T(seq, item);
+  const long long f0 = seq_frame_off(seq, item);
+  const long long row = (GLU ? 2 * f0 * C : f0 * C) + (long long)c * T;
+  float *s = stage[warp];
+  float *sg = stage_g[GLU ? warp : 0];
+  unsigned long long *bar = bars + warp;
+  if (lane == 0) {
+    mbar_init(bar, 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+  const Span sa = span_of(row, T, x_total);
+  Span sgs = sa;
+  if (GLU) sgs = span_of(row + (long long)C * T, T, x_total);
+  if (lane == 0) mbar_arrive_tx(bar, sa.bytes + (GLU ? sgs.bytes : 0u));
+  span_issue(s + 4, x, sa, bar, lane);
+  if (GLU) span_issue(sg + 4, x, sgs, bar, lane);
+  // per-channel parameters while the copies are in flight
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; k++) wk[k] = __ldg(w + (long long)c * K + k);
+  const float bias = b ? __ldg(b + c) : 0.0f;
+  const bool gbias = GLU && glu_bias != nullptr;
+  const float ba = gbias ? __ldg(glu_bias + c) : 0.0f;
+  const float bg = gbias ? __ldg(glu_bias + C + c) : 0.0f;
+  float mean = 0.0f, den = 1.0f, gam = 1.0f, bet = 0.0f;
+  if (BN) {
+    mean = __ldg(bn + c);
+    den = sqrtf(__ldg(bn + C + c) + bn_eps);
+    gam = __ldg(bn + 2 * C + c);
+    bet = __ldg(bn + 3 * C + c);
+  }
+  const int off = sa.off;
+  const bool ok = mbar_wait(bar, 0);
+  if (__any_sync(PK_FULL_MASK, !ok)) {   // the copy never landed: give up this row
+    if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+    mbar_wait(bar, 0);
+    return;
+  }
+  __syncwarp();   // tail floats copied by other lanes are visible
+  if (GLU) {
+    // chunks [g_lo, g_hi) lie wholly inside the row (entries 4q - off .. 4q - off + 3)
+    const int g_lo = off > 0 ? 1 : 0;
+    const int g_hi = (T + off) >> 2;
+    const int n_head = off > 0 ? (4 - off < T ? 4 - off : T) : 0;
+    const int tail0 = g_hi > g_lo ? 4 * g_hi - off : n_head;
+    const int n_left = n_head + (T - tail0);
+    for (int q = g_lo + lane; q < g_hi; q += 32)
+      st4(s + 4 + 4 * q, glu4(ld4(s + 4 + 4 * q), ld4(sg + 4 + 4 * q), ba, bg, gbias));
+    if (lane < n_left) {
+      const int t = lane < n_head ? lane : tail0 + (lane - n_head);
+      float aa = s[4 + off + t], gg = sg[4 + off + t];
+      if (gbias) {
+        aa = aa + ba;
+        gg = gg + bg;
+      }
+      s[4 + off + t] = glu1(aa, gg);
+    }
+    __syncwarp();
+  }
+  float *orow = out + f0 * C + (long long)c * T;   // orow - off is 16-byte aligned
+  // output chunks [c_lo, c_hi] have every tap inside the row: 4q - off >= 4 and
+  // 4q - off + 7 <= T - 1
+  const int c_lo = 1 + ((off + 3) >> 2);
+  const int c_hi = (T - 8 + off) >= 0 ? (T - 8 + off) >> 2 : -1;
+  for (int q = c_lo + lane; q <= c_hi; q += 32) {
+    const int t0 = 4 * q - off;
+    const float4 a0 = ld4(s + 4 * q), a1 = ld4(s + 4 * q + 4), a2 = ld4(s + 4 * q + 8);
+    const float win[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
+                           a2.x, a2.y, a2.z, a2.w};
+    // outputs (t0, t0+1) and (t0+2, t0+3) as packed pairs; each output's
+    // multiply-add chain runs in the same k order as the scalar form
+    float2 v01 = splat2(bias), v23 = splat2(bias);
+#pragma unroll
+    for (int k = 0; k < K; k++) {
+      v01 = fma2(make_float2(win[k], win[k + 1]), splat2(wk[k]), v01);
+      v23 = fma2(make_float2(win[k + 2], win[k + 3]), splat2(wk[k]), v23);
+    }
+    if (BN) {
+      v01 = make_float2(((v01.x - mean) / den) * gam + bet, ((v01.y - mean) / den) * gam + bet);
+      v23 = make_float2(((v23.x - mean) / den) * gam + bet, ((v23.y - mean) / den) * gam + bet);
+    }
+    if (SW == DW_SWISH_POLY) {
+      v01 = swish_poly2(v01);
+      v23 = swish_poly2(v23);
+    }
+    st4(orow + t0, make_float4(v01.x, v01.y, v23.x, v23.y));
+  }
+  // leftover outputs: [0, h_end) and [t_beg, T), one per lane
+  const int h_end = c_hi >= c_lo ? 4 * c_lo - off : T;
+  const int t_beg = c_hi >= c_lo ? 4 * c_hi - off + 4 : T;
+  const int n_out = h_end + (T - t_beg);
+  if (lane < n_out) {
+    const int t = lane < h_end ? lane : t_beg + (lane - h_end);
+    float val = bias;
+#pragma unroll
+    for (int k = 0; k < K; k++) {
+      const int tt = t - 4 + k;
+      if (tt >= 0 && tt < T) val = fmaf(s[4 + off + tt], wk[k], val);
+    }
+    orow[t] = dwa_finish<SW, BN>(val, mean, den, gam, bet);
+  }
+}
+
 static unsigned per_item_grid(long long work, int n_items) {
   long long g = (work + GLU_THREADS - 1) / GLU_THREADS;
   long long cap = ((long long)pkcu_sm_count() * 16 + n_items - 1) / n_items;
@@ -352,9 +523,28 @@ static unsigned per_item_grid(long long work, int n_items) {
 // glu_bias, may be NULL) is applied while staging.
 static int launch_dwconv(const float *x, const float *w, const float *b, const float *bn,
                          float bn_eps, int apply_swish, float *out, int C, int K, SeqDev sd,
-                         cudaStream_t s, int glu = 0, const float *glu_bias = nullptr) {
+                         long long frames, cudaStream_t s, int glu = 0,
+                         const float *glu_bias = nullptr) {
   dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
-  if (K == 9 && 4 * ((sd.max_T + 3) / 4) + 8 <= DW_ROW_MAX) {
+  if (K == 9 && C % 8 == 0 && PK_ALIGNED16(x) && PK_ALIGNED16(out) &&
+      dwa_row_need(sd.max_T) <= DWA_ROW) {
+    const long long x_total = (glu ? 2 : 1) * frames * C;
+#define PK_DW_AL(SWV, BNV, GLUV)                                                         \
+  dwconv_al_kernel<SWV, BNV, GLUV><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, \
+                                                                 sd, glu_bias, x_total)
+#define PK_DW_AL_SW(BNV, GLUV)                                  \
+  do {                                                          \
+    if (apply_swish) PK_DW_AL(DW_SWISH_POLY, BNV, GLUV);        \
+    else PK_DW_AL(DW_SWISH_NONE, BNV, GLUV);                    \
+  } while (0)
+    if (bn) {
+      if (glu) PK_DW_AL_SW(true, true); else PK_DW_AL_SW(true, false);
+    } else {
+      if (glu) PK_DW_AL_SW(false, true); else PK_DW_AL_SW(false, false);
+    }
+#undef PK_DW_AL_SW
+#undef PK_DW_AL
+  } else if (K == 9 && 4 * ((sd.max_T + 3) / 4) + 8 <= DW_ROW_MAX) {
     // every item's C*T_b is a multiple of 8 when C is: no scalar Swish tail
     const int sw = !apply_swish ? DW_SWISH_NONE : (C % 8 == 0 ? DW_SWISH_POLY : DW_SWISH_TAIL);
 #define PK_DW_ROW(SWV, BNV, GLUV)                                                        \
@@ -386,6 +576,8 @@ static int launch_dwconv(const float *x, const float *w, const float *b, const f
 }  // namespace pk
 
 using namespace pk;
+
+PK_WAIT_TIMEOUTS_ACCESSOR(pk_conv_wait_timeouts)
 
 extern "C" int pkcu_glu(const float *in, const float *bias, float *out, int C, int layout,
                         const pkcu_seq *seq, pkcu_stream_t stream) {
@@ -419,7 +611,8 @@ extern "C" int pkcu_dwconv_bn_swish(const float *x, const float *w, const float 
   if (seq->dev.n_items > 65535)
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_dwconv_bn_swish: at most 65535 items per call");
   if (seq->frames == 0) return PKCU_OK;
-  launch_dwconv(x, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, (cudaStream_t)stream);
+  launch_dwconv(x, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, seq->frames,
+                (cudaStream_t)stream);
   return pkcu_launch_status("pkcu_dwconv_bn_swish");
 }
 
@@ -433,8 +626,8 @@ extern "C" int pkcu_glu_dwconv_bn_swish(const float *pw1, const float *pw1_bias,
   if (seq->dev.n_items > 65535)
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_glu_dwconv_bn_swish: at most 65535 items per call");
   if (seq->frames == 0) return PKCU_OK;
-  launch_dwconv(pw1, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, (cudaStream_t)stream, 1,
-                pw1_bias);
+  launch_dwconv(pw1, w, b, bn, bn_eps, apply_swish, out, C, K, seq->dev, seq->frames,
+                (cudaStream_t)stream, 1, pw1_bias);
   return pkcu_launch_status("pkcu_glu_dwconv_bn_swish");
 }
 
@@ -445,6 +638,6 @@ extern "C" int pkcu_depthwise_conv1d(const float *x, const float *w, const float
                      DW_MAX_K);
   if (C == 0 || T == 0) return PKCU_OK;
   pkcu_seq_dev sd = {1, T, T, nullptr, nullptr, nullptr, nullptr, nullptr};
-  launch_dwconv(x, w, b, nullptr, 0.0f, 0, out, C, K, sd, (cudaStream_t)stream);
+  launch_dwconv(x, w, b, nullptr, 0.0f, 0, out, C, K, sd, T, (cudaStream_t)stream);
   return pkcu_launch_status("pkcu_depthwise_conv1d");
 }

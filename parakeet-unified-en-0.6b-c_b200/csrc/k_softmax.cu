@@ -215,112 +215,289 @@ relpos_scores_cta_kernel(const float *ac, const float *__restrict__ bd, float *S
 }
 
 // ── pipelined score rows ─────────────────────────────────────────────────────
-// Persistent warps walk the flat list of score rows of every item. Each warp
-// double-buffers in shared memory: while it computes row n (registers), the
-// async copies of row n+1's ac row and bd band are in flight, so the HBM
-// stream never waits on the softmax arithmetic. Rows of up to 32*NPL entries.
-constexpr int PIPE_WARPS = 8;
+// Persistent warps, each owning a contiguous range of score rows (all items'
+// rows in flat order), ROWS rows at a time: lane group g = lane / LPR
+// (LPR = 32 / ROWS lanes) computes row r + g, so the per-row bookkeeping, the
+// copy issue and the reductions of ROWS rows share their instructions. Each
+// warp keeps a ring of NBUF buffers in shared memory: while it computes one
+// group of rows, the bulk copies of the next NBUF - 1 groups' ac rows and bd
+// bands (issued by the group leaders, completion on each buffer's mbarrier)
+// are in flight.
+//
+// S and ac have the same layout, so a score row starts at the same offset mod
+// 4 floats (off) in both. The entries are processed in the 4-float chunks of
+// that alignment: chunk q holds row entries j = 4q + e - off (e = 0..3). The
+// main loop takes the chunks that lie wholly inside [0, len8) -- lane li of
+// the group owns chunks q_lo + li + LPR k -- with one 16-byte shared load of
+// ac and one 16-byte store of S each and the arithmetic as packed pairs. The
+// leftover entries (at most 3 before the first such chunk and 10 after the
+// last: the row's unaligned head, and its tail including the len % 8 entries
+// that take libm expf) are taken one per lane in a separate step, so no lane
+// runs an edge path inside the main loop. The bd band has an alignment of
+// its own: it is staged 0 or 4 floats further in, so that the band entries
+// of chunk q start `shift` (0..3) floats into chunk slot q and are cut out of
+// slots q and q + 1.
+constexpr int PIPE_WARPS = 2;   // warps per CTA
+constexpr int NBUF = 4;         // ring slots per warp (3 row groups in flight)
 
 struct RowLoc {
   long long ac, bd;   // first element of the ac row / of the used bd band
-  int T, valid;
+  int T, i, valid;
 };
 
-// Row indices fit in 32 bits (the launcher checks H * frames < 2^31), so the
-// decomposition row -> (item, head-row r, query i) uses 32-bit unsigned
-// division; only the element offsets are 64-bit.
+// Ragged batches: rows of item b are [H*frame_off[b], H*frame_off[b+1]).
 __device__ __forceinline__ RowLoc locate_row(const SeqDev &seq, unsigned row, unsigned total_rows) {
   RowLoc o;
   o.valid = row < total_rows;
-  if (!o.valid) { o.ac = o.bd = 0; o.T = 0; return o; }
-  int item;
-  unsigned r;
-  if (seq.uniform_T > 0) {
-    const unsigned per = (unsigned)(PK_H * seq.uniform_T);
-    item = (int)(row / per);
-    r = row - (unsigned)item * per;
-  } else {   // rows of item b: [H*frame_off[b], H*frame_off[b+1])
-    int lo = 0, hi = seq.n_items;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if ((unsigned)(PK_H * __ldg(seq.frame_off + mid)) <= row) lo = mid; else hi = mid;
-    }
-    item = lo;
-    r = row - (unsigned)(PK_H * __ldg(seq.frame_off + lo));
+  if (!o.valid) { o.ac = o.bd = 0; o.T = 1; o.i = 0; return o; }
+  int lo = 0, hi = seq.n_items;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if ((unsigned)(PK_H * __ldg(seq.frame_off + mid)) <= row) lo = mid; else hi = mid;
   }
-  const int T = seq_T(seq, item);
-  const int i = (int)(r % (unsigned)T);
-  o.ac = seq_score_off(seq, item) + (long long)r * T;
-  o.bd = seq_bd_off(seq, item) + (long long)r * (2 * T - 1) + (T - 1 - i);
+  const unsigned r = row - (unsigned)(PK_H * __ldg(seq.frame_off + lo));
+  const int T = seq_T(seq, lo);
+  o.i = (int)(r % (unsigned)T);
+  o.ac = seq_score_off(seq, lo) + (long long)r * T;
+  o.bd = seq_bd_off(seq, lo) + (long long)r * (2 * T - 1) + (T - 1 - o.i);
   o.T = T;
   return o;
 }
 
-template <int NPL, bool SOFTMAX>
+// Uniform batches: row n of the flat list has ac = n T and
+// bd = n (2T - 1) + T - 1 - i = 2 ac - n + T - 1 - i with i = n mod T.
+__device__ __forceinline__ RowLoc uniform_row(unsigned row, unsigned total_rows, int T, int i) {
+  RowLoc o;
+  o.valid = row < total_rows;
+  o.T = T;
+  o.i = i;
+  o.ac = (long long)row * T;
+  o.bd = 2 * o.ac - row + (T - 1 - i);
+  return o;
+}
+
+// Lane li == 0 of each group posts its row's copies into (ac buffer, bd
+// buffer) on mbarrier bar (one arrival per group); lanes of the group copy the
+// row's tail floats. Returns off | shift << 8.
+__device__ __forceinline__ int issue_row(float *abuf, float *bbuf, const RowLoc &loc,
+                                         const float *ac, const float *bd, long long ac_total,
+                                         long long bd_total, unsigned long long *bar, int li) {
+  if (!loc.valid) {
+    if (li == 0) mbar_arrive_tx(bar, 0);
+    return 0;
+  }
+  const Span sa = span_of(loc.ac, loc.T, ac_total);
+  const Span sb = span_of(loc.bd, loc.T, bd_total);
+  const int d = sb.off - sa.off;   // -3 .. 3
+  const int pad = d < 0 ? 4 : 0;
+  if (li == 0) mbar_arrive_tx(bar, sa.bytes + sb.bytes);
+  span_issue(abuf, ac, sa, bar, li);
+  span_issue(bbuf + pad, bd, sb, bar, li);
+  return sa.off | ((d + pad) << 8);
+}
+
+// v[k] = (ac + bd) * scale for the chunks q0 + LPR k, the band cut at shift SH.
+template <int SH, int NCH, int LPR>
+__device__ __forceinline__ void combine_chunks(float4 (&v)[NCH], const float *sa, const float *sbd,
+                                               int q0, float scale) {
+#pragma unroll
+  for (int k = 0; k < NCH; k++) {
+    const int q = q0 + LPR * k;
+    const float4 a = ld4(sa + 4 * q);
+    const float4 lo = ld4(sbd + 4 * q);
+    float4 b = lo;
+    if (SH != 0) {
+      const float4 hi = ld4(sbd + 4 * q + 4);
+      if (SH == 1) b = make_float4(lo.y, lo.z, lo.w, hi.x);
+      if (SH == 2) b = make_float4(lo.z, lo.w, hi.x, hi.y);
+      if (SH == 3) b = make_float4(lo.w, hi.x, hi.y, hi.z);
+    }
+    const float2 c01 = mul2(add2(make_float2(a.x, a.y), make_float2(b.x, b.y)), splat2(scale));
+    const float2 c23 = mul2(add2(make_float2(a.z, a.w), make_float2(b.z, b.w)), splat2(scale));
+    v[k] = make_float4(c01.x, c01.y, c23.x, c23.y);
+  }
+}
+
+__device__ __forceinline__ float max4(float4 v) {
+  return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+}
+
+template <int LPR>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(PK_FULL_MASK, v, o));
+  return v;
+}
+template <int LPR>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(PK_FULL_MASK, v, o);
+  return v;
+}
+
+// 1/s as the IEEE quotient: the fast reciprocal is exact on [1, 2^126), where
+// every softmax sum lies unless the row holds +-inf or NaN.
+__device__ __forceinline__ float recip_sum(float s) {
+  return (s >= 1.0f && s < 0x1p126f) ? rcp_1_2e126(s) : __frcp_rn(s);
+}
+
+// A ring slot's row: ac offset, length and off | shift << 8 | valid << 16.
+struct SlotRow {
+  long long ac;
+  int T, pk;
+};
+
+// Computes one group's rows from ring slot `slot` (see the kernel).
+template <int NCH, int ROWS, bool SOFTMAX>
+__device__ __forceinline__ void score_rows(const float *sa, const SlotRow &cur, float *S,
+                                           float scale, int li);
+
+// Shared memory per warp: NBUF buffers x ROWS rows x (ac, bd) x stg floats.
+template <int NCH, int ROWS, bool SOFTMAX>
 __global__ void __launch_bounds__(32 * PIPE_WARPS)
 relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *S, float scale,
                           SeqDev seq, unsigned total_rows, long long ac_total, long long bd_total,
-                          int stage) {
+                          unsigned rows_per_warp) {
+  constexpr int LPR = 32 / ROWS;
+  constexpr int STG = 4 * LPR * NCH + 8;   // floats per staged ac row or bd band
   extern __shared__ float4 pipe_smem4[];
+  __shared__ unsigned long long bars[PIPE_WARPS][NBUF];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // per warp: [buf0 ac | buf0 bd | buf1 ac | buf1 bd], `stage` floats each
-  float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * 4 * stage;
-  const unsigned nw = gridDim.x * PIPE_WARPS;
-  unsigned row = blockIdx.x * PIPE_WARPS + warp;
-  RowLoc cur = locate_row(seq, row, total_rows);
-  int off_ac = 0, off_bd = 0;
-  if (cur.valid) {
-    off_ac = cp_async_span(wb, ac, cur.ac, cur.T, ac_total, lane);
-    off_bd = cp_async_span(wb + stage, bd, cur.bd, cur.T, bd_total, lane);
-  }
-  cp_async_commit();
-  int buf = 0;
-  for (; cur.valid; row += nw) {
-    // prefetch the next row into the other buffer
-    const RowLoc nxt = locate_row(seq, row + nw, total_rows);
-    int noff_ac = 0, noff_bd = 0;
-    float *nb = wb + (buf ^ 1) * 2 * stage;
-    if (nxt.valid) {
-      noff_ac = cp_async_span(nb, ac, nxt.ac, nxt.T, ac_total, lane);
-      noff_bd = cp_async_span(nb + stage, bd, nxt.bd, nxt.T, bd_total, lane);
-    }
-    cp_async_commit();
-    cp_async_wait<1>();   // this lane's copies of the current row have landed
-    __syncwarp();         // ... and every other lane's
-    const float *sa = wb + buf * 2 * stage + off_ac;
-    const float *sb = wb + buf * 2 * stage + stage + off_bd;
-    const int len = cur.T;
-    float v[NPL];
+  const int g = lane / LPR, li = lane % LPR;
+  // buffer b, row g: ac at wb + ((b * ROWS + g) * 2) * STG, bd STG floats later
+  float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * NBUF * ROWS * 2 * STG;
+  unsigned long long *bar = bars[warp];
+  if (lane == 0) {
 #pragma unroll
-    for (int k = 0; k < NPL; k += 2) {
-      const int j0 = lane + 32 * k, j1 = j0 + 32;
-      if (32 * k + 63 < len) {   // warp-uniform: both slots inside the row
-        const float2 c = mul2(add2(make_float2(sa[j0], sa[j1]), make_float2(sb[j0], sb[j1])),
-                              splat2(scale));   // (ac + bd) * scale, each rounded
-        v[k] = c.x;
-        v[k + 1] = c.y;
-        continue;
+    for (int b = 0; b < NBUF; b++) mbar_init(bar + b, ROWS);
+    mbar_init_fence();
+  }
+  __syncwarp();
+  const unsigned wid = blockIdx.x * PIPE_WARPS + warp;
+  const unsigned long long first = (unsigned long long)wid * rows_per_warp;
+  if (first >= total_rows) return;
+  const unsigned r_end = (unsigned)min((unsigned long long)total_rows, first + rows_per_warp);
+  const bool uniform = seq.uniform_T > 0;
+  const int uT = uniform ? seq.uniform_T : 1;
+  // ring: slot n % NBUF holds group n; groups 0 .. NBUF-2 are issued up
+  // front, group n + NBUF - 1 while group n is computed. The loop is unrolled
+  // over the slots so that each slot's row record stays in registers.
+  SlotRow slot[NBUF];
+  unsigned irow = (unsigned)first + g;   // this group's row of the next group to issue
+  int iu = uniform ? (int)(irow % (unsigned)uT) : 0;
+  auto issue = [&](int b) -> SlotRow {
+    const RowLoc loc = uniform ? uniform_row(irow, r_end, uT, iu) : locate_row(seq, irow, r_end);
+    float *p = wb + ((b * ROWS + g) * 2) * STG;
+    const int pk = issue_row(p, p + STG, loc, ac, bd, ac_total, bd_total, bar + b, li);
+    irow += ROWS;
+    if (uniform) {
+      iu += ROWS;
+      while (iu >= uT) iu -= uT;
+    }
+    SlotRow r;
+    r.ac = loc.ac;
+    r.T = loc.T;
+    r.pk = pk | (loc.valid ? 1 << 16 : 0);
+    return r;
+  };
+#pragma unroll
+  for (int b = 0; b < NBUF - 1; b++) slot[b] = issue(b);
+  unsigned parity = 0;   // bit b: phase parity of buffer b's next completion
+  unsigned base = (unsigned)first;
+  while (true) {
+#pragma unroll
+    for (int b = 0; b < NBUF; b++) {   // compile-time slot b computes group n
+      if (base >= r_end) return;       // nothing in flight: later groups are past the range
+      slot[(b + NBUF - 1) % NBUF] = issue((b + NBUF - 1) % NBUF);   // the slot freed last
+      const bool ok = mbar_wait(bar + b, (parity >> b) & 1);
+      if (__any_sync(PK_FULL_MASK, !ok)) {   // a copy never landed: give up this warp
+        if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+#pragma unroll
+        for (int o = 0; o < NBUF; o++)
+          if (o != b) mbar_wait(bar + o, (parity >> o) & 1);
+        return;
       }
-      const float2 a = make_float2(j0 < len ? sa[j0] : 0.0f, j1 < len ? sa[j1] : 0.0f);
-      const float2 b = make_float2(j0 < len ? sb[j0] : 0.0f, j1 < len ? sb[j1] : 0.0f);
-      const float2 c = mul2(add2(a, b), splat2(scale));
-      v[k] = j0 < len ? c.x : 0.0f;
-      v[k + 1] = j1 < len ? c.y : 0.0f;
+      parity ^= 1u << b;
+      __syncwarp();   // tail floats copied by other lanes are visible
+      score_rows<NCH, ROWS, SOFTMAX>(wb + ((b * ROWS + g) * 2) * STG, slot[b], S, scale, li);
+      __syncwarp();   // every lane is done with this buffer before it is refilled
+      base += ROWS;
     }
-    if (SOFTMAX) softmax_regs<NPL>(v, len, lane);
-    float *dst = S + cur.ac;
-#pragma unroll
-    for (int k = 0; k < NPL; k++) {
-      const int j = lane + 32 * k;
-      if (32 * k + 31 < len || j < len) dst[j] = v[k];
-    }
-    __syncwarp();         // the buffer is refilled two rows from now
-    cur = nxt;
-    off_ac = noff_ac;
-    off_bd = noff_bd;
-    buf ^= 1;
   }
-  cp_async_wait<0>();
+}
+
+template <int NCH, int ROWS, bool SOFTMAX>
+__device__ __forceinline__ void score_rows(const float *sa, const SlotRow &cur, float *S,
+                                           float scale, int li) {
+  constexpr int LPR = 32 / ROWS;
+  constexpr int STG = 4 * LPR * NCH + 8;
+  const bool valid = (cur.pk >> 16) & 1;
+  {   // every lane runs the group reductions; stores only for a valid row
+      const float *sbd = sa + STG;
+      const int T = cur.T, off = cur.pk & 0xff, sh = (cur.pk >> 8) & 0xff;
+      const int len8 = T & ~7;
+      const int q_lo = off > 0 ? 1 : 0;
+      const int q_hi = (len8 + off) >> 2;   // chunks [q_lo, q_hi) lie inside [0, len8)
+      const int n_head = off > 0 ? min(4 - off, T) : 0;
+      const int tail0 = q_hi > q_lo ? 4 * q_hi - off : n_head;
+      const int n_left = n_head + (T - tail0);
+      // leftover entry of this lane (li < n_left)
+      const int jl = li < n_head ? li : tail0 + (li - n_head);
+      const bool has_left = li < n_left;
+      float vl = 0.0f;
+      if (has_left) vl = (sa[off + jl] + sbd[off + sh + jl]) * scale;
+      const int q0 = q_lo + li;
+      float4 v[NCH];
+      switch (sh) {
+        case 0: combine_chunks<0, NCH, LPR>(v, sa, sbd, q0, scale); break;
+        case 1: combine_chunks<1, NCH, LPR>(v, sa, sbd, q0, scale); break;
+        case 2: combine_chunks<2, NCH, LPR>(v, sa, sbd, q0, scale); break;
+        default: combine_chunks<3, NCH, LPR>(v, sa, sbd, q0, scale); break;
+      }
+      float el = vl;   // the leftover entry's output
+      if (SOFTMAX) {
+        float mx = has_left ? vl : -INFINITY;
+#pragma unroll
+        for (int k = 0; k < NCH; k++)
+          if (q0 + LPR * k < q_hi) mx = fmaxf(mx, max4(v[k]));
+        mx = group_max<LPR>(mx);
+        float2 s2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < NCH; k++) {   // polynomial exp (every main entry is below len8)
+          float2 d01 = sub2(make_float2(v[k].x, v[k].y), splat2(mx));
+          float2 d23 = sub2(make_float2(v[k].z, v[k].w), splat2(mx));
+          d01.x = fmaxf(d01.x, -87.0f);   // arguments are <= 0 or NaN
+          d01.y = fmaxf(d01.y, -87.0f);
+          d23.x = fmaxf(d23.x, -87.0f);
+          d23.y = fmaxf(d23.y, -87.0f);
+          const float2 e01 = exp_poly2_clamped(d01), e23 = exp_poly2_clamped(d23);
+          if (q0 + LPR * k < q_hi) s2 = add2(s2, add2(e01, e23));
+          v[k] = make_float4(e01.x, e01.y, e23.x, e23.y);
+        }
+        // leftovers: polynomial below len8, libm expf on the len % 8 tail
+        el = 0.0f;
+        if (has_left) {
+          const float d = vl - mx;
+          el = jl < len8 ? exp_poly_nonpos(d) : expf(d);
+        }
+        const float inv = recip_sum(group_sum<LPR>(s2.x + s2.y + el));
+        const float2 inv2 = splat2(inv);
+#pragma unroll
+        for (int k = 0; k < NCH; k++) {
+          const float2 o01 = mul2(make_float2(v[k].x, v[k].y), inv2);
+          const float2 o23 = mul2(make_float2(v[k].z, v[k].w), inv2);
+          v[k] = make_float4(o01.x, o01.y, o23.x, o23.y);
+        }
+        el = el * inv;
+      }
+      if (valid) {
+        float *dst = S + cur.ac - off;   // 16-byte aligned
+#pragma unroll
+        for (int k = 0; k < NCH; k++)
+          if (q0 + LPR * k < q_hi) st4(dst + 4 * (q0 + LPR * k), v[k]);
+        if (has_left) S[cur.ac + jl] = el;
+      }
+  }
 }
 
 // relative_shift alone: out[h,i,j] = bd[h,i,T-1-i+j] (exact gather).
@@ -348,23 +525,28 @@ static void launch_scores_warp(const float *ac, const float *bd, float *S, float
                                                                               seq->dev);
 }
 
-template <int NPL, bool SOFTMAX>
+template <int NCH, int ROWS, bool SOFTMAX>
 static void launch_scores_pipe(const float *ac, const float *bd, float *S, float scale,
                                const pkcu_seq *seq, cudaStream_t s) {
-  const int stage = ((seq->dev.max_T + 8 + 3) / 4) * 4;
-  const size_t smem = sizeof(float) * 4 * (size_t)stage * PIPE_WARPS;
+  constexpr int STG = 4 * (32 / ROWS) * NCH + 8;
+  const size_t smem = sizeof(float) * NBUF * ROWS * 2 * (size_t)STG * PIPE_WARPS;
   static int flags[64];
-  smem_optin(relpos_scores_pipe_kernel<NPL, SOFTMAX>, smem, flags);
+  smem_optin(relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX>, smem, flags);
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, relpos_scores_pipe_kernel<NPL, SOFTMAX>,
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX>,
                                                 32 * PIPE_WARPS, smem);
   if (per_sm < 1) per_sm = 1;
   const long long rows = (long long)PK_H * seq->frames;
-  long long grid = (rows + PIPE_WARPS - 1) / PIPE_WARPS;
+  long long grid = (rows + PIPE_WARPS * ROWS - 1) / (PIPE_WARPS * ROWS);
   const long long cap = (long long)pkcu_sm_count() * per_sm;
   if (grid > cap) grid = cap;
-  relpos_scores_pipe_kernel<NPL, SOFTMAX><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
-      ac, bd, S, scale, seq->dev, (unsigned)rows, seq->score_elems, seq->bd_elems, stage);
+  // contiguous row ranges, a multiple of ROWS rows per warp
+  const long long warps = grid * PIPE_WARPS;
+  long long per_warp = (rows + warps - 1) / warps;
+  per_warp = (per_warp + ROWS - 1) / ROWS * ROWS;
+  relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
+      ac, bd, S, scale, seq->dev, (unsigned)rows, seq->score_elems, seq->bd_elems,
+      (unsigned)per_warp);
 }
 
 // The pipelined kernel indexes rows in 32 bits (and nw + row must not wrap).
@@ -377,11 +559,18 @@ static int launch_scores(const float *ac, const float *bd, float *S, float scale
                          const pkcu_seq *seq, cudaStream_t s) {
   const int T = seq->dev.max_T;
   const int npl = (T + 31) / 32;
-  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && npl <= 16 && pipe_rows_fit(seq)) {
-    if (npl <= 4) launch_scores_pipe<4, SOFTMAX>(ac, bd, S, scale, seq, s);
-    else if (npl <= 8) launch_scores_pipe<8, SOFTMAX>(ac, bd, S, scale, seq, s);
-    else if (npl <= 12) launch_scores_pipe<12, SOFTMAX>(ac, bd, S, scale, seq, s);
-    else launch_scores_pipe<16, SOFTMAX>(ac, bd, S, scale, seq, s);
+  // chunks per lane: a row of T entries at offset off <= 3 spans (T + 6) / 4
+  // chunks; two rows per warp (16 lanes each) up to 8 chunks per lane, one
+  // row per warp above that
+  const int nq = (T + 6) / 4;
+  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && PK_ALIGNED16(S) && nq <= 32 * 8 && pipe_rows_fit(seq)) {
+    if (nq <= 16 * 1) launch_scores_pipe<1, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 16 * 2) launch_scores_pipe<2, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 16 * 4) launch_scores_pipe<4, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 16 * 6) launch_scores_pipe<6, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 16 * 8) launch_scores_pipe<8, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 32 * 6) launch_scores_pipe<6, 1, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else launch_scores_pipe<8, 1, SOFTMAX>(ac, bd, S, scale, seq, s);
     return PKCU_OK;
   }
   if (npl <= 4) launch_scores_warp<4, SOFTMAX>(ac, bd, S, scale, seq, s);
@@ -421,6 +610,8 @@ static int check_scores(const float *ac, const float *bd, const float *S, const 
 }  // namespace pk
 
 using namespace pk;
+
+PK_WAIT_TIMEOUTS_ACCESSOR(pk_softmax_wait_timeouts)
 
 extern "C" int pkcu_softmax_rows(float *x, int n_rows, int len, pkcu_stream_t stream) {
   if (!x || n_rows < 0 || len <= 0) return pkcu_fail(PKCU_ERR_ARG, "pkcu_softmax_rows: bad argument");

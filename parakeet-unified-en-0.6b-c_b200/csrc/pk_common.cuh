@@ -282,6 +282,119 @@ __device__ __forceinline__ int cp_async_span(float *dst, const float *src, long 
   return (int)(start - a0);
 }
 
+// ── bulk asynchronous copies (TMA engine) with mbarrier completion ──────────
+// One thread issues cp.async.bulk (no multicast) for a whole 16-byte aligned
+// span; the copy engine signals the bytes it wrote on a shared-memory mbarrier
+// that the consumers wait on. Waits are bounded by the global nanosecond
+// timer: a wait that runs out counts a timeout in the translation unit's
+// g_wait_timeouts (read by the host through pkcu_wait_timeouts()) and the
+// kernel abandons its work instead of spinning forever.
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Makes initialised mbarriers visible to the copy engine.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(unsigned long long *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes,
+                                         unsigned long long *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr unsigned long long PK_WAIT_NS = 1000000000ULL;   // 1 s per wait
+
+// Waits that ran out in this translation unit's kernels since the last reset.
+static __device__ unsigned g_wait_timeouts;
+
+// Host accessor of g_wait_timeouts for one translation unit (current device).
+#define PK_WAIT_TIMEOUTS_ACCESSOR(fn)                                              \
+  extern "C" int fn(unsigned *count, int reset) {                                  \
+    unsigned v = 0;                                                                \
+    if (cudaMemcpyFromSymbol(&v, pk::g_wait_timeouts, sizeof v) != cudaSuccess)    \
+      return PKCU_ERR_CUDA;                                                        \
+    if (reset) {                                                                   \
+      const unsigned zero = 0;                                                     \
+      if (cudaMemcpyToSymbol(pk::g_wait_timeouts, &zero, sizeof zero) != cudaSuccess) \
+        return PKCU_ERR_CUDA;                                                      \
+    }                                                                              \
+    *count = v;                                                                    \
+    return PKCU_OK;                                                                \
+  }
+
+// Waits until phase `parity` of bar has completed, at most `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(unsigned long long *bar, unsigned parity,
+                                          unsigned long long limit_ns = PK_WAIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
+// Geometry of one row of n floats starting at element `start` of a 16-byte
+// aligned array of `total` floats, copied as its 16-byte aligned superset:
+// dst[k] = src[a0 + k] for k < bytes / 4 (bulk), then the n_tail floats that
+// a 16-byte chunk would have read past the array's end as plain loads, at
+// dst[bytes / 4 ...]. off = start - a0 is the row's offset in dst.
+struct Span {
+  long long a0;
+  unsigned bytes;
+  int n_tail, off;
+};
+__device__ __forceinline__ Span span_of(long long start, int n, long long total) {
+  Span s;
+  s.a0 = start & ~3LL;
+  long long a1 = (start + n + 3) & ~3LL;
+  const long long lim = total & ~3LL;
+  if (a1 > lim) a1 = lim > s.a0 ? lim : s.a0;
+  s.bytes = (unsigned)(a1 - s.a0) * 4u;
+  const long long tail = start + n - a1;
+  s.n_tail = tail > 0 ? (int)tail : 0;
+  s.off = (int)(start - s.a0);
+  return s;
+}
+// Asks the copy engine to bring a span into L2 (no completion to wait for).
+__device__ __forceinline__ void prefetch_l2(const float *src, const Span &s) {
+  if (s.bytes)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + s.a0), "r"(s.bytes)
+                 : "memory");
+}
+
+// Lane 0 issues the bulk copy of a span (its bytes are part of an
+// expect-tx already posted on bar); lanes < n_tail copy the tail floats.
+__device__ __forceinline__ void span_issue(float *dst, const float *src, const Span &s,
+                                           unsigned long long *bar, int lane) {
+  if (lane == 0 && s.bytes) bulk_g2s(dst, src + s.a0, s.bytes, bar);
+  if (lane < s.n_tail) dst[s.bytes / 4 + lane] = src[s.a0 + s.bytes / 4 + lane];
+}
+
 // Raises a kernel's dynamic shared-memory limit once per device (the first
 // launch on each device; later launches, including ones under stream
 // capture, make no attribute call). `flags` is a per-kernel static array.

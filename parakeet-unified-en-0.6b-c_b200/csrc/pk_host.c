@@ -62,6 +62,16 @@ int pkcu_device(void)
     return dev;
 }
 
+int pkcu_wait_timeouts(unsigned *count, int reset)
+{
+    if (!count) return pkcu_fail(PKCU_ERR_ARG, "pkcu_wait_timeouts: NULL count");
+    unsigned a = 0, b = 0;
+    if (pk_softmax_wait_timeouts(&a, reset) != PKCU_OK || pk_conv_wait_timeouts(&b, reset) != PKCU_OK)
+        return pkcu_fail(PKCU_ERR_CUDA, "pkcu_wait_timeouts: reading the device counters failed");
+    *count = a + b;
+    return PKCU_OK;
+}
+
 int pkcu_sm_count(void)
 {
     int dev = 0;

@@ -48,6 +48,10 @@ int pkcu_launch_status(const char *what);
 int pkcu_sm_count(void);
 /* Current device index, or 0. */
 int pkcu_device(void);
+/* Per-translation-unit counters of device waits that ran out (k_softmax.cu,
+ * k_conv.cu); read and optionally reset on the current device. */
+int pk_softmax_wait_timeouts(unsigned *count, int reset);
+int pk_conv_wait_timeouts(unsigned *count, int reset);
 
 #define PK_ALIGNED16(p) ((((uintptr_t)(p)) & 15u) == 0)
 

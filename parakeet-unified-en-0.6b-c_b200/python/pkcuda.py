@@ -24,6 +24,7 @@ PKCU_ACT_RELU, PKCU_ACT_TANH = 0, 1
 # Symbols declared by include/pkcuda.h (checked by the CPU test suite).
 EXPORTED = (
     "pkcu_status_string", "pkcu_last_error", "pkcu_version", "pkcu_selftest",
+    "pkcu_wait_timeouts", "pkcu_selftest_wait",
     "pkcu_seq_create", "pkcu_seq_destroy", "pkcu_seq_n_items", "pkcu_seq_frames",
     "pkcu_seq_score_elems", "pkcu_seq_bd_elems", "pkcu_seq_pos_rows",
     "pk_layer_norm", "pk_layer_norm_rows", "pk_layer_norm_rows_inplace", "pk_swish", "pk_relu",
@@ -56,6 +57,8 @@ _SIGS = {
     "pkcu_last_error": (C.c_char_p, []),
     "pkcu_version": (C.c_char_p, []),
     "pkcu_selftest": (I, [C.POINTER(C.c_ulonglong)]),
+    "pkcu_wait_timeouts": (I, [C.POINTER(C.c_uint), I]),
+    "pkcu_selftest_wait": (I, [C.POINTER(C.c_int)]),
     "pkcu_seq_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
     "pkcu_seq_destroy": (None, [VP]),
     "pkcu_seq_n_items": (I, [VP]),

@@ -103,6 +103,19 @@ def _release_device_arrays():
         pass
 
 
+@pytest.fixture(autouse=True)
+def _no_wait_timeouts(request):
+    """After every GPU test: no bounded device wait (bulk-copy kernels) ran out."""
+    yield
+    if request.node.get_closest_marker("gpu") is None or "cuda" not in request.fixturenames:
+        return
+    import ctypes as C
+    import pkcuda
+    n = C.c_uint(0)
+    pkcuda.call("pkcu_wait_timeouts", C.byref(n), 1)
+    assert n.value == 0, f"{n.value} device wait(s) ran out"
+
+
 @pytest.fixture(scope="session")
 def cuda():
     """The CUDA library and torch on cuda:0 (gpu tests only)."""

@@ -133,6 +133,25 @@ def test_encoder_nongemm_vs_reference_block(cuda, reference):
         assert_close(item_view(L, role, got[role], 0), caps[role], role)
 
 
+def test_chunked_long_audio_24_blocks(cuda, oracle):
+    """3200 frames in 8 chunks of 400 + 8-frame overlaps, the
+    edge chunks 408 frames and the interior ones 416 (csrc/encoder.c:531-543),
+    as one ragged batch through all 24 blocks; every chunk against the
+    restatement run chunk by chunk, block by block."""
+    lengths = [408] + [416] * 6 + [408]
+    blocks, items = make_batch(lengths, 24, seed=3200)
+    L, gx, got = run_gpu(cuda, lengths, blocks, items)
+    for i, (si, x) in enumerate(items):
+        for p in blocks:
+            x, caps = oracle.conformer_block(x, p, si)
+        # 24 renormalised blocks: per-op rounding differences compound slightly
+        assert_close(L.frames_of(gx, i), x, f"x chunk {i}", atol=2e-5, rtol=1e-4)
+        for role in ("S", "dw", "h2", "ln_ff2"):
+            assert_close(item_view(L, role, got[role], i), caps[role], f"{role} chunk {i}",
+                         atol=2e-5, rtol=1e-4)
+    assert np.isfinite(gx).all()
+
+
 def test_encoder_nongemm_24_blocks_stays_bounded(cuda, oracle):
     """24 blocks (the model depth): residual stream within tolerance of the
     restatement after every LN_out renormalisation."""

@@ -27,6 +27,19 @@ def test_selftest_reciprocal(cuda):
     assert bad.value == 0
 
 
+def test_selftest_wait_bound(cuda, oracle):
+    """A bounded device wait on a copy that never comes gives up after 20 ms,
+    reports it, and the context stays usable."""
+    import ctypes as C
+    t = C.c_int(-1)
+    cuda.call("pkcu_selftest_wait", C.byref(t))
+    assert t.value == 1
+    x = rng(5).standard_normal(4096).astype(np.float32)
+    g = dev(x)
+    cuda.call("pkcu_swish", g.data_ptr(), x.size, cuda.stream_handle())
+    assert_bitexact(host(g), oracle.swish(x), "swish after the timed-out wait")
+
+
 def test_swish_dense_sweep(cuda, oracle):
     """Swish body bit-exact against the restatement on a dense sweep of
     [-100, 100] (every 509th float of that range)."""
@@ -163,7 +176,8 @@ def test_softmax_rows(cuda, oracle, R, n):
     assert_close(host(xd), oracle.softmax_rows(x), f"softmax {R}x{n}")
 
 
-@pytest.mark.parametrize("lengths", RAGGED + [[1100, 33], [600, 7], [512, 1]])
+@pytest.mark.parametrize("lengths", RAGGED + [[1100, 33], [600, 7], [512, 1], [1000, 12, 13, 15],
+                                     [129, 130, 131, 126]])
 def test_relpos_scores(cuda, oracle, lengths):
     r = rng(11 + sum(lengths))
     L = Layout(lengths)
@@ -309,16 +323,22 @@ def test_glu(cuda, oracle, lengths):
         assert_close(host(out), oracle.glu_time_first(tf), "glu time-first")
 
 
-@pytest.mark.parametrize("C,T,K,bias", [(1024, 375, 9, True), (16, 1, 9, True), (16, 2, 9, False),
-                                        (8, 5, 3, True), (32, 129, 9, True), (4, 300, 31, True),
-                                        (6, 40, 1, True), (1024, 32, 9, True)])
-def test_depthwise_conv1d(cuda, oracle, C, T, K, bias):
+@pytest.mark.parametrize("C,T,K,bias,offset", [
+    (1024, 375, 9, True, 0), (16, 1, 9, True, 0), (16, 2, 9, False, 0), (8, 5, 3, True, 0),
+    (32, 129, 9, True, 0), (4, 300, 31, True, 0), (6, 40, 1, True, 0), (1024, 32, 9, True, 0),
+    (8, 7, 9, True, 0), (8, 11, 9, True, 0), (8, 15, 9, True, 0), (8, 16, 9, True, 0),
+    (64, 375, 9, True, 1), (24, 642, 9, True, 0), (24, 645, 9, True, 0), (24, 646, 9, True, 0),
+    (16, 900, 9, True, 0)])
+def test_depthwise_conv1d(cuda, oracle, C, T, K, bias, offset):
+    """offset != 0 misaligns x (the bulk-copy path needs 16-byte aligned rows); T = 646 and
+    900 exceed the shared-memory row and take the chunked path."""
     r = rng(C * T + K)
     x = r.standard_normal((C, T)).astype(np.float32)
     w = (0.3 * r.standard_normal((C, K))).astype(np.float32)
     b = (0.1 * r.standard_normal(C)).astype(np.float32) if bias else None
+    buf = dev(np.concatenate([np.zeros(offset, np.float32), x.reshape(-1)]))
     out = empty((C, T))
-    cuda.call("pkcu_depthwise_conv1d", dev(x).data_ptr(), dev(w).data_ptr(),
+    cuda.call("pkcu_depthwise_conv1d", buf[offset:].data_ptr(), dev(w).data_ptr(),
               dev(b).data_ptr() if bias else None, out.data_ptr(), C, T, K, cuda.stream_handle())
     assert_bitexact(host(out), oracle.depthwise_conv1d(x, w, b), "dwconv")
 
