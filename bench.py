@@ -54,6 +54,11 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-aux", action="store_true", help="skip the standalone-kernel table")
+    ap.add_argument("--aux-only", action="store_true",
+                    help="time only the standalone kernels (one JSON object), e.g. for ncu")
+    ap.add_argument("--aux-reps", type=int, default=5,
+                    help="timed launches per standalone kernel (0: one untimed launch each)")
     return ap.parse_args()
 
 
@@ -365,6 +370,112 @@ def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
     return table
 
 
+def time_aux_kernels(stream, reps=5):
+    """The tensor_ops entry points that are not part of the encoder block
+    sequence, each timed alone (CUDA events on the bench stream, one warm-up
+    launch) at a size above the 126 MB L2, with algorithmic bytes (each input
+    read once, each output written once): plain LayerNorm [R, 1024]; row softmax over the
+    score rows of 256 utterances (in place); Swish / ReLU (in place); int8
+    dequant of 24 blocks' QKV + out weights; int4 dequant of 24 blocks' FF1 +
+    FF2 weights with the reference's G = 32 scales along N and with G = 128
+    along K; the RNN-T joint add + ReLU / tanh and the greedy argmax at 256
+    utterances x 416 frames (J = 640, V = 1025). A device fill of the int4
+    output size is timed beside them as the write-only reference point."""
+    import torch
+    import pkcuda
+    sh = stream.cuda_stream
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(8)
+    out = {}
+
+    def timed(name, shape, nbytes, fn):
+        fn()
+        torch.cuda.synchronize()
+        if reps == 0:
+            out[name] = {"shape": shape, "ms": None, "bytes": nbytes, "gbs": None}
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        out[name] = {"shape": shape, "ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+    f32 = dict(device=dev, dtype=torch.float32)
+    R, Dm = 96000, D
+    x = torch.randn(R * Dm, generator=g, **f32)
+    gam = 1 + 0.1 * torch.randn(Dm, generator=g, **f32)
+    bet = 0.1 * torch.randn(Dm, generator=g, **f32)
+    y = torch.empty_like(x)
+    timed("layer_norm_rows", [R, Dm], 8 * R * Dm + 8 * Dm,
+          lambda: pkcuda.call("pkcu_layer_norm_rows", x.data_ptr(), gam.data_ptr(), bet.data_ptr(),
+                              y.data_ptr(), R, Dm, sh))
+    del x, y
+    rows, n = 256 * H * 375, 375
+    sc = 4 * torch.randn(rows * n, generator=g, **f32)
+    timed("softmax_rows", [rows, n], 8 * rows * n,
+          lambda: pkcuda.call("pkcu_softmax_rows", sc.data_ptr(), rows, n, sh))
+    del sc
+    nv = 64 << 20
+    v = 4 * torch.randn(nv, generator=g, **f32)
+    timed("swish", [nv], 8 * nv, lambda: pkcuda.call("pkcu_swish", v.data_ptr(), nv, sh))
+    timed("relu", [nv], 8 * nv, lambda: pkcuda.call("pkcu_relu", v.data_ptr(), nv, sh))
+    del v
+    n8 = 24 * (1024 * 3072 + 1024 * 1024)
+    q8 = torch.randint(-127, 128, (n8,), generator=g, device=dev, dtype=torch.int8)
+    o8 = torch.empty(n8, **f32)
+    timed("dequant_i8", [n8], 5 * n8,
+          lambda: pkcuda.call("pkcu_dequant_i8", q8.data_ptr(), 3e-3, o8.data_ptr(), n8, sh))
+    del q8, o8
+    K4, N4 = 24 * 2 * 1024, 4096     # 24 blocks of FF1 [1024, 4096] + FF2 (same count)
+    p4 = torch.randint(0, 256, (K4 * N4 // 2,), generator=g, device=dev, dtype=torch.uint8)
+    o4 = torch.empty(K4 * N4, **f32)
+    for G, axis, tag in ((32, pkcuda.PKCU_GROUP_ALONG_N, "dequant_i4_g32_n"),
+                         (128, pkcuda.PKCU_GROUP_ALONG_K, "dequant_i4_g128_k")):
+        s4 = 1e-3 + 2e-2 * torch.rand(K4 * N4 // G, generator=g, **f32)
+        timed(tag, [K4, N4], K4 * N4 // 2 + 4 * K4 * N4 // G + 4 * K4 * N4,
+              lambda: pkcuda.call("pkcu_dequant_i4", p4.data_ptr(), s4.data_ptr(), o4.data_ptr(),
+                                  K4, N4, G, axis, sh))
+        del s4
+    # reference point for write-dominated kernels: torch's fill of the same
+    # 805 MB (a library kernel, write-only traffic)
+    timed("fill_reference_write_only", [K4, N4], 4 * K4 * N4, lambda: o4.fill_(1.0))
+    del p4, o4
+    B, T, J, V = 256, 416, 640, 1025
+    enc = torch.randn(B * T * J, generator=g, **f32)
+    pred = torch.randn(B * J, generator=g, **f32)
+    jo = torch.empty_like(enc)
+    for act, tag in ((pkcuda.PKCU_ACT_RELU, "joint_add_relu"), (pkcuda.PKCU_ACT_TANH, "joint_add_tanh")):
+        timed(tag, [B, T, J], 8 * B * T * J + 4 * B * J,
+              lambda: pkcuda.call("pkcu_joint_add_act", enc.data_ptr(), pred.data_ptr(), jo.data_ptr(),
+                                  B, T, J, act, sh))
+    del enc, pred, jo
+    logits = torch.randn(B * T * V, generator=g, **f32)
+    am = torch.empty(B * T, device=dev, dtype=torch.int32)
+    timed("argmax_rows", [B * T, V], 4 * B * T * V + 4 * B * T,
+          lambda: pkcuda.call("pkcu_argmax_rows", logits.data_ptr(), am.data_ptr(), B * T, V, sh))
+    del logits, am
+    torch.cuda.synchronize()
+    return out
+
+
+def aux_only(args, local_rank):
+    import torch
+    import pkcuda
+    torch.cuda.set_device(local_rank)
+    pkcuda.lib()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        aux = time_aux_kernels(stream, reps=args.aux_reps)
+    peak, peak_kind = measured_peak()
+    print(json.dumps({"kernels_aux": {k: {**v, "frac": v["gbs"] / peak if v["gbs"] else None}
+                                      for k, v in aux.items()},
+                      "peak_gbs": peak, "peak_kind": peak_kind}), flush=True)
+
+
 def ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -434,6 +545,9 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
+    aux = None
+    if rank == 0 and not args.no_aux:
+        aux = time_aux_kernels(stream)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = RefRunner(args.T, args.blocks)
@@ -462,6 +576,9 @@ def _ours(args, rank, world, local_rank, stream):
         "kernels": {k: {"ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
                         "frac": round(v["gbs"] / peak, 3), "launches_per_step": v["launches_per_step"]}
                     for k, v in table.items()},
+        "kernels_aux": None if aux is None else {
+            k: {"shape": v["shape"], "ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
+                "frac": round(v["gbs"] / peak, 3)} for k, v in aux.items()},
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,
@@ -525,6 +642,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.aux_only:
+        if rank == 0:
+            aux_only(args, local_rank)
+        return
     if args.impl == "reference":
         if world > 1 and rank != 0:
             return

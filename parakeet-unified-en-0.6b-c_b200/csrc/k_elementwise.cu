@@ -29,13 +29,12 @@ __global__ void __launch_bounds__(EW_THREADS) swish_vec_kernel(float *x, long lo
   const long long n8 = n & ~7LL, n4 = n8 >> 2;
   const long long stride = (long long)gridDim.x * blockDim.x;
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; i + 3 * stride < n4; i += 4 * stride) {
-    float4 a = ld4(x + 4 * i), b = ld4(x + 4 * (i + stride));
-    float4 c = ld4(x + 4 * (i + 2 * stride)), d = ld4(x + 4 * (i + 3 * stride));
-    st4(x + 4 * i, swish4(a));
-    st4(x + 4 * (i + stride), swish4(b));
-    st4(x + 4 * (i + 2 * stride), swish4(c));
-    st4(x + 4 * (i + 3 * stride), swish4(d));
+  for (; i + 7 * stride < n4; i += 8 * stride) {   // 8 float4 loads in flight per thread
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = ld4(x + 4 * (i + j * stride));
+#pragma unroll
+    for (int j = 0; j < 8; j++) st4(x + 4 * (i + j * stride), swish4(v[j]));
   }
   for (; i < n4; i += stride) st4(x + 4 * i, swish4(ld4(x + 4 * i)));
   if (blockIdx.x == 0 && threadIdx.x < n - n8) x[n8 + threadIdx.x] = swish_tail(x[n8 + threadIdx.x]);
@@ -60,6 +59,15 @@ __global__ void __launch_bounds__(EW_THREADS) relu_kernel(float *x, long long n,
   long long done = 0;
   if (vec) {
     const long long n4 = n >> 2;
+    for (; i + 3 * stride < n4; i += 4 * stride) {   // 4 float4 loads in flight per thread
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = ld4(x + 4 * (i + j * stride));
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        st4(x + 4 * (i + j * stride), make_float4(relu1(v[j].x), relu1(v[j].y), relu1(v[j].z),
+                                                  relu1(v[j].w)));
+    }
     for (; i < n4; i += stride) {
       float4 v = ld4(x + 4 * i);
       st4(x + 4 * i, make_float4(relu1(v.x), relu1(v.y), relu1(v.z), relu1(v.w)));

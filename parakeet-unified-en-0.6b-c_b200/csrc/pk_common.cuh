@@ -208,6 +208,28 @@ __device__ __forceinline__ float sigmoid_libm(float b) {
   return d < 0x1p126f ? rcp_1_2e126(d) : __frcp_rn(d);
 }
 
+// ── exact division by a run-time divisor ─────────────────────────────────────
+// n / d for n < 2^32 and 1 <= d < 2^32 as a 64-bit multiply-high with
+// m = floor(2^64 / d) + 1: n*m/2^64 = n/d + err with 0 < err < 2^-32 <= 1/d,
+// and the fractional part of n/d is at most 1 - 1/d, so the floor is exact.
+// m = 0 stands for d = 1. Computed on the host once per launch.
+struct FastDiv {
+  unsigned long long m;
+};
+static inline FastDiv make_fastdiv(unsigned d) {
+  FastDiv f;
+  if (d <= 1) {
+    f.m = 0;
+  } else {
+    const unsigned long long all = ~0ULL;   // 2^64 - 1
+    f.m = all / d + (all % d == d - 1 ? 1 : 0) + 1;   // floor(2^64 / d) + 1
+  }
+  return f;
+}
+__device__ __forceinline__ unsigned fast_div(unsigned n, FastDiv f) {
+  return f.m ? (unsigned)__umul64hi((unsigned long long)n, f.m) : n;
+}
+
 // ── ragged batches ───────────────────────────────────────────────────────────
 //
 // A batch of independent utterances / chunks with per-item frame counts T_b.

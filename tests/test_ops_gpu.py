@@ -400,14 +400,17 @@ def test_glu_dwconv_fused(cuda, oracle, lengths, K, with_bias):
 
 # ── weights ───────────────────────────────────────────────────────────────────
 
-@pytest.mark.parametrize("n,offset", [(1024 * 3072, 0), (1003, 0), (4099, 3)])
-def test_dequant_i8(cuda, oracle, n, offset):
+@pytest.mark.parametrize("n,offset,out_off", [(1024 * 3072, 0, 0), (1003, 0, 0), (4099, 3, 1),
+                                             (4102, 4, 0), (4101, 0, 1), (5, 0, 0)])
+def test_dequant_i8(cuda, oracle, n, offset, out_off):
+    """offset / out_off misalign the int8 input (by bytes) and the output (by
+    floats): the vector path needs 4-byte int8 and 16-byte output alignment."""
     import torch
     r = rng(n)
     q = r.integers(-127, 128, size=n, dtype=np.int8)
     s = float(np.float32(r.uniform(1e-3, 1e-2)))
     buf = dev(np.concatenate([np.zeros(offset, np.int8), q]))
-    out = empty(n + 1)[1:] if offset else empty(n)
+    out = empty(n + out_off)[out_off:]
     cuda.call("pkcu_dequant_i8", buf[offset:].data_ptr(), s, out.data_ptr(), n,
               cuda.stream_handle())
     assert_bitexact(host(out), oracle.dequant_i8(q, s), "int8")
@@ -432,7 +435,9 @@ def test_requant_qkv(cuda, oracle):
 
 @pytest.mark.parametrize("K,N,G,axis", [(1024, 4096, 32, 1), (4096, 1024, 32, 1),
                                         (1024, 4096, 128, 0), (4096, 1024, 128, 0),
-                                        (6, 18, 3, 1), (16, 10, 8, 0)])
+                                        (6, 18, 3, 1), (16, 10, 8, 0), (8, 24, 2, 1),
+                                        (24, 40, 4, 0), (3, 8, 8, 1), (5, 16, 16, 1),
+                                        (128, 72, 8, 1)])
 def test_dequant_i4(cuda, oracle, K, N, G, axis):
     r = rng(K + N + G)
     q = r.integers(-8, 8, size=(K, N)).astype(np.int8)
@@ -476,7 +481,7 @@ def test_joint_add_act(cuda, oracle, B, T, J):
     assert_close(host(out), oracle.joint_add_act(enc, pred, 1), "tanh")
 
 
-@pytest.mark.parametrize("R,V", [(32 * 416, 1025), (7, 1), (5, 33), (3, 4000)])
+@pytest.mark.parametrize("R,V", [(32 * 416, 1025), (7, 1), (5, 33), (3, 4000), (8, 100)])
 def test_argmax_rows(cuda, oracle, R, V):
     import torch
     r = rng(R + V)
@@ -487,6 +492,10 @@ def test_argmax_rows(cuda, oracle, R, V):
         lg[2, V // 2] = np.nan             # NaN elsewhere ignored
         lg[3, :] = -np.inf
         lg[4, V - 1] = lg[4, 1] = 50.0     # tie between 1 and V-1 -> 1
+    if R >= 8 and V >= 70:
+        lg[5, 35] = lg[5, 3] = np.inf      # tie inside one lane's entries (j, j + 32) -> 3
+        lg[6, 2] = lg[6, 66] = 9.0         # same lane, first of the two -> 2
+        lg[7, :] = np.nan                  # all NaN -> 0
     out = empty(R, torch.int32)
     cuda.call("pkcu_argmax_rows", dev(lg).data_ptr(), out.data_ptr(), R, V, cuda.stream_handle())
     assert_bitexact(host(out), oracle.argmax_rows(lg), "argmax")
