@@ -349,7 +349,8 @@ dwconv_row_kernel(const float *__restrict__ x, const float *__restrict__ w,
 // chunk q (entries t = 4q + e - off) at s[4 + 4q + e].
 //
 // The GLU gate runs 4 entries at a time on the chunks wholly inside the row
-// and one entry per lane on the at most 6 entries outside them. The conv runs
+// and one entry per lane on the at most 6 entries outside them (16 lanes per
+// row, two rows per warp). The conv runs
 // 4 outputs at a time on the chunks whose 9-tap windows s[4q .. 4q + 11] lie
 // wholly inside the row -- packed tap chains, packed Swish, one 16-byte store
 // -- and one output per lane, with the out-of-row taps skipped, on the at most
@@ -391,38 +392,48 @@ __device__ __forceinline__ float dwa_finish(float val, float mean, float den, fl
   return val;
 }
 
+// Two channel rows per warp (lane group g = lane / 16 takes row 2w + g), so
+// the copy issue, the parameter loads and the one-output-per-lane edge steps
+// of both rows share their instructions; DWA_WARPS warps = 8 channels per CTA
+// (C % 8 == 0 on this path, so every row of a CTA exists).
+constexpr int DWA_WARPS = 4, DWA_RPW = 2, DWA_LPR = 32 / DWA_RPW;
+constexpr int DWA_CH = DWA_WARPS * DWA_RPW;
+
 template <int SW, bool BN, bool GLU>
-__global__ void __launch_bounds__(32 * DW_WARPS)
+__global__ void __launch_bounds__(32 * DWA_WARPS)
 dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
                  const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
                  float *__restrict__ out, int C, SeqDev seq, const float *__restrict__ glu_bias,
                  long long x_total) {
   static_assert(SW == DW_SWISH_NONE || SW == DW_SWISH_POLY, "no scalar Swish tail here");
   constexpr int K = 9;
-  __shared__ __align__(16) float stage[DW_WARPS][DWA_ROW];
-  __shared__ __align__(16) float stage_g[GLU ? DW_WARPS : 1][GLU ? DWA_ROW : 4];
-  __shared__ unsigned long long bars[DW_WARPS];
+  constexpr int LPR = DWA_LPR;
+  __shared__ __align__(16) float stage[DWA_CH][DWA_ROW];
+  __shared__ __align__(16) float stage_g[GLU ? DWA_CH : 1][GLU ? DWA_ROW : 4];
+  __shared__ unsigned long long bars[DWA_WARPS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * DW_WARPS + warp;
-  if (c >= C) return;
+  const int g = lane / LPR, li = lane % LPR;
+  const int slot = warp * DWA_RPW + g;
+  const int c = blockIdx.x * DWA_CH + slot;
+  if (blockIdx.x * DWA_CH + warp * DWA_RPW >= C) return;   // whole warp
   const int item = blockIdx.y;
   const int T = seq_T(seq, item);
   const long long f0 = seq_frame_off(seq, item);
   const long long row = (GLU ? 2 * f0 * C : f0 * C) + (long long)c * T;
-  float *s = stage[warp];
-  float *sg = stage_g[GLU ? warp : 0];
+  float *s = stage[slot];
+  float *sg = stage_g[GLU ? slot : 0];
   unsigned long long *bar = bars + warp;
   if (lane == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar, DWA_RPW);   // one arrival per row
     mbar_init_fence();
   }
   __syncwarp();
   const Span sa = span_of(row, T, x_total);
   Span sgs = sa;
   if (GLU) sgs = span_of(row + (long long)C * T, T, x_total);
-  if (lane == 0) mbar_arrive_tx(bar, sa.bytes + (GLU ? sgs.bytes : 0u));
-  span_issue(s + 4, x, sa, bar, lane);
-  if (GLU) span_issue(sg + 4, x, sgs, bar, lane);
+  if (li == 0) mbar_arrive_tx(bar, sa.bytes + (GLU ? sgs.bytes : 0u));
+  span_issue(s + 4, x, sa, bar, li);
+  if (GLU) span_issue(sg + 4, x, sgs, bar, li);
   // per-channel parameters while the copies are in flight
   float wk[K];
 #pragma unroll
@@ -453,10 +464,10 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
     const int n_head = off > 0 ? (4 - off < T ? 4 - off : T) : 0;
     const int tail0 = g_hi > g_lo ? 4 * g_hi - off : n_head;
     const int n_left = n_head + (T - tail0);
-    for (int q = g_lo + lane; q < g_hi; q += 32)
+    for (int q = g_lo + li; q < g_hi; q += LPR)
       st4(s + 4 + 4 * q, glu4(ld4(s + 4 + 4 * q), ld4(sg + 4 + 4 * q), ba, bg, gbias));
-    if (lane < n_left) {
-      const int t = lane < n_head ? lane : tail0 + (lane - n_head);
+    if (li < n_left) {
+      const int t = li < n_head ? li : tail0 + (li - n_head);
       float aa = s[4 + off + t], gg = sg[4 + off + t];
       if (gbias) {
         aa = aa + ba;
@@ -471,7 +482,7 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
   // 4q - off + 7 <= T - 1
   const int c_lo = 1 + ((off + 3) >> 2);
   const int c_hi = (T - 8 + off) >= 0 ? (T - 8 + off) >> 2 : -1;
-  for (int q = c_lo + lane; q <= c_hi; q += 32) {
+  for (int q = c_lo + li; q <= c_hi; q += LPR) {
     const int t0 = 4 * q - off;
     const float4 a0 = ld4(s + 4 * q), a1 = ld4(s + 4 * q + 4), a2 = ld4(s + 4 * q + 8);
     const float win[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w,
@@ -498,8 +509,8 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
   const int h_end = c_hi >= c_lo ? 4 * c_lo - off : T;
   const int t_beg = c_hi >= c_lo ? 4 * c_hi - off + 4 : T;
   const int n_out = h_end + (T - t_beg);
-  if (lane < n_out) {
-    const int t = lane < h_end ? lane : t_beg + (lane - h_end);
+  if (li < n_out) {
+    const int t = li < h_end ? li : t_beg + (li - h_end);
     float val = bias;
 #pragma unroll
     for (int k = 0; k < K; k++) {
@@ -526,11 +537,12 @@ static int launch_dwconv(const float *x, const float *w, const float *b, const f
                          long long frames, cudaStream_t s, int glu = 0,
                          const float *glu_bias = nullptr) {
   dim3 grid((unsigned)((C + DW_WARPS - 1) / DW_WARPS), (unsigned)sd.n_items);
-  if (K == 9 && C % 8 == 0 && PK_ALIGNED16(x) && PK_ALIGNED16(out) &&
+  if (K == 9 && C % DWA_CH == 0 && PK_ALIGNED16(x) && PK_ALIGNED16(out) &&
       dwa_row_need(sd.max_T) <= DWA_ROW) {
+    const dim3 grid_al((unsigned)(C / DWA_CH), (unsigned)sd.n_items);
     const long long x_total = (glu ? 2 : 1) * frames * C;
 #define PK_DW_AL(SWV, BNV, GLUV)                                                         \
-  dwconv_al_kernel<SWV, BNV, GLUV><<<grid, 32 * DW_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, \
+  dwconv_al_kernel<SWV, BNV, GLUV><<<grid_al, 32 * DWA_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, \
                                                                  sd, glu_bias, x_total)
 #define PK_DW_AL_SW(BNV, GLUV)                                  \
   do {                                                          \
