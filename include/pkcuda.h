@@ -348,6 +348,56 @@ int  pkcu_encoder_nongemm_host(pkcu_encoder_ws *ws, float *x_host,
                                const pkcu_block_params *blocks, int n_blocks,
                                pkcu_stream_t stream);
 
+/* ── 4. weights: the reference checkpoint format on the device ─────────────
+ * Replaces pk_load_weights / lookup_weight / pk_free_weights
+ * (csrc/weights.c:240-402, 551-564) for a GPU engine: weights.bin +
+ * weights.json as written by extract_weights.py:894-945. Open parses the
+ * manifest and reads the file on the host (no CUDA call); upload puts every
+ * tensor in its own 256-byte aligned slot of one device allocation on the
+ * current device and builds each block's fused QKV weight and bias as the
+ * reference does after loading (csrc/weights.c:403-544). Device pointers
+ * stay valid until pkcu_weights_destroy. */
+#define PKCU_DTYPE_F32 0
+#define PKCU_DTYPE_I8  1   /* per-tensor scale */
+#define PKCU_DTYPE_I4  2   /* packed [K, N/2], fp32 group scales [K, N/32] */
+
+typedef struct pkcu_weights pkcu_weights;
+
+typedef struct {
+    int dtype;                  /* PKCU_DTYPE_*, as stored */
+    int ndim;
+    long long shape[4];         /* manifest shape (int4: the packed [K, N/2]) */
+    long long numel;            /* elements (float32, int8) or packed bytes (int4) */
+    float scale;                /* int8 per-tensor scale, else 0 */
+    long long n_scales;         /* int4 group scales, else 0 */
+    const void *host;           /* the bytes in the host copy of weights.bin */
+    const float *host_scales;   /* int4 */
+    const void *dev;            /* device copy; NULL before upload */
+    const float *dev_scales;    /* int4, device */
+} pkcu_tensor;
+
+int pkcu_weights_open(const char *bin_path, const char *json_path, pkcu_weights **out);
+int pkcu_weights_upload(pkcu_weights *w, pkcu_stream_t stream);   /* synchronous */
+void pkcu_weights_destroy(pkcu_weights *w);
+int pkcu_weights_count(const pkcu_weights *w);
+const char *pkcu_weights_name(const pkcu_weights *w, int index);   /* manifest order */
+/* Conformer blocks present (layers.0 .. with a linear_q weight). */
+int pkcu_weights_blocks(const pkcu_weights *w);
+/* lookup_weight (csrc/weights.c:240-266): PKCU_ERR_ARG if the name is absent. */
+int pkcu_weights_find(const pkcu_weights *w, const char *name, pkcu_tensor *t);
+/* Any tensor as fp32 on the device: float32 copied, int8 (float)q * scale,
+ * int4 (float)nibble * scale[k, col/32], the reference's dequant formulas. */
+int pkcu_weights_dequant(const pkcu_weights *w, const char *name, float *out,
+                         pkcu_stream_t stream);
+/* Block b's fused QKV (csrc/weights.c:403-544): int8 [D, 3D] at the common
+ * scale (*bits = 8, *scale = max(sq, sk, sv)) when q, k, v are int8; fp32
+ * [D, 3D] (*bits = 32) when they are float32 or int4; bias = [Bq | Bk | Bv]. */
+int pkcu_weights_fused_qkv(const pkcu_weights *w, int block, const void **weight, int *bits,
+                           float *scale, const float **bias);
+/* The non-GEMM parameters of block b for pkcu_encoder_nongemm (qkv_b is the
+ * fused bias above). */
+int pkcu_weights_block_params(const pkcu_weights *w, int block, pkcu_block_params *p);
+
 #ifdef __cplusplus
 }
 #endif

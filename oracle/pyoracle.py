@@ -124,6 +124,7 @@ _REF_SIGS = {
     "pkref_pool_threads": (C.c_int, []),
     "pkref_load_fused_qkv": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_size_t,
                                       FP, C.POINTER(C.c_int)]),
+    "pkref_manifest_scales": (C.c_int, [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, FP]),
 }
 
 _oracle = None
@@ -475,6 +476,27 @@ class Reference:
                                              out.nbytes, _fp(scales), C.byref(bits))
         assert rc == 0 and bits.value == 8, (rc, bits.value)
         return out, scales
+
+    def manifest_scales(self, json_path, names):
+        """The int8 scale the reference's manifest parser reads for each name."""
+        arr = (C.c_char_p * len(names))(*[n.encode() for n in names])
+        out = np.zeros(len(names), np.float32)
+        n = self.L.pkref_manifest_scales(str(json_path).encode(), arr, len(names), _fp(out))
+        assert n >= 0
+        return out
+
+    def load_fused_qkv_file(self, bin_path, json_path):
+        """Loads a checkpoint with the reference's pk_load_weights; returns block
+        0's fused QKV (int8 or fp32 [1024, 3072]), (sq, sk, sv, scale) and bits."""
+        buf = np.empty(D * 3 * D * 4, np.uint8)
+        scales = np.zeros(4, np.float32)
+        bits = C.c_int(0)
+        rc = self.L.pkref_load_fused_qkv(str(bin_path).encode(), str(json_path).encode(),
+                                         buf.ctypes.data, buf.nbytes, _fp(scales), C.byref(bits))
+        assert rc == 0, rc
+        if bits.value == 8:
+            return buf[:D * 3 * D].view(np.int8).reshape(D, 3 * D).copy(), scales, 8
+        return buf.view(np.float32).reshape(D, 3 * D).copy(), scales, bits.value
 
     def conformer_block(self, x, params: dict, standins: dict):
         """The reference's conformer_block with GEMMs replaced by the stand-ins;

@@ -43,6 +43,9 @@ EXPORTED = (
     "pkcu_encoder_ws_create", "pkcu_encoder_ws_destroy", "pkcu_encoder_ws_device",
     "pkcu_encoder_ws_device_bytes", "pkcu_encoder_ws_h2d_bytes", "pkcu_encoder_ws_d2h_bytes",
     "pkcu_encoder_nongemm_host",
+    "pkcu_weights_open", "pkcu_weights_upload", "pkcu_weights_destroy", "pkcu_weights_count",
+    "pkcu_weights_name", "pkcu_weights_blocks", "pkcu_weights_find", "pkcu_weights_dequant",
+    "pkcu_weights_fused_qkv", "pkcu_weights_block_params",
 )
 
 
@@ -54,6 +57,17 @@ VP, I, LL, F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
 
 _SIGS = {
     "pkcu_status_string": (C.c_char_p, [I]),
+    "pkcu_weights_open": (I, [C.c_char_p, C.c_char_p, C.POINTER(VP)]),
+    "pkcu_weights_upload": (I, [VP, VP]),
+    "pkcu_weights_destroy": (None, [VP]),
+    "pkcu_weights_count": (I, [VP]),
+    "pkcu_weights_name": (C.c_char_p, [VP, I]),
+    "pkcu_weights_blocks": (I, [VP]),
+    "pkcu_weights_find": (I, [VP, C.c_char_p, VP]),
+    "pkcu_weights_dequant": (I, [VP, C.c_char_p, VP, VP]),
+    "pkcu_weights_fused_qkv": (I, [VP, I, C.POINTER(VP), C.POINTER(I), C.POINTER(C.c_float),
+                                   C.POINTER(VP)]),
+    "pkcu_weights_block_params": (I, [VP, I, VP]),
     "pkcu_last_error": (C.c_char_p, []),
     "pkcu_version": (C.c_char_p, []),
     "pkcu_selftest": (I, [C.POINTER(C.c_ulonglong)]),
@@ -242,6 +256,72 @@ class GemmOutputs(C.Structure):
 
 class GemmInputs(C.Structure):
     _fields_ = [(f, VP) for f in GEMM_IN_FIELDS]
+
+
+PKCU_DTYPE_F32, PKCU_DTYPE_I8, PKCU_DTYPE_I4 = 0, 1, 2
+
+
+class Tensor(C.Structure):
+    """pkcu_tensor: one manifest entry (include/pkcuda.h)."""
+    _fields_ = [("dtype", I), ("ndim", I), ("shape", C.c_longlong * 4), ("numel", C.c_longlong),
+                ("scale", C.c_float), ("n_scales", C.c_longlong), ("host", VP),
+                ("host_scales", VP), ("dev", VP), ("dev_scales", VP)]
+
+    @property
+    def dims(self):
+        return tuple(self.shape[d] for d in range(self.ndim))
+
+
+class Weights:
+    """A weights.bin / weights.json checkpoint (the reference's format):
+    parsed on the host when opened, copied to the current device by upload()."""
+
+    def __init__(self, bin_path, json_path):
+        h = VP()
+        check(lib().pkcu_weights_open(str(bin_path).encode(), str(json_path).encode(), C.byref(h)),
+              "pkcu_weights_open")
+        self.h = h
+
+    def upload(self, stream=None):
+        call("pkcu_weights_upload", self.h, stream)
+
+    def names(self):
+        L = lib()
+        return [L.pkcu_weights_name(self.h, i).decode() for i in range(L.pkcu_weights_count(self.h))]
+
+    def blocks(self) -> int:
+        return lib().pkcu_weights_blocks(self.h)
+
+    def find(self, name) -> Tensor:
+        t = Tensor()
+        call("pkcu_weights_find", self.h, name.encode(), C.byref(t))
+        return t
+
+    def dequant(self, name, out_ptr, stream=None):
+        call("pkcu_weights_dequant", self.h, name.encode(), out_ptr, stream)
+
+    def fused_qkv(self, block):
+        w, b = VP(), VP()
+        bits, scale = I(), C.c_float()
+        call("pkcu_weights_fused_qkv", self.h, block, C.byref(w), C.byref(bits), C.byref(scale),
+             C.byref(b))
+        return w.value, bits.value, scale.value, b.value
+
+    def block_params(self, block) -> "BlockParams":
+        p = BlockParams()
+        call("pkcu_weights_block_params", self.h, block, C.byref(p))
+        return p
+
+    def close(self):
+        if self.h:
+            lib().pkcu_weights_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def block_params_array(blocks):

@@ -28,6 +28,22 @@ def empty(shape, dtype=None):
     return t
 
 
+class _DeviceView:
+    """A device address seen as a 1-D array (the CUDA array interface)."""
+
+    def __init__(self, ptr, n, dtype):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": np.dtype(dtype).str,
+                                         "data": (int(ptr), False), "version": 3}
+
+
+def from_device(ptr, n, dtype):
+    """Host copy of n elements of dtype at a device address owned elsewhere."""
+    import torch
+    t = torch.as_tensor(_DeviceView(ptr, n, dtype), device="cuda")
+    torch.cuda.synchronize()
+    return t.cpu().numpy().copy()
+
+
 def host(t):
     import torch
     torch.cuda.synchronize()
