@@ -348,6 +348,47 @@ int  pkcu_encoder_nongemm_host(pkcu_encoder_ws *ws, float *x_host,
                                const pkcu_block_params *blocks, int n_blocks,
                                pkcu_stream_t stream);
 
+/* ── pre-encode: subsampling and input scaling (csrc/encoder.c:103-175, 578-593) ──
+ * For a batch of utterances of T_b mel frames (mel per utterance [128, T_b],
+ * utterance after utterance): conv0 (1 -> 256, 3x3 stride 2) + ReLU and the
+ * depthwise 3x3 stride-2 conv fused in one kernel, the first 1x1 conv (GEMM),
+ * its bias + ReLU folded into the second depthwise conv, the second 1x1 conv
+ * (GEMM), its bias + ReLU folded into the flatten, the output projection
+ * (GEMM), then x = (proj + bias) * sqrt(1024), the blocks' input [F', 1024].
+ * Output frames per utterance T'_b = ceil(ceil(ceil(T_b/2)/2)/2). The
+ * [256, *] tensors are channel-major across the batch: row c holds every
+ * utterance's plane in turn, so each 1x1 conv is one GEMM
+ * [256 x 256] x [256 x P] (P = pkcu_pre_plan_p2 / _p3). */
+typedef struct pkcu_pre_plan pkcu_pre_plan;
+int pkcu_pre_plan_create(const int *mel_lengths, int n_items, pkcu_pre_plan **out);
+void pkcu_pre_plan_destroy(pkcu_pre_plan *p);
+long long pkcu_pre_plan_p2(const pkcu_pre_plan *p);      /* columns of pw1's [256, P2] */
+long long pkcu_pre_plan_p3(const pkcu_pre_plan *p);      /* columns of pw2's [256, P3] */
+long long pkcu_pre_plan_frames(const pkcu_pre_plan *p);  /* F' = sum of T'_b */
+/* The T'_b batch descriptor for pkcu_encoder_nongemm (owned by the plan). */
+const pkcu_seq *pkcu_pre_plan_out_seq(const pkcu_pre_plan *p);
+
+typedef struct {   /* [256, 1, 3, 3] weights, [256] / [1024] biases (csrc/parakeet.h:59-76) */
+    const float *conv0_w, *conv0_b, *conv2_w, *conv2_b, *conv3_b;
+    const float *conv5_w, *conv5_b, *conv6_b, *out_b;
+} pkcu_pre_params;
+typedef struct {   /* GEMM products, bias not added */
+    float *pw1;    /* [256, P2] = W3 [256, 256] x s2d */
+    float *pw2;    /* [256, P3] = W6 x s3d */
+    float *proj;   /* [F', 1024] = flat x W_out [4096, 1024] */
+} pkcu_pre_gemm_outputs;
+typedef struct {
+    float *s2d;    /* [256, P2] */
+    float *s3d;    /* [256, P3] */
+    float *flat;   /* [F', 4096] */
+} pkcu_pre_gemm_inputs;
+enum { PKCU_GEMM_PRE_PW1 = 16, PKCU_GEMM_PRE_PW2, PKCU_GEMM_PRE_OUT };
+/* Runs the stage; hook (block -1) at each GEMM as in pkcu_encoder_nongemm. */
+int pkcu_pre_encode(const float *mel, const pkcu_pre_params *params,
+                    const pkcu_pre_gemm_outputs *gemm_out, const pkcu_pre_gemm_inputs *gemm_in,
+                    float *x, const pkcu_pre_plan *plan, pkcu_gemm_hook hook, void *hook_user,
+                    pkcu_stream_t stream);
+
 /* ── 4. weights: the reference checkpoint format on the device ─────────────
  * Replaces pk_load_weights / lookup_weight / pk_free_weights
  * (csrc/weights.c:240-402, 551-564) for a GPU engine: weights.bin +
@@ -397,6 +438,8 @@ int pkcu_weights_fused_qkv(const pkcu_weights *w, int block, const void **weight
 /* The non-GEMM parameters of block b for pkcu_encoder_nongemm (qkv_b is the
  * fused bias above). */
 int pkcu_weights_block_params(const pkcu_weights *w, int block, pkcu_block_params *p);
+/* The pre-encode parameters (pre_encode.conv.{0,2,3,5,6}.*, pre_encode.out.bias). */
+int pkcu_weights_pre_params(const pkcu_weights *w, pkcu_pre_params *p);
 
 #ifdef __cplusplus
 }

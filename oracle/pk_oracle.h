@@ -72,4 +72,11 @@ void or_dequant_i4_qkv(const uint8_t *pq, const uint8_t *pk, const uint8_t *pv,
                        const float *sq, const float *sk, const float *sv,
                        float *fused, int K, int D, int group);
 
+
+/* Pre-encode subsampling + input scaling (pk_oracle_preencode.c). */
+int or_pre_out_frames(int T);
+int or_pre_encode(const float *mel, int T, const float *const *params, const float *y2,
+                  const float *y3, const float *proj, float *s2d_cap, float *s3d_cap,
+                  float *flat_cap, float *x_out);
+
 #endif

@@ -78,6 +78,8 @@ class _Lib:
 
 
 _ORACLE_SIGS = {
+    "or_pre_out_frames": (C.c_int, [C.c_int]),
+    "or_pre_encode": (C.c_int, [FP, C.c_int, FPP, FP, FP, FP, FP, FP, FP, FP]),
     "or_exp_poly": (C.c_float, [C.c_float]),
     "or_layer_norm_rows": (None, [FP, FP, FP, FP, C.c_int, C.c_int]),
     "or_layer_norm_rows_inplace": (None, [FP, FP, FP, C.c_int, C.c_int]),
@@ -125,6 +127,7 @@ _REF_SIGS = {
     "pkref_load_fused_qkv": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_size_t,
                                       FP, C.POINTER(C.c_int)]),
     "pkref_manifest_scales": (C.c_int, [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, FP]),
+    "pkref_pre_encode": (C.c_int, [FP, C.c_int, FPP, FP, FP, FP, FP, FP, FP, FP]),
 }
 
 _oracle = None
@@ -300,6 +303,11 @@ class Oracle:
         self.L.or_conformer_block(_fp(xx), T, p, s, o)
         return xx, caps
 
+    def pre_encode(self, mel, params: dict, standins: dict):
+        """Pre-encode subsampling + scaling of one utterance (mel [128, T]):
+        returns (x [T', 1024], {s2d, s3d, flat}: the GEMM inputs)."""
+        return _pre_call(self.L.or_pre_encode, mel, params, standins)
+
     def joint_add_act(self, enc, pred, act):
         enc, pred = f32(enc), f32(pred)
         B, T, J = enc.shape
@@ -358,6 +366,50 @@ def standin_shapes(T: int) -> dict:
     return {"ff1_h": (T, FF), "ff1_out": (T, D), "qkv": (T, 3 * D), "P": (L, D),
             "ac": (H, T, T), "bd": (H, T, L), "attn_h": (H, T, DH), "att_out": (T, D),
             "pw1": (2 * D, T), "pw2": (D, T), "ff2_h": (T, FF), "ff2_out": (T, D)}
+
+
+PRE_PARAM_ROLES = ("conv0_w", "conv0_b", "conv2_w", "conv2_b", "conv3_b", "conv5_w",
+                   "conv5_b", "conv6_b", "out_b")
+PRE_C, PRE_MELS = 256, 128
+
+
+def pre_dims(T: int) -> dict:
+    """Heights and widths after each stride-2 stage for T mel frames."""
+    h1 = (T + 2 - 3) // 2 + 1
+    h2 = (h1 + 2 - 3) // 2 + 1
+    h3 = (h2 + 2 - 3) // 2 + 1
+    return {"H1": h1, "W1": 64, "H2": h2, "W2": 32, "H3": h3, "W3": 16}
+
+
+def pre_param_shapes() -> dict:
+    return {"conv0_w": (PRE_C, 1, 3, 3), "conv0_b": (PRE_C,), "conv2_w": (PRE_C, 1, 3, 3),
+            "conv2_b": (PRE_C,), "conv3_b": (PRE_C,), "conv5_w": (PRE_C, 1, 3, 3),
+            "conv5_b": (PRE_C,), "conv6_b": (PRE_C,), "out_b": (D,)}
+
+
+def random_pre_inputs(rng, T: int):
+    """Seeded pre-encode inputs: (params, stand-ins y2 / y3 / proj, mel [128, T])."""
+    d = pre_dims(T)
+    ps = {k: (0.3 * rng.standard_normal(s)).astype(np.float32) for k, s in pre_param_shapes().items()}
+    si = {"y2": rng.standard_normal((PRE_C, d["H2"] * d["W2"])).astype(np.float32),
+          "y3": rng.standard_normal((PRE_C, d["H3"] * d["W3"])).astype(np.float32),
+          "proj": rng.standard_normal((d["H3"], D)).astype(np.float32)}
+    mel = rng.standard_normal((PRE_MELS, T)).astype(np.float32)
+    return ps, si, mel
+
+
+def _pre_call(fn, mel, params, si):
+    T = mel.shape[1]
+    d = pre_dims(T)
+    caps = {"s2d": np.empty((PRE_C, d["H2"] * d["W2"]), np.float32),
+            "s3d": np.empty((PRE_C, d["H3"] * d["W3"]), np.float32),
+            "flat": np.empty((d["H3"], PRE_C * d["W3"]), np.float32)}
+    x = np.empty((d["H3"], D), np.float32)
+    p = _ptr_array([f32(params[r]) for r in PRE_PARAM_ROLES])
+    n = fn(_fp(f32(mel)), T, p, _fp(f32(si["y2"])), _fp(f32(si["y3"])), _fp(f32(si["proj"])),
+           _fp(caps["s2d"]), _fp(caps["s3d"]), _fp(caps["flat"]), _fp(x))
+    assert n == d["H3"], (n, d)
+    return x, caps
 
 
 def param_shapes() -> dict:
@@ -476,6 +528,11 @@ class Reference:
                                              out.nbytes, _fp(scales), C.byref(bits))
         assert rc == 0 and bits.value == 8, (rc, bits.value)
         return out, scales
+
+    def pre_encode(self, mel, params: dict, standins: dict):
+        """The reference's own pre_encode_and_scale (csrc/encoder.c:103-175,
+        578-593) with its 1x1 convolutions and projection as stand-ins."""
+        return _pre_call(self.L.pkref_pre_encode, mel, params, standins)
 
     def manifest_scales(self, json_path, names):
         """The int8 scale the reference's manifest parser reads for each name."""

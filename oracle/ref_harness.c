@@ -63,18 +63,36 @@ void pkh_sgemm_st(CBLAS_ORDER order, CBLAS_TRANSPOSE transA, CBLAS_TRANSPOSE tra
 void pkh_pointwise_conv1d(const float *x, const float *w, const float *b,
                           float *out, int Cin, int Cout, int T);
 
+void pkh_conv2d(const float *x, const float *w, const float *b, float *out, int Cin, int H,
+                int W, int Cout, int Kh, int Kw, int sh, int sw, int ph, int pw, int groups);
+
 #define pk_wmatmul          pkh_wmatmul
 #define cblas_sgemm_st      pkh_sgemm_st
 #define pk_pointwise_conv1d pkh_pointwise_conv1d
+#define pk_conv2d           pkh_conv2d
 #include "encoder.c"
 #undef pk_wmatmul
 #undef cblas_sgemm_st
 #undef pk_pointwise_conv1d
+#undef pk_conv2d
+
+/* Pre-encode stand-ins (pkref_pre_encode): the two 1x1 convolutions and the
+ * output projection of csrc/encoder.c:128-164 are the GEMMs of that stage. */
+static int g_pre;
+static const float *g_pre_y[3];   /* pw1 [256, P2], pw2 [256, P3], proj [T', 1024] */
+static float *g_pre_cap[3];       /* their inputs: [256, P2], [256, P3], [T', 4096] */
+static int g_pre_pw;
 
 static void copy_rows(float *C, int ldc, const float *src, int M, int N)
 {
     for (int i = 0; i < M; i++)
         memcpy(C + (size_t)i * ldc, src + (size_t)i * N, (size_t)N * sizeof(float));
+}
+
+static void capture_rows_dense(float *dst, const float *src, int ld, int M, int N)
+{
+    for (int i = 0; i < M; i++)
+        memcpy(dst + (size_t)i * N, src + (size_t)i * ld, (size_t)N * sizeof(float));
 }
 
 /* Copies an [M, N] operand with leading dimension ld into a dense buffer. */
@@ -86,9 +104,33 @@ static void capture(int role, size_t off, const float *src, int ld, int M, int N
         memcpy(dst + off + (size_t)i * N, src + (size_t)i * ld, (size_t)N * sizeof(float));
 }
 
+/* pk_conv2d (csrc/tensor_ops.c:439-475) as pre_encode calls it: the reference's
+ * own code for the 3x3 convolutions; during pkref_pre_encode the 1x1
+ * convolutions become stand-ins, out = GEMM output + bias (the bias the
+ * reference's loop starts from), with their input captured. */
+void pkh_conv2d(const float *x, const float *w, const float *b, float *out, int Cin, int H,
+                int W, int Cout, int Kh, int Kw, int sh, int sw, int ph, int pw, int groups)
+{
+    if (g_pre && Kh == 1 && Kw == 1 && groups == 1 && g_pre_pw < 2) {
+        const int k = g_pre_pw++;
+        const size_t P = (size_t)H * W;
+        if (g_pre_cap[k]) memcpy(g_pre_cap[k], x, (size_t)Cin * P * sizeof(float));
+        for (int oc = 0; oc < Cout; oc++)
+            for (size_t p = 0; p < P; p++)
+                out[oc * P + p] = g_pre_y[k][oc * P + p] + b[oc];
+        return;
+    }
+    pk_conv2d(x, w, b, out, Cin, H, W, Cout, Kh, Kw, sh, sw, ph, pw, groups);
+}
+
 void pkh_wmatmul(const float *A, const Weight *W, float *C,
                  int M, int N, int K, float alpha, float beta)
 {
+    if (g_pre) {   /* pre_encode's output projection */
+        if (g_pre_cap[2]) capture_rows_dense(g_pre_cap[2], A, K, M, K);
+        copy_rows(C, N, g_pre_y[2], M, N);
+        return;
+    }
     static const int role_of_call[7] = {
         PKH_FF1_H, PKH_FF1_OUT, PKH_QKV, PKH_P, PKH_ATT_OUT, PKH_FF2_H, PKH_FF2_OUT
     };
@@ -249,6 +291,41 @@ int pkref_load_fused_qkv(const char *bin_path, const char *json_path, void *out,
     pk_free_weights(m);
     free(m);
     return rc;
+}
+
+/* The reference's pre-encode and scaling (csrc/encoder.c:103-175, 578-593) for
+ * one utterance of T mel frames (mel [128, T]): pre_encode_and_scale with the
+ * two 1x1 convolutions and the output projection as stand-ins (y2 [256, P2],
+ * y3 [256, P3], proj [T', 1024], P = rows x width after each stride-2 stage)
+ * whose inputs are captured (s2d, s3d, flat; any may be NULL). params: conv0_w,
+ * conv0_b, conv2_w, conv2_b, conv3_b, conv5_w, conv5_b, conv6_b, out_b.
+ * x_out [T', 1024]. Returns T', or -1. */
+int pkref_pre_encode(const float *mel, int T, const float *const *params, const float *y2,
+                     const float *y3, const float *proj, float *s2d, float *s3d, float *flat,
+                     float *x_out)
+{
+    PkModel *m = (PkModel *)calloc(1, sizeof(PkModel));
+    if (!m) return -1;
+    PreEncodeWeights *w = &m->enc.pre_encode;
+    w->conv0_w = params[0]; w->conv0_b = params[1];
+    w->conv2_w = params[2]; w->conv2_b = params[3];
+    w->conv3_b = params[4];
+    w->conv5_w = params[5]; w->conv5_b = params[6];
+    w->conv6_b = params[7];
+    w->out_b = params[8];
+    g_pre = 1;
+    g_pre_pw = 0;
+    g_pre_y[0] = y2; g_pre_y[1] = y3; g_pre_y[2] = proj;
+    g_pre_cap[0] = s2d; g_pre_cap[1] = s3d; g_pre_cap[2] = flat;
+    float *x = NULL;
+    const int Tp = pre_encode_and_scale(m, mel, T, &x);
+    g_pre = 0;
+    if (x) {
+        memcpy(x_out, x, (size_t)Tp * PK_D_MODEL * sizeof(float));
+        free(x);
+    }
+    free(m);
+    return x ? Tp : -1;
 }
 
 /* Number of threads the process-wide reference pool runs with (PK_THREADS). */

@@ -626,3 +626,25 @@ int pkcu_weights_block_params(const pkcu_weights *w, int block, pkcu_block_param
 }
 
 int pkcu_weights_blocks(const pkcu_weights *w) { return w ? w->n_blocks : 0; }
+
+int pkcu_weights_pre_params(const pkcu_weights *w, pkcu_pre_params *p)
+{
+    int st = need_upload(w, "pkcu_weights_pre_params");
+    if (st) return st;
+    if (!p) return pkcu_fail(PKCU_ERR_ARG, "pkcu_weights_pre_params: NULL params");
+    static const char *names[9] = {
+        "pre_encode.conv.0.weight", "pre_encode.conv.0.bias", "pre_encode.conv.2.weight",
+        "pre_encode.conv.2.bias", "pre_encode.conv.3.bias", "pre_encode.conv.5.weight",
+        "pre_encode.conv.5.bias", "pre_encode.conv.6.bias", "pre_encode.out.bias"};
+    const float *v[9];
+    for (int i = 0; i < 9; i++) {
+        const Entry *e = find(w, names[i]);
+        if (!e || e->dtype != PKCU_DTYPE_F32)
+            return pkcu_fail(PKCU_ERR_ARG, "pkcu_weights_pre_params: no float32 '%s'", names[i]);
+        v[i] = (const float *)(w->arena + e->slot);
+    }
+    p->conv0_w = v[0]; p->conv0_b = v[1]; p->conv2_w = v[2]; p->conv2_b = v[3];
+    p->conv3_b = v[4]; p->conv5_w = v[5]; p->conv5_b = v[6]; p->conv6_b = v[7];
+    p->out_b = v[8];
+    return PKCU_OK;
+}

@@ -45,7 +45,9 @@ EXPORTED = (
     "pkcu_encoder_nongemm_host",
     "pkcu_weights_open", "pkcu_weights_upload", "pkcu_weights_destroy", "pkcu_weights_count",
     "pkcu_weights_name", "pkcu_weights_blocks", "pkcu_weights_find", "pkcu_weights_dequant",
-    "pkcu_weights_fused_qkv", "pkcu_weights_block_params",
+    "pkcu_weights_fused_qkv", "pkcu_weights_block_params", "pkcu_weights_pre_params",
+    "pkcu_pre_plan_create", "pkcu_pre_plan_destroy", "pkcu_pre_plan_p2", "pkcu_pre_plan_p3",
+    "pkcu_pre_plan_frames", "pkcu_pre_plan_out_seq", "pkcu_pre_encode",
 )
 
 
@@ -68,6 +70,14 @@ _SIGS = {
     "pkcu_weights_fused_qkv": (I, [VP, I, C.POINTER(VP), C.POINTER(I), C.POINTER(C.c_float),
                                    C.POINTER(VP)]),
     "pkcu_weights_block_params": (I, [VP, I, VP]),
+    "pkcu_weights_pre_params": (I, [VP, VP]),
+    "pkcu_pre_plan_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
+    "pkcu_pre_plan_destroy": (None, [VP]),
+    "pkcu_pre_plan_p2": (LL, [VP]),
+    "pkcu_pre_plan_p3": (LL, [VP]),
+    "pkcu_pre_plan_frames": (LL, [VP]),
+    "pkcu_pre_plan_out_seq": (VP, [VP]),
+    "pkcu_pre_encode": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP]),
     "pkcu_last_error": (C.c_char_p, []),
     "pkcu_version": (C.c_char_p, []),
     "pkcu_selftest": (I, [C.POINTER(C.c_ulonglong)]),
@@ -399,3 +409,87 @@ def encoder_nongemm(x, blocks_arr, n_blocks, gout: GemmOutputs, gin: GemmInputs,
     call("pkcu_encoder_nongemm", x if isinstance(x, int) else ptr(x), C.cast(blocks_arr, VP), n_blocks,
          C.cast(C.pointer(gout), VP), C.cast(C.pointer(gin), VP), seq.handle, None, None,
          stream_handle(stream))
+
+
+# ── pre-encode subsampling (pkcu_pre_encode) ────────────────────────────────
+PRE_PARAM_FIELDS = ("conv0_w", "conv0_b", "conv2_w", "conv2_b", "conv3_b", "conv5_w", "conv5_b",
+                    "conv6_b", "out_b")
+PRE_GEMM_OUT_FIELDS = ("pw1", "pw2", "proj")
+PRE_GEMM_IN_FIELDS = ("s2d", "s3d", "flat")
+PKCU_GEMM_PRE_PW1, PKCU_GEMM_PRE_PW2, PKCU_GEMM_PRE_OUT = 16, 17, 18
+GEMM_HOOK = C.CFUNCTYPE(I, VP, I, I, VP)
+
+
+class PreParams(C.Structure):
+    _fields_ = [(f, VP) for f in PRE_PARAM_FIELDS]
+
+
+class PreGemmOutputs(C.Structure):
+    _fields_ = [(f, VP) for f in PRE_GEMM_OUT_FIELDS]
+
+
+class PreGemmInputs(C.Structure):
+    _fields_ = [(f, VP) for f in PRE_GEMM_IN_FIELDS]
+
+
+def _struct(cls, fields, d):
+    s = cls()
+    for f in fields:
+        setattr(s, f, d[f] if isinstance(d[f], int) else ptr(d[f]))
+    return s
+
+
+class PrePlan:
+    """pkcu_pre_plan: a batch of utterances of T_b mel frames each."""
+
+    def __init__(self, mel_lengths):
+        self.mel_lengths = [int(t) for t in mel_lengths]
+        arr = (I * len(self.mel_lengths))(*self.mel_lengths)
+        h = VP()
+        check(lib().pkcu_pre_plan_create(arr, len(self.mel_lengths), C.byref(h)),
+              "pkcu_pre_plan_create")
+        self.handle = h
+
+    @property
+    def p2(self) -> int:
+        return lib().pkcu_pre_plan_p2(self.handle)
+
+    @property
+    def p3(self) -> int:
+        return lib().pkcu_pre_plan_p3(self.handle)
+
+    @property
+    def frames(self) -> int:
+        return lib().pkcu_pre_plan_frames(self.handle)
+
+    @property
+    def out_seq(self) -> int:
+        """Address of the plan's pkcu_seq of output frames (owned by the plan)."""
+        return lib().pkcu_pre_plan_out_seq(self.handle)
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_pre_plan_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def pre_encode(mel, params, gout, gin, x, plan: PrePlan, hook=None, stream=None) -> None:
+    """params / gout / gin: {field: tensor or address}; hook: a GEMM_HOOK or None."""
+    p = _struct(PreParams, PRE_PARAM_FIELDS, params)
+    go = _struct(PreGemmOutputs, PRE_GEMM_OUT_FIELDS, gout)
+    gi = _struct(PreGemmInputs, PRE_GEMM_IN_FIELDS, gin)
+    call("pkcu_pre_encode", mel if isinstance(mel, int) else ptr(mel), C.byref(p), C.byref(go),
+         C.byref(gi), x if isinstance(x, int) else ptr(x), plan.handle,
+         C.cast(hook, VP) if hook is not None else None, None, stream_handle(stream))

@@ -114,6 +114,19 @@ def main():
     for k, v in caps.items():
         g["blk_cap_" + k] = v
 
+    rng = np.random.default_rng(1010)  # pre-encode subsampling + scaling, T = 11 mel frames
+    # (H1 = 6, H2 = 3, T' = 2); the 1x1 convolutions and the projection are
+    # stand-ins, their inputs captured.
+    ps, si, mel = po.random_pre_inputs(rng, 11)
+    xo, caps = R.pre_encode(mel, ps, si)
+    g["pre_mel"], g["pre_x_out"] = mel, xo
+    for k, v in ps.items():
+        g["pre_p_" + k] = v
+    for k, v in si.items():
+        g["pre_si_" + k] = v
+    for k, v in caps.items():
+        g["pre_cap_" + k] = v
+
     np.savez_compressed(OUT, **g)
     print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT) / 1e6:.2f} MB")
 

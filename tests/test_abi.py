@@ -107,3 +107,22 @@ def test_uniform_seq_needs_no_device(L):
     assert L.pkcu_seq_bd_elems(h) == 4 * 8 * 375 * 749
     assert L.pkcu_seq_pos_rows(h) == 4 * 749
     L.pkcu_seq_destroy(h)
+
+
+def test_pre_plan_sizes_and_validation(L):
+    """pkcu_pre_plan: output frames ceil(ceil(ceil(T/2)/2)/2) per utterance
+    (csrc/encoder.c:116-152); a uniform batch keeps no device arrays."""
+    h = C.c_void_p()
+    arr = (C.c_int * 4)(3000, 3000, 3000, 3000)
+    assert L.pkcu_pre_plan_create(arr, 4, C.byref(h)) == 0
+    assert L.pkcu_pre_plan_frames(h) == 4 * 375
+    assert L.pkcu_pre_plan_p2(h) == 4 * 32 * 750
+    assert L.pkcu_pre_plan_p3(h) == 4 * 16 * 375
+    assert L.pkcu_pre_plan_out_seq(h)
+    L.pkcu_pre_plan_destroy(h)
+    bad = (C.c_int * 2)(11, 0)
+    h2 = C.c_void_p()
+    assert L.pkcu_pre_plan_create(bad, 2, C.byref(h2)) == 1 and not h2.value
+    assert L.pkcu_pre_plan_create(arr, 0, C.byref(h2)) == 1
+    assert L.pkcu_pre_encode(None, None, None, None, None, None, None, None, None) == 1
+    assert b"pkcu_pre_encode" in L.pkcu_last_error()

@@ -92,6 +92,22 @@ def test_golden_block(oracle, golden):
         assert_close(caps[k], golden["blk_cap_" + k], "block " + k)
 
 
+def _golden_pre(g):
+    ps = {k: g["pre_p_" + k] for k in po.PRE_PARAM_ROLES}
+    si = {k: g["pre_si_" + k] for k in ("y2", "y3", "proj")}
+    return ps, si, g["pre_mel"]
+
+
+def test_golden_pre_encode(oracle, golden):
+    """Pre-encode subsampling + scaling (csrc/encoder.c:103-175, 578-593): every
+    3x3 convolution, bias, ReLU, flatten and the sqrt(1024) scale bit for bit."""
+    ps, si, mel = _golden_pre(golden)
+    xo, caps = oracle.pre_encode(mel, ps, si)
+    assert_bitexact(xo, golden["pre_x_out"], "pre x")
+    for k in ("s2d", "s3d", "flat"):
+        assert_bitexact(caps[k], golden["pre_cap_" + k], "pre " + k)
+
+
 # ── the reference library at BASELINE shapes ─────────────────────────────────
 
 def test_ref_layer_norm_T375(oracle, reference):
@@ -150,6 +166,19 @@ def test_ref_block(oracle, reference, T):
             assert_bitexact(co[k], cr[k], k)
         else:
             assert_close(co[k], cr[k], k)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4, 5, 8, 9, 33, 257, 3000])
+def test_ref_pre_encode(oracle, reference, T):
+    """The reference's own pre_encode_and_scale (its pk_conv2d, pk_relu, flatten
+    and scaling; the 1x1 convolutions and projection as stand-ins) against the
+    restatement: bit-exact, odd and even T, down to one mel frame."""
+    ps, si, mel = po.random_pre_inputs(np.random.default_rng(300 + T), T)
+    xo, co = oracle.pre_encode(mel, ps, si)
+    xr, cr = reference.pre_encode(mel, ps, si)
+    assert_bitexact(xo, xr, "x")
+    for k in co:
+        assert_bitexact(co[k], cr[k], k)
 
 
 # ── known answers ────────────────────────────────────────────────────────────
