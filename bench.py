@@ -57,6 +57,10 @@ def parse_args():
     ap.add_argument("--no-aux", action="store_true", help="skip the standalone-kernel table")
     ap.add_argument("--aux-only", action="store_true",
                     help="time only the standalone kernels (one JSON object), e.g. for ncu")
+    ap.add_argument("--pre-only", action="store_true",
+                    help="with --aux-only: time only the pre-encode stage")
+    ap.add_argument("--pre-utts", type=int, default=64,
+                    help="utterances of 3000 mel frames in the pre-encode timing")
     ap.add_argument("--aux-reps", type=int, default=5,
                     help="timed launches per standalone kernel (0: one untimed launch each)")
     return ap.parse_args()
@@ -370,7 +374,7 @@ def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
     return table
 
 
-def time_aux_kernels(stream, reps=5):
+def time_aux_kernels(stream, reps=5, pre_utts=64, pre_only=False):
     """The tensor_ops entry points that are not part of the encoder block
     sequence, each timed alone (CUDA events on the bench stream, one warm-up
     launch) at a size above the 126 MB L2, with algorithmic bytes (each input
@@ -383,6 +387,8 @@ def time_aux_kernels(stream, reps=5):
     output size is timed beside them as the write-only reference point."""
     import torch
     import pkcuda
+    if pre_only:
+        return time_pre_encode(stream, reps, pre_utts)
     sh = stream.cuda_stream
     dev = torch.device("cuda", torch.cuda.current_device())
     g = torch.Generator(device=dev)
@@ -458,8 +464,85 @@ def time_aux_kernels(stream, reps=5):
     timed("argmax_rows", [B * T, V], 4 * B * T * V + 4 * B * T,
           lambda: pkcuda.call("pkcu_argmax_rows", logits.data_ptr(), am.data_ptr(), B * T, V, sh))
     del logits, am
+    out.update(time_pre_encode(stream, reps, pre_utts))
     torch.cuda.synchronize()
     return out
+
+
+PRE_UTTS, PRE_MEL_T = 64, 3000
+
+
+def pre_encode_bytes(n, T):
+    """Algorithmic bytes of the pre-encode kernels for n utterances of T mel
+    frames (each input read once, each output written once; weights ignored)."""
+    h1 = (T + 1) // 2
+    h2 = (h1 + 1) // 2
+    h3 = (h2 + 1) // 2
+    s2, s3 = 4 * 256 * 32 * h2, 4 * 256 * 16 * h3
+    return {"pre_conv0_dw2": n * (4 * 128 * T + s2), "pre_dw5": n * (s2 + s3),
+            "pre_flatten": n * (s3 + 4 * 4096 * h3), "pre_out_scale": n * 8 * 1024 * h3}
+
+
+def time_pre_encode(stream, reps, n_utts=PRE_UTTS):
+    """pkcu_pre_encode over 64 utterances x 3000 mel frames (30 s each ->
+    375 frames), GEMM products as seeded stand-ins. A GEMM hook records a CUDA
+    event at each GEMM point, which splits the stage into its four kernels."""
+    import torch
+    import pkcuda
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    f32 = dict(device=dev, dtype=torch.float32)
+    n, T = n_utts, PRE_MEL_T
+    plan = pkcuda.PrePlan([T] * n)
+    P2, P3, F = plan.p2, plan.p3, plan.frames
+    mel = torch.randn(n * 128 * T, generator=g, **f32)
+    params = {k: 0.3 * torch.randn(1024 if k == "out_b" else 256 * (9 if k.endswith("_w") else 1),
+                                   generator=g, **f32) for k in pkcuda.PRE_PARAM_FIELDS}
+    gout = {"pw1": torch.randn(256 * P2, generator=g, **f32),
+            "pw2": torch.randn(256 * P3, generator=g, **f32),
+            "proj": torch.randn(F * 1024, generator=g, **f32)}
+    gin = {"s2d": torch.empty(256 * P2, **f32), "s3d": torch.empty(256 * P3, **f32),
+           "flat": torch.empty(F * 4096, **f32)}
+    x = torch.empty(F * 1024, **f32)
+    marks = []
+
+    def on_gemm(user, block, gemm, s):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append(ev)
+        return 0
+
+    hook = pkcuda.GEMM_HOOK(on_gemm)
+
+    def once():
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append(ev)
+        pkcuda.pre_encode(mel, params, gout, gin, x, plan, hook=hook, stream=stream)
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append(ev)
+
+    once()
+    torch.cuda.synchronize()
+    names = ("pre_conv0_dw2", "pre_dw5", "pre_flatten", "pre_out_scale")
+    ms = dict.fromkeys(names, 0.0)
+    for _ in range(max(reps, 1)):
+        marks.clear()
+        once()
+        marks[-1].synchronize()
+        for i, k in enumerate(names):
+            ms[k] += marks[i].elapsed_time(marks[i + 1]) / max(reps, 1)
+    nb = pre_encode_bytes(n, T)
+    res = {k: {"shape": [n, 128, T], "ms": ms[k], "bytes": nb[k],
+               "gbs": nb[k] / (ms[k] * 1e-3) / 1e9} for k in names}
+    tot_ms, tot_b = sum(ms.values()), sum(nb.values())
+    res["pre_encode_stage"] = {"shape": [n, 128, T], "ms": tot_ms, "bytes": tot_b,
+                               "gbs": tot_b / (tot_ms * 1e-3) / 1e9,
+                               "frames_per_s": n * ((((T + 1) // 2 + 1) // 2 + 1) // 2) / (tot_ms * 1e-3)}
+    plan.close()
+    return res
 
 
 def aux_only(args, local_rank):
@@ -469,7 +552,8 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        aux = time_aux_kernels(stream, reps=args.aux_reps)
+        aux = time_aux_kernels(stream, reps=args.aux_reps, pre_utts=args.pre_utts,
+                               pre_only=args.pre_only)
     peak, peak_kind = measured_peak()
     print(json.dumps({"kernels_aux": {k: {**v, "frac": v["gbs"] / peak if v["gbs"] else None}
                                       for k, v in aux.items()},
@@ -578,7 +662,9 @@ def _ours(args, rank, world, local_rank, stream):
                     for k, v in table.items()},
         "kernels_aux": None if aux is None else {
             k: {"shape": v["shape"], "ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
-                "frac": round(v["gbs"] / peak, 3)} for k, v in aux.items()},
+                "frac": round(v["gbs"] / peak, 3),
+                **({"frames_per_s": round(v["frames_per_s"])} if "frames_per_s" in v else {})}
+            for k, v in aux.items()},
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,

@@ -23,131 +23,252 @@
 // utterance, as the encoder blocks take x.
 //
 // conv0's output (the largest tensor of the stage, 256 x 64 floats per two mel
-// frames) is never written: front_kernel computes it tile by tile in shared
-// memory and applies dw2 there.
+// frames) is never written: pre_front_kernel computes it row by row in
+// registers and feeds each value straight into the dw2 accumulators.
 #include "pk_common.cuh"
 
 namespace pk {
 
 constexpr int PRE_C = 256, PRE_MELS = 128;
-constexpr int PF_R2 = 4;                        // dw2 output rows per CTA
-constexpr int PF_S1 = 2 * PF_R2 + 1;            // conv0 rows they read
-constexpr int PF_MEL = 2 * PF_S1 + 1;           // mel frames those read
-constexpr int PF_CG = 8;                        // channels per pass
-constexpr int PF_THREADS = 256;
+constexpr int PF_R2 = 16;                       // dw2 output rows per CTA
+constexpr int PF_MEL = 4 * PF_R2 + 3;           // mel frames their conv0 rows read
+constexpr int PF_LD = 132;                      // float2 per staged frame: mel bin m at m + 4
+constexpr int PF_THREADS = 256;                 // 64 channel pairs x 4 column quarters
 
 __device__ __forceinline__ int half_up(int h) { return (h + 1) >> 1; }   // (h + 2 - 3) / 2 + 1
 
-// conv0 + bias + ReLU + dw2 + bias for dw2 rows [a, a + PF_R2) of one item.
-__global__ void __launch_bounds__(PF_THREADS)
-pre_front_kernel(const float *__restrict__ mel, const float *__restrict__ w0,
-                 const float *__restrict__ b0, const float *__restrict__ w2,
-                 const float *__restrict__ b2, float *__restrict__ s2d, SeqDev seq_mel,
+__device__ __forceinline__ float relu1(float v) { return v < 0.0f ? 0.0f : v; }
+
+// One conv0 output row (staged-frame row pair 2 li .. 2 li + 2), + bias,
+// ReLU, for this thread's channel pair and column quarter q, each value fed at
+// once to the dw2 accumulators of that quarter (dw2 columns 8q .. 8q + 7):
+//   MODE 1: row 2 oh      -> tap row kh = 1 of dw2 row oh (A)
+//   MODE 2: row 2 oh + 1  -> kh = 2 of row oh (A) and kh = 0 of row oh + 1 (B)
+// Quarter q produces conv0 columns 16q - 1 .. 16q + 15 (column -1 does not
+// exist). Columns are visited left to right and rows top to bottom, so every
+// output's taps arrive in the reference's (kh, kw) order. With EDGE, tap rows
+// outside the mel frames are skipped as the reference skips them.
+template <int MODE, bool EDGE>
+__device__ __forceinline__ void pf_row(const float2 (*__restrict__ tile)[PF_LD], int li, int t0,
+                                       int T, int q, const float2 (&w0)[9], float2 b0,
+                                       const float2 (&w2)[9], float2 (&A)[8], float2 (&B)[8]) {
+  bool ok[3];
+  float2 cm[3], c0[3], c1[3];
+#pragma unroll
+  for (int kh = 0; kh < 3; kh++) {
+    const int t = t0 + 2 * li + kh;
+    ok[kh] = !EDGE || (t >= 0 && t < T);
+    const float2 *row = tile[2 * li + kh];
+    cm[kh] = row[32 * q + 1];                                          // mel bin 32q - 3
+    const float4 v = *reinterpret_cast<const float4 *>(row + 32 * q + 2);   // bins 32q - 2, 32q - 1
+    c0[kh] = make_float2(v.x, v.y);
+    c1[kh] = make_float2(v.z, v.w);
+  }
+  constexpr int KA = MODE == 1 ? 3 : 6;   // tap row of A
+#pragma unroll
+  for (int u = 0; u < 17; u++) {
+    if (u > 0 || q > 0) {                 // conv0 column w1 = 16q - 1 + u exists
+      float2 s = b0;
+#pragma unroll
+      for (int kh = 0; kh < 3; kh++) {
+        if (!ok[kh]) continue;
+        if (u != 1 || q > 0) s = fma2(cm[kh], w0[kh * 3 + 0], s);   // mel bin 2 w1 - 1 >= 0
+        s = fma2(c0[kh], w0[kh * 3 + 1], s);
+        s = fma2(c1[kh], w0[kh * 3 + 2], s);
+      }
+      s = make_float2(relu1(s.x), relu1(s.y));
+      const int v = u - 1;                // column within the quarter's 16
+      if (v >= 0 && (v & 1) == 0) {       // even: kw = 1 of dw2 column v / 2
+        A[v / 2] = fma2(s, w2[KA + 1], A[v / 2]);
+        if (MODE == 2) B[v / 2] = fma2(s, w2[1], B[v / 2]);
+      } else {                            // odd: kw = 2 of (v - 1) / 2, kw = 0 of (v + 1) / 2
+        if (v >= 1) {
+          A[(v - 1) / 2] = fma2(s, w2[KA + 2], A[(v - 1) / 2]);
+          if (MODE == 2) B[(v - 1) / 2] = fma2(s, w2[2], B[(v - 1) / 2]);
+        }
+        if (v + 1 < 16) {
+          A[(v + 1) / 2] = fma2(s, w2[KA + 0], A[(v + 1) / 2]);
+          if (MODE == 2) B[(v + 1) / 2] = fma2(s, w2[0], B[(v + 1) / 2]);
+        }
+      }
+    }
+    if (u + 1 < 17) {                     // slide to column w1 + 1: bins 2 w1 + 2, 2 w1 + 3
+#pragma unroll
+      for (int kh = 0; kh < 3; kh++) {
+        cm[kh] = c1[kh];
+        const float4 v =
+            *reinterpret_cast<const float4 *>(tile[2 * li + kh] + 32 * q + 2 * u + 4);
+        c0[kh] = make_float2(v.x, v.y);
+        c1[kh] = make_float2(v.z, v.w);
+      }
+    }
+  }
+}
+
+constexpr int PF_SLD = 36;   // floats per channel row of the output stage (32 + pad)
+constexpr size_t PF_SMEM = sizeof(float2) * PF_MEL * PF_LD + sizeof(float) * 128 * PF_SLD;
+
+// dw2 row oh of this CTA's 128 channels, written through the shared stage so
+// that every 8 lanes store one whole 128-byte channel row: a thread's own
+// outputs (8 columns x 2 channels) would otherwise be 32 scattered 16-byte
+// pieces per warp store.
+__device__ __forceinline__ void pf_store(float *__restrict__ stage, float *__restrict__ s2d,
+                                         long long P2, long long col0, int q, int cp,
+                                         const float2 (&acc)[8]) {
+  __syncthreads();   // the previous row's copy-out has read the stage
+  float *r0 = stage + cp * PF_SLD + 8 * q, *r1 = stage + (64 + cp) * PF_SLD + 8 * q;
+  *reinterpret_cast<float4 *>(r0) = make_float4(acc[0].x, acc[1].x, acc[2].x, acc[3].x);
+  *reinterpret_cast<float4 *>(r0 + 4) = make_float4(acc[4].x, acc[5].x, acc[6].x, acc[7].x);
+  *reinterpret_cast<float4 *>(r1) = make_float4(acc[0].y, acc[1].y, acc[2].y, acc[3].y);
+  *reinterpret_cast<float4 *>(r1 + 4) = make_float4(acc[4].y, acc[5].y, acc[6].y, acc[7].y);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int e = threadIdx.x + i * PF_THREADS, r = e >> 3, j = e & 7;
+    const int c = (r < 64 ? 0 : 64) + 64 * blockIdx.z + r;   // stage row r -> channel
+    st4(s2d + (long long)c * P2 + col0 + 4 * j,
+        *reinterpret_cast<const float4 *>(stage + r * PF_SLD + 4 * j));
+  }
+}
+
+// conv0 rows 2a - 1 .. 2(a + nrows) - 1 in order: odd rows finish the previous
+// dw2 row and start the next, even rows add the middle tap row.
+template <bool EDGE>
+__device__ __forceinline__ void pf_tile(const float2 (*__restrict__ tile)[PF_LD], int a, int nrows,
+                                        int T, int H1, int q, const float2 (&w0)[9], float2 b0,
+                                        const float2 (&w2)[9], float2 b2, float *__restrict__ stage,
+                                        float *__restrict__ s2d, long long P2, long long q0,
+                                        int cp) {
+  const int t0 = 4 * a - 3;
+  float2 prev[8], cur[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) prev[j] = b2;
+  for (int k = 0; k <= nrows; k++) {
+    const int oh = a + k;
+#pragma unroll
+    for (int j = 0; j < 8; j++) cur[j] = b2;
+    if (!EDGE || (2 * oh - 1 >= 0 && 2 * oh - 1 < H1))
+      pf_row<2, EDGE>(tile, 2 * k, t0, T, q, w0, b0, w2, prev, cur);
+    if (k < nrows) pf_row<1, EDGE>(tile, 2 * k + 1, t0, T, q, w0, b0, w2, cur, cur);
+    if (k > 0) pf_store(stage, s2d, P2, q0 + 32LL * (oh - 1), q, cp, prev);
+#pragma unroll
+    for (int j = 0; j < 8; j++) prev[j] = cur[j];
+  }
+}
+
+// conv0 (1 -> 256, 3x3 stride 2) + bias + ReLU + dw2 (depthwise 3x3 stride 2)
+// + bias for dw2 rows [a, a + PF_R2) of one item and channels c, c + 128 for
+// c in [64 z, 64 z + 64) (z = blockIdx.z). conv0's output never leaves
+// registers. Thread = (column quarter, channel pair c, c + 128): warps 2q and
+// 2q + 1 take quarter q, so every lane of a warp reads the same staged mel
+// value (a shared-memory broadcast) and the pair shares it through
+// fma.rn.f32x2. Staged frames hold each mel bin twice (v, v) for that.
+__global__ void __launch_bounds__(PF_THREADS, 2)
+pre_front_kernel(const float *__restrict__ mel, const float *__restrict__ w0g,
+                 const float *__restrict__ b0g, const float *__restrict__ w2g,
+                 const float *__restrict__ b2g, float *__restrict__ s2d, SeqDev seq_mel,
                  SeqDev seq2, long long P2) {
-  __shared__ float tile[PF_MEL][PRE_MELS];
-  __shared__ float s1[PF_CG][PF_S1][64];
+  extern __shared__ float4 pf_smem4[];
+  float2 (*tile)[PF_LD] = reinterpret_cast<float2 (*)[PF_LD]>(pf_smem4);
+  float *stage = reinterpret_cast<float *>(tile + PF_MEL);
   const int item = blockIdx.y;
   const int T = seq_T(seq_mel, item);
   const int H1 = half_up(T), H2 = half_up(H1);
   const int a = blockIdx.x * PF_R2;
   if (a >= H2) return;
+  const int nrows = min(PF_R2, H2 - a);
   const long long mel0 = seq_frame_off(seq_mel, item) * PRE_MELS;   // item's [128, T] block
   const long long q0 = seq_frame_off(seq2, item) * 32;              // item's first s2d column
-  // mel frames t = 4a - 3 + j, j < PF_MEL, transposed into tile[j][m]
   const int t0 = 4 * a - 3;
-  for (int e = threadIdx.x; e < PF_MEL * PRE_MELS; e += PF_THREADS) {
-    const int m = e / PF_MEL, j = e - m * PF_MEL;
-    const int t = t0 + j;
-    tile[j][m] = (t >= 0 && t < T) ? __ldg(mel + mel0 + (long long)m * T + t) : 0.0f;
-  }
-  const int r1_0 = 2 * a - 1;   // conv0 row of s1[.][0]
-  for (int cg = 0; cg < PRE_C; cg += PF_CG) {
-    __syncthreads();   // tile loaded / previous pass's s1 consumed
-    for (int e = threadIdx.x; e < PF_CG * PF_S1 * 64; e += PF_THREADS) {
-      const int w1 = e & 63, i = (e >> 6) % PF_S1, cl = e / (64 * PF_S1);
-      const int c = cg + cl, r1 = r1_0 + i;
-      if (r1 < 0 || r1 >= H1) continue;   // never read below
-      const float *wc = w0 + c * 9;
-      float val = __ldg(b0 + c);
+  constexpr int BATCH = 5;   // loads in flight per thread
+  for (int e0 = threadIdx.x; e0 < PF_MEL * PRE_MELS; e0 += BATCH * PF_THREADS) {
+    float v[BATCH];
 #pragma unroll
-      for (int kh = 0; kh < 3; kh++) {
-        const int t = 2 * r1 - 1 + kh;   // tile row 2i + kh
-        if (t < 0 || t >= T) continue;
-#pragma unroll
-        for (int kw = 0; kw < 3; kw++) {
-          const int m = 2 * w1 - 1 + kw;
-          if (m >= 0 && m < PRE_MELS) val = fmaf(tile[2 * i + kh][m], __ldg(wc + kh * 3 + kw), val);
-        }
-      }
-      s1[cl][i][w1] = val < 0.0f ? 0.0f : val;
+    for (int b = 0; b < BATCH; b++) {
+      const int e = e0 + b * PF_THREADS, m = e / PF_MEL, t = t0 + e - m * PF_MEL;
+      v[b] = (e < PF_MEL * PRE_MELS && t >= 0 && t < T)
+                 ? __ldg(mel + mel0 + (long long)m * T + t) : 0.0f;
     }
-    __syncthreads();
-    for (int e = threadIdx.x; e < PF_CG * PF_R2 * 32; e += PF_THREADS) {
-      const int ow = e & 31, r = (e >> 5) % PF_R2, cl = e / (32 * PF_R2);
-      const int c = cg + cl, oh = a + r;
-      if (oh >= H2) continue;
-      const float *wc = w2 + c * 9;
-      float val = __ldg(b2 + c);
 #pragma unroll
-      for (int kh = 0; kh < 3; kh++) {
-        const int r1 = 2 * oh - 1 + kh;   // s1 row 2r + kh
-        if (r1 < 0 || r1 >= H1) continue;
-#pragma unroll
-        for (int kw = 0; kw < 3; kw++) {
-          const int w1 = 2 * ow - 1 + kw;
-          if (w1 >= 0 && w1 < 64) val = fmaf(s1[cl][2 * r + kh][w1], __ldg(wc + kh * 3 + kw), val);
-        }
-      }
-      s2d[(long long)c * P2 + q0 + oh * 32 + ow] = val;
+    for (int b = 0; b < BATCH; b++) {
+      const int e = e0 + b * PF_THREADS, m = e / PF_MEL;
+      if (e < PF_MEL * PRE_MELS) tile[e - m * PF_MEL][m + 4] = make_float2(v[b], v[b]);
     }
   }
-}
-
-// The item holding global row g of a sequence of per-item row counts.
-__device__ __forceinline__ int seq_item_of(const SeqDev &s, long long g) {
-  if (s.uniform_T > 0) return (int)(g / s.uniform_T);
-  int lo = 0, hi = s.n_items;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (__ldg(s.frame_off + mid) <= g) lo = mid; else hi = mid;
+  const int warp = threadIdx.x >> 5, q = warp >> 1;
+  const int cp = (warp & 1) * 32 + (threadIdx.x & 31);   // channel pair within the CTA
+  const int c_lo = 64 * blockIdx.z + cp, c_hi = c_lo + 128;
+  float2 w0[9], w2[9];
+#pragma unroll
+  for (int k = 0; k < 9; k++) {
+    w0[k] = make_float2(__ldg(w0g + c_lo * 9 + k), __ldg(w0g + c_hi * 9 + k));
+    w2[k] = make_float2(__ldg(w2g + c_lo * 9 + k), __ldg(w2g + c_hi * 9 + k));
   }
-  return lo;
+  const float2 b0 = make_float2(__ldg(b0g + c_lo), __ldg(b0g + c_hi));
+  const float2 b2 = make_float2(__ldg(b2g + c_lo), __ldg(b2g + c_hi));
+  __syncthreads();
+  if (a == 0 || 4 * (a + nrows) > T)
+    pf_tile<true>(tile, a, nrows, T, H1, q, w0, b0, w2, b2, stage, s2d, P2, q0, cp);
+  else
+    pf_tile<false>(tile, a, nrows, T, H1, q, w0, b0, w2, b2, stage, s2d, P2, q0, cp);
 }
 
-// s3d[c, 16 g3 + ow] = b5[c] + taps of relu(y2 + b3) (dw5 on the pw1 output):
-// one output per thread.
+constexpr int P5_R3 = 64;                  // dw5 output rows per CTA
+constexpr int P5_IN = 2 * P5_R3 + 1;       // input rows they read
+constexpr int P5_LD = 40;                  // floats per staged row: even columns, odd columns, pad
+
+// s3d[c, item, oh, ow] = b5[c] + taps of relu(y2 + b3[c]) (dw5 applied to the
+// pw1 product): one CTA per (64 output rows, channel, item). The input rows
+// are contiguous in y2's channel row, so they are staged with coalesced
+// 16-byte loads (bias + ReLU applied once per element), split into even and
+// odd columns; with a row pitch of 40 floats the two output rows a warp
+// computes read disjoint bank halves.
 __global__ void __launch_bounds__(256)
 pre_dw5_kernel(const float *__restrict__ y2, const float *__restrict__ b3,
                const float *__restrict__ w5, const float *__restrict__ b5, float *__restrict__ s3d,
                SeqDev seq2, SeqDev seq3, long long P2, long long P3) {
-  const long long n = (long long)PRE_C * P3;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(e / P3);
-    const long long q = e - (long long)c * P3;
-    const long long g3 = q >> 4;
-    const int ow = (int)(q & 15);
-    const int item = seq_item_of(seq3, g3);
-    const int oh = (int)(g3 - seq_frame_off(seq3, item));
-    const int H2 = seq_T(seq2, item);
-    const float *yc = y2 + (long long)c * P2 + seq_frame_off(seq2, item) * 32;
-    const float bc = __ldg(b3 + c);
-    const float *wc = w5 + c * 9;
-    float val = __ldg(b5 + c);
+  __shared__ __align__(16) float tile[P5_IN * P5_LD];
+  const int c = blockIdx.y, item = blockIdx.z;
+  const int H2 = seq_T(seq2, item), H3 = seq_T(seq3, item);
+  const int o0 = blockIdx.x * P5_R3;
+  if (o0 >= H3) return;
+  const int nout = min(P5_R3, H3 - o0);
+  const int r0 = 2 * o0 - 1;                                 // input row of staged row 0
+  const int rlo = max(r0, 0), rhi = min(2 * (o0 + nout) - 1, H2 - 1);
+  const float *src = y2 + (long long)c * P2 + seq_frame_off(seq2, item) * 32;
+  const float bc = __ldg(b3 + c);
+  // 8 lanes per 128-byte row; a warp stages rows R, R+2, R+1, R+3 (lane groups
+  // 0..3) so that each half-warp's 8-byte stores cover all 32 banks.
+  const int n4 = ((rhi - rlo + 4) >> 2) * 32;
+  for (int e = threadIdx.x; e < n4; e += 256) {
+    const int sub = (e >> 3) & 3, k = e & 7;
+    const int r = rlo + 4 * (e >> 5) + ((sub & 1) << 1) + (sub >> 1);
+    if (r > rhi) continue;
+    float4 v = ldg4_stream(src + (long long)r * 32 + 4 * k);
+    v = make_float4(relu1(v.x + bc), relu1(v.y + bc), relu1(v.z + bc), relu1(v.w + bc));
+    float *row = tile + (r - r0) * P5_LD;
+    *reinterpret_cast<float2 *>(row + 2 * k) = make_float2(v.x, v.z);        // columns 4k, 4k+2
+    *reinterpret_cast<float2 *>(row + 16 + 2 * k) = make_float2(v.y, v.w);   // columns 4k+1, 4k+3
+  }
+  float w[9];
+#pragma unroll
+  for (int k = 0; k < 9; k++) w[k] = __ldg(w5 + c * 9 + k);
+  const float bias = __ldg(b5 + c);
+  __syncthreads();
+  float *dst = s3d + (long long)c * P3 + (seq_frame_off(seq3, item) + o0) * 16;
+  for (int o = threadIdx.x; o < nout * 16; o += 256) {
+    const int ol = o >> 4, ow = o & 15, oh = o0 + ol;
+    float val = bias;
 #pragma unroll
     for (int kh = 0; kh < 3; kh++) {
-      const int r2 = 2 * oh - 1 + kh;
-      if (r2 < 0 || r2 >= H2) continue;
-#pragma unroll
-      for (int kw = 0; kw < 3; kw++) {
-        const int w2 = 2 * ow - 1 + kw;
-        if (w2 < 0 || w2 >= 32) continue;
-        float v = __ldg(yc + r2 * 32 + w2) + bc;
-        v = v < 0.0f ? 0.0f : v;
-        val = fmaf(v, __ldg(wc + kh * 3 + kw), val);
-      }
+      const int r = 2 * oh - 1 + kh;
+      if (r < 0 || r >= H2) continue;
+      const float *row = tile + (2 * ol + kh) * P5_LD;
+      if (ow > 0) val = fmaf(row[16 + ow - 1], w[kh * 3 + 0], val);   // column 2 ow - 1
+      val = fmaf(row[ow], w[kh * 3 + 1], val);                        // column 2 ow
+      val = fmaf(row[16 + ow], w[kh * 3 + 2], val);                   // column 2 ow + 1
     }
-    s3d[e] = val;
+    dst[o] = val;
   }
 }
 
@@ -261,18 +382,23 @@ extern "C" int pkcu_pre_encode(const float *mel, const pkcu_pre_params *prm,
                          go->pw1, go->pw2, go->proj, gi->s2d, gi->s3d, gi->flat};
   for (const float *q : need)
     if (!q) return pkcu_fail(PKCU_ERR_ARG, "pkcu_pre_encode: NULL parameter or buffer");
-  if (!PK_ALIGNED16(go->pw2) || !PK_ALIGNED16(go->proj) || !PK_ALIGNED16(gi->flat) ||
-      !PK_ALIGNED16(x) || !PK_ALIGNED16(prm->out_b))
-    return pkcu_fail(PKCU_ERR_ARG, "pkcu_pre_encode: pw2, proj, flat, x, out_b must be 16-byte aligned");
+  if (!PK_ALIGNED16(go->pw1) || !PK_ALIGNED16(go->pw2) || !PK_ALIGNED16(go->proj) ||
+      !PK_ALIGNED16(gi->s2d) || !PK_ALIGNED16(gi->flat) || !PK_ALIGNED16(x) ||
+      !PK_ALIGNED16(prm->out_b))
+    return pkcu_fail(PKCU_ERR_ARG,
+                     "pkcu_pre_encode: pw1, pw2, proj, s2d, flat, x, out_b must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   const SeqDev sm = plan->mel->dev, s2 = plan->rows2->dev, s3 = plan->rows3->dev;
   const unsigned tiles = (unsigned)((s2.max_T + PF_R2 - 1) / PF_R2);
-  pre_front_kernel<<<dim3(tiles, (unsigned)sm.n_items), PF_THREADS, 0, s>>>(
+  static int optin[64];
+  smem_optin(pre_front_kernel, PF_SMEM, optin);
+  pre_front_kernel<<<dim3(tiles, (unsigned)sm.n_items, 2), PF_THREADS, PF_SMEM, s>>>(
       mel, prm->conv0_w, prm->conv0_b, prm->conv2_w, prm->conv2_b, gi->s2d, sm, s2, plan->P2);
   int st = pkcu_launch_status("pkcu_pre_encode: conv0 + dw2");
   if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_PRE_PW1, stream);
   if (st) return st;
-  pre_dw5_kernel<<<flat_grid((long long)PRE_C * plan->P3), 256, 0, s>>>(
+  const unsigned tiles3 = (unsigned)((s3.max_T + P5_R3 - 1) / P5_R3);
+  pre_dw5_kernel<<<dim3(tiles3, PRE_C, (unsigned)s3.n_items), 256, 0, s>>>(
       go->pw1, prm->conv3_b, prm->conv5_w, prm->conv5_b, gi->s3d, s2, s3, plan->P2, plan->P3);
   st = pkcu_launch_status("pkcu_pre_encode: dw5");
   if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_PRE_PW2, stream);
