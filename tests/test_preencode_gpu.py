@@ -63,10 +63,11 @@ def make_items(lengths, seed):
     return params, items
 
 
-def run_gpu(cuda, lengths, params, items, hook=None):
+def run_gpu(cuda, lengths, params, items, hook=None, params_on_device=False):
+    """params: host arrays, or device addresses with params_on_device."""
     L = PreLayout(lengths)
     mel = dev(np.concatenate([m.reshape(-1) for _, m in items]))
-    pd = {k: dev(v) for k, v in params.items()}
+    pd = dict(params) if params_on_device else {k: dev(v) for k, v in params.items()}
     gout = {"pw1": dev(np.concatenate([si["y2"] for si, _ in items], axis=1)),
             "pw2": dev(np.concatenate([si["y3"] for si, _ in items], axis=1)),
             "proj": dev(np.concatenate([si["proj"] for si, _ in items]))}

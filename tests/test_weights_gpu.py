@@ -9,6 +9,8 @@ views) on files in the reference's format.
     the restatement of its int4 branch (:488-544) for int4 q/k/v;
   * the block parameters the loader hands out drive pkcu_encoder_nongemm to
     the same result as the restatement given the file's parameters."""
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -123,3 +125,23 @@ def test_block_params_drive_the_encoder_sequence(cuda, oracle, ckpt_i8):
             got = host(xd)
     want, _ = oracle.conformer_block(x, wf.block_params(tensors, 1), si)
     assert_close(got, want, "x after block 1")
+
+
+def test_pre_params_drive_the_pre_encode_stage(cuda, oracle, ckpt_i8):
+    """pkcu_weights_pre_params: the pre-encode parameters from the loader drive
+    pkcu_pre_encode to the restatement's result given the file's values."""
+    from test_preencode_gpu import make_items, run_gpu
+    tensors = ckpt_i8[0]
+    params = wf.pre_params(tensors)
+    lengths = [37, 8]
+    _, items = make_items(lengths, seed=12)
+    with cuda.Weights(ckpt_i8[1], ckpt_i8[2]) as w:
+        w.upload(cuda.stream_handle())
+        pp = cuda.PreParams()
+        cuda.call("pkcu_weights_pre_params", w.h, C.byref(pp))
+        dev_params = {f: getattr(pp, f) for f in cuda.PRE_PARAM_FIELDS}
+        L, got = run_gpu(cuda, lengths, dev_params, items, params_on_device=True)
+    for i, (si, mel) in enumerate(items):
+        xo, caps = oracle.pre_encode(mel, params, si)
+        assert_bitexact(L.rows(got["x"], i, D), xo, f"x item {i}")
+        assert_bitexact(L.plane(got["s2d"], i, 2), caps["s2d"], f"s2d item {i}")

@@ -45,6 +45,14 @@ MATRICES = {"self_attn.linear_q.weight": (D, D), "self_attn.linear_k.weight": (D
             "feed_forward2.linear2.weight": (FF, D)}
 
 
+# pre-encode parameters the non-GEMM stage takes (csrc/weights.c:310-321), by role
+PRE_NAMES = {"conv0_w": "pre_encode.conv.0.weight", "conv0_b": "pre_encode.conv.0.bias",
+             "conv2_w": "pre_encode.conv.2.weight", "conv2_b": "pre_encode.conv.2.bias",
+             "conv3_b": "pre_encode.conv.3.bias", "conv5_w": "pre_encode.conv.5.weight",
+             "conv5_b": "pre_encode.conv.5.bias", "conv6_b": "pre_encode.conv.6.bias",
+             "out_b": "pre_encode.out.bias"}
+
+
 def pack_int4(q: np.ndarray) -> np.ndarray:
     """[K, N] values in [-8, 7] -> [K, N/2] bytes, even column in the low nibble."""
     return ((q[:, 0::2] & 0x0F) | ((q[:, 1::2] & 0x0F) << 4)).astype(np.uint8)
@@ -53,6 +61,10 @@ def pack_int4(q: np.ndarray) -> np.ndarray:
 def make_tensors(rng, n_blocks: int, attn: str, ff: str) -> dict:
     """{name: {"data": array, "scale": float | None, "scales": array | None}}."""
     t = {}
+    for role, nm in PRE_NAMES.items():
+        shape = (256, 1, 3, 3) if role.endswith("_w") else (D if role == "out_b" else 256,)
+        t[nm] = {"data": (0.3 * rng.standard_normal(shape)).astype(np.float32), "scale": None,
+                 "scales": None}
     for b in range(n_blocks):
         for role, nm in ROLE_NAMES.items():
             shape = ROLE_SHAPES.get(role, (D,))
@@ -133,3 +145,8 @@ def block_params(tensors: dict, b: int) -> dict:
     p["qkv_b"] = np.concatenate(
         [tensors[f"layers.{b}.self_attn.linear_{m}.bias"]["data"] for m in QKV])
     return p
+
+
+def pre_params(tensors: dict) -> dict:
+    """The pre-encode stage's parameters (the restatement's roles)."""
+    return {role: tensors[nm]["data"] for role, nm in PRE_NAMES.items()}
