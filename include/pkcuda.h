@@ -389,6 +389,58 @@ int pkcu_pre_encode(const float *mel, const pkcu_pre_params *params,
                     float *x, const pkcu_pre_plan *plan, pkcu_gemm_hook hook, void *hook_user,
                     pkcu_stream_t stream);
 
+/* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────
+ * Replaces pk_greedy_decode for a batch of utterances (the encoder outputs of
+ * n_utts utterances of T_b frames, frames of every utterance in turn). Every
+ * utterance goes through the reference's own sequence -- a decoder step on
+ * blank, then per frame up to 10 x { joint, first-maximum argmax; blank ->
+ * next frame; else emit the token and run a decoder step } -- one joint
+ * evaluation per utterance per iteration. The non-GEMM work (embedding rows,
+ * LSTM cells csrc/tensor_ops.c:594-629, joint bias adds + add + ReLU
+ * csrc/decoder.c:38-76, bias + argmax, the state machine) runs as kernels;
+ * each matrix-vector product of the reference is a batched GEMM that the
+ * hook enqueues (block = -1, gemm = PKCU_GEMM_DEC_*), computed for every
+ * utterance's row: rows that do not need it ignore it. */
+typedef struct pkcu_decoder pkcu_decoder;
+typedef struct {
+    const float *embed;        /* [1025, 640] decoder.prediction.embed.weight (16-byte aligned) */
+    const float *lstm0_b;      /* [5120] decoder.lstm.0.B */
+    const float *lstm1_b;      /* [5120] decoder.lstm.1.B */
+    const float *joint_enc_b;  /* [640] (16-byte aligned) */
+    const float *joint_pred_b; /* [640] (16-byte aligned) */
+    const float *joint_out_b;  /* [1025] joint.joint_net.2.bias */
+} pkcu_dec_params;
+typedef struct {   /* products the hook writes, bias not added (device, owned by the decoder) */
+    float *enc;    /* [F, 640]   = encoder output [F, 1024] x joint.enc.weight   (DEC_ENC, once) */
+    float *pred;   /* [B, 640]   = h1 x joint.pred.weight                         (DEC_PRED) */
+    float *out;    /* [B, 1025]  = hidden x joint.out.weight                      (DEC_OUT) */
+    float *g0i, *g0r, *g1i, *g1r;   /* [B, 2560] = x0 W_i0^T, h0 W_r0^T, h0 W_i1^T, h1 W_r1^T */
+} pkcu_dec_gemm_outputs;
+typedef struct {   /* the products' inputs, written by the decode (device, owned by the decoder) */
+    float *x0;     /* [B, 640] embedding rows of the tokens whose decoder step is pending */
+    float *h0;     /* [B, 640] layer-0 hidden state: input of W_r0 (before its cell), of W_i1 (after) */
+    float *h1;     /* [B, 640] layer-1 hidden state: input of W_r1 (before), of joint.pred (after) */
+    float *hidden; /* [B, 640] joint hidden (zeros for finished utterances) */
+} pkcu_dec_gemm_inputs;
+enum { PKCU_GEMM_DEC_ENC = 32, PKCU_GEMM_DEC_L0_WI, PKCU_GEMM_DEC_L0_WR, PKCU_GEMM_DEC_L1_WI,
+       PKCU_GEMM_DEC_L1_WR, PKCU_GEMM_DEC_PRED, PKCU_GEMM_DEC_OUT };
+/* Device state and buffers for a batch of utterances of frames[b] >= 1 frames
+ * (B = n_utts, F = sum of frames). */
+int  pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder **out);
+void pkcu_decoder_destroy(pkcu_decoder *dec);
+int  pkcu_decoder_buffers(const pkcu_decoder *dec, pkcu_dec_gemm_outputs *gemm_out,
+                          pkcu_dec_gemm_inputs *gemm_in);
+/* Runs the decode to the end (the host polls the device every 8 iterations).
+ * Order per iteration: L0_WI, L0_WR, L1_WI, L1_WR, PRED, OUT hooks, with the
+ * kernels between them; DEC_ENC once before the first. */
+int  pkcu_greedy_decode(pkcu_decoder *dec, const pkcu_dec_params *params, pkcu_gemm_hook hook,
+                        void *hook_user, pkcu_stream_t stream);
+int  pkcu_decoder_iterations(const pkcu_decoder *dec);   /* of the last decode */
+/* Host copies (any may be NULL): n_tokens[B], evals[B] (joint evaluations per
+ * utterance), tokens[10 F] (utterance b's tokens start at 10 x its first frame). */
+int  pkcu_decoder_results(const pkcu_decoder *dec, int *n_tokens, int *evals, int *tokens,
+                          pkcu_stream_t stream);
+
 /* ── 4. weights: the reference checkpoint format on the device ─────────────
  * Replaces pk_load_weights / lookup_weight / pk_free_weights
  * (csrc/weights.c:240-402, 551-564) for a GPU engine: weights.bin +

@@ -79,4 +79,15 @@ int or_pre_encode(const float *mel, int T, const float *const *params, const flo
                   const float *y3, const float *proj, float *s2d_cap, float *s3d_cap,
                   float *flat_cap, float *x_out);
 
+/* Greedy RNN-T decode of one utterance (pk_oracle_decode.c), GEMM products as
+ * caller stand-ins. */
+enum { OR_DEC_ENC = 0, OR_DEC_PRED, OR_DEC_OUT, OR_DEC_L0_WI, OR_DEC_L0_WR, OR_DEC_L1_WI,
+       OR_DEC_L1_WR };
+typedef void (*or_dec_gemm_fn)(void *user, int gemm, int iter, const float *in, int n_in,
+                               float *out, int n_out);
+int or_greedy_decode(int T, const float *embed, const float *B0, const float *B1,
+                     const float *enc_b, const float *pred_b, const float *out_b,
+                     or_dec_gemm_fn gemm, void *user, int *tokens, int max_tokens,
+                     float *state, int *n_iters);
+
 #endif

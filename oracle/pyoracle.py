@@ -22,6 +22,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_ORACLE = os.path.join(HERE, "liboracle.so")
 LIB_REF = os.path.join(HERE, "_ref", "libpkref.so")
+LIB_REF_DEC = os.path.join(HERE, "_ref", "libpkref_dec.so")
 
 D, H, DH, FF = 1024, 8, 128, 4096
 
@@ -77,7 +78,16 @@ class _Lib:
             fn.argtypes = args
 
 
+# Greedy RNN-T decode: the products it consumes, in the numbering of
+# pk_oracle_decode.c / ref_dec_harness.c (OR_DEC_*).
+DEC_H, DEC_V, DEC_BLANK = 640, 1025, 1024
+DEC_PRODUCTS = ("enc", "pred", "out", "l0_wi", "l0_wr", "l1_wi", "l1_wr")
+DEC_PARAM_ROLES = ("embed", "B0", "B1", "enc_b", "pred_b", "out_b")
+DEC_GEMM_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_int, FP, C.c_int, FP, C.c_int)
+_DEC_ARGS = [C.c_int, FP, FP, FP, FP, FP, FP, DEC_GEMM_FN, C.c_void_p, I32P, C.c_int]
+
 _ORACLE_SIGS = {
+    "or_greedy_decode": (C.c_int, _DEC_ARGS + [FP, I32P]),
     "or_pre_out_frames": (C.c_int, [C.c_int]),
     "or_pre_encode": (C.c_int, [FP, C.c_int, FPP, FP, FP, FP, FP, FP, FP, FP]),
     "or_exp_poly": (C.c_float, [C.c_float]),
@@ -132,6 +142,18 @@ _REF_SIGS = {
 
 _oracle = None
 _ref = None
+_ref_dec = None
+
+
+def ref_dec_available() -> bool:
+    return os.path.exists(LIB_REF_DEC)
+
+
+def ref_dec_lib():
+    global _ref_dec
+    if _ref_dec is None:
+        _ref_dec = _Lib(LIB_REF_DEC, {"pkref_greedy_decode": (C.c_int, _DEC_ARGS + [I32P])}).lib
+    return _ref_dec
 
 
 def oracle_lib():
@@ -568,3 +590,72 @@ class Reference:
         rc = self.L.pkref_conformer_blocks(_fp(xx), T, 1, p, s, o, 1, FP())
         assert rc == 0
         return xx, caps
+
+
+# ── greedy RNN-T decode ─────────────────────────────────────────────────────
+
+def random_dec_params(rng):
+    """Seeded decoder parameters: embedding [1025, 640], LSTM biases B [5120]
+    per layer, joint biases (enc, pred [640], out [1025])."""
+    return {"embed": (0.5 * rng.standard_normal((DEC_V, DEC_H))).astype(np.float32),
+            "B0": (0.1 * rng.standard_normal(8 * DEC_H)).astype(np.float32),
+            "B1": (0.1 * rng.standard_normal(8 * DEC_H)).astype(np.float32),
+            "enc_b": (0.1 * rng.standard_normal(DEC_H)).astype(np.float32),
+            "pred_b": (0.1 * rng.standard_normal(DEC_H)).astype(np.float32),
+            "out_b": (0.1 * rng.standard_normal(DEC_V)).astype(np.float32)}
+
+
+def random_dec_products(rng, T: int, p_blank: float, max_iters: int | None = None):
+    """Stand-in products for one utterance of T frames: enc [T, 640] and, per
+    iteration, pred [640], out [1025] (the blank logit raised by 8 with
+    probability p_blank, so that blank wins), l{0,1}_w{i,r} [2560]."""
+    n = max_iters if max_iters is not None else 10 * T + 2
+    out = rng.standard_normal((n, DEC_V)).astype(np.float32)
+    out[rng.random(n) < p_blank, DEC_BLANK] += 8.0
+    return {"enc": rng.standard_normal((max(T, 1), DEC_H)).astype(np.float32),
+            "pred": rng.standard_normal((n, DEC_H)).astype(np.float32),
+            "out": out,
+            **{g: (0.5 * rng.standard_normal((n, 4 * DEC_H))).astype(np.float32)
+               for g in ("l0_wi", "l0_wr", "l1_wi", "l1_wr")}}
+
+
+class DecodeProducts:
+    """Serves stand-in products to a decode (table[name][iter] -> row; enc by
+    frame) and records the input each product was computed from
+    (inputs[name][iter])."""
+
+    def __init__(self, table: dict):
+        self.table = {DEC_PRODUCTS.index(k): np.ascontiguousarray(v, np.float32)
+                      for k, v in table.items()}
+        self.inputs = {k: {} for k in DEC_PRODUCTS}
+        self.fn = DEC_GEMM_FN(self._serve)
+
+    def _serve(self, user, g, it, inp, n_in, out, n_out):
+        row = self.table[g][it]
+        assert row.size == n_out, (DEC_PRODUCTS[g], row.size, n_out)
+        C.memmove(out, row.ctypes.data, 4 * n_out)
+        if n_in:
+            self.inputs[DEC_PRODUCTS[g]][it] = np.ctypeslib.as_array(inp, (n_in,)).copy()
+
+
+def _dec_call(fn, T, params, products, extra):
+    p = [f32(params[r]) for r in DEC_PARAM_ROLES]
+    cap = 10 * T + 1
+    tokens = np.zeros(cap, np.int32)
+    n_iters = C.c_int(0)
+    n = fn(T, *[_fp(a) for a in p], products.fn, None, tokens.ctypes.data_as(I32P), cap,
+           *extra, C.byref(n_iters))
+    assert n >= 0
+    return tokens[:n].copy(), n_iters.value
+
+
+def oracle_greedy_decode(T, params, products: DecodeProducts):
+    """The restatement: (tokens, joint evaluations, final state [h0, h1, c0, c1])."""
+    state = np.zeros(4 * DEC_H, np.float32)
+    tok, it = _dec_call(oracle_lib().or_greedy_decode, T, params, products, [_fp(state)])
+    return tok, it, state.reshape(4, DEC_H)
+
+
+def reference_greedy_decode(T, params, products: DecodeProducts):
+    """The reference's own pk_greedy_decode: (tokens, joint evaluations)."""
+    return _dec_call(ref_dec_lib().pkref_greedy_decode, T, params, products, [])

@@ -48,6 +48,8 @@ EXPORTED = (
     "pkcu_weights_fused_qkv", "pkcu_weights_block_params", "pkcu_weights_pre_params",
     "pkcu_pre_plan_create", "pkcu_pre_plan_destroy", "pkcu_pre_plan_p2", "pkcu_pre_plan_p3",
     "pkcu_pre_plan_frames", "pkcu_pre_plan_out_seq", "pkcu_pre_encode",
+    "pkcu_decoder_create", "pkcu_decoder_destroy", "pkcu_decoder_buffers", "pkcu_greedy_decode",
+    "pkcu_decoder_iterations", "pkcu_decoder_results",
 )
 
 
@@ -78,6 +80,12 @@ _SIGS = {
     "pkcu_pre_plan_frames": (LL, [VP]),
     "pkcu_pre_plan_out_seq": (VP, [VP]),
     "pkcu_pre_encode": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP]),
+    "pkcu_decoder_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
+    "pkcu_decoder_destroy": (None, [VP]),
+    "pkcu_decoder_buffers": (I, [VP, VP, VP]),
+    "pkcu_greedy_decode": (I, [VP, VP, VP, VP, VP]),
+    "pkcu_decoder_iterations": (I, [VP]),
+    "pkcu_decoder_results": (I, [VP, VP, VP, VP, VP]),
     "pkcu_last_error": (C.c_char_p, []),
     "pkcu_version": (C.c_char_p, []),
     "pkcu_selftest": (I, [C.POINTER(C.c_ulonglong)]),
@@ -493,3 +501,77 @@ def pre_encode(mel, params, gout, gin, x, plan: PrePlan, hook=None, stream=None)
     call("pkcu_pre_encode", mel if isinstance(mel, int) else ptr(mel), C.byref(p), C.byref(go),
          C.byref(gi), x if isinstance(x, int) else ptr(x), plan.handle,
          C.cast(hook, VP) if hook is not None else None, None, stream_handle(stream))
+
+
+# ── batched greedy RNN-T decode (pkcu_greedy_decode) ────────────────────────
+DEC_PARAM_FIELDS = ("embed", "lstm0_b", "lstm1_b", "joint_enc_b", "joint_pred_b", "joint_out_b")
+DEC_OUT_FIELDS = ("enc", "pred", "out", "g0i", "g0r", "g1i", "g1r")
+DEC_IN_FIELDS = ("x0", "h0", "h1", "hidden")
+(PKCU_GEMM_DEC_ENC, PKCU_GEMM_DEC_L0_WI, PKCU_GEMM_DEC_L0_WR, PKCU_GEMM_DEC_L1_WI,
+ PKCU_GEMM_DEC_L1_WR, PKCU_GEMM_DEC_PRED, PKCU_GEMM_DEC_OUT) = range(32, 39)
+
+
+class DecParams(C.Structure):
+    _fields_ = [(f, VP) for f in DEC_PARAM_FIELDS]
+
+
+class DecGemmOutputs(C.Structure):
+    _fields_ = [(f, VP) for f in DEC_OUT_FIELDS]
+
+
+class DecGemmInputs(C.Structure):
+    _fields_ = [(f, VP) for f in DEC_IN_FIELDS]
+
+
+class Decoder:
+    """pkcu_decoder: device state for a batch of utterances of frames[b] frames."""
+
+    def __init__(self, frames):
+        self.frames = [int(t) for t in frames]
+        arr = (I * len(self.frames))(*self.frames)
+        h = VP()
+        check(lib().pkcu_decoder_create(arr, len(self.frames), C.byref(h)), "pkcu_decoder_create")
+        self.handle = h
+        go, gi = DecGemmOutputs(), DecGemmInputs()
+        call("pkcu_decoder_buffers", self.handle, C.byref(go), C.byref(gi))
+        self.gemm_out = {f: getattr(go, f) for f in DEC_OUT_FIELDS}
+        self.gemm_in = {f: getattr(gi, f) for f in DEC_IN_FIELDS}
+
+    def decode(self, params, hook=None, stream=None) -> None:
+        """params: {field: tensor or address}; hook: a GEMM_HOOK or None."""
+        p = _struct(DecParams, DEC_PARAM_FIELDS, params)
+        call("pkcu_greedy_decode", self.handle, C.byref(p),
+             C.cast(hook, VP) if hook is not None else None, None, stream_handle(stream))
+
+    @property
+    def iterations(self) -> int:
+        return lib().pkcu_decoder_iterations(self.handle)
+
+    def results(self):
+        """(n_tokens [B], evals [B], tokens per utterance as lists)."""
+        import numpy as np
+        B, F = len(self.frames), sum(self.frames)
+        n = np.zeros(B, np.int32)
+        ev = np.zeros(B, np.int32)
+        tok = np.zeros(10 * F, np.int32)
+        call("pkcu_decoder_results", self.handle, n.ctypes.data, ev.ctypes.data, tok.ctypes.data,
+             None)
+        off = np.concatenate([[0], np.cumsum(self.frames)]) * 10
+        return n, ev, [tok[off[b]:off[b] + n[b]].copy() for b in range(B)]
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_decoder_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

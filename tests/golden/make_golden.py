@@ -127,6 +127,26 @@ def main():
     for k, v in caps.items():
         g["pre_cap_" + k] = v
 
+    rng = np.random.default_rng(1011)  # greedy RNN-T decode, T = 6 frames, p_blank 0.5
+    # Values on a 1/64 grid keep the fixture compressible; only the embedding
+    # rows the decode reads (blank + emitted tokens) and the product rows of
+    # the iterations it ran are stored (the rest is zero / unused).
+    def grid(a):
+        return (np.round(a * 64) / 64).astype(np.float32)
+    params = {k: grid(v) for k, v in po.random_dec_params(rng).items()}
+    table = {k: grid(v) for k, v in po.random_dec_products(rng, 6, 0.5).items()}
+    prod = po.DecodeProducts(table)
+    tok, iters = po.reference_greedy_decode(6, params, prod)
+    rows = np.unique(np.concatenate([[po.DEC_BLANK], tok])).astype(np.int32)
+    g["dec_embed_rows"], g["dec_embed"] = rows, params["embed"][rows]
+    for k in ("B0", "B1", "enc_b", "pred_b", "out_b"):
+        g["dec_p_" + k] = params[k]
+    for k, v in table.items():
+        g["dec_t_" + k] = v if k == "enc" else v[:iters + 1]
+    g["dec_tokens"], g["dec_iters"] = tok.astype(np.int32), np.array([iters], np.int32)
+    g["dec_hidden"] = np.stack([prod.inputs["out"][k] for k in range(iters)])
+    g["dec_h1"] = np.stack([prod.inputs["pred"][k] for k in range(iters)])
+
     np.savez_compressed(OUT, **g)
     print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT) / 1e6:.2f} MB")
 

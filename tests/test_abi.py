@@ -126,3 +126,15 @@ def test_pre_plan_sizes_and_validation(L):
     assert L.pkcu_pre_plan_create(arr, 0, C.byref(h2)) == 1
     assert L.pkcu_pre_encode(None, None, None, None, None, None, None, None, None) == 1
     assert b"pkcu_pre_encode" in L.pkcu_last_error()
+
+
+def test_decoder_validation(L):
+    """pkcu_decoder_create / pkcu_greedy_decode reject bad arguments before any
+    CUDA call (utterances need at least one frame)."""
+    h = C.c_void_p()
+    bad = (C.c_int * 3)(4, 0, 9)
+    assert L.pkcu_decoder_create(bad, 3, C.byref(h)) == 1 and not h.value
+    assert b"utterance 1" in L.pkcu_last_error()
+    assert L.pkcu_decoder_create(bad, 0, C.byref(h)) == 1
+    assert L.pkcu_greedy_decode(None, None, None, None, None) == 1
+    assert L.pkcu_decoder_iterations(None) == -1

@@ -1,0 +1,134 @@
+"""GPU parity of the batched greedy RNN-T decode (pkcu_greedy_decode) against
+the restatement of csrc/decoder.c:80-132 (pinned to the reference's own
+pk_greedy_decode on the CPU).
+
+The matrix-vector products are stand-ins: each utterance has a seeded table of
+products (pyoracle.random_dec_products), and the test's GEMM hook writes row b
+of every batched product from utterance b's table at the current iteration.
+The restatement replays each utterance alone with the same table, so the two
+decodes see the same products, and:
+  * tokens, token counts and joint evaluations per utterance match exactly;
+  * the joint hidden rows (the input of joint.out) match bit for bit, and so
+    do the embedding rows fed to the LSTM;
+  * the LSTM hidden states (inputs of W_r and joint.pred) match within the
+    tolerance (CUDA expf / tanhf against glibc's).
+"""
+import contextlib
+
+import numpy as np
+import pytest
+
+import pyoracle as po
+from conftest import assert_bitexact, assert_close
+from gpuhelp import dev, from_device
+
+pytestmark = pytest.mark.gpu
+
+H, V = po.DEC_H, po.DEC_V
+NAME = {32: "enc", 33: "l0_wi", 34: "l0_wr", 35: "l1_wi", 36: "l1_wr", 37: "pred", 38: "out"}
+OUT_FIELD = {"enc": "enc", "pred": "pred", "out": "out", "l0_wi": "g0i", "l0_wr": "g0r",
+             "l1_wi": "g1i", "l1_wr": "g1r"}
+IN_FIELD = {"l0_wi": "x0", "l0_wr": "h0", "l1_wi": "h0", "l1_wr": "h1", "pred": "h1",
+            "out": "hidden"}
+
+
+def to_device(ptr, a):
+    """Copies a host array into device memory at ptr (owned elsewhere)."""
+    import torch
+    from gpuhelp import _DeviceView
+    a = np.ascontiguousarray(a, np.float32).reshape(-1)
+    t = torch.as_tensor(_DeviceView(ptr, a.size, np.float32), device="cuda")
+    t.copy_(torch.from_numpy(a))
+
+
+class TableHook:
+    """Batched products from per-utterance tables, iteration by iteration;
+    records every product's input rows per iteration."""
+
+    def __init__(self, cuda, dec, tables):
+        self.dec, self.tables = dec, tables
+        self.B = len(tables)
+        self.iter = 0
+        self.inputs = {k: [] for k in IN_FIELD}
+        self.calls = []
+        self.fn = cuda.GEMM_HOOK(self._hook)
+
+    def _rows(self, name):
+        n = V if name == "out" else (4 * H if name.startswith("l") else H)
+        a = np.zeros((self.B, n), np.float32)
+        for b, t in enumerate(self.tables):
+            if self.iter < t[name].shape[0]:
+                a[b] = t[name][self.iter]
+        return a
+
+    def _hook(self, user, block, gemm, stream):
+        import torch
+        name = NAME[gemm]
+        self.calls.append(gemm)
+        ctx = (torch.cuda.stream(torch.cuda.ExternalStream(stream)) if stream
+               else contextlib.nullcontext())
+        with ctx:
+            if name == "enc":
+                to_device(self.dec.gemm_out["enc"],
+                          np.concatenate([t["enc"][:f] for t, f in zip(self.tables, self.dec.frames)]))
+                return 0
+            src = self.dec.gemm_in[IN_FIELD[name]]
+            self.inputs[name].append(from_device(src, self.B * H, np.float32).reshape(self.B, H))
+            to_device(self.dec.gemm_out[OUT_FIELD[name]], self._rows(name))
+        if name == "out":
+            self.iter += 1
+        return 0
+
+
+def device_params(params):
+    return {"embed": dev(params["embed"]), "lstm0_b": dev(params["B0"]),
+            "lstm1_b": dev(params["B1"]), "joint_enc_b": dev(params["enc_b"]),
+            "joint_pred_b": dev(params["pred_b"]), "joint_out_b": dev(params["out_b"])}
+
+
+def run_case(cuda, frames, p_blank, seed):
+    rng = np.random.default_rng(seed)
+    params = po.random_dec_params(rng)
+    tables = [po.random_dec_products(rng, T, pb) for T, pb in zip(frames, p_blank)]
+    with cuda.Decoder(frames) as dec:
+        hook = TableHook(cuda, dec, tables)
+        dec.decode(device_params(params), hook=hook.fn)
+        n_tok, evals, tokens = dec.results()
+        iters = dec.iterations
+        h_final = from_device(dec.gemm_in["h0"], 2 * len(frames) * H, np.float32).reshape(2, -1, H)
+    assert hook.calls[0] == 32 and hook.calls[1:7] == [33, 34, 35, 36, 37, 38]
+    assert iters == hook.iter
+    for b, (T, table) in enumerate(zip(frames, tables)):
+        prod = po.DecodeProducts(table)
+        tok_o, it_o, state = po.oracle_greedy_decode(T, params, prod)
+        assert n_tok[b] == len(tok_o), (b, n_tok[b], len(tok_o))
+        assert_bitexact(tokens[b], tok_o.astype(np.int32), f"tokens of utterance {b}")
+        assert evals[b] == it_o, (b, evals[b], it_o)
+        for k in range(it_o):
+            assert_bitexact(hook.inputs["out"][k][b], prod.inputs["out"][k], f"hidden {b} iter {k}")
+            assert_close(hook.inputs["pred"][k][b], prod.inputs["pred"][k], f"h1 {b} iter {k}")
+        for k, x in prod.inputs["l0_wi"].items():
+            assert_bitexact(hook.inputs["l0_wi"][k][b], x, f"embedding row {b} iter {k}")
+            assert_close(hook.inputs["l0_wr"][k][b], prod.inputs["l0_wr"][k], f"h0 {b} iter {k}")
+            assert_close(hook.inputs["l1_wr"][k][b], prod.inputs["l1_wr"][k], f"h1 {b} iter {k}")
+        assert_close(h_final[0, b], state[0], f"final h0 {b}")
+        assert_close(h_final[1, b], state[1], f"final h1 {b}")
+    return n_tok, evals
+
+
+def test_decode_ragged(cuda):
+    """Ragged batch: one frame, the 10-symbol cap on every frame (p_blank 0),
+    mostly-blank and all-blank utterances side by side."""
+    n_tok, _ = run_case(cuda, [1, 5, 13, 40, 2, 3], [0.5, 0.0, 0.6, 0.8, 0.3, 1.0], seed=71)
+    assert n_tok[1] == 50 and n_tok[5] == 0
+
+
+def test_decode_uniform(cuda):
+    run_case(cuda, [16] * 4, [0.7] * 4, seed=72)
+
+
+def test_decode_batch64(cuda):
+    rng = np.random.default_rng(73)
+    frames = rng.integers(1, 60, size=64).tolist()
+    p_blank = rng.uniform(0.5, 0.95, size=64).tolist()
+    run_case(cuda, frames, p_blank, seed=74)

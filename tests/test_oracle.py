@@ -108,6 +108,24 @@ def test_golden_pre_encode(oracle, golden):
         assert_bitexact(caps[k], golden["pre_cap_" + k], "pre " + k)
 
 
+def test_golden_greedy_decode(oracle, golden):
+    """The reference's own pk_greedy_decode (csrc/decoder.c:80-132) on 6 frames
+    with stand-in products: tokens, joint evaluations, joint hidden rows bit
+    for bit, LSTM state within the tolerance."""
+    params = {k: golden["dec_p_" + k] for k in ("B0", "B1", "enc_b", "pred_b", "out_b")}
+    embed = np.zeros((po.DEC_V, po.DEC_H), np.float32)
+    embed[golden["dec_embed_rows"]] = golden["dec_embed"]
+    params["embed"] = embed
+    table = {k: golden["dec_t_" + k] for k in po.DEC_PRODUCTS}
+    prod = po.DecodeProducts(table)
+    tok, iters, _ = po.oracle_greedy_decode(6, params, prod)
+    assert_bitexact(tok.astype(np.int32), golden["dec_tokens"], "tokens")
+    assert iters == int(golden["dec_iters"][0])
+    for k in range(iters):
+        assert_bitexact(prod.inputs["out"][k], golden["dec_hidden"][k], f"hidden {k}")
+        assert_close(prod.inputs["pred"][k], golden["dec_h1"][k], f"h1 {k}")
+
+
 # ── the reference library at BASELINE shapes ─────────────────────────────────
 
 def test_ref_layer_norm_T375(oracle, reference):
@@ -179,6 +197,36 @@ def test_ref_pre_encode(oracle, reference, T):
     assert_bitexact(xo, xr, "x")
     for k in co:
         assert_bitexact(co[k], cr[k], k)
+
+
+@pytest.mark.parametrize("T,p_blank", [(0, 0.5), (1, 0.5), (3, 1.0), (5, 0.0), (13, 0.6),
+                                       (40, 0.8), (64, 0.9)])
+def test_ref_greedy_decode(T, p_blank):
+    """The reference's own pk_greedy_decode, pk_joint, pk_decoder_step and
+    pk_lstm_step (matrix-vector products as stand-ins) against the
+    restatement: same tokens and joint evaluations (the 10-symbol cap at
+    p_blank 0, no symbol at 1), the same input for every product -- bit for
+    bit for the embedding rows and joint hidden rows, within the tolerance for
+    the LSTM states (glibc expf / tanhf under the reference's -ffast-math)."""
+    if not po.ref_dec_available():
+        pytest.skip("oracle/_ref/libpkref_dec.so not built (reference tree absent)")
+    rng = np.random.default_rng(500 + T)
+    params = po.random_dec_params(rng)
+    table = po.random_dec_products(rng, T, p_blank)
+    a, b = po.DecodeProducts(table), po.DecodeProducts(table)
+    tok_o, it_o, _ = po.oracle_greedy_decode(T, params, a)
+    tok_r, it_r = po.reference_greedy_decode(T, params, b)
+    assert_bitexact(tok_o, tok_r, "tokens")
+    assert it_o == it_r
+    if p_blank == 0.0:
+        assert len(tok_o) == 10 * T
+    for g in po.DEC_PRODUCTS[1:]:
+        assert sorted(a.inputs[g]) == sorted(b.inputs[g]), g
+        for k in a.inputs[g]:
+            if g in ("out", "l0_wi"):
+                assert_bitexact(a.inputs[g][k], b.inputs[g][k], f"{g} {k}")
+            else:
+                assert_close(a.inputs[g][k], b.inputs[g][k], f"{g} {k}")
 
 
 # ── known answers ────────────────────────────────────────────────────────────
