@@ -59,6 +59,8 @@ def parse_args():
                     help="time only the standalone kernels (one JSON object), e.g. for ncu")
     ap.add_argument("--pre-only", action="store_true",
                     help="with --aux-only: time only the pre-encode stage")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="with --aux-only: time only the batched greedy decode")
     ap.add_argument("--pre-utts", type=int, default=64,
                     help="utterances of 3000 mel frames in the pre-encode timing")
     ap.add_argument("--aux-reps", type=int, default=5,
@@ -469,6 +471,93 @@ def time_aux_kernels(stream, reps=5, pre_utts=64, pre_only=False):
     return out
 
 
+DEC_UTTS, DEC_T = 256, 375
+
+
+def time_decode(stream, reps):
+    """pkcu_greedy_decode over 256 utterances x 375 encoder frames with the
+    products resident as seeded stand-ins (no hook: the products are GEMMs
+    outside the path). Static products make every utterance either always
+    advance (blank wins: 375 iterations, joint + argmax only) or always emit
+    (the 10-symbol cap on every frame: 3750 iterations, both LSTM layers on
+    every row). Reported per case: device time per decode, per iteration, and
+    joint evaluations per second."""
+    import torch
+    import pkcuda
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(10)
+    f32 = dict(device=dev, dtype=torch.float32)
+    B, T = DEC_UTTS, DEC_T
+    params = {"embed": 0.5 * torch.randn(1025 * 640, generator=g, **f32),
+              "lstm0_b": 0.1 * torch.randn(5120, generator=g, **f32),
+              "lstm1_b": 0.1 * torch.randn(5120, generator=g, **f32),
+              "joint_enc_b": 0.1 * torch.randn(640, generator=g, **f32),
+              "joint_pred_b": 0.1 * torch.randn(640, generator=g, **f32),
+              "joint_out_b": 0.1 * torch.randn(1025, generator=g, **f32)}
+    res = {}
+    with pkcuda.Decoder([T] * B) as dec:
+        sizes = {"enc": B * T * 640, "pred": B * 640, "out": B * 1025, "g0i": B * 2560,
+                 "g0r": B * 2560, "g1i": B * 2560, "g1r": B * 2560}
+        views = {k: torch.as_tensor(_DevView(dec.gemm_out[k], n), device=dev) for k, n in sizes.items()}
+        for k, v in views.items():
+            v.copy_(torch.randn(v.numel(), generator=g, **f32))
+        out = views["out"].view(B, 1025)
+        for case, blank in (("decode_all_blank", 100.0), ("decode_always_emit", -100.0)):
+            out[:, 1024] = blank
+            dec.decode(params, stream=stream)          # warm-up
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(max(reps, 1)):
+                dec.decode(params, stream=stream)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / max(reps, 1)
+            it = dec.iterations
+            n_tok, evals, _ = dec.results()
+            res[case] = {"utterances": B, "frames": T, "ms": round(ms, 4), "iterations": it,
+                         "us_per_iteration": round(1e3 * ms / it, 3),
+                         "joint_evals_per_s": round(int(evals.sum()) / (ms * 1e-3)),
+                         "tokens": int(n_tok.sum()), "frames_per_s": round(B * T / (ms * 1e-3))}
+    return res
+
+
+def cpu_decode_baseline(T=DEC_T, seconds=1.0):
+    """The reference's own pk_greedy_decode (oracle/_ref/libpkref_dec.so) on
+    the host, one core, with the same static-product cases as time_decode:
+    joint evaluations per second per case over a bounded sample of utterances."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    if not po.ref_dec_available():
+        return {"unavailable": "oracle/_ref/libpkref_dec.so not built"}
+    rng = np.random.default_rng(11)
+    params = po.random_dec_params(rng)
+    t = po.random_dec_products(rng, T, 0.0, max_iters=1)
+    rows = {k: (t[k] if k == "enc" else t[k][0].copy()) for k in po.DEC_PRODUCTS}
+    out = {"cores": 1, "kind": "reference", "unit": "joint evaluations/s"}
+    for case, blank in (("decode_all_blank", 100.0), ("decode_always_emit", -100.0)):
+        rows["out"][po.DEC_BLANK] = blank
+        n_utts, evals, t0 = 0, 0, time.perf_counter()
+        while n_utts < 1 or time.perf_counter() - t0 < seconds / 2:
+            evals += po.reference_greedy_decode_static(T, params, rows)[1]
+            n_utts += 1
+        dt = time.perf_counter() - t0
+        out[case] = {"joint_evals_per_s": round(evals / dt), "utterances": n_utts, "seconds": round(dt, 3)}
+    out["sample"] = (f"utterances of T={T} decoded one after another through the reference's "
+                     f"pk_greedy_decode, products served from fixed rows in C")
+    return out
+
+
+class _DevView:
+    """A device address seen as a 1-D float32 array (the CUDA array interface)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (int(ptr), False),
+                                         "version": 3}
+
+
 PRE_UTTS, PRE_MEL_T = 64, 3000
 
 
@@ -552,6 +641,12 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
+        if args.decode_only:
+            dec = time_decode(stream, args.aux_reps)
+            if not args.no_cpu_baseline:
+                dec["cpu_baseline"] = cpu_decode_baseline()
+            print(json.dumps({"decode": dec}), flush=True)
+            return
         aux = time_aux_kernels(stream, reps=args.aux_reps, pre_utts=args.pre_utts,
                                pre_only=args.pre_only)
     peak, peak_kind = measured_peak()
@@ -629,9 +724,12 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = None
+    aux = decode = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
+        decode = time_decode(stream, 3)
+        if world == 1 and not args.no_cpu_baseline:
+            decode["cpu_baseline"] = cpu_decode_baseline()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = RefRunner(args.T, args.blocks)
@@ -665,6 +763,7 @@ def _ours(args, rank, world, local_rank, stream):
                 "frac": round(v["gbs"] / peak, 3),
                 **({"frames_per_s": round(v["frames_per_s"])} if "frames_per_s" in v else {})}
             for k, v in aux.items()},
+        "decode": decode,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,

@@ -152,7 +152,10 @@ def ref_dec_available() -> bool:
 def ref_dec_lib():
     global _ref_dec
     if _ref_dec is None:
-        _ref_dec = _Lib(LIB_REF_DEC, {"pkref_greedy_decode": (C.c_int, _DEC_ARGS + [I32P])}).lib
+        _ref_dec = _Lib(LIB_REF_DEC, {
+            "pkref_greedy_decode": (C.c_int, _DEC_ARGS + [I32P]),
+            "pkref_greedy_decode_static": (C.c_int, [C.c_int, FP, FP, FP, FP, FP, FP, FPP, I32P,
+                                                     C.c_int, I32P])}).lib
     return _ref_dec
 
 
@@ -659,3 +662,20 @@ def oracle_greedy_decode(T, params, products: DecodeProducts):
 def reference_greedy_decode(T, params, products: DecodeProducts):
     """The reference's own pk_greedy_decode: (tokens, joint evaluations)."""
     return _dec_call(ref_dec_lib().pkref_greedy_decode, T, params, products, [])
+
+
+def reference_greedy_decode_static(T, params, rows: dict):
+    """The reference's pk_greedy_decode with fixed product rows served from C
+    (rows["enc"] [T, 640], one row for each other product): the reference's own
+    non-GEMM decode work with no Python in the loop. Returns (tokens, joint
+    evaluations)."""
+    p = [f32(params[r]) for r in DEC_PARAM_ROLES]
+    rr = [f32(rows[k]) for k in DEC_PRODUCTS]
+    cap = 10 * T + 1
+    tokens = np.zeros(cap, np.int32)
+    n_iters = C.c_int(0)
+    n = ref_dec_lib().pkref_greedy_decode_static(T, *[_fp(a) for a in p], _ptr_array(rr),
+                                                 tokens.ctypes.data_as(I32P), cap,
+                                                 C.byref(n_iters))
+    assert n >= 0
+    return tokens[:n].copy(), n_iters.value

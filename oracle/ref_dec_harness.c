@@ -88,3 +88,25 @@ int pkref_greedy_decode(int T, const float *embed, const float *B0, const float 
     free(m);
     return n;
 }
+
+/* Products from fixed rows, for timing the reference's non-GEMM decode work
+ * alone: enc row t of rows[D_ENC] ([T, 640]), the same row every time for the
+ * others (rows[g], g = D_PRED .. D_L1_WR). */
+static const float *g_rows[D_N];
+
+static void static_products(void *user, int gemm, int iter, const float *in, int n_in, float *out,
+                            int n_out)
+{
+    (void)user; (void)in; (void)n_in;
+    const float *src = gemm == D_ENC ? g_rows[D_ENC] + (size_t)iter * (size_t)n_out : g_rows[gemm];
+    memcpy(out, src, sizeof(float) * (size_t)n_out);
+}
+
+int pkref_greedy_decode_static(int T, const float *embed, const float *B0, const float *B1,
+                               const float *enc_b, const float *pred_b, const float *out_b,
+                               const float *const *rows, int *tokens, int max_tokens, int *n_iters)
+{
+    for (int g = 0; g < D_N; g++) g_rows[g] = rows[g];
+    return pkref_greedy_decode(T, embed, B0, B1, enc_b, pred_b, out_b, static_products, NULL,
+                               tokens, max_tokens, n_iters);
+}

@@ -7,16 +7,17 @@
 // blank token, per frame t up to 10 times { joint(enc_t, pred); argmax; blank
 // -> next frame; else emit and run a decoder step }. Here every utterance of
 // the batch advances by one joint evaluation per iteration:
-//   1. embedding rows of the tokens whose decoder step is pending   (x0)
+//      (x0 holds the embedding row of each pending row's token)
 //      -> hooks L0_WI (x0 W_i0^T), L0_WR (h0 W_r0^T)
-//   2. LSTM layer 0 cell on the pending rows                         (h0, c0)
+//   1. LSTM layer 0 cell on the pending rows                         (h0, c0)
 //      -> hooks L1_WI (h0 W_i1^T), L1_WR (h1 W_r1^T)
-//   3. LSTM layer 1 cell on the pending rows                         (h1, c1)
+//   2. LSTM layer 1 cell on the pending rows                         (h1, c1)
 //      -> hook PRED (h1 joint.pred)
-//   4. joint hidden of the active rows: relu((enc_t + b_enc) + (pred + b_pred))
+//   3. joint hidden of the active rows: relu((enc_t + b_enc) + (pred + b_pred))
 //      -> hook OUT (hidden joint.out)
-//   5. logits + b_out, first-maximum argmax, state update: blank -> next
-//      frame; else emit, pending step, next frame after the 10th symbol.
+//   4. logits + b_out, first-maximum argmax, state update: blank -> next
+//      frame; else emit, copy the token's embedding row into x0 (the next
+//      iteration's pending decoder step), next frame after the 10th symbol.
 // Each utterance thus goes through exactly the reference's sequence of
 // operations (its k-th joint evaluation is iteration k; the decoder step that
 // precedes it runs in the same iteration), interleaved with the others.
@@ -33,12 +34,17 @@ struct DecState {      // one entry per utterance
   int *live;           // rows still active or pending after the last select
 };
 
-__global__ void dec_init_kernel(DecState st, float *__restrict__ lstm, int B) {
-  // lstm: h0, h1, c0, c1, each [B, 640]
+__global__ void dec_init_kernel(DecState st, float *__restrict__ lstm, float *__restrict__ x0,
+                                const float *__restrict__ embed, int B) {
+  // lstm: h0, h1, c0, c1, each [B, 640]; x0 = the blank token's embedding row
   const long long n4 = 4LL * B * DEC_H4;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n4;
-       e += (long long)gridDim.x * blockDim.x)
+       e += (long long)gridDim.x * blockDim.x) {
     st4(lstm + 4 * e, make_float4(0.f, 0.f, 0.f, 0.f));
+    if (e < (long long)B * DEC_H4)
+      st4(x0 + 4 * e, __ldg(reinterpret_cast<const float4 *>(embed + (long long)DEC_BLANK * DEC_H) +
+                            e % DEC_H4));
+  }
   for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < B; b += gridDim.x * blockDim.x) {
     st.t[b] = 0;
     st.s[b] = 0;
@@ -46,19 +52,6 @@ __global__ void dec_init_kernel(DecState st, float *__restrict__ lstm, int B) {
     st.last[b] = DEC_BLANK;   // the first decoder step runs on blank (csrc/decoder.c:95-97)
     st.pending[b] = 1;
     st.evals[b] = 0;
-  }
-}
-
-// x0[b] = embed[last[b]] (pk_decoder_step, csrc/decoder.c:19); resets the
-// live count of this iteration.
-__global__ void dec_embed_kernel(const float *__restrict__ embed, const int *__restrict__ last,
-                                 float *__restrict__ x0, int B, int *live) {
-  if (blockIdx.x == 0 && threadIdx.x == 0) *live = 0;
-  const long long n4 = (long long)B * DEC_H4;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n4;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(e / DEC_H4), j4 = (int)(e - (long long)b * DEC_H4);
-    st4(x0 + 4 * e, __ldg(reinterpret_cast<const float4 *>(embed + (long long)last[b] * DEC_H) + j4));
   }
 }
 
@@ -91,11 +84,13 @@ __global__ void dec_cell_kernel(const float *__restrict__ gi, const float *__res
 }
 
 // pk_joint's hidden (csrc/decoder.c:44-67) for the active rows: enc_proj + bias,
-// pred_proj + bias, their sum, ReLU; inactive rows get zeros.
+// pred_proj + bias, their sum, ReLU; inactive rows get zeros. Resets the live
+// count that this iteration's select accumulates.
 __global__ void dec_joint_kernel(const float *__restrict__ encp, const float *__restrict__ enc_b,
                                  const float *__restrict__ pred, const float *__restrict__ pred_b,
                                  float *__restrict__ hidden, const int *__restrict__ t, SeqDev seq,
-                                 int B) {
+                                 int B, int *live) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *live = 0;
   const long long n4 = (long long)B * DEC_H4;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n4;
        e += (long long)gridDim.x * blockDim.x) {
@@ -123,7 +118,8 @@ constexpr int SEL_ROWS = 8;   // rows (warps) per CTA
 // then the greedy state machine of csrc/decoder.c:99-129 for one row.
 __global__ void __launch_bounds__(32 * SEL_ROWS)
 dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b, DecState st,
-                  int *__restrict__ tokens, SeqDev seq, int B) {
+                  int *__restrict__ tokens, const float *__restrict__ embed, float *__restrict__ x0,
+                  SeqDev seq, int B) {
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * SEL_ROWS + (threadIdx.x >> 5);
   if (b >= B) return;
@@ -146,8 +142,13 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
     const int oi = __shfl_xor_sync(PK_FULL_MASK, bi, o);
     if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
   }
-  if (lane != 0) return;
   const int best = (isnan(l[0] + __ldg(out_b)) || bi == INT_MAX) ? 0 : bi;
+  if (best != DEC_BLANK) {             // the next decoder step's input (csrc/decoder.c:19)
+    const float4 *src = reinterpret_cast<const float4 *>(embed + (long long)best * DEC_H);
+    float4 *dst = reinterpret_cast<float4 *>(x0 + (long long)b * DEC_H);
+    for (int j = lane; j < DEC_H4; j += 32) dst[j] = __ldg(src + j);
+  }
+  if (lane != 0) return;
   st.evals[b] += 1;
   int t = tb, s = st.s[b], pend = 0;
   if (best == DEC_BLANK) {
@@ -194,10 +195,20 @@ struct pkcu_decoder {
   int *live_host;          // page-locked poll target
   int iterations;          // of the last decode
   int device;
+  // Without a hook, DEC_POLL iterations and the poll copy are one CUDA graph,
+  // captured on `gs` for the parameter pointers in `gp` and replayed.
+  cudaStream_t gs;
+  cudaEvent_t ev_in, ev_out;
+  cudaGraphExec_t graph;
+  pkcu_dec_params gp;
 };
 
 extern "C" void pkcu_decoder_destroy(pkcu_decoder *d) {
   if (!d) return;
+  if (d->graph) cudaGraphExecDestroy(d->graph);
+  if (d->ev_in) cudaEventDestroy(d->ev_in);
+  if (d->ev_out) cudaEventDestroy(d->ev_out);
+  if (d->gs) cudaStreamDestroy(d->gs);
   if (d->block) cudaFree(d->block);
   if (d->live_host) cudaFreeHost(d->live_host);
   pkcu_seq_destroy(d->seq);
@@ -280,6 +291,75 @@ extern "C" int pkcu_decoder_buffers(const pkcu_decoder *d, pkcu_dec_gemm_outputs
 
 extern "C" int pkcu_decoder_iterations(const pkcu_decoder *d) { return d ? d->iterations : -1; }
 
+constexpr int DEC_POLL = 8;   // iterations between two reads of the live count
+
+// One iteration (kernels and hooks) on stream s.
+static int dec_iteration(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
+                         void *hook_user, cudaStream_t s) {
+  const int B = d->B;
+  const SeqDev seq = d->seq->dev;
+  const size_t BH = (size_t)B * DEC_H;
+  float *h0 = d->lstm, *h1 = d->lstm + BH, *c0 = d->lstm + 2 * BH, *c1 = d->lstm + 3 * BH;
+  const pkcu_stream_t ps = (pkcu_stream_t)s;
+  int st = PKCU_OK;
+  if (hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L0_WI, ps);
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L0_WR, ps);
+  if (st) return st;
+  dec_cell_kernel<<<dec_grid(BH), 256, 0, s>>>(d->g0i, d->g0r, prm->lstm0_b, h0, c0, d->st.pending, B);
+  st = pkcu_launch_status("pkcu_greedy_decode: lstm 0");
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L1_WI, ps);
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L1_WR, ps);
+  if (st) return st;
+  dec_cell_kernel<<<dec_grid(BH), 256, 0, s>>>(d->g1i, d->g1r, prm->lstm1_b, h1, c1, d->st.pending, B);
+  st = pkcu_launch_status("pkcu_greedy_decode: lstm 1");
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_PRED, ps);
+  if (st) return st;
+  dec_joint_kernel<<<dec_grid(BH / 4), 256, 0, s>>>(d->encp, prm->joint_enc_b, d->pred,
+                                                   prm->joint_pred_b, d->hidden, d->st.t, seq, B,
+                                                   d->st.live);
+  st = pkcu_launch_status("pkcu_greedy_decode: joint");
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_OUT, ps);
+  if (st) return st;
+  dec_select_kernel<<<(unsigned)((B + SEL_ROWS - 1) / SEL_ROWS), 32 * SEL_ROWS, 0, s>>>(
+      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B);
+  return pkcu_launch_status("pkcu_greedy_decode: select");
+}
+
+static bool same_params(const pkcu_dec_params &a, const pkcu_dec_params &b) {
+  return a.embed == b.embed && a.lstm0_b == b.lstm0_b && a.lstm1_b == b.lstm1_b &&
+         a.joint_enc_b == b.joint_enc_b && a.joint_pred_b == b.joint_pred_b &&
+         a.joint_out_b == b.joint_out_b;
+}
+
+// Captures DEC_POLL iterations + the copy of the live count into d->graph.
+static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm) {
+  if (d->graph) {
+    cudaGraphExecDestroy(d->graph);
+    d->graph = nullptr;
+  }
+  if (!d->gs && (cudaStreamCreateWithFlags(&d->gs, cudaStreamNonBlocking) != cudaSuccess ||
+                 cudaEventCreateWithFlags(&d->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+                 cudaEventCreateWithFlags(&d->ev_out, cudaEventDisableTiming) != cudaSuccess))
+    return pkcu_launch_status("pkcu_greedy_decode: graph stream");
+  if (cudaStreamBeginCapture(d->gs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return pkcu_launch_status("pkcu_greedy_decode: begin capture");
+  int st = PKCU_OK;
+  for (int i = 0; i < DEC_POLL && !st; i++) st = dec_iteration(d, prm, nullptr, nullptr, d->gs);
+  if (!st && cudaMemcpyAsync(d->live_host, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, d->gs) !=
+                 cudaSuccess)
+    st = pkcu_launch_status("pkcu_greedy_decode: capture poll copy");
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(d->gs, &g);
+  if (!st && ce != cudaSuccess) st = pkcu_launch_status("pkcu_greedy_decode: end capture");
+  if (!st && cudaGraphInstantiate(&d->graph, g, 0) != cudaSuccess) {
+    d->graph = nullptr;
+    st = pkcu_launch_status("pkcu_greedy_decode: instantiate");
+  }
+  if (g) cudaGraphDestroy(g);
+  if (!st) d->gp = *prm;
+  return st;
+}
+
 extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
                                   void *hook_user, pkcu_stream_t stream) {
   if (!d || !prm) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode: NULL argument");
@@ -292,46 +372,37 @@ extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, p
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode: embed, joint_enc_b, joint_pred_b must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   const int B = d->B;
-  const SeqDev seq = d->seq->dev;
   const size_t BH = (size_t)B * DEC_H;
-  float *h0 = d->lstm, *h1 = d->lstm + BH, *c0 = d->lstm + 2 * BH, *c1 = d->lstm + 3 * BH;
   int max_T = 0;
   for (int b = 0; b < B; b++) max_T = d->seq->lengths[b] > max_T ? d->seq->lengths[b] : max_T;
   // every evaluation emits or advances; at most 10 emissions per frame, then
   // one more iteration for the last pending decoder step
   const long long max_iters = (long long)DEC_MAX_SYM * max_T + 2;
-  constexpr int POLL = 8;
   d->iterations = 0;
-  dec_init_kernel<<<dec_grid((long long)BH), 256, 0, s>>>(d->st, d->lstm, B);
+  dec_init_kernel<<<dec_grid((long long)BH), 256, 0, s>>>(d->st, d->lstm, d->x0, prm->embed, B);
   int st = pkcu_launch_status("pkcu_greedy_decode: init");
   if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_ENC, stream);
-  for (long long it = 0; !st && it < max_iters; it++) {
-    dec_embed_kernel<<<dec_grid(BH / 4), 256, 0, s>>>(prm->embed, d->st.last, d->x0, B, d->st.live);
-    st = pkcu_launch_status("pkcu_greedy_decode: embed");
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L0_WI, stream);
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L0_WR, stream);
-    if (st) break;
-    dec_cell_kernel<<<dec_grid(BH), 256, 0, s>>>(d->g0i, d->g0r, prm->lstm0_b, h0, c0,
-                                                  d->st.pending, B);
-    st = pkcu_launch_status("pkcu_greedy_decode: lstm 0");
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L1_WI, stream);
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_L1_WR, stream);
-    if (st) break;
-    dec_cell_kernel<<<dec_grid(BH), 256, 0, s>>>(d->g1i, d->g1r, prm->lstm1_b, h1, c1,
-                                                  d->st.pending, B);
-    st = pkcu_launch_status("pkcu_greedy_decode: lstm 1");
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_PRED, stream);
-    if (st) break;
-    dec_joint_kernel<<<dec_grid(BH / 4), 256, 0, s>>>(d->encp, prm->joint_enc_b, d->pred,
-                                                     prm->joint_pred_b, d->hidden, d->st.t, seq, B);
-    st = pkcu_launch_status("pkcu_greedy_decode: joint");
-    if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_OUT, stream);
-    if (st) break;
-    dec_select_kernel<<<(unsigned)((B + SEL_ROWS - 1) / SEL_ROWS), 32 * SEL_ROWS, 0, s>>>(
-        d->out, prm->joint_out_b, d->st, d->tokens, seq, B);
-    st = pkcu_launch_status("pkcu_greedy_decode: select");
+  if (st) return st;
+  if (!hook) {
+    if (!d->graph || !same_params(d->gp, *prm)) st = dec_capture(d, prm);
+    if (st) return st;
+    if (cudaEventRecord(d->ev_in, s) != cudaSuccess || cudaStreamWaitEvent(d->gs, d->ev_in, 0) != cudaSuccess)
+      return pkcu_launch_status("pkcu_greedy_decode: join");
+    for (long long it = 0; it < max_iters; it += DEC_POLL) {
+      if (cudaGraphLaunch(d->graph, d->gs) != cudaSuccess || cudaStreamSynchronize(d->gs) != cudaSuccess)
+        return pkcu_launch_status("pkcu_greedy_decode: graph");
+      d->iterations += DEC_POLL;
+      if (*d->live_host == 0) break;
+    }
+    if (cudaEventRecord(d->ev_out, d->gs) != cudaSuccess || cudaStreamWaitEvent(s, d->ev_out, 0) != cudaSuccess)
+      return pkcu_launch_status("pkcu_greedy_decode: join");
+    return PKCU_OK;
+  }
+  for (long long it = 0; it < max_iters; it++) {
+    st = dec_iteration(d, prm, hook, hook_user, s);
+    if (st) return st;
     d->iterations = (int)(it + 1);
-    if (!st && ((it + 1) % POLL == 0 || it + 1 == max_iters)) {
+    if ((it + 1) % DEC_POLL == 0 || it + 1 == max_iters) {
       if (cudaMemcpyAsync(d->live_host, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, s) !=
               cudaSuccess ||
           cudaStreamSynchronize(s) != cudaSuccess)
@@ -339,7 +410,7 @@ extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, p
       if (*d->live_host == 0) break;
     }
   }
-  return st;
+  return PKCU_OK;
 }
 
 extern "C" int pkcu_decoder_results(const pkcu_decoder *d, int *n_tokens, int *evals, int *tokens,

@@ -132,3 +132,39 @@ def test_decode_batch64(cuda):
     frames = rng.integers(1, 60, size=64).tolist()
     p_blank = rng.uniform(0.5, 0.95, size=64).tolist()
     run_case(cuda, frames, p_blank, seed=74)
+
+
+def test_decode_graph_no_hook(cuda):
+    """Without a hook the decode replays a captured CUDA graph of 8 iterations;
+    the products are whatever the caller left in the decoder's buffers (here
+    one fixed row per utterance: it always emits -- the 10-symbol cap on every
+    frame -- or always advances). Run twice to reuse the captured graph."""
+    frames = [3, 7, 1, 12, 5, 9]
+    emits = [True, False, True, False, False, True]
+    rng = np.random.default_rng(75)
+    params = po.random_dec_params(rng)
+    rows = {k: [] for k in ("pred", "out", "l0_wi", "l0_wr", "l1_wi", "l1_wr")}
+    tables = []
+    for T, em in zip(frames, emits):
+        t = po.random_dec_products(rng, T, 0.0, max_iters=1)
+        t["out"][0, po.DEC_BLANK] = -100.0 if em else 100.0
+        for k in rows:
+            rows[k].append(t[k][0])
+        n = 10 * T + 2
+        tables.append({k: (v if k == "enc" else np.repeat(v, n, axis=0)) for k, v in t.items()})
+    with cuda.Decoder(frames) as dec:
+        to_device(dec.gemm_out["enc"], np.concatenate([t["enc"][:f] for t, f in zip(tables, frames)]))
+        for k, f in (("pred", "pred"), ("out", "out"), ("l0_wi", "g0i"), ("l0_wr", "g0r"),
+                     ("l1_wi", "g1i"), ("l1_wr", "g1r")):
+            to_device(dec.gemm_out[f], np.stack(rows[k]))
+        dp = device_params(params)
+        for _ in range(2):
+            dec.decode(dp)
+            n_tok, evals, tokens = dec.results()
+            need = max(10 * T + 1 if em else T for T, em in zip(frames, emits))
+            assert dec.iterations % 8 == 0 and need <= dec.iterations < need + 8
+            for b, (T, table) in enumerate(zip(frames, tables)):
+                tok_o, it_o, _ = po.oracle_greedy_decode(T, params, po.DecodeProducts(table))
+                assert_bitexact(tokens[b], tok_o.astype(np.int32), f"tokens {b}")
+                assert evals[b] == it_o
+                assert n_tok[b] == (10 * T if emits[b] else 0)
