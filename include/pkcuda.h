@@ -389,6 +389,22 @@ int pkcu_pre_encode(const float *mel, const pkcu_pre_params *params,
                     float *x, const pkcu_pre_plan *plan, pkcu_gemm_hook hook, void *hook_user,
                     pkcu_stream_t stream);
 
+/* ── GEMMs with the non-GEMM epilogue fused (tcgen05 tensor cores) ─────────
+ * A [M, K] x W [K, N] (row-major fp32, the reference's pk_wmatmul layout,
+ * csrc/tensor_ops.c:50-61) computed on the B200's tensor cores with fp32-level
+ * accuracy (each fp32 operand split into three bf16 parts, nine bf16 MMAs per
+ * product, fp32 accumulation), the bias / activation / residual applied to the
+ * accumulator tile before the single store. N, K multiples of 4; A, W, bias and
+ * the output 16-byte aligned. */
+/* D = Swish(A W + bias): FF linear1 + bias + Swish (csrc/encoder.c:193-196). */
+int pkcu_gemm_bias_swish(const float *A, const float *W, const float *bias, float *D,
+                         int M, int N, int K, pkcu_stream_t stream);
+/* X = X + scale * (A W + bias), in place: FF linear2 + the 0.5-scaled macaron
+ * residual (csrc/encoder.c:198-216, scale 0.5), attention output projection +
+ * residual (:418-434, scale 1). */
+int pkcu_gemm_bias_residual(const float *A, const float *W, const float *bias, float *X,
+                            float scale, int M, int N, int K, pkcu_stream_t stream);
+
 /* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────
  * Replaces pk_greedy_decode for a batch of utterances (the encoder outputs of
  * n_utts utterances of T_b frames, frames of every utterance in turn). Every

@@ -138,7 +138,13 @@ _REF_SIGS = {
                                       FP, C.POINTER(C.c_int)]),
     "pkref_manifest_scales": (C.c_int, [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, FP]),
     "pkref_pre_encode": (C.c_int, [FP, C.c_int, FPP, FP, FP, FP, FP, FP, FP, FP]),
+    "pk_wmatmul": (None, [FP, C.c_void_p, FP, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float]),
 }
+
+
+class RefWeight(C.Structure):
+    """The reference's Weight (csrc/parakeet.h:52-57)."""
+    _fields_ = [("data", C.c_void_p), ("scale", C.c_float), ("scales", FP), ("bits", C.c_int)]
 
 _oracle = None
 _ref = None
@@ -553,6 +559,41 @@ class Reference:
                                              out.nbytes, _fp(scales), C.byref(bits))
         assert rc == 0 and bits.value == 8, (rc, bits.value)
         return out, scales
+
+    def wmatmul(self, A, W):
+        """A [M, K] x W [K, N] through the reference's pk_wmatmul with an fp32
+        Weight (csrc/tensor_ops.c:50-61)."""
+        A, W = f32(A), f32(W)
+        M, K = A.shape
+        N = W.shape[1]
+        w = RefWeight(W.ctypes.data, 0.0, FP(), 32)
+        out = np.empty((M, N), np.float32)
+        self.L.pk_wmatmul(_fp(A), C.byref(w), _fp(out), M, N, K, 1.0, 0.0)
+        return out
+
+    def ff_linear1(self, A, W, b):
+        """feed_forward's first half (csrc/encoder.c:193-196): pk_wmatmul, the
+        per-row pk_bias_add, pk_swish."""
+        h = self.wmatmul(A, W)
+        b = f32(b)
+        for t in range(h.shape[0]):
+            self.L.pk_bias_add(_fp(h[t]), _fp(b), h.shape[1])
+        self.L.pk_swish(_fp(h), h.size)
+        return h
+
+    def linear_residual(self, x, A, W, b, scale):
+        """pk_wmatmul + per-row pk_bias_add, then x + scale * out as
+        feed_forward's macaron residual (scale 0.5, csrc/encoder.c:198-216: the
+        AVX2 body is fma(out, 0.5, x)) or the attention residual (scale 1,
+        :418-434: x + out)."""
+        out = self.wmatmul(A, W)
+        b = f32(b)
+        for t in range(out.shape[0]):
+            self.L.pk_bias_add(_fp(out[t]), _fp(b), out.shape[1])
+        x = f32(x)
+        if scale == 1.0:
+            return (x + out).astype(np.float32)
+        return (x.astype(np.float64) + np.float64(scale) * out.astype(np.float64)).astype(np.float32)
 
     def pre_encode(self, mel, params: dict, standins: dict):
         """The reference's own pre_encode_and_scale (csrc/encoder.c:103-175,

@@ -50,6 +50,7 @@ EXPORTED = (
     "pkcu_pre_plan_frames", "pkcu_pre_plan_out_seq", "pkcu_pre_encode",
     "pkcu_decoder_create", "pkcu_decoder_destroy", "pkcu_decoder_buffers", "pkcu_greedy_decode",
     "pkcu_decoder_iterations", "pkcu_decoder_results",
+    "pkcu_gemm_bias_swish", "pkcu_gemm_bias_residual",
 )
 
 
@@ -80,6 +81,8 @@ _SIGS = {
     "pkcu_pre_plan_frames": (LL, [VP]),
     "pkcu_pre_plan_out_seq": (VP, [VP]),
     "pkcu_pre_encode": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP]),
+    "pkcu_gemm_bias_swish": (I, [VP, VP, VP, VP, I, I, I, VP]),
+    "pkcu_gemm_bias_residual": (I, [VP, VP, VP, VP, F, I, I, I, VP]),
     "pkcu_decoder_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
     "pkcu_decoder_destroy": (None, [VP]),
     "pkcu_decoder_buffers": (I, [VP, VP, VP]),

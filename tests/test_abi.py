@@ -138,3 +138,13 @@ def test_decoder_validation(L):
     assert L.pkcu_decoder_create(bad, 0, C.byref(h)) == 1
     assert L.pkcu_greedy_decode(None, None, None, None, None) == 1
     assert L.pkcu_decoder_iterations(None) == -1
+
+
+def test_gemm_validation(L):
+    """The fused GEMMs reject NULL operands, N or K not a multiple of 4 and
+    misaligned pointers before any CUDA call."""
+    assert L.pkcu_gemm_bias_swish(None, 16, 16, 16, 4, 8, 8, None) == 1
+    assert L.pkcu_gemm_bias_swish(16, 16, 16, 16, 4, 6, 8, None) == 1
+    assert b"multiples of 4" in L.pkcu_last_error()
+    assert L.pkcu_gemm_bias_residual(16, 16, 16, 20, C.c_float(0.5), 4, 8, 8, None) == 1
+    assert b"aligned" in L.pkcu_last_error()
