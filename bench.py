@@ -59,6 +59,10 @@ def parse_args():
                     help="time only the standalone kernels (one JSON object), e.g. for ncu")
     ap.add_argument("--pre-only", action="store_true",
                     help="with --aux-only: time only the pre-encode stage")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="with --aux-only: time only the GEMMs with fused epilogues")
+    ap.add_argument("--gemm-rows", type=int, default=24000,
+                    help="rows M of the fused-GEMM timing")
     ap.add_argument("--decode-only", action="store_true",
                     help="with --aux-only: time only the batched greedy decode")
     ap.add_argument("--pre-utts", type=int, default=64,
@@ -471,6 +475,80 @@ def time_aux_kernels(stream, reps=5, pre_utts=64, pre_only=False):
     return out
 
 
+GEMM_ROWS = 24000   # 64 utterances x 375 frames
+
+
+def time_fused_gemms(stream, reps, M=GEMM_ROWS):
+    """The GEMMs with fused epilogues at the feed-forward shapes, M = 24000
+    rows: FF linear1 [M, 1024] x [1024, 4096] + bias + Swish, FF linear2
+    [M, 4096] x [4096, 1024] + bias + 0.5 residual. Beside each, the unfused
+    path it replaces: torch's fp32 GEMM (cuBLAS, TF32 off) followed by this
+    library's separate bias + Swish / residual kernel. Reported: ms, fp32
+    TFLOP/s (2 M N K / t) and, for the fused form, the bf16 tensor-core rate
+    it runs at (nine bf16 MMAs per fp32 product) against the measured bf16 peak."""
+    import torch
+    import pkcuda
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(12)
+    f32 = dict(device=dev, dtype=torch.float32)
+    sh = stream.cuda_stream
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16_peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        bf16_peak = 1590.0
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(max(reps, 1)):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / max(reps, 1)
+
+    res = {}
+    for name, N, K in (("ff1_gemm_bias_swish", 4096, 1024), ("ff2_gemm_bias_residual", 1024, 4096)):
+        A = torch.randn(M, K, generator=g, **f32)
+        W = torch.randn(K, N, generator=g, **f32) / K ** 0.5
+        b = 0.1 * torch.randn(N, generator=g, **f32)
+        X = torch.randn(M, N, generator=g, **f32)
+        if name.startswith("ff1"):
+            fused = lambda: pkcuda.call("pkcu_gemm_bias_swish", A.data_ptr(), W.data_ptr(),
+                                        b.data_ptr(), X.data_ptr(), M, N, K, sh)
+
+            def unfused():
+                H = torch.mm(A, W)
+                pkcuda.call("pkcu_bias_swish_rows", H.data_ptr(), b.data_ptr(), H.data_ptr(), M, N, sh)
+        else:
+            fused = lambda: pkcuda.call("pkcu_gemm_bias_residual", A.data_ptr(), W.data_ptr(),
+                                        b.data_ptr(), X.data_ptr(), 0.5, M, N, K, sh)
+
+            def unfused():
+                H = torch.mm(A, W)
+                pkcuda.call("pkcu_residual_add", X.data_ptr(), H.data_ptr(), b.data_ptr(),
+                            C.c_float(0.5), M, N, sh)
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            ms_f, ms_u = timed(fused), timed(unfused)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+        flop = 2.0 * M * N * K
+        res[name] = {"M": M, "N": N, "K": K, "ms": round(ms_f, 4),
+                     "tflops_fp32": round(flop / ms_f / 1e9, 1),
+                     "tensor_bf16_tflops": round(9 * flop / ms_f / 1e9, 1),
+                     "tensor_frac": round(9 * flop / ms_f / 1e9 / bf16_peak, 3),
+                     "unfused_cublas_fp32_ms": round(ms_u, 4),
+                     "speedup_vs_unfused": round(ms_u / ms_f, 2)}
+        del A, W, b, X
+    torch.cuda.synchronize()
+    return res
+
+
 DEC_UTTS, DEC_T = 256, 375
 
 
@@ -641,6 +719,10 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
+        if args.gemm_only:
+            print(json.dumps({"fused_gemms": time_fused_gemms(stream, args.aux_reps, args.gemm_rows)}),
+                  flush=True)
+            return
         if args.decode_only:
             dec = time_decode(stream, args.aux_reps)
             if not args.no_cpu_baseline:
@@ -724,10 +806,11 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = decode = None
+    aux = decode = gemms = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
         decode = time_decode(stream, 3)
+        gemms = time_fused_gemms(stream, 3)
         if world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = cpu_decode_baseline()
     cpu = None
@@ -764,6 +847,7 @@ def _ours(args, rank, world, local_rank, stream):
                 **({"frames_per_s": round(v["frames_per_s"])} if "frames_per_s" in v else {})}
             for k, v in aux.items()},
         "decode": decode,
+        "fused_gemms": gemms,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,
