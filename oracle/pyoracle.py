@@ -23,6 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_ORACLE = os.path.join(HERE, "liboracle.so")
 LIB_REF = os.path.join(HERE, "_ref", "libpkref.so")
 LIB_REF_DEC = os.path.join(HERE, "_ref", "libpkref_dec.so")
+LIB_REF_FULL = os.path.join(HERE, "_ref", "libpkref_full.so")
 
 D, H, DH, FF = 1024, 8, 128, 4096
 
@@ -720,3 +721,33 @@ def reference_greedy_decode_static(T, params, rows: dict):
                                                  C.byref(n_iters))
     assert n >= 0
     return tokens[:n].copy(), n_iters.value
+
+
+# ── the reference engine end to end (oracle/_ref/libpkref_full.so) ──────────
+
+def ref_full_available() -> bool:
+    return os.path.exists(LIB_REF_FULL)
+
+
+_ref_full = None
+
+
+def reference_transcribe(bin_path, json_path, mel):
+    """pk_load_weights + pk_encoder + pk_greedy_decode of the reference on one
+    mel spectrogram [128, T]: (encoder output [T', 1024], tokens)."""
+    global _ref_full
+    if _ref_full is None:
+        _ref_full = _Lib(LIB_REF_FULL, {"pkref_transcribe": (
+            C.c_int, [C.c_char_p, C.c_char_p, FP, C.c_int, FP, C.c_longlong, I32P, C.c_int,
+                      I32P])}).lib
+    mel = f32(mel)
+    T = mel.shape[1]
+    Tp = T // 8 + 4
+    enc = np.zeros((Tp, D), np.float32)
+    tok = np.zeros(10 * Tp + 1, np.int32)
+    nt = C.c_int(0)
+    got = _ref_full.pkref_transcribe(str(bin_path).encode(), str(json_path).encode(), _fp(mel), T,
+                                     _fp(enc), enc.size, tok.ctypes.data_as(I32P), tok.size,
+                                     C.byref(nt))
+    assert got > 0, "reference failed to load the checkpoint"
+    return enc[:got].copy(), tok[:nt.value].copy()

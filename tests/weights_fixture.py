@@ -150,3 +150,76 @@ def block_params(tensors: dict, b: int) -> dict:
 def pre_params(tensors: dict) -> dict:
     """The pre-encode stage's parameters (the restatement's roles)."""
     return {role: tensors[nm]["data"] for role, nm in PRE_NAMES.items()}
+
+
+def _int8(rng, K, N):
+    """int8 [K, N] with the per-tensor scale that gives the dequantised weights
+    a standard deviation of about 1/sqrt(K) (U{-127..127} has sd ~73.3)."""
+    return {"data": rng.integers(-127, 128, size=(K, N), dtype=np.int8),
+            "scale": float(np.float32(1.0 / (73.3 * np.sqrt(K)))), "scales": None}
+
+
+def _f32(a):
+    return {"data": np.ascontiguousarray(a, np.float32), "scale": None, "scales": None}
+
+
+def full_model_tensors(rng, enc_gain: float = 1.0, blank_bias: float = 1.5) -> dict:
+    """Every tensor pk_load_weights looks up (csrc/weights.c:309-396) for one
+    conformer block plus the pre-encode, positional table and decoder:
+    attention, feed-forward and pre-encode projections int8 (the reference's
+    int8 manifest), everything else float32. Scales keep activations O(1)."""
+    t = {}
+    for role, nm in PRE_NAMES.items():
+        shape = (256, 1, 3, 3) if role.endswith("_w") else (D if role == "out_b" else 256,)
+        t[nm] = _f32(0.3 * rng.standard_normal(shape))
+    for k in ("3", "6"):
+        t[f"pre_encode.conv.{k}.weight"] = _f32(rng.standard_normal((256, 256, 1, 1)) / 16.0)
+    t["pre_encode.out.weight"] = _int8(rng, 4096, D)
+    pos = np.arange(9999, dtype=np.float64)[:, None] - 4999.0
+    inv = np.exp(-np.log(10000.0) * np.arange(0, D, 2, dtype=np.float64) / D)
+    pe = np.zeros((9999, D))
+    pe[:, 0::2], pe[:, 1::2] = np.sin(pos * inv), np.cos(pos * inv)
+    t["pos_encoding.pe_table"] = _f32(pe)
+    for role, nm in ROLE_NAMES.items():
+        shape = ROLE_SHAPES.get(role, (D,))
+        if role.startswith("norm") and role.endswith("_w"):
+            a = 1.0 + 0.1 * rng.standard_normal(shape)
+        elif role == "dw_w":
+            a = 0.3 * rng.standard_normal(shape)
+        else:
+            a = 0.1 * rng.standard_normal(shape)
+        t[f"layers.0.{nm}"] = _f32(a)
+    for m in QKV:
+        t[f"layers.0.self_attn.linear_{m}.bias"] = _f32(0.1 * rng.standard_normal(D))
+    for nm, (K, N) in MATRICES.items():
+        t[f"layers.0.{nm}"] = _int8(rng, K, N)
+    t["layers.0.conv.pointwise_conv1.weight"] = _f32(rng.standard_normal((2 * D, D, 1)) / 32.0)
+    t["layers.0.conv.pointwise_conv2.weight"] = _f32(rng.standard_normal((D, D, 1)) / 32.0)
+    Hd, V = 640, 1025
+    t["decoder.prediction.embed.weight"] = _f32(0.5 * rng.standard_normal((V, Hd)))
+    for l in range(2):
+        t[f"decoder.lstm.{l}.W_i"] = _f32(rng.standard_normal((1, 4 * Hd, Hd)) / np.sqrt(Hd))
+        t[f"decoder.lstm.{l}.W_r"] = _f32(rng.standard_normal((1, 4 * Hd, Hd)) / np.sqrt(Hd))
+        t[f"decoder.lstm.{l}.B"] = _f32(0.1 * rng.standard_normal((1, 8 * Hd)))
+    t["joint.enc.weight"] = _f32(enc_gain * rng.standard_normal((D, Hd)) / np.sqrt(D))
+    t["joint.enc.bias"] = _f32(0.1 * rng.standard_normal(Hd))
+    t["joint.pred.weight"] = _f32(rng.standard_normal((Hd, Hd)) / np.sqrt(Hd))
+    t["joint.pred.bias"] = _f32(0.1 * rng.standard_normal(Hd))
+    t["joint.out.weight"] = _f32(rng.standard_normal((Hd, V)) / np.sqrt(Hd))
+    out_b = 0.1 * rng.standard_normal(V)
+    out_b[1024] += blank_bias   # blank wins some of the time
+    t["joint.joint_net.2.bias"] = _f32(out_b)
+    return t
+
+
+def write_full_checkpoint(dirpath, rng, n_blocks: int = 24, **kw):
+    """A complete checkpoint: block 0's tensors written once, blocks
+    1 .. n_blocks-1 as manifest entries aliasing block 0's bytes."""
+    tensors = full_model_tensors(rng, **kw)
+    bin_path, json_path, manifest = write_checkpoint(dirpath, tensors)
+    for b in range(1, n_blocks):
+        for name in [n for n in manifest if n.startswith("layers.0.")]:
+            manifest[name.replace("layers.0.", f"layers.{b}.", 1)] = dict(manifest[name])
+    with open(json_path, "w") as f:
+        json.dump(manifest, f, indent=2)
+    return tensors, bin_path, json_path
