@@ -405,6 +405,24 @@ int pkcu_gemm_bias_swish(const float *A, const float *W, const float *bias, floa
 int pkcu_gemm_bias_residual(const float *A, const float *W, const float *bias, float *X,
                             float scale, int M, int N, int K, pkcu_stream_t stream);
 
+/* ── the encoder stack on the GPU, GEMMs included ──────────────────────────
+ * Replaces encode_blocks (csrc/encoder.c:495-512) for a batch: fp32 device
+ * copies of every block's GEMM weights from an uploaded checkpoint (int8 /
+ * int4 dequantised once, the fused QKV as the reference's loader builds it),
+ * then pkcu_encoder_nongemm with its twelve GEMM points done by the library
+ * (cuBLAS single-precision GEMMs, no TF32; the positional projection of each
+ * utterance's slice of pos_encoding.pe_table, csrc/encoder.c:220-227). */
+typedef struct pkcu_weights pkcu_weights;   /* a loaded checkpoint (section 4 below) */
+typedef struct pkcu_encoder_model pkcu_encoder_model;
+int  pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_encoder_model **out);
+void pkcu_encoder_model_destroy(pkcu_encoder_model *m);
+int  pkcu_encoder_model_blocks(const pkcu_encoder_model *m);
+/* All blocks on x [frames, 1024] in place; gemm_out / gemm_in: device buffers
+ * for the batch (those of a 1-group pkcu_encoder_ws fit). */
+int  pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_outputs *gemm_out,
+                          const pkcu_gemm_inputs *gemm_in, const pkcu_seq *seq,
+                          pkcu_stream_t stream);
+
 /* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────
  * Replaces pk_greedy_decode for a batch of utterances (the encoder outputs of
  * n_utts utterances of T_b frames, frames of every utterance in turn). Every

@@ -51,6 +51,8 @@ EXPORTED = (
     "pkcu_decoder_create", "pkcu_decoder_destroy", "pkcu_decoder_buffers", "pkcu_greedy_decode",
     "pkcu_decoder_iterations", "pkcu_decoder_results",
     "pkcu_gemm_bias_swish", "pkcu_gemm_bias_residual",
+    "pkcu_encoder_model_create", "pkcu_encoder_model_destroy", "pkcu_encoder_model_blocks",
+    "pkcu_encoder_forward",
 )
 
 
@@ -82,6 +84,10 @@ _SIGS = {
     "pkcu_pre_plan_out_seq": (VP, [VP]),
     "pkcu_pre_encode": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP]),
     "pkcu_gemm_bias_swish": (I, [VP, VP, VP, VP, I, I, I, VP]),
+    "pkcu_encoder_model_create": (I, [VP, VP, C.POINTER(VP)]),
+    "pkcu_encoder_model_destroy": (None, [VP]),
+    "pkcu_encoder_model_blocks": (I, [VP]),
+    "pkcu_encoder_forward": (I, [VP, VP, VP, VP, VP, VP]),
     "pkcu_gemm_bias_residual": (I, [VP, VP, VP, VP, F, I, I, I, VP]),
     "pkcu_decoder_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
     "pkcu_decoder_destroy": (None, [VP]),
@@ -565,6 +571,42 @@ class Decoder:
     def close(self):
         if self.handle:
             lib().pkcu_decoder_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class EncoderModel:
+    """pkcu_encoder_model: every block's GEMM weights of an uploaded checkpoint
+    as fp32 device copies; forward() runs all blocks, GEMMs included."""
+
+    def __init__(self, weights: "Weights", stream=None):
+        h = VP()
+        check(lib().pkcu_encoder_model_create(weights.h, stream_handle(stream), C.byref(h)),
+              "pkcu_encoder_model_create")
+        self.handle = h
+
+    @property
+    def blocks(self) -> int:
+        return lib().pkcu_encoder_model_blocks(self.handle)
+
+    def forward(self, x_addr: int, gout: GemmOutputs, gin: GemmInputs, seq: Seq, stream=None):
+        call("pkcu_encoder_forward", self.handle, x_addr, C.byref(gout), C.byref(gin), seq.handle,
+             stream_handle(stream))
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_encoder_model_destroy(self.handle)
             self.handle = VP()
 
     def __enter__(self):

@@ -112,36 +112,42 @@ def gpu_run(cuda, bp, jp, mel):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def pre_encode_gpu(cuda, w, eng, mel):
+    """pkcu_pre_encode with its three GEMMs done by torch: (x [T', 1024], T')."""
+    plan = cuda.PrePlan([MEL_T])
+    P2, P3, T = plan.p2, plan.p3, plan.frames
+    pp = cuda.PreParams()
+    cuda.call("pkcu_weights_pre_params", w.h, C.byref(pp))
+    pre_out = {"pw1": empty(256 * P2), "pw2": empty(256 * P3), "proj": empty(T * D)}
+    pre_in = {"s2d": empty(256 * P2), "s3d": empty(256 * P3), "flat": empty(T * 4096)}
+    x = empty(T * D)
+
+    def pre_hook(user, block, gemm, s):
+        with eng.stream(s):
+            if gemm == 16:
+                view(pre_out["pw1"].data_ptr(), 256, P2).copy_(
+                    eng.weight("pre_encode.conv.3.weight", (256, 256)) @ pre_in["s2d"].view(256, P2))
+            elif gemm == 17:
+                view(pre_out["pw2"].data_ptr(), 256, P3).copy_(
+                    eng.weight("pre_encode.conv.6.weight", (256, 256)) @ pre_in["s3d"].view(256, P3))
+            else:
+                pre_out["proj"].view(T, D).copy_(
+                    pre_in["flat"].view(T, 4096) @ eng.weight("pre_encode.out.weight"))
+        return 0
+
+    ph = cuda.GEMM_HOOK(pre_hook)
+    cuda.pre_encode(dev(mel.reshape(-1)), {f: getattr(pp, f) for f in cuda.PRE_PARAM_FIELDS},
+                    pre_out, pre_in, x, plan, hook=ph)
+    plan.close()
+    return x, T
+
+
 def _gpu_run(cuda, bp, jp, mel):
     import torch
     with cuda.Weights(bp, jp) as w:
         w.upload(cuda.stream_handle())
         eng = Engine(cuda, w)
-        # ── pre-encode ──
-        plan = cuda.PrePlan([MEL_T])
-        P2, P3, T = plan.p2, plan.p3, plan.frames
-        pp = cuda.PreParams()
-        cuda.call("pkcu_weights_pre_params", w.h, C.byref(pp))
-        pre_out = {"pw1": empty(256 * P2), "pw2": empty(256 * P3), "proj": empty(T * D)}
-        pre_in = {"s2d": empty(256 * P2), "s3d": empty(256 * P3), "flat": empty(T * 4096)}
-        x = empty(T * D)
-
-        def pre_hook(user, block, gemm, s):
-            with eng.stream(s):
-                if gemm == 16:
-                    view(pre_out["pw1"].data_ptr(), 256, P2).copy_(
-                        eng.weight("pre_encode.conv.3.weight", (256, 256)) @ pre_in["s2d"].view(256, P2))
-                elif gemm == 17:
-                    view(pre_out["pw2"].data_ptr(), 256, P3).copy_(
-                        eng.weight("pre_encode.conv.6.weight", (256, 256)) @ pre_in["s3d"].view(256, P3))
-                else:
-                    pre_out["proj"].view(T, D).copy_(
-                        pre_in["flat"].view(T, 4096) @ eng.weight("pre_encode.out.weight"))
-            return 0
-
-        ph = cuda.GEMM_HOOK(pre_hook)
-        cuda.pre_encode(dev(mel.reshape(-1)), {f: getattr(pp, f) for f in cuda.PRE_PARAM_FIELDS},
-                        pre_out, pre_in, x, plan, hook=ph)
+        x, T = pre_encode_gpu(cuda, w, eng, mel)
         # ── 24 conformer blocks ──
         L = Layout([T])
         shapes = po.standin_shapes(T)
@@ -220,7 +226,6 @@ def _gpu_run(cuda, bp, jp, mel):
                   "joint_out_b": w.find("joint.joint_net.2.bias").dev}
             dec.decode(dp, hook=dh)
             n_tok, _, toks = dec.results()
-        plan.close()
     return enc, toks[0]
 
 
@@ -236,3 +241,34 @@ def test_pipeline_matches_reference_engine(cuda, model, tmp_path):
           f"{np.abs(enc_ref).max():.3f}); {len(tok_ref)} tokens")
     assert err <= 5e-5, f"encoder output differs by {err:.3e}"
     assert len(tok) == len(tok_ref) and (tok == tok_ref).all(), (len(tok), len(tok_ref))
+
+
+def test_encoder_forward_matches_reference_engine(cuda, model, tmp_path):
+    """The encoder stack through pkcu_encoder_forward -- the library's own GEMMs
+    (cuBLAS fp32) on the fp32 weights pkcu_encoder_model_create made from the
+    uploaded checkpoint -- after pkcu_pre_encode, against the reference's
+    pk_encoder on the same checkpoint and spectrogram."""
+    if not po.ref_full_available():
+        pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
+    import torch
+    tensors, bp, jp, mel = model
+    enc_ref, _ = reference_run(bp, jp, mel, tmp_path)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with cuda.Weights(bp, jp) as w:
+            w.upload(cuda.stream_handle())
+            x, T = pre_encode_gpu(cuda, w, Engine(cuda, w), mel)
+            with cuda.EncoderModel(w) as em, cuda.Seq([T]) as seq:
+                assert em.blocks == 24
+                ws = cuda.EncoderWorkspace(seq, 1)
+                xa, gout, gin = ws.device()
+                view(xa, T, D).copy_(x.view(T, D))
+                em.forward(xa, gout, gin, seq)
+                enc = host(view(xa, T, D)).copy()
+                ws.close()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    err = np.abs(enc.astype(np.float64) - enc_ref).max()
+    print(f"pkcu_encoder_forward: max |gpu - reference| = {err:.3e}")
+    assert err <= 5e-5, f"encoder output differs by {err:.3e}"
