@@ -63,6 +63,8 @@ def parse_args():
                     help="with --aux-only: time only the GEMMs with fused epilogues")
     ap.add_argument("--gemm-rows", type=int, default=24000,
                     help="rows M of the fused-GEMM timing")
+    ap.add_argument("--forward-only", action="store_true",
+                    help="with --aux-only: time only the encoder stack with its GEMMs")
     ap.add_argument("--decode-only", action="store_true",
                     help="with --aux-only: time only the batched greedy decode")
     ap.add_argument("--pre-utts", type=int, default=64,
@@ -549,6 +551,93 @@ def time_fused_gemms(stream, reps, M=GEMM_ROWS):
     return res
 
 
+FWD_UTTS = 32
+
+
+def encoder_gemm_flops(T):
+    """GEMM FLOPs of one conformer block per utterance of T frames (FF 2 x
+    (1024x4096 + 4096x1024), QKV, output, positional on 2T-1 rows, the per-head
+    score / positional-score / context products, the two pointwise convs)."""
+    L = 2 * T - 1
+    return 2 * (T * (2 * 2 * D * FF + D * 3 * D + D * D + 2 * D * D + D * D) + L * D * D
+                + H * (T * T * DH + T * L * DH + T * T * DH))
+
+
+def _synthetic_checkpoint():
+    import tempfile
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import weights_fixture as wf
+    d = tempfile.mkdtemp(prefix="pk_bench_ckpt_")
+    _, bp, jp = wf.write_full_checkpoint(d, np.random.default_rng(5), blank_bias=0.0)
+    return d, bp, jp
+
+
+def time_encoder_forward(stream, reps, n_utts=FWD_UTTS, T=375):
+    """pkcu_encoder_forward: all 24 blocks, GEMMs included (cuBLAS fp32 on fp32
+    weights), over n_utts x T frames of a synthetic checkpoint in the
+    reference's format (int8 projections dequantised once)."""
+    import shutil
+    import torch
+    import pkcuda
+    d, bp, jp = _synthetic_checkpoint()
+    try:
+        with pkcuda.Weights(bp, jp) as w:
+            w.upload(stream)
+            with pkcuda.EncoderModel(w, stream) as em, pkcuda.Seq([T] * n_utts) as seq:
+                ws = pkcuda.EncoderWorkspace(seq, 1)
+                xa, gout, gin = ws.device()
+                x = torch.as_tensor(_DevView(xa, n_utts * T * D), device="cuda")
+                x.copy_(torch.randn(n_utts * T * D, device="cuda"))
+                em.forward(xa, gout, gin, seq, stream)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(max(reps, 1)):
+                    em.forward(xa, gout, gin, seq, stream)
+                e1.record(stream)
+                e1.synchronize()
+                ms = e0.elapsed_time(e1) / max(reps, 1)
+                ws.close()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    flop = 24 * n_utts * encoder_gemm_flops(T)
+    return {"utterances": n_utts, "frames": T, "blocks": 24, "ms": round(ms, 3),
+            "frames_per_s": round(n_utts * T / (ms * 1e-3)),
+            "gemm_tflops_fp32": round(flop / (ms * 1e-3) / 1e12, 1)}
+
+
+def cpu_encoder_baseline(T=375):
+    """The reference's own pk_encoder (oracle/_ref/libpkref_full.so, its GEMMs
+    included, PK_THREADS = min(cores, 16)) on one utterance of T frames of the
+    same synthetic checkpoint; the load is outside the timed call."""
+    import shutil
+    import numpy as np
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("PK_THREADS", str(min(cores, 16)))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    if not po.ref_full_available():
+        return {"unavailable": "oracle/_ref/libpkref_full.so not built"}
+    d, bp, jp = _synthetic_checkpoint()
+    try:
+        lib = C.CDLL(po.LIB_REF_FULL)
+        lib.pkref_model_load.argtypes = [C.c_char_p, C.c_char_p]
+        lib.pkref_model_encode.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_longlong]
+        if lib.pkref_model_load(bp.encode(), jp.encode()) != 0:
+            return {"unavailable": "reference failed to load the synthetic checkpoint"}
+        mel = np.random.default_rng(7).standard_normal((128, 8 * T)).astype(np.float32)
+        t0 = time.perf_counter()
+        tp = lib.pkref_model_encode(mel.ctypes.data, 8 * T, None, 0)
+        dt = time.perf_counter() - t0
+        lib.pkref_model_free()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"value": round(tp / dt, 1), "unit": "frames/s", "cores": int(os.environ["PK_THREADS"]),
+            "kind": "reference", "sample": f"1 utterance of {8 * T} mel frames ({tp} encoder frames) "
+                                           f"through the reference's pk_encoder, {dt:.2f} s"}
+
+
 DEC_UTTS, DEC_T = 256, 375
 
 
@@ -719,6 +808,12 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
+        if args.forward_only:
+            fwd = time_encoder_forward(stream, args.aux_reps)
+            if not args.no_cpu_baseline:
+                fwd["cpu_baseline"] = cpu_encoder_baseline()
+            print(json.dumps({"encoder_forward": fwd}), flush=True)
+            return
         if args.gemm_only:
             print(json.dumps({"fused_gemms": time_fused_gemms(stream, args.aux_reps, args.gemm_rows)}),
                   flush=True)
@@ -806,11 +901,14 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = decode = gemms = None
+    aux = decode = gemms = forward = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
         decode = time_decode(stream, 3)
         gemms = time_fused_gemms(stream, 3)
+        forward = time_encoder_forward(stream, 2)
+        if world == 1 and not args.no_cpu_baseline:
+            forward["cpu_baseline"] = cpu_encoder_baseline()
         if world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = cpu_decode_baseline()
     cpu = None
@@ -848,6 +946,7 @@ def _ours(args, rank, world, local_rank, stream):
             for k, v in aux.items()},
         "decode": decode,
         "fused_gemms": gemms,
+        "encoder_forward": forward,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,

@@ -42,3 +42,41 @@ int pkref_transcribe(const char *bin_path, const char *json_path, const float *m
     free(m);
     return Tp;
 }
+
+/* For timing the reference encoder alone: load once, encode many times. */
+static PkModel *g_model;
+
+int pkref_model_load(const char *bin_path, const char *json_path)
+{
+    pk_verbose = 0;
+    if (g_model) return -1;
+    g_model = (PkModel *)calloc(1, sizeof(PkModel));
+    if (!g_model) return -1;
+    if (pk_load_weights(g_model, bin_path, json_path) != 0) {
+        free(g_model);
+        g_model = NULL;
+        return -1;
+    }
+    return 0;
+}
+
+/* pk_encoder on mel [128, n_frames] with the loaded model; returns T'. */
+int pkref_model_encode(const float *mel, int n_frames, float *enc_out, long long enc_cap)
+{
+    if (!g_model) return -1;
+    float *enc = NULL;
+    int Tp = 0;
+    pk_encoder(g_model, mel, n_frames, &enc, &Tp);
+    const long long n = (long long)Tp * PK_D_MODEL;
+    if (enc_out) memcpy(enc_out, enc, sizeof(float) * (size_t)(n < enc_cap ? n : enc_cap));
+    free(enc);
+    return Tp;
+}
+
+void pkref_model_free(void)
+{
+    if (!g_model) return;
+    pk_free_weights(g_model);
+    free(g_model);
+    g_model = NULL;
+}

@@ -9,6 +9,9 @@
 //                                                     (:198-216, s = 0.5), the
 //                                                     attention output projection
 //                                                     + residual (:418-434, s = 1)
+//   pk_gemm_f32_rm           C = A B                  the plain projections of the
+//                                                     library's own encoder forward
+//                                                     (pk_encoder_model.c)
 //
 // A [M, K], W [K, N] (row-major, the reference's weight layout), fp32 in and
 // out like the reference's sgemm. The products run on the 5th-generation
@@ -65,6 +68,7 @@ using SwishGemm = FastF32<cutlass::epilogue::fusion::LinCombPerColBiasEltAct<
     cutlass::epilogue::thread::SiLu, float, float, float, float>>::Gemm;
 using ResidualGemm = FastF32<cutlass::epilogue::fusion::PerColResAddPerColBiasEltAct<
     ScaledIdentity, float, float, float, float>>::Gemm;
+using PlainGemm = FastF32<cutlass::epilogue::fusion::LinearCombination<float, float, float, float>>::Gemm;
 
 // Per-device workspace for kernels that ask for one (grown, never shrunk).
 static void *g_ws[64];
@@ -158,4 +162,24 @@ extern "C" int pkcu_gemm_bias_residual(const float *A, const float *W, const flo
   args.epilogue.thread.bias_ptr = bias;
   args.epilogue.thread.activation.scale = scale;
   return run<ResidualGemm>(args, (cudaStream_t)stream, what);
+}
+
+// C[M, N] = A[M, K] B[K, N], row-major with packed rows (the library's own
+// projections, pk_encoder_model.c). Returns PKCU_ERR_ARG when the shape does
+// not suit the kernel (N or K not a multiple of 4, misaligned pointers) so the
+// caller can take another GEMM.
+extern "C" int pk_gemm_f32_rm(const float *A, const float *B, float *C, int M, int N, int K,
+                              pkcu_stream_t stream) {
+  const char *what = "pk_gemm_f32_rm";
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || N % 4 || K % 4 || !PK_ALIGNED16(A) ||
+      !PK_ALIGNED16(B) || !PK_ALIGNED16(C))
+    return PKCU_ERR_ARG;
+  auto sd = strides<PlainGemm>(M, N, K);
+  typename PlainGemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
+                                     {M, N, K, 1},
+                                     {A, get<0>(sd), B, get<1>(sd)},
+                                     {{}, C, get<2>(sd), C, get<2>(sd)}};
+  args.epilogue.thread.alpha = 1.0f;
+  args.epilogue.thread.beta = 0.0f;
+  return run<PlainGemm>(args, (cudaStream_t)stream, what);
 }

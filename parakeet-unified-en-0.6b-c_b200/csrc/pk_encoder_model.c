@@ -6,8 +6,10 @@
  * (pkcu_weights_dequant: int8 (float)q * scale, int4 (float)nibble * group
  * scale, fp32 copied; the fused QKV as the reference's loader builds it), so a
  * forward pass is fp32 throughout like the reference's (csrc/encoder.c). The
- * products are cuBLAS single-precision GEMMs (no TF32): the row-major
- * projections of the block (FF, QKV, output), and per utterance the
+ * row-major projections of the block (FF, QKV, output) run on the tensor cores
+ * with fp32 accuracy (k_gemm.cu: three bf16 parts per operand, nine MMAs per
+ * product); the other products are cuBLAS single-precision GEMMs (no TF32):
+ * per utterance the
  * positional projection of its slice of the sinusoidal table
  * (csrc/encoder.c:220-227), the per-head score, positional-score and context
  * products and the two pointwise convolutions, as strided batches over heads
@@ -164,6 +166,15 @@ static int rm_gemm(cublasHandle_t h, int M, int N, int K, const float *A, int ld
                                       : pkcu_fail(PKCU_ERR_CUDA, "cuBLAS SGEMM failed (%d)", (int)s);
 }
 
+/* Row-major projection of the whole batch: the fp32-accurate tensor-core GEMM
+ * when the shape suits it, cuBLAS SGEMM otherwise. */
+static int proj(cublasHandle_t h, int M, int N, int K, const float *A, const float *B, float *C,
+                pkcu_stream_t stream)
+{
+    if (pk_gemm_f32_rm(A, B, C, M, N, K, stream) == PKCU_OK) return PKCU_OK;
+    return rm_gemm(h, M, N, K, A, K, 0, B, N, 0, 0, C, N, 0, 1);
+}
+
 static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
 {
     Fwd *f = (Fwd *)user;
@@ -176,12 +187,12 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     const int n = f->seq->dev.n_items, uni = f->seq->dev.uniform_T;
     const long long F = f->seq->frames;
     switch (gemm) {   /* the row-major projections of the whole batch */
-    case PKCU_GEMM_FF1_1: return rm_gemm(h, (int)F, PK_FF, PK_D, gi->ln_ff1, PK_D, 0, W[W_FF1_1], PK_FF, 0, 0, go->ff1_h, PK_FF, 0, 1);
-    case PKCU_GEMM_FF1_2: return rm_gemm(h, (int)F, PK_D, PK_FF, gi->h1, PK_FF, 0, W[W_FF1_2], PK_D, 0, 0, go->ff1_out, PK_D, 0, 1);
-    case PKCU_GEMM_QKV:   return rm_gemm(h, (int)F, 3 * PK_D, PK_D, gi->ln_sa, PK_D, 0, W[W_QKV], 3 * PK_D, 0, 0, go->qkv, 3 * PK_D, 0, 1);
-    case PKCU_GEMM_OUT:   return rm_gemm(h, (int)F, PK_D, PK_D, gi->attn, PK_D, 0, W[W_OUT], PK_D, 0, 0, go->att_out, PK_D, 0, 1);
-    case PKCU_GEMM_FF2_1: return rm_gemm(h, (int)F, PK_FF, PK_D, gi->ln_ff2, PK_D, 0, W[W_FF2_1], PK_FF, 0, 0, go->ff2_h, PK_FF, 0, 1);
-    case PKCU_GEMM_FF2_2: return rm_gemm(h, (int)F, PK_D, PK_FF, gi->h2, PK_FF, 0, W[W_FF2_2], PK_D, 0, 0, go->ff2_out, PK_D, 0, 1);
+    case PKCU_GEMM_FF1_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff1, W[W_FF1_1], go->ff1_h, stream);
+    case PKCU_GEMM_FF1_2: return proj(h, (int)F, PK_D, PK_FF, gi->h1, W[W_FF1_2], go->ff1_out, stream);
+    case PKCU_GEMM_QKV:   return proj(h, (int)F, 3 * PK_D, PK_D, gi->ln_sa, W[W_QKV], go->qkv, stream);
+    case PKCU_GEMM_OUT:   return proj(h, (int)F, PK_D, PK_D, gi->attn, W[W_OUT], go->att_out, stream);
+    case PKCU_GEMM_FF2_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff2, W[W_FF2_1], go->ff2_h, stream);
+    case PKCU_GEMM_FF2_2: return proj(h, (int)F, PK_D, PK_FF, gi->h2, W[W_FF2_2], go->ff2_out, stream);
     default: break;
     }
     /* per utterance (all utterances in one batch when the lengths agree) */

@@ -55,6 +55,12 @@ int pk_conv_wait_timeouts(unsigned *count, int reset);
 
 #define PK_ALIGNED16(p) ((((uintptr_t)(p)) & 15u) == 0)
 
+/* fp32-accurate tensor-core GEMM (k_gemm.cu): C[M, N] = A[M, K] B[K, N],
+ * row-major, packed rows; PKCU_ERR_ARG (without a message) when N or K is not
+ * a multiple of 4 or a pointer is not 16-byte aligned. */
+int pk_gemm_f32_rm(const float *A, const float *B, float *C, int M, int N, int K,
+                   pkcu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
