@@ -423,6 +423,23 @@ int  pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_outpu
                           const pkcu_gemm_inputs *gemm_in, const pkcu_seq *seq,
                           pkcu_stream_t stream);
 
+/* ── mel spectrograms to tokens on the GPU ─────────────────────────────────
+ * pre_encode_and_scale + encode_blocks + pk_greedy_decode (csrc/encoder.c:
+ * 578-593, 495-512; csrc/decoder.c:80-132) for a batch of utterances, every
+ * GEMM done by the library (fp32-accurate tensor-core GEMMs where the shape
+ * suits them, cuBLAS single precision elsewhere). */
+typedef struct pkcu_asr pkcu_asr;
+int  pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out);
+void pkcu_asr_destroy(pkcu_asr *m);
+/* Encoder frames of an utterance of mel_frames frames: ceil(ceil(ceil(T/2)/2)/2). */
+int  pkcu_asr_encoder_frames(int mel_frames);
+/* mel: device, n_utts spectrograms [128, mel_frames[b]] one after another.
+ * tokens (host, capacity 10 x the sum of encoder frames) receives utterance
+ * b's tokens from 10 x the number of encoder frames before it; n_tokens (host)
+ * their counts. Synchronous; allocates its working buffers per call. */
+int  pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
+                         int *tokens, int *n_tokens, pkcu_stream_t stream);
+
 /* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────
  * Replaces pk_greedy_decode for a batch of utterances (the encoder outputs of
  * n_utts utterances of T_b frames, frames of every utterance in turn). Every

@@ -734,7 +734,10 @@ _ref_full = None
 
 def reference_transcribe(bin_path, json_path, mel):
     """pk_load_weights + pk_encoder + pk_greedy_decode of the reference on one
-    mel spectrogram [128, T]: (encoder output [T', 1024], tokens)."""
+    mel spectrogram [128, T]: (encoder output [T', 1024], tokens). The
+    reference's decode reads uninitialised heap memory through a beta = 0
+    sgemv (pk_lstm_step): run it in a process started with
+    MALLOC_PERTURB_=255 for a result that does not depend on heap history."""
     global _ref_full
     if _ref_full is None:
         _ref_full = _Lib(LIB_REF_FULL, {"pkref_transcribe": (

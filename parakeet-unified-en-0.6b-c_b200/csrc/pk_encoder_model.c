@@ -266,3 +266,227 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
     free(off);
     return st;
 }
+
+/* ── mel spectrograms to tokens: pre-encode, the encoder stack, greedy decode ──
+ * pre_encode_and_scale + encode_blocks + pk_greedy_decode (csrc/encoder.c:
+ * 578-593, 495-512; csrc/decoder.c:80-132) for a batch of utterances, every
+ * GEMM done by the library: the pre-encode's 1x1 convolutions and projection
+ * and joint.enc on the fp32-accurate tensor-core GEMM (cuBLAS SGEMM when a
+ * shape does not suit it), the decoder's per-iteration products (B rows) on
+ * cuBLAS SGEMM. */
+
+struct pkcu_asr {
+    pkcu_encoder_model *enc;
+    cublasHandle_t blas;
+    float *owned;                      /* fp32 copies of int8 / int4 weights */
+    const float *w3, *w6, *w_out;      /* pre-encode 1x1 convs [256, 256], projection [4096, 1024] */
+    pkcu_pre_params pre;
+    const float *wi[2], *wr[2];        /* LSTM W_i, W_r [2560, 640] */
+    const float *j_enc, *j_pred, *j_out;   /* [1024, 640], [640, 640], [640, 1025] */
+    pkcu_dec_params dec;
+};
+
+void pkcu_asr_destroy(pkcu_asr *m)
+{
+    if (!m) return;
+    pkcu_encoder_model_destroy(m->enc);
+    if (m->blas) cublasDestroy(m->blas);
+    if (m->owned) cudaFree(m->owned);
+    free(m);
+}
+
+int pkcu_asr_encoder_frames(int mel_frames)
+{
+    int h = mel_frames;
+    for (int s = 0; s < 3; s++) h = (h + 1) / 2;
+    return h;
+}
+
+/* Device fp32 view of a checkpoint tensor of numel elements: the stored copy
+ * for float32, else dequantised into *dst (advanced past it). */
+static int fp32_tensor(const pkcu_weights *w, const char *name, long long numel, float **dst,
+                       const float **out, pkcu_stream_t stream)
+{
+    pkcu_tensor t;
+    int st = pkcu_weights_find(w, name, &t);
+    if (st) return st;
+    if (t.numel != numel)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_create: '%s' has %lld elements, expected %lld", name,
+                         t.numel, numel);
+    if (t.dtype == PKCU_DTYPE_F32) {
+        *out = (const float *)t.dev;
+        return PKCU_OK;
+    }
+    st = pkcu_weights_dequant(w, name, *dst, stream);
+    if (st) return st;
+    *out = *dst;
+    *dst += (numel + 63) & ~63LL;
+    return PKCU_OK;
+}
+
+int pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out)
+{
+    if (!out) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_create: NULL out");
+    *out = NULL;
+    pkcu_asr *m = (pkcu_asr *)calloc(1, sizeof(*m));
+    if (!m) return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_create: host allocation");
+    int st = pkcu_encoder_model_create(w, stream, &m->enc);
+    if (!st && cublasCreate(&m->blas) != CUBLAS_STATUS_SUCCESS) {
+        m->blas = NULL;
+        st = pkcu_fail(PKCU_ERR_CUDA, "pkcu_asr_create: cublasCreate failed");
+    }
+    /* room for every weight below should the checkpoint quantise it */
+    const long long room = 2 * 65536 + 4096LL * PK_D + 4 * 2560LL * 640 + PK_D * 640LL +
+                           640LL * 640 + 640LL * 1025 + 16 * 64;
+    if (!st && cudaMalloc((void **)&m->owned, sizeof(float) * (size_t)room) != cudaSuccess) {
+        cudaGetLastError();
+        m->owned = NULL;
+        st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_create: weight copies");
+    }
+    float *dst = m->owned;
+    if (!st) st = fp32_tensor(w, "pre_encode.conv.3.weight", 65536, &dst, &m->w3, stream);
+    if (!st) st = fp32_tensor(w, "pre_encode.conv.6.weight", 65536, &dst, &m->w6, stream);
+    if (!st) st = fp32_tensor(w, "pre_encode.out.weight", 4096LL * PK_D, &dst, &m->w_out, stream);
+    if (!st) st = pkcu_weights_pre_params(w, &m->pre);
+    char name[64];
+    for (int l = 0; l < 2 && !st; l++) {
+        snprintf(name, sizeof(name), "decoder.lstm.%d.W_i", l);
+        st = fp32_tensor(w, name, 2560LL * 640, &dst, &m->wi[l], stream);
+        snprintf(name, sizeof(name), "decoder.lstm.%d.W_r", l);
+        if (!st) st = fp32_tensor(w, name, 2560LL * 640, &dst, &m->wr[l], stream);
+    }
+    if (!st) st = fp32_tensor(w, "joint.enc.weight", PK_D * 640LL, &dst, &m->j_enc, stream);
+    if (!st) st = fp32_tensor(w, "joint.pred.weight", 640LL * 640, &dst, &m->j_pred, stream);
+    if (!st) st = fp32_tensor(w, "joint.out.weight", 640LL * 1025, &dst, &m->j_out, stream);
+    static const char *const dn[6] = {"decoder.prediction.embed.weight", "decoder.lstm.0.B",
+                                      "decoder.lstm.1.B", "joint.enc.bias", "joint.pred.bias",
+                                      "joint.joint_net.2.bias"};
+    static const long long dnum[6] = {1025LL * 640, 5120, 5120, 640, 640, 1025};
+    const float *dp[6] = {0};
+    for (int i = 0; i < 6 && !st; i++) st = fp32_tensor(w, dn[i], dnum[i], &dst, &dp[i], stream);
+    if (!st) {
+        m->dec.embed = dp[0]; m->dec.lstm0_b = dp[1]; m->dec.lstm1_b = dp[2];
+        m->dec.joint_enc_b = dp[3]; m->dec.joint_pred_b = dp[4]; m->dec.joint_out_b = dp[5];
+        if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+            st = pkcu_launch_status("pkcu_asr_create");
+    }
+    if (st) {
+        pkcu_asr_destroy(m);
+        return st;
+    }
+    *out = m;
+    return PKCU_OK;
+}
+
+typedef struct {
+    pkcu_asr *m;
+    pkcu_pre_gemm_outputs go;
+    pkcu_pre_gemm_inputs gi;
+    long long P2, P3, F;
+} PreCtx;
+
+static int pre_hook(void *user, int block, int gemm, pkcu_stream_t stream)
+{
+    (void)block;
+    PreCtx *c = (PreCtx *)user;
+    cublasHandle_t h = c->m->blas;
+    if (cublasSetStream(h, (cudaStream_t)stream) != CUBLAS_STATUS_SUCCESS)
+        return pkcu_fail(PKCU_ERR_CUDA, "cublasSetStream failed");
+    switch (gemm) {
+    case PKCU_GEMM_PRE_PW1: return proj(h, 256, (int)c->P2, 256, c->m->w3, c->gi.s2d, c->go.pw1, stream);
+    case PKCU_GEMM_PRE_PW2: return proj(h, 256, (int)c->P3, 256, c->m->w6, c->gi.s3d, c->go.pw2, stream);
+    case PKCU_GEMM_PRE_OUT: return proj(h, (int)c->F, PK_D, 4096, c->gi.flat, c->m->w_out, c->go.proj, stream);
+    }
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: unknown pre-encode GEMM %d", gemm);
+}
+
+typedef struct {
+    pkcu_asr *m;
+    pkcu_dec_gemm_outputs go;
+    pkcu_dec_gemm_inputs gi;
+    const float *x;
+    long long F;
+    int B;
+} DecCtx;
+
+static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
+{
+    (void)block;
+    DecCtx *c = (DecCtx *)user;
+    cublasHandle_t h = c->m->blas;
+    if (cublasSetStream(h, (cudaStream_t)stream) != CUBLAS_STATUS_SUCCESS)
+        return pkcu_fail(PKCU_ERR_CUDA, "cublasSetStream failed");
+    const int B = c->B, Hd = 640;
+    switch (gemm) {
+    case PKCU_GEMM_DEC_ENC:   return proj(h, (int)c->F, Hd, PK_D, c->x, c->m->j_enc, c->go.enc, stream);
+    case PKCU_GEMM_DEC_L0_WI: return rm_gemm(h, B, 4 * Hd, Hd, c->gi.x0, Hd, 0, c->m->wi[0], Hd, 0, 1, c->go.g0i, 4 * Hd, 0, 1);
+    case PKCU_GEMM_DEC_L0_WR: return rm_gemm(h, B, 4 * Hd, Hd, c->gi.h0, Hd, 0, c->m->wr[0], Hd, 0, 1, c->go.g0r, 4 * Hd, 0, 1);
+    case PKCU_GEMM_DEC_L1_WI: return rm_gemm(h, B, 4 * Hd, Hd, c->gi.h0, Hd, 0, c->m->wi[1], Hd, 0, 1, c->go.g1i, 4 * Hd, 0, 1);
+    case PKCU_GEMM_DEC_L1_WR: return rm_gemm(h, B, 4 * Hd, Hd, c->gi.h1, Hd, 0, c->m->wr[1], Hd, 0, 1, c->go.g1r, 4 * Hd, 0, 1);
+    case PKCU_GEMM_DEC_PRED:  return rm_gemm(h, B, Hd, Hd, c->gi.h1, Hd, 0, c->m->j_pred, Hd, 0, 0, c->go.pred, Hd, 0, 1);
+    case PKCU_GEMM_DEC_OUT:   return rm_gemm(h, B, 1025, Hd, c->gi.hidden, Hd, 0, c->m->j_out, 1025, 0, 0, c->go.out, 1025, 0, 1);
+    }
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: unknown decoder GEMM %d", gemm);
+}
+
+int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
+                        int *tokens, int *n_tokens, pkcu_stream_t stream)
+{
+    if (!m || !mel || !mel_frames || n_utts <= 0 || !tokens || !n_tokens)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: bad argument");
+    pkcu_pre_plan *plan = NULL;
+    pkcu_encoder_ws *ws = NULL;
+    pkcu_decoder *dec = NULL;
+    float *pre = NULL;
+    int *enc_frames = NULL;
+    int st = pkcu_pre_plan_create(mel_frames, n_utts, &plan);
+    PreCtx pc = {m};
+    if (!st) {
+        pc.P2 = pkcu_pre_plan_p2(plan);
+        pc.P3 = pkcu_pre_plan_p3(plan);
+        pc.F = pkcu_pre_plan_frames(plan);
+        const long long n2 = 256 * pc.P2, n3 = 256 * pc.P3;
+        const long long total = 2 * n2 + 2 * n3 + pc.F * 4096 + pc.F * PK_D;
+        if (cudaMalloc((void **)&pre, sizeof(float) * (size_t)total) != cudaSuccess) {
+            cudaGetLastError();
+            pre = NULL;
+            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: pre-encode buffers");
+        } else {
+            pc.gi.s2d = pre;
+            pc.go.pw1 = pre + n2;
+            pc.gi.s3d = pre + 2 * n2;
+            pc.go.pw2 = pre + 2 * n2 + n3;
+            pc.gi.flat = pre + 2 * n2 + 2 * n3;
+            pc.go.proj = pc.gi.flat + pc.F * 4096;
+        }
+    }
+    const pkcu_seq *seq = plan ? pkcu_pre_plan_out_seq(plan) : NULL;
+    float *x = NULL;
+    pkcu_gemm_outputs go;
+    pkcu_gemm_inputs gi;
+    if (!st) st = pkcu_encoder_ws_create(seq, 1, &ws);
+    if (!st) st = pkcu_encoder_ws_device(ws, &x, &go, &gi);
+    if (!st) st = pkcu_pre_encode(mel, &m->pre, &pc.go, &pc.gi, x, plan, pre_hook, &pc, stream);
+    if (!st) st = pkcu_encoder_forward(m->enc, x, &go, &gi, seq, stream);
+    if (!st) {
+        enc_frames = (int *)malloc(sizeof(int) * (size_t)n_utts);
+        if (!enc_frames) st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: host allocation");
+        for (int i = 0; i < n_utts && !st; i++) enc_frames[i] = pkcu_asr_encoder_frames(mel_frames[i]);
+    }
+    if (!st) st = pkcu_decoder_create(enc_frames, n_utts, &dec);
+    DecCtx dc = {m};
+    if (!st) {
+        st = pkcu_decoder_buffers(dec, &dc.go, &dc.gi);
+        dc.x = x;
+        dc.F = pc.F;
+        dc.B = n_utts;
+    }
+    if (!st) st = pkcu_greedy_decode(dec, &m->dec, dec_hook, &dc, stream);
+    if (!st) st = pkcu_decoder_results(dec, n_tokens, NULL, tokens, stream);
+    pkcu_decoder_destroy(dec);
+    pkcu_encoder_ws_destroy(ws);
+    pkcu_pre_plan_destroy(plan);
+    if (pre) cudaFree(pre);
+    free(enc_frames);
+    return st;
+}

@@ -52,7 +52,8 @@ EXPORTED = (
     "pkcu_decoder_iterations", "pkcu_decoder_results",
     "pkcu_gemm_bias_swish", "pkcu_gemm_bias_residual",
     "pkcu_encoder_model_create", "pkcu_encoder_model_destroy", "pkcu_encoder_model_blocks",
-    "pkcu_encoder_forward",
+    "pkcu_encoder_forward", "pkcu_asr_create", "pkcu_asr_destroy", "pkcu_asr_encoder_frames",
+    "pkcu_asr_transcribe",
 )
 
 
@@ -88,6 +89,10 @@ _SIGS = {
     "pkcu_encoder_model_destroy": (None, [VP]),
     "pkcu_encoder_model_blocks": (I, [VP]),
     "pkcu_encoder_forward": (I, [VP, VP, VP, VP, VP, VP]),
+    "pkcu_asr_create": (I, [VP, VP, C.POINTER(VP)]),
+    "pkcu_asr_destroy": (None, [VP]),
+    "pkcu_asr_encoder_frames": (I, [I]),
+    "pkcu_asr_transcribe": (I, [VP, VP, C.POINTER(I), I, C.POINTER(I), C.POINTER(I), VP]),
     "pkcu_gemm_bias_residual": (I, [VP, VP, VP, VP, F, I, I, I, VP]),
     "pkcu_decoder_create": (I, [C.POINTER(I), I, C.POINTER(VP)]),
     "pkcu_decoder_destroy": (None, [VP]),
@@ -607,6 +612,48 @@ class EncoderModel:
     def close(self):
         if self.handle:
             lib().pkcu_encoder_model_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class ASR:
+    """pkcu_asr: mel spectrograms to tokens with the library's own GEMMs."""
+
+    def __init__(self, weights: "Weights", stream=None):
+        h = VP()
+        check(lib().pkcu_asr_create(weights.h, stream_handle(stream), C.byref(h)), "pkcu_asr_create")
+        self.handle = h
+
+    def transcribe(self, mel, mel_frames, stream=None):
+        """mel: device tensor of the spectrograms [128, T_b] one after another;
+        returns one token array per utterance."""
+        import numpy as np
+        n = len(mel_frames)
+        mf = (I * n)(*[int(t) for t in mel_frames])
+        enc = [lib().pkcu_asr_encoder_frames(int(t)) for t in mel_frames]
+        cap = 10 * sum(enc)
+        tok = (I * cap)()
+        cnt = (I * n)()
+        call("pkcu_asr_transcribe", self.handle, mel if isinstance(mel, int) else ptr(mel), mf, n,
+             tok, cnt, stream_handle(stream))
+        t = np.frombuffer(tok, dtype=np.int32)
+        off = np.concatenate([[0], np.cumsum(enc)]) * 10
+        return [t[off[b]:off[b] + cnt[b]].copy() for b in range(n)]
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_asr_destroy(self.handle)
             self.handle = VP()
 
     def __enter__(self):

@@ -48,7 +48,15 @@ def model(tmp_path_factory):
 
 def reference_run(bp, jp, mel, tmp):
     """The reference engine in a fresh process (its loader keeps file-scope
-    state between loads): (encoder output, tokens)."""
+    state between loads): (encoder output, tokens).
+
+    Run with glibc's MALLOC_PERTURB_=255, which makes every allocation start
+    zeroed: the reference's pk_lstm_step fills a freshly malloc'd gates buffer
+    through cblas_sgemv with beta = 0, and that sgemv computes
+    alpha * acc + beta * y (csrc/tensor_ops.c:601-606, csrc/blas.c:67), so NaN
+    or Inf bytes left in the allocation poison the LSTM state and the tokens
+    then depend on the process's heap history. Zeroed allocations give the
+    result the code intends (beta = 0 overwrites)."""
     np.save(tmp / "mel.npy", mel)
     code = ("import sys, numpy as np; sys.path[:0] = sys.argv[1:3]; import pyoracle as po; "
             "e, t = po.reference_transcribe(sys.argv[3], sys.argv[4], np.load(sys.argv[5])); "
@@ -58,7 +66,7 @@ def reference_run(bp, jp, mel, tmp):
     subprocess.run([sys.executable, "-c", code, os.path.join(root, "oracle"),
                     os.path.join(root, "tests"), bp, jp, str(tmp / "mel.npy"),
                     str(tmp / "enc.npy"), str(tmp / "tok.npy")], check=True,
-                   capture_output=True)
+                   capture_output=True, env={**os.environ, "MALLOC_PERTURB_": "255"})
     return np.load(tmp / "enc.npy"), np.load(tmp / "tok.npy")
 
 
@@ -272,3 +280,26 @@ def test_encoder_forward_matches_reference_engine(cuda, model, tmp_path):
     err = np.abs(enc.astype(np.float64) - enc_ref).max()
     print(f"pkcu_encoder_forward: max |gpu - reference| = {err:.3e}")
     assert err <= 5e-5, f"encoder output differs by {err:.3e}"
+
+
+def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):
+    """pkcu_asr_transcribe -- mel to tokens with every GEMM done by the library --
+    on a ragged batch of two spectrograms (200 and 136 mel frames) against the
+    reference engine run on each alone."""
+    if not po.ref_full_available():
+        pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
+    tensors, bp, jp, mel = model
+    mel2 = np.random.default_rng(8).standard_normal((128, 136)).astype(np.float32)
+    want = []
+    for i, m in enumerate((mel, mel2)):
+        d = tmp_path / f"u{i}"
+        d.mkdir()
+        want.append(reference_run(bp, jp, m, d)[1])
+    with cuda.Weights(bp, jp) as w:
+        w.upload(cuda.stream_handle())
+        with cuda.ASR(w) as asr:
+            got = asr.transcribe(dev(np.concatenate([mel.reshape(-1), mel2.reshape(-1)])),
+                                 [mel.shape[1], mel2.shape[1]])
+    for b in range(2):
+        assert len(got[b]) == len(want[b]) and (got[b] == want[b]).all(), \
+            (b, len(got[b]), len(want[b]))
