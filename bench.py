@@ -65,6 +65,10 @@ def parse_args():
                     help="rows M of the fused-GEMM timing")
     ap.add_argument("--forward-only", action="store_true",
                     help="with --aux-only: time only the encoder stack with its GEMMs")
+    ap.add_argument("--asr-decode-only", action="store_true",
+                    help="with --aux-only: time only pkcu_asr_decode")
+    ap.add_argument("--asr-only", action="store_true",
+                    help="with --aux-only: time only mel-to-tokens transcription")
     ap.add_argument("--decode-only", action="store_true",
                     help="with --aux-only: time only the batched greedy decode")
     ap.add_argument("--pre-utts", type=int, default=64,
@@ -563,19 +567,89 @@ def encoder_gemm_flops(T):
                 + H * (T * T * DH + T * L * DH + T * T * DH))
 
 
-def _synthetic_checkpoint():
+def _synthetic_checkpoint(blank_bias=0.0):
     import tempfile
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import weights_fixture as wf
     d = tempfile.mkdtemp(prefix="pk_bench_ckpt_")
-    _, bp, jp = wf.write_full_checkpoint(d, np.random.default_rng(5), blank_bias=0.0)
+    _, bp, jp = wf.write_full_checkpoint(d, np.random.default_rng(5), blank_bias=blank_bias)
     return d, bp, jp
 
 
+DEC_PROFILES = {"about_1_token_per_frame": 3.5, "10_tokens_every_frame": 0.0}
+
+
+def time_asr_decode(stream, reps, n_utts=256, T=375, cpu=True):
+    """pkcu_asr_decode (the decode alone, a batched pk_greedy_decode with the
+    model's own product kernels) on n_utts x T encoder frames of N(0, 1),
+    through the public API (host tokens out), for two emission profiles set by
+    the checkpoint's blank bias; beside each, the reference's own
+    pk_greedy_decode on one such utterance (its sgemv products, host cores)."""
+    import shutil
+    import numpy as np
+    import torch
+    import pkcuda
+    out = {}
+    for name, bb in DEC_PROFILES.items():
+        d, bp, jp = _synthetic_checkpoint(blank_bias=bb)
+        try:
+            enc = np.random.default_rng(21).standard_normal((n_utts * T, D)).astype(np.float32)
+            with pkcuda.Weights(bp, jp) as w:
+                w.upload(stream)
+                with pkcuda.ASR(w, stream) as asr:
+                    x = torch.from_numpy(enc).cuda()
+                    toks = asr.decode(x, [T] * n_utts, stream)
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    for _ in range(max(reps, 1)):
+                        toks = asr.decode(x, [T] * n_utts, stream)
+                    dt = (time.perf_counter() - t0) / max(reps, 1)
+            ntok = int(sum(len(t) for t in toks))
+            r = {"utterances": n_utts, "frames": T, "blank_bias": bb, "seconds_per_call": round(dt, 4),
+                 "frames_per_s": round(n_utts * T / dt), "tokens_per_frame": round(ntok / (n_utts * T), 3)}
+            if cpu:
+                r["cpu_baseline"] = _cpu_ref_decode(bp, jp, enc[:T], T)
+            out[name] = r
+        finally:
+            shutil.rmtree(d, ignore_errors=True)
+    out["note"] = ("host wall clock of the synchronous call: decoder set-up, the encoder projection, "
+                   "the decode graph, tokens copied to the host")
+    return out
+
+
+def _cpu_ref_decode(bp, jp, enc, T):
+    """The reference's pk_greedy_decode on one utterance's encoder rows."""
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("PK_THREADS", str(min(cores, 16)))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import tempfile
+    import numpy as np
+    import pyoracle as po
+    if not po.ref_full_available():
+        return {"unavailable": "oracle/_ref/libpkref_full.so not built"}
+    with tempfile.TemporaryDirectory() as td:
+        ep = os.path.join(td, "enc.npy")
+        np.save(ep, np.ascontiguousarray(enc, np.float32))
+        code = ("import ctypes as C, sys, time, numpy as np; L = C.CDLL(sys.argv[1]); "
+                "L.pkref_model_load.argtypes = [C.c_char_p, C.c_char_p]; "
+                "L.pkref_model_decode.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int]; "
+                "assert L.pkref_model_load(sys.argv[2].encode(), sys.argv[3].encode()) == 0; "
+                "e = np.load(sys.argv[4]); tok = np.zeros(10 * e.shape[0], np.int32); "
+                "t0 = time.perf_counter(); n = L.pkref_model_decode(e.ctypes.data, e.shape[0], tok.ctypes.data, tok.size); "
+                "print(time.perf_counter() - t0, n)")
+        o = subprocess.run([sys.executable, "-c", code, po.LIB_REF_FULL, bp, jp, ep], capture_output=True,
+                           text=True, check=True, env={**os.environ, "MALLOC_PERTURB_": "255"}).stdout.split()
+    dt, n = float(o[-2]), int(o[-1])
+    return {"value": round(T / dt, 1), "unit": "frames/s", "cores": int(os.environ["PK_THREADS"]),
+            "kind": "reference", "sample": f"1 utterance of {T} encoder frames through the reference's "
+                                           f"pk_greedy_decode, {dt:.2f} s, {n} tokens"}
+
+
 def time_encoder_forward(stream, reps, n_utts=FWD_UTTS, T=375):
-    """pkcu_encoder_forward: all 24 blocks, GEMMs included (cuBLAS fp32 on fp32
-    weights), over n_utts x T frames of a synthetic checkpoint in the
+    """pkcu_encoder_forward: all 24 blocks, GEMMs included (the tcgen05
+    FastFP32 GEMM for the row-major projections, cuBLAS fp32 for the rest, on
+    fp32 weights), over n_utts x T frames of a synthetic checkpoint in the
     reference's format (int8 projections dequantised once)."""
     import shutil
     import torch
@@ -636,6 +710,74 @@ def cpu_encoder_baseline(T=375):
     return {"value": round(tp / dt, 1), "unit": "frames/s", "cores": int(os.environ["PK_THREADS"]),
             "kind": "reference", "sample": f"1 utterance of {8 * T} mel frames ({tp} encoder frames) "
                                            f"through the reference's pk_encoder, {dt:.2f} s"}
+
+
+ASR_UTTS, ASR_MEL = 32, 3000
+
+
+def time_asr(stream, reps, n_utts=ASR_UTTS, mel_frames=ASR_MEL):
+    """pkcu_asr_transcribe: n_utts spectrograms of 3000 mel frames (30 s each)
+    to tokens -- pre-encode, 24 blocks, greedy decode, every GEMM done by the
+    library -- on a synthetic checkpoint in the reference's format."""
+    import shutil
+    import torch
+    import pkcuda
+    d, bp, jp = _synthetic_checkpoint()
+    try:
+        with pkcuda.Weights(bp, jp) as w:
+            w.upload(stream)
+            with pkcuda.ASR(w, stream) as asr:
+                g = torch.Generator(device="cuda")
+                g.manual_seed(13)
+                mel = torch.randn(n_utts * 128 * mel_frames, generator=g, device="cuda")
+                frames = [mel_frames] * n_utts
+                out = asr.transcribe(mel, frames, stream)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                for _ in range(max(reps, 1)):
+                    out = asr.transcribe(mel, frames, stream)
+                dt = (time.perf_counter() - t0) / max(reps, 1)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    enc = n_utts * (((mel_frames + 1) // 2 + 1) // 2 + 1) // 2
+    return {"utterances": n_utts, "mel_frames": mel_frames, "seconds_per_call": round(dt, 4),
+            "utterances_per_s": round(n_utts / dt, 2), "encoder_frames_per_s": round(enc / dt),
+            "audio_seconds_per_s": round(n_utts * mel_frames / 100.0 / dt, 1),
+            "tokens": int(sum(len(o) for o in out)),
+            "note": "host wall clock of the synchronous call (it allocates its buffers per call)"}
+
+
+def cpu_asr_baseline(mel_frames=ASR_MEL):
+    """The reference's own pk_encoder + pk_greedy_decode on one 30 s
+    utterance of the same synthetic checkpoint (load outside the timed call;
+    run with allocations zeroed, see tests/test_pipeline_gpu.py)."""
+    import shutil
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("PK_THREADS", str(min(cores, 16)))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    if not po.ref_full_available():
+        return {"unavailable": "oracle/_ref/libpkref_full.so not built"}
+    d, bp, jp = _synthetic_checkpoint()
+    code = ("import ctypes as C, sys, time, numpy as np; L = C.CDLL(sys.argv[1]); "
+            "L.pkref_model_load.argtypes = [C.c_char_p, C.c_char_p]; "
+            "L.pkref_model_transcribe.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int]; "
+            "assert L.pkref_model_load(sys.argv[2].encode(), sys.argv[3].encode()) == 0; "
+            "T = int(sys.argv[4]); mel = np.random.default_rng(7).standard_normal((128, T)).astype(np.float32); "
+            "tok = np.zeros(10 * T, np.int32); t0 = time.perf_counter(); "
+            "n = L.pkref_model_transcribe(mel.ctypes.data, T, tok.ctypes.data, tok.size); "
+            "print(time.perf_counter() - t0, n)")
+    try:
+        out = subprocess.run([sys.executable, "-c", code, po.LIB_REF_FULL, bp, jp, str(mel_frames)],
+                             capture_output=True, text=True, check=True,
+                             env={**os.environ, "MALLOC_PERTURB_": "255"}).stdout.split()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    dt, n = float(out[-2]), int(out[-1])
+    return {"value": round(1.0 / dt, 4), "unit": "utterances/s", "cores": int(os.environ["PK_THREADS"]),
+            "kind": "reference", "sample": f"1 utterance of {mel_frames} mel frames through the "
+                                           f"reference's pk_encoder + pk_greedy_decode, {dt:.2f} s, "
+                                           f"{n} tokens"}
 
 
 DEC_UTTS, DEC_T = 256, 375
@@ -808,6 +950,16 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
+        if args.asr_decode_only:
+            print(json.dumps({"asr_decode": time_asr_decode(stream, args.aux_reps,
+                                                            cpu=not args.no_cpu_baseline)}), flush=True)
+            return
+        if args.asr_only:
+            asr = time_asr(stream, args.aux_reps)
+            if not args.no_cpu_baseline:
+                asr["cpu_baseline"] = cpu_asr_baseline()
+            print(json.dumps({"asr": asr}), flush=True)
+            return
         if args.forward_only:
             fwd = time_encoder_forward(stream, args.aux_reps)
             if not args.no_cpu_baseline:
@@ -901,14 +1053,17 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = decode = gemms = forward = None
+    aux = decode = gemms = forward = asr = asr_dec = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
         decode = time_decode(stream, 3)
         gemms = time_fused_gemms(stream, 3)
         forward = time_encoder_forward(stream, 2)
+        asr = time_asr(stream, 1)
+        asr_dec = time_asr_decode(stream, 2, cpu=world == 1 and not args.no_cpu_baseline)
         if world == 1 and not args.no_cpu_baseline:
             forward["cpu_baseline"] = cpu_encoder_baseline()
+            asr["cpu_baseline"] = cpu_asr_baseline()
         if world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = cpu_decode_baseline()
     cpu = None
@@ -947,6 +1102,8 @@ def _ours(args, rank, world, local_rank, stream):
         "decode": decode,
         "fused_gemms": gemms,
         "encoder_forward": forward,
+        "asr": asr,
+        "asr_decode": asr_dec,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,

@@ -439,6 +439,20 @@ int  pkcu_asr_encoder_frames(int mel_frames);
  * their counts. Synchronous; allocates its working buffers per call. */
 int  pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
                          int *tokens, int *n_tokens, pkcu_stream_t stream);
+/* The decode alone, a batched pk_greedy_decode (csrc/decoder.c:80-132) with
+ * the model's decoder: enc (device, 16-byte aligned) holds the encoder
+ * outputs [enc_frames[b], 1024] of n_utts utterances one after another;
+ * tokens / n_tokens as for pkcu_asr_transcribe. */
+int  pkcu_asr_decode(pkcu_asr *m, const float *enc, const int *enc_frames, int n_utts,
+                     int *tokens, int *n_tokens, pkcu_stream_t stream);
+/* How pkcu_asr_transcribe and pkcu_asr_decode decode: FUSED (the default) -- the decoder's own
+ * product kernels (pkcu_greedy_decode_fused); GRAPH -- cuBLAS products at the
+ * decoder's GEMM hooks inside its CUDA graph (pkcu_greedy_decode_graph);
+ * EAGER -- the same products launched one at a time (pkcu_greedy_decode). */
+#define PKCU_ASR_DECODE_FUSED 0
+#define PKCU_ASR_DECODE_GRAPH 1
+#define PKCU_ASR_DECODE_EAGER 2
+int  pkcu_asr_set_decode_mode(pkcu_asr *m, int mode);
 
 /* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────
  * Replaces pk_greedy_decode for a batch of utterances (the encoder outputs of
@@ -486,6 +500,31 @@ int  pkcu_decoder_buffers(const pkcu_decoder *dec, pkcu_dec_gemm_outputs *gemm_o
  * kernels between them; DEC_ENC once before the first. */
 int  pkcu_greedy_decode(pkcu_decoder *dec, const pkcu_dec_params *params, pkcu_gemm_hook hook,
                         void *hook_user, pkcu_stream_t stream);
+/* The same decode with the hook's per-iteration GEMMs inside the decoder's
+ * CUDA graph of 8 iterations: the hook must be capture-safe (only stream-
+ * ordered work on the stream it is given, e.g. cuBLAS calls, no synchronisation
+ * or allocation) and its work must not depend on the iteration. It is called
+ * 8 times per product while the graph is captured, and again only when the
+ * hook, its user pointer or the parameter pointers change; DEC_ENC is called
+ * once per decode outside the graph. */
+int  pkcu_greedy_decode_graph(pkcu_decoder *dec, const pkcu_dec_params *params,
+                              pkcu_gemm_hook hook, void *hook_user, pkcu_stream_t stream);
+/* The decode with its own products: the decoder's weights in the reference's
+ * layouts -- LSTM W_i / W_r [2560, 640] (csrc/decoder.c:20-27), joint.pred
+ * [640, 640] and joint.out [640, 1025] as (in, out) (csrc/decoder.c:53-72),
+ * device, 16-byte aligned; the LSTM matrices must outlive the decodes, the
+ * joint matrices are copied (transposed) by pkcu_decoder_set_weights. */
+typedef struct {
+    const float *lstm0_wi, *lstm0_wr, *lstm1_wi, *lstm1_wr;
+    const float *joint_pred, *joint_out;
+} pkcu_dec_weights;
+int  pkcu_decoder_set_weights(pkcu_decoder *dec, const pkcu_dec_weights *w, pkcu_stream_t stream);
+/* Runs the decode with every product but DEC_ENC done by the decoder's own
+ * kernels (fp32; per iteration: LSTM layer 0 and 1 with their cells, pred +
+ * joint hidden, out, argmax + state), replayed as a CUDA graph of 8
+ * iterations. The encoder projection (the DEC_ENC product) must be in
+ * gemm_out.enc before the call. */
+int  pkcu_greedy_decode_fused(pkcu_decoder *dec, const pkcu_dec_params *params, pkcu_stream_t stream);
 int  pkcu_decoder_iterations(const pkcu_decoder *dec);   /* of the last decode */
 /* Host copies (any may be NULL): n_tokens[B], evals[B] (joint evaluations per
  * utterance), tokens[10 F] (utterance b's tokens start at 10 x its first frame). */

@@ -683,6 +683,48 @@ class DecodeProducts:
             self.inputs[DEC_PRODUCTS[g]][it] = np.ctypeslib.as_array(inp, (n_in,)).copy()
 
 
+def random_dec_weights(rng):
+    """Seeded decoder weights in the reference's layouts: LSTM W_i, W_r
+    [2560, 640] per layer, joint.pred [640, 640] and joint.out [640, 1025]
+    as (in, out); entries N(0, 1/640)."""
+    s = 1.0 / np.sqrt(DEC_H)
+    m = lambda *shape: (s * rng.standard_normal(shape)).astype(np.float32)
+    return {"lstm0_wi": m(4 * DEC_H, DEC_H), "lstm0_wr": m(4 * DEC_H, DEC_H),
+            "lstm1_wi": m(4 * DEC_H, DEC_H), "lstm1_wr": m(4 * DEC_H, DEC_H),
+            "joint_pred": m(DEC_H, DEC_H), "joint_out": m(DEC_H, DEC_V)}
+
+
+class WeightProducts:
+    """Serves every product of a decode computed from the decoder's weights
+    (float64 accumulation, rounded once to fp32) and its input row, as the
+    reference's cblas_sgemv calls would (csrc/decoder.c:20-27, 53-72); the
+    encoder projection rows come from enc [T, 640] by frame. Records, per
+    joint evaluation, the gap between the two largest logits (bias added)."""
+
+    def __init__(self, weights: dict, enc, out_b):
+        w = {k: np.asarray(v, np.float64) for k, v in weights.items()}
+        self.mats = {DEC_PRODUCTS.index("l0_wi"): w["lstm0_wi"], DEC_PRODUCTS.index("l0_wr"): w["lstm0_wr"],
+                     DEC_PRODUCTS.index("l1_wi"): w["lstm1_wi"], DEC_PRODUCTS.index("l1_wr"): w["lstm1_wr"],
+                     DEC_PRODUCTS.index("pred"): w["joint_pred"].T, DEC_PRODUCTS.index("out"): w["joint_out"].T}
+        self.enc = np.ascontiguousarray(enc, np.float32)
+        self.out_b = np.asarray(out_b, np.float32)
+        self.gaps = []
+        self.fn = DEC_GEMM_FN(self._serve)
+
+    def _serve(self, user, g, it, inp, n_in, out, n_out):
+        if g == DEC_PRODUCTS.index("enc"):
+            row = self.enc[it]
+        else:
+            x = np.ctypeslib.as_array(inp, (n_in,)).astype(np.float64)
+            row = (self.mats[g] @ x).astype(np.float32)
+            if g == DEC_PRODUCTS.index("out"):
+                top = np.sort(row + self.out_b)[-2:]
+                self.gaps.append(float(top[1] - top[0]))
+        assert row.size == n_out
+        row = np.ascontiguousarray(row, np.float32)
+        C.memmove(out, row.ctypes.data, 4 * n_out)
+
+
 def _dec_call(fn, T, params, products, extra):
     p = [f32(params[r]) for r in DEC_PARAM_ROLES]
     cap = 10 * T + 1

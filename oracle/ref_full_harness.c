@@ -80,3 +80,31 @@ void pkref_model_free(void)
     free(g_model);
     g_model = NULL;
 }
+
+/* pk_encoder + pk_greedy_decode on mel [128, n_frames] with the loaded model
+ * (pkref_model_load); returns the number of tokens, or -1. */
+int pkref_model_transcribe(const float *mel, int n_frames, int *tokens, int tok_cap)
+{
+    if (!g_model) return -1;
+    float *enc = NULL;
+    int Tp = 0;
+    pk_encoder(g_model, mel, n_frames, &enc, &Tp);
+    int *tok = NULL;
+    const int nt = pk_greedy_decode(g_model, enc, Tp, &tok);
+    for (int i = 0; i < nt && i < tok_cap; i++) tokens[i] = tok[i];
+    free(tok);
+    free(enc);
+    return nt;
+}
+
+/* pk_greedy_decode (its own sgemv products) on encoder output enc [T, 1024]
+ * with the loaded model; returns the number of tokens, or -1. */
+int pkref_model_decode(const float *enc, int T, int *tokens, int tok_cap)
+{
+    if (!g_model) return -1;
+    int *tok = NULL;
+    const int nt = pk_greedy_decode(g_model, enc, T, &tok);
+    for (int i = 0; i < nt && i < tok_cap; i++) tokens[i] = tok[i];
+    free(tok);
+    return nt;
+}

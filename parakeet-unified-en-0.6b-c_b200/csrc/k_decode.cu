@@ -171,6 +171,348 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
   if (t < T || pend) atomicAdd(st.live, 1);
 }
 
+// ── the decode's own products (pkcu_greedy_decode_fused) ─────────────────
+// Every product of an iteration has M = batch rows and K = 640: a skinny
+// fp32 GEMM whose weights (31 MB for all six) stay in L2 from one iteration
+// to the next. Each warp holds DEC_RW weight rows (of K contiguous floats) in
+// registers -- lane l owns k in [20 l, 20 l + 20) -- and streams the input
+// rows of its CTA's batch slice: per row 5 float4 loads, 40 packed f32x2
+// FMAs and a 6-shuffle reduce-scatter that leaves row r's dot product in
+// lanes 8 r .. 8 r + 7. The LSTM kernel applies the cell to its own gate
+// products, the pred kernel the joint bias + add + ReLU, so an iteration is
+// five kernels: lstm 0, lstm 1, pred + joint, out, select.
+
+constexpr int DEC_RK = DEC_H / 32;   // consecutive k per lane
+constexpr int DEC_RW = 4;            // weight rows per warp
+constexpr int LSTM_UNITS = 4;        // hidden units per CTA: 8 warps = unit x {W_i, W_r}
+
+// Rows rows[0..3] of W [nrows, 640] (rows past nrows read as 0), this lane's
+// k range, kept as float4 so that every packed FMA takes an aligned pair.
+__device__ __forceinline__ void dec_load_rows(float4 (&w)[DEC_RW][DEC_RK / 4], const float *__restrict__ W,
+                                              const int (&rows)[DEC_RW], int nrows, int lane) {
+#pragma unroll
+  for (int r = 0; r < DEC_RW; r++) {
+#pragma unroll
+    for (int i = 0; i < DEC_RK / 4; i++)
+      w[r][i] = rows[r] < nrows
+                    ? __ldg(reinterpret_cast<const float4 *>(W + (long long)rows[r] * DEC_H + DEC_RK * lane) + i)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// This lane's partial dot products (its 20 k) of the warp's 4 rows with the
+// input row x [640] (shared memory).
+__device__ __forceinline__ void dec_dot_partial(const float4 (&w)[DEC_RW][DEC_RK / 4], const float *x, int lane,
+                                                float *v) {
+  float4 xv[DEC_RK / 4];
+#pragma unroll
+  for (int i = 0; i < DEC_RK / 4; i++) xv[i] = *reinterpret_cast<const float4 *>(x + DEC_RK * lane + 4 * i);
+#pragma unroll
+  for (int r = 0; r < DEC_RW; r++) {
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < DEC_RK / 4; i++) {
+      acc = fma2(make_float2(w[r][i].x, w[r][i].y), make_float2(xv[i].x, xv[i].y), acc);
+      acc = fma2(make_float2(w[r][i].z, w[r][i].w), make_float2(xv[i].z, xv[i].w), acc);
+    }
+    v[r] = acc.x + acc.y;
+  }
+}
+
+// Reduce-scatter of 16 per-lane values v[j] over the warp: returns, in lanes
+// 2 j' and 2 j' + 1, the warp-wide sum of value j' (bit-identical in both).
+// Lane bit 4 keeps values 0..7 or 8..15, bit 3 half of those, then bits 2 and
+// 1; bit 0 sums the pair.
+__device__ __forceinline__ float dec_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+    const bool hi = lane & bit;
+#pragma unroll
+    for (int i = 0; i < half; i++) {
+      const float send = hi ? v[i] : v[i + half];
+      const float keep = hi ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(PK_FULL_MASK, send, bit);
+    }
+  }
+  return v[0] + __shfl_xor_sync(PK_FULL_MASK, v[0], 1);
+}
+
+// Input rows are staged through shared memory in groups of DEC_G batch rows,
+// double-buffered with cp.async so that the next group's loads overlap this
+// group's FMAs, together with what the epilogue needs per row.
+constexpr int DEC_G = 8;
+constexpr int DEC_H4Q = DEC_H / 4;
+
+struct LstmStage {
+  float x[DEC_G][2][DEC_H];   // x and h_in rows
+  float4 c[DEC_G];            // c[b][j0 .. j0 + 3] (this CTA's units)
+  float4 h[DEC_G];            // h_in[b][j0 .. j0 + 3]
+  int use[DEC_G];             // pending and in range
+};
+struct RowStage {
+  float x[DEC_G][DEC_H];
+  int use[DEC_G];             // active (t < T) and in range
+  long long enc_row[DEC_G];   // frame index of the row's current frame
+};
+constexpr size_t DEC_LSTM_SMEM = 2 * sizeof(LstmStage);
+static_assert(DEC_G == 8, "one staging warp per row slot of a 256-thread CTA");
+constexpr size_t DEC_ROW_SMEM = 2 * sizeof(RowStage);
+
+// Warp w of the 8 stages row slot w: its NSRC source rows (when `use`) as
+// 5 x 32 16-byte copies each, at offsets fixed at compile time.
+template <int NSRC>
+__device__ __forceinline__ void dec_stage_row(float *x, const float *s0, const float *s1, long long b, bool use,
+                                              int lane) {
+  if (!use) return;
+#pragma unroll
+  for (int which = 0; which < NSRC; which++) {
+    const float *src = (which ? s1 : s0) + b * DEC_H + 4 * lane;
+    float *dst = x + which * DEC_H + 4 * lane;
+#pragma unroll
+    for (int k = 0; k < DEC_H4Q / 32; k++) cp_async16(dst + 128 * k, src + 128 * k);
+  }
+}
+
+__device__ __forceinline__ void lstm_stage(LstmStage *st, const float *x, const float *h_in, const float *c,
+                                           const int *pending, int j0, int g0, int b_hi) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = g0 + w;
+  const bool in = b < b_hi;
+  const bool use = in && pending[b] != 0;
+  dec_stage_row<2>(&st->x[w][0][0], x, h_in, b, use, lane);
+  if (lane == 0) {
+    st->use[w] = use;
+    if (in) {
+      cp_async16(&st->c[w], c + (long long)b * DEC_H + j0);
+      cp_async16(&st->h[w], h_in + (long long)b * DEC_H + j0);
+    }
+  }
+}
+
+// Work split of the product kernels: the flattened space f = group * B + b
+// (group = the CTA-sized set of weight rows, b = batch row) is cut into equal
+// shares of `per` rows, one per CTA (the grid is about two CTAs per SM). A
+// share covers one or more segments (group, rows [b_lo, b_hi)); the macro
+// opens the loop over them -- every thread of the CTA runs the same segments
+// -- and the kernel body closes it.
+#define DEC_SEGMENTS(n_groups)                                                         \
+  const long long f_end = min((long long)(n_groups) * B, (long long)(blockIdx.x + 1) * per); \
+  for (long long f = (long long)blockIdx.x * per; f < f_end;) {                       \
+    const int grp = (int)(f / B);                                                      \
+    const int b_lo = (int)(f - (long long)grp * B);                                    \
+    const int b_hi = (int)min((long long)B, b_lo + (f_end - f));                        \
+    f += b_hi - b_lo;
+
+// One LSTM layer (pk_lstm_step, csrc/tensor_ops.c:596-629) for the pending
+// rows of its segments: a segment's group owns hidden units j0 = 4 group ..
+// j0 + 3; warp 2u + m computes gate rows {q 640 + j0 + u} of
+// W_i with x (m = 0) or of W_r with h_in (m = 1); the gates (W_r h + W_i x) +
+// (B[i] + B[4H + i]) then go through the cell (warp 0, one lane per row and
+// unit). h_out is a separate buffer (other CTAs still read h_in); rows that
+// are not pending copy h_in.
+__global__ void __launch_bounds__(256, 2) dec_lstm_kernel(const float *__restrict__ Wi, const float *__restrict__ Wr,
+                                                          const float *__restrict__ bias, const float *__restrict__ x,
+                                                          const float *__restrict__ h_in, float *__restrict__ h_out,
+                                                          float *__restrict__ c, const int *__restrict__ pending,
+                                                          int B, int per) {
+  extern __shared__ __align__(16) unsigned char dec_smem[];
+  LstmStage *stage = reinterpret_cast<LstmStage *>(dec_smem);
+  __shared__ float g[2][DEC_G][LSTM_UNITS][2][4];   // [group parity][row slot][unit][W_i, W_r][gate]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u = warp >> 1, m = warp & 1;
+  DEC_SEGMENTS(DEC_H / LSTM_UNITS)
+  const int j0 = grp * LSTM_UNITS;
+  lstm_stage(stage, x, h_in, c, pending, j0, b_lo, b_hi);
+  cp_async_commit();
+  float4 w[DEC_RW][DEC_RK / 4];
+  const int rows[DEC_RW] = {j0 + u, DEC_H + j0 + u, 2 * DEC_H + j0 + u, 3 * DEC_H + j0 + u};
+  dec_load_rows(w, m ? Wr : Wi, rows, 4 * DEC_H, lane);
+  // the epilogue lane (warp 0): row slot eb, unit eu; bias sums B[i] + B[4H + i]
+  const int eb = lane / LSTM_UNITS, eu = lane % LSTM_UNITS, ej = j0 + eu;
+  float bs[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) bs[q] = __ldg(bias + q * DEC_H + ej) + __ldg(bias + 4 * DEC_H + q * DEC_H + ej);
+  for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
+    const int par = it & 1;
+    const LstmStage *cur = stage + par;
+    if (g0 + DEC_G < b_hi) lstm_stage(stage + (par ^ 1), x, h_in, c, pending, j0, g0 + DEC_G, b_hi);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    // the epilogue lane's inputs, read before the buffer can be restaged
+    const int euse = warp == 0 ? cur->use[eb] : 0;
+    const float ec = warp == 0 ? reinterpret_cast<const float *>(&cur->c[eb])[eu] : 0.f;
+    const float eh = warp == 0 ? reinterpret_cast<const float *>(&cur->h[eb])[eu] : 0.f;
+#pragma unroll
+    for (int h = 0; h < DEC_G / 4; h++) {   // 4 rows x 4 gates per reduction
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        if (cur->use[4 * h + k]) {   // warp-uniform
+          dec_dot_partial(w, cur->x[4 * h + k][m], lane, v + 4 * k);
+        } else {
+          v[4 * k] = v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = 0.f;
+        }
+      }
+      const float t = dec_reduce16(v, lane);
+      if ((lane & 1) == 0) g[par][4 * h + (lane >> 3)][u][m][(lane >> 1) & 3] = t;
+    }
+    __syncthreads();
+    if (warp == 0 && g0 + eb < b_hi) {
+      const long long e = (long long)(g0 + eb) * DEC_H + ej;
+      if (euse) {
+        float gt[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) gt[q] = (g[par][eb][eu][1][q] + g[par][eb][eu][0][q]) + bs[q];
+        const float ig = dec_sigmoid(gt[0]), og = dec_sigmoid(gt[1]), fg = dec_sigmoid(gt[2]);
+        const float cg = tanhf(gt[3]);
+        const float cn = fg * ec + ig * cg;
+        c[e] = cn;
+        h_out[e] = og * tanhf(cn);
+      } else {
+        h_out[e] = eh;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  }
+}
+
+__device__ __forceinline__ void row_stage(RowStage *st, const float *src, const int *t, SeqDev seq, int g0,
+                                          int b_hi) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = g0 + w;
+  const int tb = b < b_hi ? t[b] : 0;
+  const bool use = b < b_hi && tb < seq_T(seq, b);
+  dec_stage_row<1>(&st->x[w][0], src, nullptr, b, use, lane);
+  if (lane == 0) {
+    st->use[w] = use;
+    st->enc_row[w] = use ? seq_frame_off(seq, b) + tb : 0;
+  }
+}
+
+// pk_joint's pred projection and hidden (csrc/decoder.c:44-67): for the active
+// rows hidden = relu((enc_t + b_enc) + (h1 joint.pred + b_pred)), zeros for the
+// others. JpT: joint.pred transposed, [640 out, 640 in]. Warp w of a
+// segment's group owns outputs 4 (8 group + w) .. +3. Resets the live count
+// the select accumulates.
+__global__ void __launch_bounds__(256, 2) dec_pred_joint_kernel(const float *__restrict__ JpT, const float *__restrict__ h1,
+                                                                const float *__restrict__ encp, const float *__restrict__ enc_b,
+                                                                const float *__restrict__ pred_b, float *__restrict__ hidden,
+                                                                const int *__restrict__ t, SeqDev seq, int B, int per,
+                                                                int *live) {
+  extern __shared__ __align__(16) unsigned char dec_smem[];
+  RowStage *stage = reinterpret_cast<RowStage *>(dec_smem);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *live = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  DEC_SEGMENTS(DEC_H / (8 * DEC_RW))
+  const int n0 = (grp * 8 + warp) * DEC_RW;
+  row_stage(stage, h1, t, seq, b_lo, b_hi);
+  cp_async_commit();
+  float4 w[DEC_RW][DEC_RK / 4];
+  const int rows[DEC_RW] = {n0, n0 + 1, n0 + 2, n0 + 3};
+  dec_load_rows(w, JpT, rows, DEC_H, lane);
+  const int n = n0 + ((lane >> 1) & 3);
+  const float eb = __ldg(enc_b + n), pb = __ldg(pred_b + n);
+  for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
+    const RowStage *cur = stage + (it & 1);
+    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), h1, t, seq, g0 + DEC_G, b_hi);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < DEC_G / 4; h++) {
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        if (cur->use[4 * h + k]) {
+          dec_dot_partial(w, cur->x[4 * h + k], lane, v + 4 * k);
+        } else {
+          v[4 * k] = v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = 0.f;
+        }
+      }
+      const float t = dec_reduce16(v, lane);
+      const int bb = 4 * h + (lane >> 3);   // lane pair (l, l + 1): row bb, output n0 + ((l >> 1) & 3)
+      if ((lane & 1) == 0 && g0 + bb < b_hi) {
+        float *dst = hidden + (long long)(g0 + bb) * DEC_H + n;
+        if (cur->use[bb]) {
+          const float e = __ldg(encp + cur->enc_row[bb] * DEC_H + n);
+          const float hv = (e + eb) + (t + pb);
+          *dst = hv < 0.f ? 0.f : hv;
+        } else {
+          *dst = 0.f;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  }
+}
+
+// The joint.out product (csrc/decoder.c:69-72) of the active rows; JoT:
+// joint.out transposed, [1025, 640]. The select kernel adds the bias. Warps
+// past the last row still take part in staging and barriers.
+__global__ void __launch_bounds__(256, 2) dec_out_kernel(const float *__restrict__ JoT, const float *__restrict__ hidden,
+                                                         float *__restrict__ out, const int *__restrict__ t, SeqDev seq,
+                                                         int B, int per) {
+  extern __shared__ __align__(16) unsigned char dec_smem[];
+  RowStage *stage = reinterpret_cast<RowStage *>(dec_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  DEC_SEGMENTS((DEC_V + 8 * DEC_RW - 1) / (8 * DEC_RW))
+  const int n0 = (grp * 8 + warp) * DEC_RW;
+  const bool has_rows = n0 < DEC_V;
+  row_stage(stage, hidden, t, seq, b_lo, b_hi);
+  cp_async_commit();
+  float4 w[DEC_RW][DEC_RK / 4];
+  const int rows[DEC_RW] = {n0, n0 + 1, n0 + 2, n0 + 3};
+  dec_load_rows(w, JoT, rows, DEC_V, lane);
+  const int n = n0 + ((lane >> 1) & 3);
+  for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
+    const RowStage *cur = stage + (it & 1);
+    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), hidden, t, seq, g0 + DEC_G, b_hi);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (has_rows) {
+#pragma unroll
+      for (int h = 0; h < DEC_G / 4; h++) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          if (cur->use[4 * h + k]) {   // false past b_hi
+            dec_dot_partial(w, cur->x[4 * h + k], lane, v + 4 * k);
+          } else {
+            v[4 * k] = v[4 * k + 1] = v[4 * k + 2] = v[4 * k + 3] = 0.f;
+          }
+        }
+        const float t = dec_reduce16(v, lane);
+        const int bb = 4 * h + (lane >> 3);
+        if ((lane & 1) == 0 && n < DEC_V && cur->use[bb]) out[(long long)(g0 + bb) * DEC_V + n] = t;
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  }
+}
+
+// dst [cols, rows] = src [rows, cols]^T (the joint weights, once per
+// pkcu_decoder_set_weights).
+__global__ void dec_transpose_kernel(const float *__restrict__ src, float *__restrict__ dst, int rows, int cols) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[(long long)r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[(long long)c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
 static unsigned dec_grid(long long work) {
   long long g = (work + 255) / 256;
   const long long cap = (long long)pkcu_sm_count() * 8;
@@ -189,18 +531,30 @@ struct pkcu_decoder {
   void *block;             // one device allocation for everything below
   DecState st;
   float *lstm;             // h0, h1, c0, c1 [B, 640] each
+  float *hb;               // h0', h1' [B, 640]: the fused decode's odd-iteration states
   float *x0, *hidden;      // [B, 640]
   float *encp, *pred, *out, *g0i, *g0r, *g1i, *g1r;
   int *tokens;             // [10 F]: utterance b's tokens from 10 * frame_off(b)
   int *live_host;          // page-locked poll target
   int iterations;          // of the last decode
   int device;
-  // Without a hook, DEC_POLL iterations and the poll copy are one CUDA graph,
-  // captured on `gs` for the parameter pointers in `gp` and replayed.
+  // Without a hook (or with a capture-safe one, pkcu_greedy_decode_graph),
+  // DEC_POLL iterations and the poll copy are one CUDA graph, captured on `gs`
+  // for the parameter pointers in `gp` and the hook in `ghook` / `guser`, and
+  // replayed.
   cudaStream_t gs;
   cudaEvent_t ev_in, ev_out;
   cudaGraphExec_t graph;
   pkcu_dec_params gp;
+  pkcu_gemm_hook ghook;
+  void *guser;
+  int gfused;              // the graph holds the fused iteration (weights generation gwgen)
+  unsigned gwgen;
+  // pkcu_decoder_set_weights: the LSTM matrices (caller's) and the decoder's
+  // transposed copies of joint.pred / joint.out
+  const float *lw[4];
+  float *jt;               // JpT [640, 640] then JoT [1025, 640]
+  unsigned wgen;           // 0: no weights set
 };
 
 extern "C" void pkcu_decoder_destroy(pkcu_decoder *d) {
@@ -210,6 +564,7 @@ extern "C" void pkcu_decoder_destroy(pkcu_decoder *d) {
   if (d->ev_out) cudaEventDestroy(d->ev_out);
   if (d->gs) cudaStreamDestroy(d->gs);
   if (d->block) cudaFree(d->block);
+  if (d->jt) cudaFree(d->jt);
   if (d->live_host) cudaFreeHost(d->live_host);
   pkcu_seq_destroy(d->seq);
   free(d);
@@ -239,7 +594,7 @@ extern "C" int pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder *
   const size_t sz_lstm = up(sizeof(float) * 4 * B * H), sz_bh = up(sizeof(float) * B * H);
   const size_t sz_enc = up(sizeof(float) * (size_t)F * H), sz_out = up(sizeof(float) * B * DEC_V);
   const size_t sz_g = up(sizeof(float) * B * 4 * H), sz_tok = up(sizeof(int) * DEC_MAX_SYM * (size_t)F);
-  const size_t total = sz_state + sz_lstm + 3 * sz_bh + sz_enc + sz_out + 4 * sz_g + sz_tok;
+  const size_t total = sz_state + sz_lstm + 5 * sz_bh + sz_enc + sz_out + 4 * sz_g + sz_tok;
   if (cudaMalloc(&d->block, total) != cudaSuccess) {
     cudaGetLastError();
     d->block = nullptr;
@@ -257,6 +612,7 @@ extern "C" int pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder *
   d->st = DecState{si, si + B, si + 2 * B, si + 3 * B, si + 4 * B, si + 5 * B, si + 6 * B};
   p += sz_state;
   d->lstm = (float *)p; p += sz_lstm;
+  d->hb = (float *)p; p += 2 * sz_bh;
   d->x0 = (float *)p; p += sz_bh;
   d->hidden = (float *)p; p += sz_bh;
   d->pred = (float *)p; p += sz_bh;
@@ -331,8 +687,52 @@ static bool same_params(const pkcu_dec_params &a, const pkcu_dec_params &b) {
          a.joint_out_b == b.joint_out_b;
 }
 
-// Captures DEC_POLL iterations + the copy of the live count into d->graph.
-static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm) {
+// Rows per CTA share for a product kernel over n_groups x B rows: about two
+// CTAs per SM, at least one staging group of rows; returns the grid size.
+static unsigned dec_share(int n_groups, int B, int *per) {
+  const long long total = (long long)n_groups * B, slots = 2LL * pkcu_sm_count();
+  long long p = (total + slots - 1) / slots;
+  if (p < DEC_G) p = DEC_G;
+  *per = (int)p;
+  return (unsigned)((total + p - 1) / p);
+}
+
+// One iteration of the fused decode on stream s; iteration parity picks the
+// h buffers (even: read lstm, write hb; odd: the reverse).
+static int dec_iteration_fused(pkcu_decoder *d, const pkcu_dec_params *prm, int parity, cudaStream_t s) {
+  const int B = d->B;
+  const size_t BH = (size_t)B * DEC_H;
+  float *ha = parity ? d->hb : d->lstm, *hn = parity ? d->lstm : d->hb;
+  float *c0 = d->lstm + 2 * BH, *c1 = d->lstm + 3 * BH;
+  const SeqDev seq = d->seq->dev;
+  int pl, pp, po;
+  const unsigned gl = dec_share(DEC_H / LSTM_UNITS, B, &pl);
+  const unsigned gp = dec_share(DEC_H / (8 * DEC_RW), B, &pp);
+  const unsigned go = dec_share((DEC_V + 8 * DEC_RW - 1) / (8 * DEC_RW), B, &po);
+  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[0], d->lw[1], prm->lstm0_b, d->x0, ha, hn, c0,
+                                                 d->st.pending, B, pl);
+  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[2], d->lw[3], prm->lstm1_b, hn, ha + BH, hn + BH, c1,
+                                                 d->st.pending, B, pl);
+  dec_pred_joint_kernel<<<gp, 256, DEC_ROW_SMEM, s>>>(d->jt, hn + BH, d->encp, prm->joint_enc_b,
+                                                      prm->joint_pred_b, d->hidden, d->st.t, seq, B, pp,
+                                                      d->st.live);
+  dec_out_kernel<<<go, 256, DEC_ROW_SMEM, s>>>(d->jt + DEC_H * DEC_H, d->hidden, d->out, d->st.t, seq, B, po);
+  dec_select_kernel<<<(unsigned)((B + SEL_ROWS - 1) / SEL_ROWS), 32 * SEL_ROWS, 0, s>>>(
+      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B);
+  return pkcu_launch_status("pkcu_greedy_decode_fused: iteration");
+}
+
+// Captures DEC_POLL iterations (hook form, with the hook's GEMMs if any, or
+// the fused form) + the copy of the live count into d->graph.
+static int g_dec_flags[3][64];
+
+static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
+                       void *hook_user, int fused) {
+  if (fused) {   // no attribute call under capture
+    smem_optin(dec_lstm_kernel, DEC_LSTM_SMEM, g_dec_flags[0]);
+    smem_optin(dec_pred_joint_kernel, DEC_ROW_SMEM, g_dec_flags[1]);
+    smem_optin(dec_out_kernel, DEC_ROW_SMEM, g_dec_flags[2]);
+  }
   if (d->graph) {
     cudaGraphExecDestroy(d->graph);
     d->graph = nullptr;
@@ -344,7 +744,8 @@ static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm) {
   if (cudaStreamBeginCapture(d->gs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
     return pkcu_launch_status("pkcu_greedy_decode: begin capture");
   int st = PKCU_OK;
-  for (int i = 0; i < DEC_POLL && !st; i++) st = dec_iteration(d, prm, nullptr, nullptr, d->gs);
+  for (int i = 0; i < DEC_POLL && !st; i++)
+    st = fused ? dec_iteration_fused(d, prm, i & 1, d->gs) : dec_iteration(d, prm, hook, hook_user, d->gs);
   if (!st && cudaMemcpyAsync(d->live_host, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, d->gs) !=
                  cudaSuccess)
     st = pkcu_launch_status("pkcu_greedy_decode: capture poll copy");
@@ -356,13 +757,17 @@ static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm) {
     st = pkcu_launch_status("pkcu_greedy_decode: instantiate");
   }
   if (g) cudaGraphDestroy(g);
-  if (!st) d->gp = *prm;
+  if (!st) {
+    d->gp = *prm;
+    d->ghook = hook;
+    d->guser = hook_user;
+    d->gfused = fused;
+    d->gwgen = d->wgen;
+  }
   return st;
 }
 
-extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
-                                  void *hook_user, pkcu_stream_t stream) {
-  if (!d || !prm) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode: NULL argument");
+static int check_params(const pkcu_dec_params *prm) {
   const float *need[] = {prm->embed, prm->lstm0_b, prm->lstm1_b, prm->joint_enc_b,
                          prm->joint_pred_b, prm->joint_out_b};
   for (const float *q : need)
@@ -370,34 +775,102 @@ extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, p
   if (!PK_ALIGNED16(prm->embed) || !PK_ALIGNED16(prm->joint_enc_b) ||
       !PK_ALIGNED16(prm->joint_pred_b))
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode: embed, joint_enc_b, joint_pred_b must be 16-byte aligned");
-  cudaStream_t s = (cudaStream_t)stream;
-  const int B = d->B;
-  const size_t BH = (size_t)B * DEC_H;
+  return PKCU_OK;
+}
+
+// every evaluation emits or advances; at most 10 emissions per frame, then one
+// more iteration for the last pending decoder step
+static long long max_iterations(const pkcu_decoder *d) {
   int max_T = 0;
-  for (int b = 0; b < B; b++) max_T = d->seq->lengths[b] > max_T ? d->seq->lengths[b] : max_T;
-  // every evaluation emits or advances; at most 10 emissions per frame, then
-  // one more iteration for the last pending decoder step
-  const long long max_iters = (long long)DEC_MAX_SYM * max_T + 2;
+  for (int b = 0; b < d->B; b++) max_T = d->seq->lengths[b] > max_T ? d->seq->lengths[b] : max_T;
+  return (long long)DEC_MAX_SYM * max_T + 2;
+}
+
+static int dec_start(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
+                     void *hook_user, cudaStream_t s) {
   d->iterations = 0;
-  dec_init_kernel<<<dec_grid((long long)BH), 256, 0, s>>>(d->st, d->lstm, d->x0, prm->embed, B);
+  dec_init_kernel<<<dec_grid((long long)d->B * DEC_H), 256, 0, s>>>(d->st, d->lstm, d->x0,
+                                                                    prm->embed, d->B);
   int st = pkcu_launch_status("pkcu_greedy_decode: init");
-  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_ENC, stream);
+  if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_ENC, s);
+  return st;
+}
+
+// Replays the captured DEC_POLL-iteration graph on d->gs until no utterance
+// is live, joined to the caller's stream on both sides.
+static int dec_replay(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
+                      void *hook_user, int fused, cudaStream_t s) {
+  int st = PKCU_OK;
+  if (!d->graph || !same_params(d->gp, *prm) || d->ghook != hook || d->guser != hook_user ||
+      d->gfused != fused || (fused && d->gwgen != d->wgen))
+    st = dec_capture(d, prm, hook, hook_user, fused);
   if (st) return st;
-  if (!hook) {
-    if (!d->graph || !same_params(d->gp, *prm)) st = dec_capture(d, prm);
-    if (st) return st;
-    if (cudaEventRecord(d->ev_in, s) != cudaSuccess || cudaStreamWaitEvent(d->gs, d->ev_in, 0) != cudaSuccess)
-      return pkcu_launch_status("pkcu_greedy_decode: join");
-    for (long long it = 0; it < max_iters; it += DEC_POLL) {
-      if (cudaGraphLaunch(d->graph, d->gs) != cudaSuccess || cudaStreamSynchronize(d->gs) != cudaSuccess)
-        return pkcu_launch_status("pkcu_greedy_decode: graph");
-      d->iterations += DEC_POLL;
-      if (*d->live_host == 0) break;
-    }
-    if (cudaEventRecord(d->ev_out, d->gs) != cudaSuccess || cudaStreamWaitEvent(s, d->ev_out, 0) != cudaSuccess)
-      return pkcu_launch_status("pkcu_greedy_decode: join");
-    return PKCU_OK;
+  if (cudaEventRecord(d->ev_in, s) != cudaSuccess || cudaStreamWaitEvent(d->gs, d->ev_in, 0) != cudaSuccess)
+    return pkcu_launch_status("pkcu_greedy_decode: join");
+  const long long max_iters = max_iterations(d);
+  for (long long it = 0; it < max_iters; it += DEC_POLL) {
+    if (cudaGraphLaunch(d->graph, d->gs) != cudaSuccess || cudaStreamSynchronize(d->gs) != cudaSuccess)
+      return pkcu_launch_status("pkcu_greedy_decode: graph");
+    d->iterations += DEC_POLL;
+    if (*d->live_host == 0) break;
   }
+  if (cudaEventRecord(d->ev_out, d->gs) != cudaSuccess || cudaStreamWaitEvent(s, d->ev_out, 0) != cudaSuccess)
+    return pkcu_launch_status("pkcu_greedy_decode: join");
+  return PKCU_OK;
+}
+
+extern "C" int pkcu_greedy_decode_graph(pkcu_decoder *d, const pkcu_dec_params *prm,
+                                        pkcu_gemm_hook hook, void *hook_user,
+                                        pkcu_stream_t stream) {
+  if (!d || !prm) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode_graph: NULL argument");
+  int st = check_params(prm);
+  if (!st) st = dec_start(d, prm, hook, hook_user, (cudaStream_t)stream);
+  if (!st) st = dec_replay(d, prm, hook, hook_user, 0, (cudaStream_t)stream);
+  return st;
+}
+
+extern "C" int pkcu_decoder_set_weights(pkcu_decoder *d, const pkcu_dec_weights *w, pkcu_stream_t stream) {
+  if (!d || !w) return pkcu_fail(PKCU_ERR_ARG, "pkcu_decoder_set_weights: NULL argument");
+  const float *m[] = {w->lstm0_wi, w->lstm0_wr, w->lstm1_wi, w->lstm1_wr, w->joint_pred, w->joint_out};
+  for (const float *q : m)
+    if (!q || !PK_ALIGNED16(q))
+      return pkcu_fail(PKCU_ERR_ARG, "pkcu_decoder_set_weights: NULL or not 16-byte aligned weight");
+  const size_t n = (size_t)DEC_H * DEC_H + (size_t)DEC_V * DEC_H;
+  if (!d->jt && cudaMalloc((void **)&d->jt, sizeof(float) * n) != cudaSuccess) {
+    cudaGetLastError();
+    d->jt = nullptr;
+    return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_decoder_set_weights: device allocation");
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 tb(32, 8);
+  dec_transpose_kernel<<<dim3(DEC_H / 32, DEC_H / 32), tb, 0, s>>>(w->joint_pred, d->jt, DEC_H, DEC_H);
+  dec_transpose_kernel<<<dim3((DEC_V + 31) / 32, DEC_H / 32), tb, 0, s>>>(w->joint_out, d->jt + DEC_H * DEC_H,
+                                                                         DEC_H, DEC_V);
+  const int st = pkcu_launch_status("pkcu_decoder_set_weights");
+  if (st) return st;
+  for (int i = 0; i < 4; i++) d->lw[i] = m[i];
+  d->wgen += 1;
+  return PKCU_OK;
+}
+
+extern "C" int pkcu_greedy_decode_fused(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_stream_t stream) {
+  if (!d || !prm) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode_fused: NULL argument");
+  if (!d->wgen) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode_fused: no weights (pkcu_decoder_set_weights)");
+  int st = check_params(prm);
+  if (!st) st = dec_start(d, prm, nullptr, nullptr, (cudaStream_t)stream);
+  if (!st) st = dec_replay(d, prm, nullptr, nullptr, 1, (cudaStream_t)stream);
+  return st;
+}
+
+extern "C" int pkcu_greedy_decode(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
+                                  void *hook_user, pkcu_stream_t stream) {
+  if (!d || !prm) return pkcu_fail(PKCU_ERR_ARG, "pkcu_greedy_decode: NULL argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = check_params(prm);
+  if (!st) st = dec_start(d, prm, hook, hook_user, s);
+  if (st) return st;
+  if (!hook) return dec_replay(d, prm, nullptr, nullptr, 0, s);
+  const long long max_iters = max_iterations(d);
   for (long long it = 0; it < max_iters; it++) {
     st = dec_iteration(d, prm, hook, hook_user, s);
     if (st) return st;

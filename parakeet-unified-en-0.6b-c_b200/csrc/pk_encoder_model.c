@@ -14,6 +14,7 @@
  * (csrc/encoder.c:220-227), the per-head score, positional-score and context
  * products and the two pointwise convolutions, as strided batches over heads
  * (and over utterances when the batch is uniform). */
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -155,6 +156,10 @@ static const float ONE = 1.0f, ZERO = 0.0f;
 
 /* Row-major C[M, N] = A[M, K] B[K, N] (leading dimensions lda, ldb, ldc),
  * as the column-major product C^T = B^T A^T; tb: B is stored [N, K] (C = A B^T). */
+/* The GEMM output buffers are const in pkcu_gemm_outputs (the non-GEMM
+ * kernels only read them); the GEMM hook is what writes them. */
+static float *gemm_dst(const float *p) { return (float *)p; }
+
 static int rm_gemm(cublasHandle_t h, int M, int N, int K, const float *A, int lda, long long sA,
                    const float *B, int ldb, long long sB, int tb, float *C, int ldc, long long sC,
                    int batch)
@@ -187,12 +192,12 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     const int n = f->seq->dev.n_items, uni = f->seq->dev.uniform_T;
     const long long F = f->seq->frames;
     switch (gemm) {   /* the row-major projections of the whole batch */
-    case PKCU_GEMM_FF1_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff1, W[W_FF1_1], go->ff1_h, stream);
-    case PKCU_GEMM_FF1_2: return proj(h, (int)F, PK_D, PK_FF, gi->h1, W[W_FF1_2], go->ff1_out, stream);
-    case PKCU_GEMM_QKV:   return proj(h, (int)F, 3 * PK_D, PK_D, gi->ln_sa, W[W_QKV], go->qkv, stream);
-    case PKCU_GEMM_OUT:   return proj(h, (int)F, PK_D, PK_D, gi->attn, W[W_OUT], go->att_out, stream);
-    case PKCU_GEMM_FF2_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff2, W[W_FF2_1], go->ff2_h, stream);
-    case PKCU_GEMM_FF2_2: return proj(h, (int)F, PK_D, PK_FF, gi->h2, W[W_FF2_2], go->ff2_out, stream);
+    case PKCU_GEMM_FF1_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff1, W[W_FF1_1], gemm_dst(go->ff1_h), stream);
+    case PKCU_GEMM_FF1_2: return proj(h, (int)F, PK_D, PK_FF, gi->h1, W[W_FF1_2], gemm_dst(go->ff1_out), stream);
+    case PKCU_GEMM_QKV:   return proj(h, (int)F, 3 * PK_D, PK_D, gi->ln_sa, W[W_QKV], gemm_dst(go->qkv), stream);
+    case PKCU_GEMM_OUT:   return proj(h, (int)F, PK_D, PK_D, gi->attn, W[W_OUT], gemm_dst(go->att_out), stream);
+    case PKCU_GEMM_FF2_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff2, W[W_FF2_1], gemm_dst(go->ff2_h), stream);
+    case PKCU_GEMM_FF2_2: return proj(h, (int)F, PK_D, PK_FF, gi->h2, W[W_FF2_2], gemm_dst(go->ff2_out), stream);
     default: break;
     }
     /* per utterance (all utterances in one batch when the lengths agree) */
@@ -205,30 +210,30 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
         int st = PKCU_OK;
         switch (gemm) {
         case PKCU_GEMM_POS:   /* P = pe slice [2T-1, 1024] x W_pos */
-            st = rm_gemm(h, L, PK_D, PK_D, pe, PK_D, 0, W[W_POS], PK_D, 0, 0, go->P + po * PK_D, PK_D,
+            st = rm_gemm(h, L, PK_D, PK_D, pe, PK_D, 0, W[W_POS], PK_D, 0, 0, gemm_dst(go->P) + po * PK_D, PK_D,
                          (long long)L * PK_D, per);
             break;
         case PKCU_GEMM_AC:    /* ac[h] = (Q + u)[h] K[h]^T */
             st = rm_gemm(h, T, T, PK_DH, gi->Qu + fo * PK_D, PK_DH, (long long)T * PK_DH,
-                         gi->K + fo * PK_D, PK_DH, (long long)T * PK_DH, 1, go->ac + so, T,
+                         gi->K + fo * PK_D, PK_DH, (long long)T * PK_DH, 1, gemm_dst(go->ac) + so, T,
                          (long long)T * T, Hb);
             break;
         case PKCU_GEMM_BD:    /* bd[h] = (Q + v)[h] P[h]^T (P heads [8, 2T-1, 128] per utterance) */
             st = rm_gemm(h, T, L, PK_DH, gi->Qv + fo * PK_D, PK_DH, (long long)T * PK_DH,
-                         gi->P_h + po * PK_D, PK_DH, (long long)L * PK_DH, 1, go->bd + bo, L,
+                         gi->P_h + po * PK_D, PK_DH, (long long)L * PK_DH, 1, gemm_dst(go->bd) + bo, L,
                          (long long)T * L, Hb);
             break;
         case PKCU_GEMM_AV:    /* attn[h] = S[h] V[h] */
             st = rm_gemm(h, T, PK_DH, T, gi->S + so, T, (long long)T * T, gi->V + fo * PK_D, PK_DH,
-                         (long long)T * PK_DH, 0, go->attn_h + fo * PK_D, PK_DH, (long long)T * PK_DH, Hb);
+                         (long long)T * PK_DH, 0, gemm_dst(go->attn_h) + fo * PK_D, PK_DH, (long long)T * PK_DH, Hb);
             break;
         case PKCU_GEMM_PW1:   /* [2048, T] = W_pw1 [2048, 1024] x cf [1024, T] */
             st = rm_gemm(h, 2 * PK_D, T, PK_D, W[W_PW1], PK_D, 0, gi->cf + fo * PK_D, T,
-                         (long long)PK_D * T, 0, go->pw1 + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
+                         (long long)PK_D * T, 0, gemm_dst(go->pw1) + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
             break;
         case PKCU_GEMM_PW2:   /* [1024, T] = W_pw2 x dw [1024, T] */
             st = rm_gemm(h, PK_D, T, PK_D, W[W_PW2], PK_D, 0, gi->dw + fo * PK_D, T,
-                         (long long)PK_D * T, 0, go->pw2 + fo * PK_D, T, (long long)PK_D * T, per);
+                         (long long)PK_D * T, 0, gemm_dst(go->pw2) + fo * PK_D, T, (long long)PK_D * T, per);
             break;
         default:
             return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: unknown GEMM %d", gemm);
@@ -284,7 +289,17 @@ struct pkcu_asr {
     const float *wi[2], *wr[2];        /* LSTM W_i, W_r [2560, 640] */
     const float *j_enc, *j_pred, *j_out;   /* [1024, 640], [640, 640], [640, 1025] */
     pkcu_dec_params dec;
+    int decode_mode;                   /* PKCU_ASR_DECODE_* */
 };
+
+int pkcu_asr_set_decode_mode(pkcu_asr *m, int mode)
+{
+    if (!m) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_decode_mode: NULL model");
+    if (mode != PKCU_ASR_DECODE_FUSED && mode != PKCU_ASR_DECODE_GRAPH && mode != PKCU_ASR_DECODE_EAGER)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_decode_mode: unknown mode %d", mode);
+    m->decode_mode = mode;
+    return PKCU_OK;
+}
 
 void pkcu_asr_destroy(pkcu_asr *m)
 {
@@ -429,6 +444,46 @@ static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: unknown decoder GEMM %d", gemm);
 }
 
+/* Greedy decode of encoder outputs x [sum enc_frames, 1024] with the model's
+ * decoder, in the model's decode mode; host results. */
+static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_utts, int *tokens,
+                      int *n_tokens, pkcu_stream_t stream)
+{
+    long long F = 0;
+    for (int i = 0; i < n_utts; i++) F += enc_frames[i];
+    pkcu_decoder *dec = NULL;
+    int st = pkcu_decoder_create(enc_frames, n_utts, &dec);
+    DecCtx dc = {.m = m};
+    if (!st) {
+        st = pkcu_decoder_buffers(dec, &dc.go, &dc.gi);
+        dc.x = x;
+        dc.F = F;
+        dc.B = n_utts;
+    }
+    if (!st && m->decode_mode == PKCU_ASR_DECODE_FUSED) {
+        const pkcu_dec_weights dw = {m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
+        st = pkcu_decoder_set_weights(dec, &dw, stream);
+        if (!st) st = dec_hook(&dc, -1, PKCU_GEMM_DEC_ENC, stream);
+        if (!st) st = pkcu_greedy_decode_fused(dec, &m->dec, stream);
+    } else if (!st) {
+        st = m->decode_mode == PKCU_ASR_DECODE_EAGER
+                 ? pkcu_greedy_decode(dec, &m->dec, dec_hook, &dc, stream)
+                 : pkcu_greedy_decode_graph(dec, &m->dec, dec_hook, &dc, stream);
+    }
+    if (!st) st = pkcu_decoder_results(dec, n_tokens, NULL, tokens, stream);
+    pkcu_decoder_destroy(dec);
+    return st;
+}
+
+int pkcu_asr_decode(pkcu_asr *m, const float *enc, const int *enc_frames, int n_utts, int *tokens,
+                    int *n_tokens, pkcu_stream_t stream)
+{
+    if (!m || !enc || !enc_frames || n_utts <= 0 || !tokens || !n_tokens)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_decode: bad argument");
+    if (!PK_ALIGNED16(enc)) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_decode: enc must be 16-byte aligned");
+    return asr_decode(m, enc, enc_frames, n_utts, tokens, n_tokens, stream);
+}
+
 int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
                         int *tokens, int *n_tokens, pkcu_stream_t stream)
 {
@@ -436,11 +491,10 @@ int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, in
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: bad argument");
     pkcu_pre_plan *plan = NULL;
     pkcu_encoder_ws *ws = NULL;
-    pkcu_decoder *dec = NULL;
     float *pre = NULL;
     int *enc_frames = NULL;
     int st = pkcu_pre_plan_create(mel_frames, n_utts, &plan);
-    PreCtx pc = {m};
+    PreCtx pc = {.m = m};
     if (!st) {
         pc.P2 = pkcu_pre_plan_p2(plan);
         pc.P3 = pkcu_pre_plan_p3(plan);
@@ -473,17 +527,7 @@ int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, in
         if (!enc_frames) st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: host allocation");
         for (int i = 0; i < n_utts && !st; i++) enc_frames[i] = pkcu_asr_encoder_frames(mel_frames[i]);
     }
-    if (!st) st = pkcu_decoder_create(enc_frames, n_utts, &dec);
-    DecCtx dc = {m};
-    if (!st) {
-        st = pkcu_decoder_buffers(dec, &dc.go, &dc.gi);
-        dc.x = x;
-        dc.F = pc.F;
-        dc.B = n_utts;
-    }
-    if (!st) st = pkcu_greedy_decode(dec, &m->dec, dec_hook, &dc, stream);
-    if (!st) st = pkcu_decoder_results(dec, n_tokens, NULL, tokens, stream);
-    pkcu_decoder_destroy(dec);
+    if (!st) st = asr_decode(m, x, enc_frames, n_utts, tokens, n_tokens, stream);
     pkcu_encoder_ws_destroy(ws);
     pkcu_pre_plan_destroy(plan);
     if (pre) cudaFree(pre);

@@ -53,7 +53,8 @@ EXPORTED = (
     "pkcu_gemm_bias_swish", "pkcu_gemm_bias_residual",
     "pkcu_encoder_model_create", "pkcu_encoder_model_destroy", "pkcu_encoder_model_blocks",
     "pkcu_encoder_forward", "pkcu_asr_create", "pkcu_asr_destroy", "pkcu_asr_encoder_frames",
-    "pkcu_asr_transcribe",
+    "pkcu_asr_transcribe", "pkcu_asr_set_decode_mode", "pkcu_greedy_decode_graph",
+    "pkcu_decoder_set_weights", "pkcu_greedy_decode_fused", "pkcu_asr_decode",
 )
 
 
@@ -98,6 +99,11 @@ _SIGS = {
     "pkcu_decoder_destroy": (None, [VP]),
     "pkcu_decoder_buffers": (I, [VP, VP, VP]),
     "pkcu_greedy_decode": (I, [VP, VP, VP, VP, VP]),
+    "pkcu_greedy_decode_graph": (I, [VP, VP, VP, VP, VP]),
+    "pkcu_asr_set_decode_mode": (I, [VP, I]),
+    "pkcu_asr_decode": (I, [VP, VP, C.POINTER(I), I, C.POINTER(I), C.POINTER(I), VP]),
+    "pkcu_decoder_set_weights": (I, [VP, VP, VP]),
+    "pkcu_greedy_decode_fused": (I, [VP, VP, VP]),
     "pkcu_decoder_iterations": (I, [VP]),
     "pkcu_decoder_results": (I, [VP, VP, VP, VP, VP]),
     "pkcu_last_error": (C.c_char_p, []),
@@ -529,6 +535,13 @@ class DecParams(C.Structure):
     _fields_ = [(f, VP) for f in DEC_PARAM_FIELDS]
 
 
+DEC_WEIGHT_FIELDS = ("lstm0_wi", "lstm0_wr", "lstm1_wi", "lstm1_wr", "joint_pred", "joint_out")
+
+
+class DecWeights(C.Structure):
+    _fields_ = [(f, VP) for f in DEC_WEIGHT_FIELDS]
+
+
 class DecGemmOutputs(C.Structure):
     _fields_ = [(f, VP) for f in DEC_OUT_FIELDS]
 
@@ -551,11 +564,22 @@ class Decoder:
         self.gemm_out = {f: getattr(go, f) for f in DEC_OUT_FIELDS}
         self.gemm_in = {f: getattr(gi, f) for f in DEC_IN_FIELDS}
 
-    def decode(self, params, hook=None, stream=None) -> None:
-        """params: {field: tensor or address}; hook: a GEMM_HOOK or None."""
+    def decode(self, params, hook=None, stream=None, graph=False) -> None:
+        """params: {field: tensor or address}; hook: a GEMM_HOOK or None;
+        graph=True: pkcu_greedy_decode_graph (the hook must be capture-safe)."""
         p = _struct(DecParams, DEC_PARAM_FIELDS, params)
-        call("pkcu_greedy_decode", self.handle, C.byref(p),
-             C.cast(hook, VP) if hook is not None else None, None, stream_handle(stream))
+        call("pkcu_greedy_decode_graph" if graph else "pkcu_greedy_decode", self.handle,
+             C.byref(p), C.cast(hook, VP) if hook is not None else None, None,
+             stream_handle(stream))
+
+    def set_weights(self, weights, stream=None) -> None:
+        """weights: {field: tensor or address} over DEC_WEIGHT_FIELDS."""
+        w = _struct(DecWeights, DEC_WEIGHT_FIELDS, weights)
+        call("pkcu_decoder_set_weights", self.handle, C.byref(w), stream_handle(stream))
+
+    def decode_fused(self, params, stream=None) -> None:
+        p = _struct(DecParams, DEC_PARAM_FIELDS, params)
+        call("pkcu_greedy_decode_fused", self.handle, C.byref(p), stream_handle(stream))
 
     @property
     def iterations(self) -> int:
@@ -635,6 +659,11 @@ class ASR:
         check(lib().pkcu_asr_create(weights.h, stream_handle(stream), C.byref(h)), "pkcu_asr_create")
         self.handle = h
 
+    DECODE_FUSED, DECODE_GRAPH, DECODE_EAGER = 0, 1, 2
+
+    def set_decode_mode(self, mode: int) -> None:
+        call("pkcu_asr_set_decode_mode", self.handle, int(mode))
+
     def transcribe(self, mel, mel_frames, stream=None):
         """mel: device tensor of the spectrograms [128, T_b] one after another;
         returns one token array per utterance."""
@@ -649,6 +678,21 @@ class ASR:
              tok, cnt, stream_handle(stream))
         t = np.frombuffer(tok, dtype=np.int32)
         off = np.concatenate([[0], np.cumsum(enc)]) * 10
+        return [t[off[b]:off[b] + cnt[b]].copy() for b in range(n)]
+
+    def decode(self, enc, enc_frames, stream=None):
+        """enc: device tensor of the encoder outputs [T_b, 1024] one after
+        another; returns one token array per utterance."""
+        import numpy as np
+        n = len(enc_frames)
+        ef = (I * n)(*[int(t) for t in enc_frames])
+        cap = 10 * sum(int(t) for t in enc_frames)
+        tok = (I * cap)()
+        cnt = (I * n)()
+        call("pkcu_asr_decode", self.handle, enc if isinstance(enc, int) else ptr(enc), ef, n,
+             tok, cnt, stream_handle(stream))
+        t = np.frombuffer(tok, dtype=np.int32)
+        off = np.concatenate([[0], np.cumsum([int(x) for x in enc_frames])]) * 10
         return [t[off[b]:off[b] + cnt[b]].copy() for b in range(n)]
 
     def close(self):

@@ -20,7 +20,7 @@ import pytest
 
 import pyoracle as po
 from conftest import assert_bitexact, assert_close
-from gpuhelp import dev, from_device
+from gpuhelp import _DeviceView, dev, from_device
 
 pytestmark = pytest.mark.gpu
 
@@ -168,3 +168,104 @@ def test_decode_graph_no_hook(cuda):
                 assert_bitexact(tokens[b], tok_o.astype(np.int32), f"tokens {b}")
                 assert evals[b] == it_o
                 assert n_tok[b] == (10 * T if emits[b] else 0)
+
+
+def test_decode_graph_with_hook(cuda):
+    """pkcu_greedy_decode_graph: the hook's products are captured into the
+    8-iteration graph (here device-to-device copies of one fixed row per
+    utterance, as in the test above); the hook is called 8 times per product
+    while capturing and, on the second decode with the same hook, only for
+    DEC_ENC."""
+    import torch
+    frames = [4, 9, 2, 6]
+    emits = [False, True, True, False]
+    rng = np.random.default_rng(76)
+    params = po.random_dec_params(rng)
+    rows = {k: [] for k in ("pred", "out", "l0_wi", "l0_wr", "l1_wi", "l1_wr")}
+    tables = []
+    for T, em in zip(frames, emits):
+        t = po.random_dec_products(rng, T, 0.0, max_iters=1)
+        t["out"][0, po.DEC_BLANK] = -100.0 if em else 100.0
+        for k in rows:
+            rows[k].append(t[k][0])
+        n = 10 * T + 2
+        tables.append({k: (v if k == "enc" else np.repeat(v, n, axis=0)) for k, v in t.items()})
+    field = {"pred": "pred", "out": "out", "l0_wi": "g0i", "l0_wr": "g0r", "l1_wi": "g1i",
+             "l1_wr": "g1r"}
+    src = {k: torch.as_tensor(np.stack(v)).cuda() for k, v in rows.items()}
+    enc = torch.as_tensor(np.concatenate([t["enc"][:f] for t, f in zip(tables, frames)])).cuda()
+    calls = []
+    with cuda.Decoder(frames) as dec:
+        dst = {k: torch.as_tensor(_DeviceView(dec.gemm_out[field[k]], src[k].numel(), np.float32),
+                                  device="cuda") for k in rows}
+        enc_dst = torch.as_tensor(_DeviceView(dec.gemm_out["enc"], enc.numel(), np.float32),
+                                  device="cuda")
+
+        def hook(user, block, gemm, stream):
+            name = NAME[gemm]
+            calls.append(name)
+            ctx = (torch.cuda.stream(torch.cuda.ExternalStream(stream)) if stream
+                   else contextlib.nullcontext())
+            with ctx:
+                if name == "enc":
+                    enc_dst.copy_(enc.reshape(-1))
+                else:
+                    dst[name].copy_(src[name].reshape(-1))
+            return 0
+
+        fn = cuda.GEMM_HOOK(hook)
+        dp = device_params(params)
+        torch.cuda.synchronize()
+        for rep in range(2):
+            calls.clear()
+            dec.decode(dp, hook=fn, graph=True)
+            n_tok, evals, tokens = dec.results()
+            want_calls = 1 + (6 * 8 if rep == 0 else 0)
+            assert len(calls) == want_calls and calls[0] == "enc", (rep, len(calls))
+            need = max(10 * T + 1 if em else T for T, em in zip(frames, emits))
+            assert dec.iterations % 8 == 0 and need <= dec.iterations < need + 8
+            for b, (T, table) in enumerate(zip(frames, tables)):
+                tok_o, it_o, _ = po.oracle_greedy_decode(T, params, po.DecodeProducts(table))
+                assert_bitexact(tokens[b], tok_o.astype(np.int32), f"tokens {b}")
+                assert evals[b] == it_o
+
+
+def test_decode_fused_matches_reference(cuda):
+    """pkcu_greedy_decode_fused -- the decoder's own LSTM / joint product
+    kernels -- on a ragged batch, against the restatement and the reference's
+    own pk_greedy_decode, both fed products computed in float64 from the same
+    weights (fp32 products in the kernels: tokens and joint evaluations
+    exact, LSTM states within 1e-4; the seed's smallest top-2 logit gap is
+    7e-4, far above the products' rounding). Decoded twice to replay the
+    captured graph."""
+    rng = np.random.default_rng(78)
+    frames = [23, 5, 40, 1, 17, 31, 8, 12, 64, 3]
+    B = len(frames)
+    params = po.random_dec_params(rng)
+    params["out_b"][po.DEC_BLANK] += 3.5      # about one token per frame
+    weights = po.random_dec_weights(rng)
+    encs = [rng.standard_normal((T, H)).astype(np.float32) for T in frames]
+    with cuda.Decoder(frames) as dec:
+        to_device(dec.gemm_out["enc"], np.concatenate(encs))
+        dec.set_weights({k: dev(v) for k, v in weights.items()})
+        dp = device_params(params)
+        for _ in range(2):
+            dec.decode_fused(dp)
+            n_tok, evals, tokens = dec.results()
+            h0 = from_device(dec.gemm_in["h0"], B * H, np.float32).reshape(B, H)
+            h1 = from_device(dec.gemm_in["h1"], B * H, np.float32).reshape(B, H)
+            assert dec.iterations % 8 == 0
+            err = 0.0
+            for b, T in enumerate(frames):
+                tok_o, it_o, st_o = po.oracle_greedy_decode(
+                    T, params, po.WeightProducts(weights, encs[b], params["out_b"]))
+                tok_r, it_r = po.reference_greedy_decode(
+                    T, params, po.WeightProducts(weights, encs[b], params["out_b"]))
+                assert_bitexact(tok_o, tok_r, f"restatement vs reference, utterance {b}")
+                assert it_o == it_r
+                assert_bitexact(tokens[b], tok_o.astype(np.int32), f"tokens {b}")
+                assert evals[b] == it_o and n_tok[b] == len(tok_o)
+                err = max(err, float(np.abs(h0[b] - st_o[0]).max()), float(np.abs(h1[b] - st_o[1]).max()))
+            assert err < 1e-4, err
+    print(f"fused decode: {int(sum(n_tok))} tokens over {sum(frames)} frames, "
+          f"max |h - oracle| = {err:.3g}")

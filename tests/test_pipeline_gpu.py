@@ -290,16 +290,26 @@ def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):
         pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
     tensors, bp, jp, mel = model
     mel2 = np.random.default_rng(8).standard_normal((128, 136)).astype(np.float32)
-    want = []
+    want, enc = [], []
     for i, m in enumerate((mel, mel2)):
         d = tmp_path / f"u{i}"
         d.mkdir()
-        want.append(reference_run(bp, jp, m, d)[1])
+        e, t = reference_run(bp, jp, m, d)
+        enc.append(e)
+        want.append(t)
     with cuda.Weights(bp, jp) as w:
         w.upload(cuda.stream_handle())
         with cuda.ASR(w) as asr:
-            got = asr.transcribe(dev(np.concatenate([mel.reshape(-1), mel2.reshape(-1)])),
-                                 [mel.shape[1], mel2.shape[1]])
+            mels = dev(np.concatenate([mel.reshape(-1), mel2.reshape(-1)]))
+            frames = [mel.shape[1], mel2.shape[1]]
+            got = []
+            ref_enc = dev(np.concatenate([e.reshape(-1) for e in enc]))
+            for mode in (asr.DECODE_FUSED, asr.DECODE_GRAPH, asr.DECODE_EAGER):
+                asr.set_decode_mode(mode)
+                got.append(asr.transcribe(mels, frames))
+                # the decode alone, on the reference's own encoder outputs
+                got.append(asr.decode(ref_enc, [e.shape[0] for e in enc]))
     for b in range(2):
-        assert len(got[b]) == len(want[b]) and (got[b] == want[b]).all(), \
-            (b, len(got[b]), len(want[b]))
+        for g in got:
+            assert len(g[b]) == len(want[b]) and (g[b] == want[b]).all(), \
+                (b, len(g[b]), len(want[b]))
