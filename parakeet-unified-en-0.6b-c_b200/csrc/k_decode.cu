@@ -32,6 +32,7 @@ constexpr int DEC_H4 = DEC_H / 4;
 struct DecState {      // one entry per utterance
   int *t, *s, *ntok, *last, *pending, *evals;
   int *live;           // rows still active or pending after the last select
+  int *plist, *pcount; // the pending rows, in any order (fused decode)
 };
 
 __global__ void dec_init_kernel(DecState st, float *__restrict__ lstm, float *__restrict__ x0,
@@ -52,7 +53,9 @@ __global__ void dec_init_kernel(DecState st, float *__restrict__ lstm, float *__
     st.last[b] = DEC_BLANK;   // the first decoder step runs on blank (csrc/decoder.c:95-97)
     st.pending[b] = 1;
     st.evals[b] = 0;
+    st.plist[b] = b;
   }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *st.pcount = B;
 }
 
 __device__ __forceinline__ float dec_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -113,16 +116,34 @@ __global__ void dec_joint_kernel(const float *__restrict__ encp, const float *__
 
 constexpr int SEL_ROWS = 8;   // rows (warps) per CTA
 
+// Where the fused decode keeps the new LSTM states of the pending rows until
+// the select of the same iteration commits them (null for the hook forms,
+// whose cell kernel updates h in place).
+struct DecCommit {
+  const float *h0n, *h1n;
+  float *h0, *h1;
+};
+
 // Logits = joint.out product + bias, first-maximum argmax (strict '>' in index
 // order, csrc/decoder.c:106-114; a NaN never wins, a NaN first logit keeps 0),
-// then the greedy state machine of csrc/decoder.c:99-129 for one row.
+// then the greedy state machine of csrc/decoder.c:99-129 for one row. With a
+// commit, a row that was pending first takes its new LSTM states, and a row
+// left pending is appended to the pending list.
 __global__ void __launch_bounds__(32 * SEL_ROWS)
 dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b, DecState st,
                   int *__restrict__ tokens, const float *__restrict__ embed, float *__restrict__ x0,
-                  SeqDev seq, int B) {
+                  SeqDev seq, int B, DecCommit cm) {
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * SEL_ROWS + (threadIdx.x >> 5);
   if (b >= B) return;
+  if (cm.h0 && st.pending[b]) {
+    const long long r = (long long)b * DEC_H;
+#pragma unroll
+    for (int k = 0; k < DEC_H4 / 32; k++) {
+      st4(cm.h0 + r + 4 * (lane + 32 * k), ld4(cm.h0n + r + 4 * (lane + 32 * k)));
+      st4(cm.h1 + r + 4 * (lane + 32 * k), ld4(cm.h1n + r + 4 * (lane + 32 * k)));
+    }
+  }
   const int T = seq_T(seq, b);
   const int tb = st.t[b];
   if (tb >= T) {                       // finished: its last decoder step (if any) has run
@@ -130,11 +151,21 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
     return;
   }
   const float *l = out + (long long)b * DEC_V;
+  // all of this lane's logits first (independent loads in flight), then the
+  // comparisons in index order
+  constexpr int NV = (DEC_V + 31) / 32;
+  float xv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int v = lane + 32 * i;
+    xv[i] = v < DEC_V ? l[v] + __ldg(out_b + v) : 0.f;
+  }
   float bv = -INFINITY;
   int bi = INT_MAX;
-  for (int v = lane; v < DEC_V; v += 32) {
-    const float x = l[v] + __ldg(out_b + v);
-    if (x > bv) { bv = x; bi = v; }
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int v = lane + 32 * i;
+    if (v < DEC_V && xv[i] > bv) { bv = xv[i]; bi = v; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -168,6 +199,7 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
   st.t[b] = t;
   st.s[b] = s;
   st.pending[b] = pend;
+  if (pend && cm.h0) st.plist[atomicAdd(st.pcount, 1)] = b;
   if (t < T || pend) atomicAdd(st.live, 1);
 }
 
@@ -246,8 +278,8 @@ constexpr int DEC_H4Q = DEC_H / 4;
 struct LstmStage {
   float x[DEC_G][2][DEC_H];   // x and h_in rows
   float4 c[DEC_G];            // c[b][j0 .. j0 + 3] (this CTA's units)
-  float4 h[DEC_G];            // h_in[b][j0 .. j0 + 3]
-  int use[DEC_G];             // pending and in range
+  int row[DEC_G];             // batch row b of the slot
+  int use[DEC_G];             // slot within the segment
 };
 struct RowStage {
   float x[DEC_G][DEC_H];
@@ -273,19 +305,18 @@ __device__ __forceinline__ void dec_stage_row(float *x, const float *s0, const f
   }
 }
 
+// Slot w of the group starting at list index i0: the pending row plist[i0 + w]
+// (when below i_hi), its x and h_in rows and this CTA's slice of c.
 __device__ __forceinline__ void lstm_stage(LstmStage *st, const float *x, const float *h_in, const float *c,
-                                           const int *pending, int j0, int g0, int b_hi) {
+                                           const int *plist, int j0, int i0, int i_hi) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = g0 + w;
-  const bool in = b < b_hi;
-  const bool use = in && pending[b] != 0;
+  const bool use = i0 + w < i_hi;
+  const int b = use ? plist[i0 + w] : 0;
   dec_stage_row<2>(&st->x[w][0][0], x, h_in, b, use, lane);
   if (lane == 0) {
     st->use[w] = use;
-    if (in) {
-      cp_async16(&st->c[w], c + (long long)b * DEC_H + j0);
-      cp_async16(&st->h[w], h_in + (long long)b * DEC_H + j0);
-    }
+    st->row[w] = b;
+    if (use) cp_async16(&st->c[w], c + (long long)b * DEC_H + j0);
   }
 }
 
@@ -304,26 +335,28 @@ __device__ __forceinline__ void lstm_stage(LstmStage *st, const float *x, const 
     f += b_hi - b_lo;
 
 // One LSTM layer (pk_lstm_step, csrc/tensor_ops.c:596-629) for the pending
-// rows of its segments: a segment's group owns hidden units j0 = 4 group ..
-// j0 + 3; warp 2u + m computes gate rows {q 640 + j0 + u} of
-// W_i with x (m = 0) or of W_r with h_in (m = 1); the gates (W_r h + W_i x) +
+// rows plist[0 .. *pcount): the flattened space f = group * n + i (group = 4
+// hidden units j0 .. j0 + 3, i = list index) is shared out as above. Warp
+// 2u + m of a segment computes gate rows {q 640 + j0 + u} of W_i with x
+// (m = 0) or of W_r with h_in (m = 1); the gates (W_r h + W_i x) +
 // (B[i] + B[4H + i]) then go through the cell (warp 0, one lane per row and
-// unit). h_out is a separate buffer (other CTAs still read h_in); rows that
-// are not pending copy h_in.
+// unit): c in place, the new h into h_out (other CTAs still read h_in).
 __global__ void __launch_bounds__(256, 2) dec_lstm_kernel(const float *__restrict__ Wi, const float *__restrict__ Wr,
                                                           const float *__restrict__ bias, const float *__restrict__ x,
                                                           const float *__restrict__ h_in, float *__restrict__ h_out,
-                                                          float *__restrict__ c, const int *__restrict__ pending,
-                                                          int B, int per) {
+                                                          float *__restrict__ c, const int *__restrict__ plist,
+                                                          const int *__restrict__ pcount) {
   extern __shared__ __align__(16) unsigned char dec_smem[];
   LstmStage *stage = reinterpret_cast<LstmStage *>(dec_smem);
   __shared__ float g[2][DEC_G][LSTM_UNITS][2][4];   // [group parity][row slot][unit][W_i, W_r][gate]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int u = warp >> 1, m = warp & 1;
+  const int B = *pcount;   // the segments' "batch": the list
+  if (B == 0) return;
+  const long long total = (long long)(DEC_H / LSTM_UNITS) * B;
+  const int per = (int)max((long long)DEC_G, (total + gridDim.x - 1) / gridDim.x);
   DEC_SEGMENTS(DEC_H / LSTM_UNITS)
   const int j0 = grp * LSTM_UNITS;
-  lstm_stage(stage, x, h_in, c, pending, j0, b_lo, b_hi);
-  cp_async_commit();
   float4 w[DEC_RW][DEC_RK / 4];
   const int rows[DEC_RW] = {j0 + u, DEC_H + j0 + u, 2 * DEC_H + j0 + u, 3 * DEC_H + j0 + u};
   dec_load_rows(w, m ? Wr : Wi, rows, 4 * DEC_H, lane);
@@ -332,17 +365,19 @@ __global__ void __launch_bounds__(256, 2) dec_lstm_kernel(const float *__restric
   float bs[4];
 #pragma unroll
   for (int q = 0; q < 4; q++) bs[q] = __ldg(bias + q * DEC_H + ej) + __ldg(bias + 4 * DEC_H + q * DEC_H + ej);
+  lstm_stage(stage, x, h_in, c, plist, j0, b_lo, b_hi);
+  cp_async_commit();
   for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
     const int par = it & 1;
     const LstmStage *cur = stage + par;
-    if (g0 + DEC_G < b_hi) lstm_stage(stage + (par ^ 1), x, h_in, c, pending, j0, g0 + DEC_G, b_hi);
+    if (g0 + DEC_G < b_hi) lstm_stage(stage + (par ^ 1), x, h_in, c, plist, j0, g0 + DEC_G, b_hi);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
     // the epilogue lane's inputs, read before the buffer can be restaged
     const int euse = warp == 0 ? cur->use[eb] : 0;
+    const int erow = warp == 0 ? cur->row[eb] : 0;
     const float ec = warp == 0 ? reinterpret_cast<const float *>(&cur->c[eb])[eu] : 0.f;
-    const float eh = warp == 0 ? reinterpret_cast<const float *>(&cur->h[eb])[eu] : 0.f;
 #pragma unroll
     for (int h = 0; h < DEC_G / 4; h++) {   // 4 rows x 4 gates per reduction
       float v[16];
@@ -358,33 +393,32 @@ __global__ void __launch_bounds__(256, 2) dec_lstm_kernel(const float *__restric
       if ((lane & 1) == 0) g[par][4 * h + (lane >> 3)][u][m][(lane >> 1) & 3] = t;
     }
     __syncthreads();
-    if (warp == 0 && g0 + eb < b_hi) {
-      const long long e = (long long)(g0 + eb) * DEC_H + ej;
-      if (euse) {
-        float gt[4];
+    if (warp == 0 && euse) {
+      const long long e = (long long)erow * DEC_H + ej;
+      float gt[4];
 #pragma unroll
-        for (int q = 0; q < 4; q++) gt[q] = (g[par][eb][eu][1][q] + g[par][eb][eu][0][q]) + bs[q];
-        const float ig = dec_sigmoid(gt[0]), og = dec_sigmoid(gt[1]), fg = dec_sigmoid(gt[2]);
-        const float cg = tanhf(gt[3]);
-        const float cn = fg * ec + ig * cg;
-        c[e] = cn;
-        h_out[e] = og * tanhf(cn);
-      } else {
-        h_out[e] = eh;
-      }
+      for (int q = 0; q < 4; q++) gt[q] = (g[par][eb][eu][1][q] + g[par][eb][eu][0][q]) + bs[q];
+      const float ig = dec_sigmoid(gt[0]), og = dec_sigmoid(gt[1]), fg = dec_sigmoid(gt[2]);
+      const float cg = tanhf(gt[3]);
+      const float cn = fg * ec + ig * cg;
+      c[e] = cn;
+      h_out[e] = og * tanhf(cn);
     }
   }
   cp_async_wait<0>();
   }
 }
 
-__device__ __forceinline__ void row_stage(RowStage *st, const float *src, const int *t, SeqDev seq, int g0,
-                                          int b_hi) {
+// Slot w: batch row g0 + w when active, its input row taken from src_new for
+// the rows with pending set (src_new non-null) and from src otherwise.
+__device__ __forceinline__ void row_stage(RowStage *st, const float *src, const float *src_new,
+                                          const int *pending, const int *t, SeqDev seq, int g0, int b_hi) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = g0 + w;
   const int tb = b < b_hi ? t[b] : 0;
   const bool use = b < b_hi && tb < seq_T(seq, b);
-  dec_stage_row<1>(&st->x[w][0], src, nullptr, b, use, lane);
+  const float *from = (src_new && use && pending[b]) ? src_new : src;
+  dec_stage_row<1>(&st->x[w][0], from, nullptr, b, use, lane);
   if (lane == 0) {
     st->use[w] = use;
     st->enc_row[w] = use ? seq_frame_off(seq, b) + tb : 0;
@@ -393,30 +427,35 @@ __device__ __forceinline__ void row_stage(RowStage *st, const float *src, const 
 
 // pk_joint's pred projection and hidden (csrc/decoder.c:44-67): for the active
 // rows hidden = relu((enc_t + b_enc) + (h1 joint.pred + b_pred)), zeros for the
-// others. JpT: joint.pred transposed, [640 out, 640 in]. Warp w of a
+// others; h1 is the new state (h1n) for the rows with a decoder step this
+// iteration. JpT: joint.pred transposed, [640 out, 640 in]. Warp w of a
 // segment's group owns outputs 4 (8 group + w) .. +3. Resets the live count
 // the select accumulates.
 __global__ void __launch_bounds__(256, 2) dec_pred_joint_kernel(const float *__restrict__ JpT, const float *__restrict__ h1,
+                                                                const float *__restrict__ h1n, const int *__restrict__ pending,
                                                                 const float *__restrict__ encp, const float *__restrict__ enc_b,
                                                                 const float *__restrict__ pred_b, float *__restrict__ hidden,
                                                                 const int *__restrict__ t, SeqDev seq, int B, int per,
-                                                                int *live) {
+                                                                int *live, int *pcount) {
   extern __shared__ __align__(16) unsigned char dec_smem[];
   RowStage *stage = reinterpret_cast<RowStage *>(dec_smem);
-  if (blockIdx.x == 0 && threadIdx.x == 0) *live = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   DEC_SEGMENTS(DEC_H / (8 * DEC_RW))
   const int n0 = (grp * 8 + warp) * DEC_RW;
-  row_stage(stage, h1, t, seq, b_lo, b_hi);
-  cp_async_commit();
   float4 w[DEC_RW][DEC_RK / 4];
   const int rows[DEC_RW] = {n0, n0 + 1, n0 + 2, n0 + 3};
   dec_load_rows(w, JpT, rows, DEC_H, lane);
   const int n = n0 + ((lane >> 1) & 3);
   const float eb = __ldg(enc_b + n), pb = __ldg(pred_b + n);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *live = 0;
+    *pcount = 0;   // both LSTM layers of this iteration have read it
+  }
+  row_stage(stage, h1, h1n, pending, t, seq, b_lo, b_hi);
+  cp_async_commit();
   for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
     const RowStage *cur = stage + (it & 1);
-    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), h1, t, seq, g0 + DEC_G, b_hi);
+    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), h1, h1n, pending, t, seq, g0 + DEC_G, b_hi);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -462,15 +501,15 @@ __global__ void __launch_bounds__(256, 2) dec_out_kernel(const float *__restrict
   DEC_SEGMENTS((DEC_V + 8 * DEC_RW - 1) / (8 * DEC_RW))
   const int n0 = (grp * 8 + warp) * DEC_RW;
   const bool has_rows = n0 < DEC_V;
-  row_stage(stage, hidden, t, seq, b_lo, b_hi);
-  cp_async_commit();
   float4 w[DEC_RW][DEC_RK / 4];
   const int rows[DEC_RW] = {n0, n0 + 1, n0 + 2, n0 + 3};
   dec_load_rows(w, JoT, rows, DEC_V, lane);
   const int n = n0 + ((lane >> 1) & 3);
+  row_stage(stage, hidden, nullptr, nullptr, t, seq, b_lo, b_hi);
+  cp_async_commit();
   for (int g0 = b_lo, it = 0; g0 < b_hi; g0 += DEC_G, it++) {
     const RowStage *cur = stage + (it & 1);
-    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), hidden, t, seq, g0 + DEC_G, b_hi);
+    if (g0 + DEC_G < b_hi) row_stage(stage + ((it + 1) & 1), hidden, nullptr, nullptr, t, seq, g0 + DEC_G, b_hi);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -531,7 +570,7 @@ struct pkcu_decoder {
   void *block;             // one device allocation for everything below
   DecState st;
   float *lstm;             // h0, h1, c0, c1 [B, 640] each
-  float *hb;               // h0', h1' [B, 640]: the fused decode's odd-iteration states
+  float *hb;               // h0n, h1n [B, 640]: the fused decode's new states of the pending rows
   float *x0, *hidden;      // [B, 640]
   float *encp, *pred, *out, *g0i, *g0r, *g1i, *g1r;
   int *tokens;             // [10 F]: utterance b's tokens from 10 * frame_off(b)
@@ -590,7 +629,7 @@ extern "C" int pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder *
   cudaGetDevice(&d->device);
   const size_t B = (size_t)n_utts, H = DEC_H;
   auto up = [](size_t bytes) { return (bytes + 255) & ~(size_t)255; };
-  const size_t sz_state = up(sizeof(int) * (6 * B + 1));
+  const size_t sz_state = up(sizeof(int) * (7 * B + 2));
   const size_t sz_lstm = up(sizeof(float) * 4 * B * H), sz_bh = up(sizeof(float) * B * H);
   const size_t sz_enc = up(sizeof(float) * (size_t)F * H), sz_out = up(sizeof(float) * B * DEC_V);
   const size_t sz_g = up(sizeof(float) * B * 4 * H), sz_tok = up(sizeof(int) * DEC_MAX_SYM * (size_t)F);
@@ -609,7 +648,8 @@ extern "C" int pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder *
   }
   char *p = (char *)d->block;
   int *si = (int *)p;
-  d->st = DecState{si, si + B, si + 2 * B, si + 3 * B, si + 4 * B, si + 5 * B, si + 6 * B};
+  d->st = DecState{si, si + B, si + 2 * B, si + 3 * B, si + 4 * B, si + 5 * B, si + 6 * B,
+                   si + 6 * B + 1, si + 7 * B + 1};
   p += sz_state;
   d->lstm = (float *)p; p += sz_lstm;
   d->hb = (float *)p; p += 2 * sz_bh;
@@ -677,7 +717,7 @@ static int dec_iteration(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_
   if (!st && hook) st = hook(hook_user, -1, PKCU_GEMM_DEC_OUT, ps);
   if (st) return st;
   dec_select_kernel<<<(unsigned)((B + SEL_ROWS - 1) / SEL_ROWS), 32 * SEL_ROWS, 0, s>>>(
-      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B);
+      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B, DecCommit{});
   return pkcu_launch_status("pkcu_greedy_decode: select");
 }
 
@@ -697,28 +737,29 @@ static unsigned dec_share(int n_groups, int B, int *per) {
   return (unsigned)((total + p - 1) / p);
 }
 
-// One iteration of the fused decode on stream s; iteration parity picks the
-// h buffers (even: read lstm, write hb; odd: the reverse).
-static int dec_iteration_fused(pkcu_decoder *d, const pkcu_dec_params *prm, int parity, cudaStream_t s) {
+// One iteration of the fused decode on stream s: the LSTM layers on the
+// pending list (new states into h0n / h1n), pred + joint, out, select (which
+// commits the new states and builds the next list).
+static int dec_iteration_fused(pkcu_decoder *d, const pkcu_dec_params *prm, cudaStream_t s) {
   const int B = d->B;
   const size_t BH = (size_t)B * DEC_H;
-  float *ha = parity ? d->hb : d->lstm, *hn = parity ? d->lstm : d->hb;
-  float *c0 = d->lstm + 2 * BH, *c1 = d->lstm + 3 * BH;
+  float *h0 = d->lstm, *h1 = d->lstm + BH, *c0 = d->lstm + 2 * BH, *c1 = d->lstm + 3 * BH;
+  float *h0n = d->hb, *h1n = d->hb + BH;
   const SeqDev seq = d->seq->dev;
-  int pl, pp, po;
-  const unsigned gl = dec_share(DEC_H / LSTM_UNITS, B, &pl);
+  int pp, po, pl;
+  const unsigned gl = dec_share(DEC_H / LSTM_UNITS, B, &pl);   // sized for a full list
   const unsigned gp = dec_share(DEC_H / (8 * DEC_RW), B, &pp);
   const unsigned go = dec_share((DEC_V + 8 * DEC_RW - 1) / (8 * DEC_RW), B, &po);
-  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[0], d->lw[1], prm->lstm0_b, d->x0, ha, hn, c0,
-                                                 d->st.pending, B, pl);
-  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[2], d->lw[3], prm->lstm1_b, hn, ha + BH, hn + BH, c1,
-                                                 d->st.pending, B, pl);
-  dec_pred_joint_kernel<<<gp, 256, DEC_ROW_SMEM, s>>>(d->jt, hn + BH, d->encp, prm->joint_enc_b,
+  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[0], d->lw[1], prm->lstm0_b, d->x0, h0, h0n, c0,
+                                                 d->st.plist, d->st.pcount);
+  dec_lstm_kernel<<<gl, 256, DEC_LSTM_SMEM, s>>>(d->lw[2], d->lw[3], prm->lstm1_b, h0n, h1, h1n, c1,
+                                                 d->st.plist, d->st.pcount);
+  dec_pred_joint_kernel<<<gp, 256, DEC_ROW_SMEM, s>>>(d->jt, h1, h1n, d->st.pending, d->encp, prm->joint_enc_b,
                                                       prm->joint_pred_b, d->hidden, d->st.t, seq, B, pp,
-                                                      d->st.live);
+                                                      d->st.live, d->st.pcount);
   dec_out_kernel<<<go, 256, DEC_ROW_SMEM, s>>>(d->jt + DEC_H * DEC_H, d->hidden, d->out, d->st.t, seq, B, po);
   dec_select_kernel<<<(unsigned)((B + SEL_ROWS - 1) / SEL_ROWS), 32 * SEL_ROWS, 0, s>>>(
-      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B);
+      d->out, prm->joint_out_b, d->st, d->tokens, prm->embed, d->x0, seq, B, DecCommit{h0n, h1n, h0, h1});
   return pkcu_launch_status("pkcu_greedy_decode_fused: iteration");
 }
 
@@ -745,7 +786,7 @@ static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_ho
     return pkcu_launch_status("pkcu_greedy_decode: begin capture");
   int st = PKCU_OK;
   for (int i = 0; i < DEC_POLL && !st; i++)
-    st = fused ? dec_iteration_fused(d, prm, i & 1, d->gs) : dec_iteration(d, prm, hook, hook_user, d->gs);
+    st = fused ? dec_iteration_fused(d, prm, d->gs) : dec_iteration(d, prm, hook, hook_user, d->gs);
   if (!st && cudaMemcpyAsync(d->live_host, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, d->gs) !=
                  cudaSuccess)
     st = pkcu_launch_status("pkcu_greedy_decode: capture poll copy");
