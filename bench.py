@@ -65,6 +65,11 @@ def parse_args():
                     help="rows M of the fused-GEMM timing")
     ap.add_argument("--forward-only", action="store_true",
                     help="with --aux-only: time only the encoder stack with its GEMMs")
+    ap.add_argument("--decode-fused-only", action="store_true",
+                    help="with --aux-only: time only pkcu_greedy_decode_fused (--dec-utts, --dec-frames, --dec-shift)")
+    ap.add_argument("--dec-utts", type=int, default=256)
+    ap.add_argument("--dec-frames", type=int, default=40)
+    ap.add_argument("--dec-shift", type=float, default=0.0)
     ap.add_argument("--asr-decode-only", action="store_true",
                     help="with --aux-only: time only pkcu_asr_decode")
     ap.add_argument("--asr-only", action="store_true",
@@ -580,6 +585,58 @@ def _synthetic_checkpoint(blank_bias=0.0):
 DEC_PROFILES = {"about_1_token_per_frame": 3.5, "10_tokens_every_frame": 0.0}
 
 
+def decode_fmas(pending_rows, active_rows):
+    """Multiply-adds of one fused decode iteration: per pending row both LSTM
+    layers' gate products (2 x 2 x 2560 x 640), per active row the pred
+    (640 x 640) and out (640 x 1025) products."""
+    return pending_rows * 2 * 2 * 2560 * 640 + active_rows * (640 * 640 + 640 * 1025)
+
+
+def time_decode_fused(stream, reps, n_utts=256, T=40, blank_shift=0.0):
+    """pkcu_greedy_decode_fused on device-resident inputs: seeded random
+    decoder weights and encoder projections; blank_shift raises the blank
+    logit's bias (0: every frame emits the 10-symbol cap, every row pending
+    every iteration; 3.5: a decoder step on a few rows per iteration).
+    CUDA-event time of whole decodes divided by their iterations."""
+    import numpy as np
+    import torch
+    import pkcuda
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    rng = np.random.default_rng(5)
+    params = po.random_dec_params(rng)
+    params["out_b"][po.DEC_BLANK] += blank_shift
+    w = {k: torch.from_numpy(v).cuda() for k, v in po.random_dec_weights(rng).items()}
+    dp = {"embed": params["embed"], "lstm0_b": params["B0"], "lstm1_b": params["B1"],
+          "joint_enc_b": params["enc_b"], "joint_pred_b": params["pred_b"], "joint_out_b": params["out_b"]}
+    dp = {k: torch.from_numpy(v).cuda() for k, v in dp.items()}
+    with pkcuda.Decoder([T] * n_utts) as dec:
+        enc = torch.as_tensor(_DevView(dec.gemm_out["enc"], n_utts * T * 640), device="cuda")
+        enc.copy_(torch.randn(n_utts * T * 640, generator=torch.Generator(device="cuda").manual_seed(7),
+                              device="cuda"))
+        dec.set_weights(w, stream)
+        dec.decode_fused(dp, stream)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(max(reps, 1)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dec.decode_fused(dp, stream)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        n_tok, evals, _ = dec.results()
+        iters = dec.iterations
+    n_ev = int(evals.sum())
+    # every evaluation is one active row of an iteration; the decoder steps are
+    # the tokens plus the first step of each utterance
+    fma = decode_fmas(int(n_tok.sum()) + n_utts, n_ev)
+    return {"utterances": n_utts, "frames": T, "blank_shift": blank_shift, "iterations": iters,
+            "us_per_iteration": round(best * 1000 / iters, 2), "joint_evals_per_s": round(n_ev / best * 1000),
+            "tokens": int(n_tok.sum()), "fp32_tflops": round(2 * fma / best / 1e9, 2)}
+
+
 def time_asr_decode(stream, reps, n_utts=256, T=375, cpu=True):
     """pkcu_asr_decode (the decode alone, a batched pk_greedy_decode with the
     model's own product kernels) on n_utts x T encoder frames of N(0, 1),
@@ -950,6 +1007,10 @@ def aux_only(args, local_rank):
     pkcuda.lib()
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
+        if args.decode_fused_only:
+            print(json.dumps({"decode_fused": time_decode_fused(stream, args.aux_reps, args.dec_utts,
+                                                                args.dec_frames, args.dec_shift)}), flush=True)
+            return
         if args.asr_decode_only:
             print(json.dumps({"asr_decode": time_asr_decode(stream, args.aux_reps,
                                                             cpu=not args.no_cpu_baseline)}), flush=True)
@@ -1053,7 +1114,7 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = decode = gemms = forward = asr = asr_dec = None
+    aux = decode = gemms = forward = asr = asr_dec = dec_fused = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
         decode = time_decode(stream, 3)
@@ -1061,6 +1122,8 @@ def _ours(args, rank, world, local_rank, stream):
         forward = time_encoder_forward(stream, 2)
         asr = time_asr(stream, 1)
         asr_dec = time_asr_decode(stream, 2, cpu=world == 1 and not args.no_cpu_baseline)
+        dec_fused = {"10_tokens_every_frame": time_decode_fused(stream, 2, 256, 40, 0.0),
+                     "sparse_decoder_steps": time_decode_fused(stream, 2, 256, 200, 3.5)}
         if world == 1 and not args.no_cpu_baseline:
             forward["cpu_baseline"] = cpu_encoder_baseline()
             asr["cpu_baseline"] = cpu_asr_baseline()
@@ -1104,6 +1167,7 @@ def _ours(args, rank, world, local_rank, stream):
         "encoder_forward": forward,
         "asr": asr,
         "asr_decode": asr_dec,
+        "decode_fused": dec_fused,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,

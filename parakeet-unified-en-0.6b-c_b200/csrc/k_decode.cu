@@ -22,6 +22,12 @@
 // operations (its k-th joint evaluation is iteration k; the decoder step that
 // precedes it runs in the same iteration), interleaved with the others.
 // Rows that are not pending / not active ignore the products of their row.
+//
+// The fused form (pkcu_greedy_decode_fused) runs the same iteration with the
+// decoder's own product kernels: each LSTM layer is one kernel (both gate
+// products + the cell) over the list of pending rows that the previous select
+// built, writing the new h into separate buffers that the select commits;
+// pred + joint hidden and out follow, then the same select.
 #include "pk_common.cuh"
 
 namespace pk {

@@ -148,3 +148,22 @@ def test_gemm_validation(L):
     assert b"multiples of 4" in L.pkcu_last_error()
     assert L.pkcu_gemm_bias_residual(16, 16, 16, 20, C.c_float(0.5), 4, 8, 8, None) == 1
     assert b"aligned" in L.pkcu_last_error()
+
+
+def test_fused_decode_argument_checks():
+    """The fused-decode and ASR-decode entry points reject NULL handles before
+    any CUDA call."""
+    import ctypes as C
+    import pkcuda
+    ERR_ARG = 1   # PKCU_ERR_ARG
+    L = pkcuda.lib()
+    w = pkcuda.DecWeights()
+    p = pkcuda.DecParams()
+    assert L.pkcu_decoder_set_weights(None, C.byref(w), None) == ERR_ARG
+    assert L.pkcu_greedy_decode_fused(None, C.byref(p), None) == ERR_ARG
+    assert L.pkcu_greedy_decode_graph(None, C.byref(p), None, None, None) == ERR_ARG
+    assert L.pkcu_asr_set_decode_mode(None, 0) == ERR_ARG
+    frames = (C.c_int * 1)(8)
+    tok = (C.c_int * 80)()
+    cnt = (C.c_int * 1)()
+    assert L.pkcu_asr_decode(None, None, frames, 1, tok, cnt, None) == ERR_ARG
