@@ -6,14 +6,14 @@
  * (pkcu_weights_dequant: int8 (float)q * scale, int4 (float)nibble * group
  * scale, fp32 copied; the fused QKV as the reference's loader builds it), so a
  * forward pass is fp32 throughout like the reference's (csrc/encoder.c). The
- * row-major projections of the block (FF, QKV, output) run on the tensor cores
- * with fp32 accuracy (k_gemm.cu: three bf16 parts per operand, nine MMAs per
- * product); the other products are cuBLAS single-precision GEMMs (no TF32):
- * per utterance the
- * positional projection of its slice of the sinusoidal table
- * (csrc/encoder.c:220-227), the per-head score, positional-score and context
- * products and the two pointwise convolutions, as strided batches over heads
- * (and over utterances when the batch is uniform). */
+ * row-major projections of the block (FF, QKV, output, and the positional
+ * projection of the sinusoidal table's slice, csrc/encoder.c:220-227, once per
+ * distinct utterance length) run on the tensor cores with fp32 accuracy
+ * (k_gemm.cu: three bf16 parts per operand, nine MMAs per product); the other
+ * products are cuBLAS single-precision GEMMs (no TF32): the per-head score,
+ * positional-score and context products and the two pointwise convolutions,
+ * as strided batches over heads (and over utterances when the batch is
+ * uniform). */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -154,12 +154,12 @@ typedef struct {
 
 static const float ONE = 1.0f, ZERO = 0.0f;
 
-/* Row-major C[M, N] = A[M, K] B[K, N] (leading dimensions lda, ldb, ldc),
- * as the column-major product C^T = B^T A^T; tb: B is stored [N, K] (C = A B^T). */
 /* The GEMM output buffers are const in pkcu_gemm_outputs (the non-GEMM
  * kernels only read them); the GEMM hook is what writes them. */
 static float *gemm_dst(const float *p) { return (float *)p; }
 
+/* Row-major C[M, N] = A[M, K] B[K, N] (leading dimensions lda, ldb, ldc),
+ * as the column-major product C^T = B^T A^T; tb: B is stored [N, K] (C = A B^T). */
 static int rm_gemm(cublasHandle_t h, int M, int N, int K, const float *A, int lda, long long sA,
                    const float *B, int ldb, long long sB, int tb, float *C, int ldc, long long sC,
                    int batch)
@@ -200,19 +200,35 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     case PKCU_GEMM_FF2_2: return proj(h, (int)F, PK_D, PK_FF, gi->h2, W[W_FF2_2], gemm_dst(go->ff2_out), stream);
     default: break;
     }
+    if (gemm == PKCU_GEMM_POS) {
+        /* P = pe slice [2T-1, 1024] x W_pos depends on T only: one projection
+         * per distinct length, copied to the other items of that length */
+        for (int i = 0; i < n; i++) {
+            const int T = f->seq->lengths[i], L = 2 * T - 1;
+            float *dst = gemm_dst(go->P) + f->off[4 * i + 1] * PK_D;
+            int j = 0;
+            while (j < i && f->seq->lengths[j] != T) j++;
+            int st;
+            if (j < i) {
+                st = cudaMemcpyAsync(dst, go->P + f->off[4 * j + 1] * PK_D, sizeof(float) * (size_t)L * PK_D,
+                                     cudaMemcpyDeviceToDevice, (cudaStream_t)stream) == cudaSuccess
+                         ? PKCU_OK : pkcu_fail(PKCU_ERR_CUDA, "pkcu_encoder_forward: positional copy");
+            } else {
+                const float *pe = f->m->pe + (long long)(PE_CENTER - T + 1) * PK_D;
+                st = proj(h, L, PK_D, PK_D, pe, W[W_POS], dst, stream);
+            }
+            if (st) return st;
+        }
+        return PKCU_OK;
+    }
     /* per utterance (all utterances in one batch when the lengths agree) */
     const int groups = uni ? 1 : n, per = uni ? n : 1;
     for (int i = 0; i < groups; i++) {
         const int T = uni ? uni : f->seq->lengths[i], L = 2 * T - 1, Hb = PK_H * per;
         const long long fo = f->off[4 * i], po = f->off[4 * i + 1], so = f->off[4 * i + 2],
                         bo = f->off[4 * i + 3];
-        const float *pe = f->m->pe + (long long)(PE_CENTER - T + 1) * PK_D;
         int st = PKCU_OK;
         switch (gemm) {
-        case PKCU_GEMM_POS:   /* P = pe slice [2T-1, 1024] x W_pos */
-            st = rm_gemm(h, L, PK_D, PK_D, pe, PK_D, 0, W[W_POS], PK_D, 0, 0, gemm_dst(go->P) + po * PK_D, PK_D,
-                         (long long)L * PK_D, per);
-            break;
         case PKCU_GEMM_AC:    /* ac[h] = (Q + u)[h] K[h]^T */
             st = rm_gemm(h, T, T, PK_DH, gi->Qu + fo * PK_D, PK_DH, (long long)T * PK_DH,
                          gi->K + fo * PK_D, PK_DH, (long long)T * PK_DH, 1, gemm_dst(go->ac) + so, T,
