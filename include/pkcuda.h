@@ -436,7 +436,9 @@ int  pkcu_asr_encoder_frames(int mel_frames);
 /* mel: device, n_utts spectrograms [128, mel_frames[b]] one after another.
  * tokens (host, capacity 10 x the sum of encoder frames) receives utterance
  * b's tokens from 10 x the number of encoder frames before it; n_tokens (host)
- * their counts. Synchronous; allocates its working buffers per call. */
+ * their counts. Synchronous. The working buffers (and the decoder, with its
+ * captured graph) of the last call are kept while the same lengths come again
+ * (a call with other lengths replaces them; pkcu_asr_destroy frees them). */
 int  pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
                          int *tokens, int *n_tokens, pkcu_stream_t stream);
 /* The decode alone, a batched pk_greedy_decode (csrc/decoder.c:80-132) with

@@ -296,6 +296,22 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
  * shape does not suit it), the decoder's per-iteration products (B rows) on
  * cuBLAS SGEMM. */
 
+typedef struct {
+    pkcu_asr *m;
+    pkcu_pre_gemm_outputs go;
+    pkcu_pre_gemm_inputs gi;
+    long long P2, P3, F;
+} PreCtx;
+
+typedef struct {
+    pkcu_asr *m;
+    pkcu_dec_gemm_outputs go;
+    pkcu_dec_gemm_inputs gi;
+    const float *x;
+    long long F;
+    int B;
+} DecCtx;
+
 struct pkcu_asr {
     pkcu_encoder_model *enc;
     cublasHandle_t blas;
@@ -306,7 +322,56 @@ struct pkcu_asr {
     const float *j_enc, *j_pred, *j_out;   /* [1024, 640], [640, 640], [640, 1025] */
     pkcu_dec_params dec;
     int decode_mode;                   /* PKCU_ASR_DECODE_* */
+    /* the last call's working buffers, kept while the same lengths come again */
+    int t_n, *t_frames;                /* mel frames the transcribe buffers were made for */
+    pkcu_pre_plan *t_plan;
+    float *t_pre;
+    pkcu_encoder_ws *t_ws;
+    PreCtx t_pc;
+    int d_n, *d_frames;                /* encoder frames the decoder was made for */
+    pkcu_decoder *d_dec;
+    int d_weights;                     /* pkcu_decoder_set_weights done on d_dec */
+    DecCtx d_dc;                       /* the decode hook's context (a stable address) */
 };
+
+static void asr_release_transcribe(pkcu_asr *m)
+{
+    pkcu_encoder_ws_destroy(m->t_ws);
+    pkcu_pre_plan_destroy(m->t_plan);
+    if (m->t_pre) cudaFree(m->t_pre);
+    free(m->t_frames);
+    m->t_ws = NULL;
+    m->t_plan = NULL;
+    m->t_pre = NULL;
+    m->t_frames = NULL;
+    m->t_n = 0;
+}
+
+static void asr_release_decoder(pkcu_asr *m)
+{
+    pkcu_decoder_destroy(m->d_dec);
+    free(m->d_frames);
+    m->d_dec = NULL;
+    m->d_frames = NULL;
+    m->d_n = 0;
+    m->d_weights = 0;
+}
+
+/* 1 when frames[0..n) equals the kept key (kn, kf). */
+static int same_lengths(int kn, const int *kf, int n, const int *frames)
+{
+    if (!kf || kn != n) return 0;
+    for (int i = 0; i < n; i++)
+        if (kf[i] != frames[i]) return 0;
+    return 1;
+}
+
+static int *copy_lengths(const int *frames, int n)
+{
+    int *c = (int *)malloc(sizeof(int) * (size_t)n);
+    if (c) memcpy(c, frames, sizeof(int) * (size_t)n);
+    return c;
+}
 
 int pkcu_asr_set_decode_mode(pkcu_asr *m, int mode)
 {
@@ -320,6 +385,8 @@ int pkcu_asr_set_decode_mode(pkcu_asr *m, int mode)
 void pkcu_asr_destroy(pkcu_asr *m)
 {
     if (!m) return;
+    asr_release_transcribe(m);
+    asr_release_decoder(m);
     pkcu_encoder_model_destroy(m->enc);
     if (m->blas) cublasDestroy(m->blas);
     if (m->owned) cudaFree(m->owned);
@@ -409,12 +476,6 @@ int pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out)
     return PKCU_OK;
 }
 
-typedef struct {
-    pkcu_asr *m;
-    pkcu_pre_gemm_outputs go;
-    pkcu_pre_gemm_inputs gi;
-    long long P2, P3, F;
-} PreCtx;
 
 static int pre_hook(void *user, int block, int gemm, pkcu_stream_t stream)
 {
@@ -431,14 +492,6 @@ static int pre_hook(void *user, int block, int gemm, pkcu_stream_t stream)
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: unknown pre-encode GEMM %d", gemm);
 }
 
-typedef struct {
-    pkcu_asr *m;
-    pkcu_dec_gemm_outputs go;
-    pkcu_dec_gemm_inputs gi;
-    const float *x;
-    long long F;
-    int B;
-} DecCtx;
 
 static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
 {
@@ -461,33 +514,46 @@ static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
 }
 
 /* Greedy decode of encoder outputs x [sum enc_frames, 1024] with the model's
- * decoder, in the model's decode mode; host results. */
+ * decoder, in the model's decode mode; host results. The decoder (with its
+ * captured graph) is kept for the next call with the same lengths. */
 static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_utts, int *tokens,
                       int *n_tokens, pkcu_stream_t stream)
 {
+    int st = PKCU_OK;
+    if (!same_lengths(m->d_n, m->d_frames, n_utts, enc_frames)) {
+        asr_release_decoder(m);
+        st = pkcu_decoder_create(enc_frames, n_utts, &m->d_dec);
+        if (!st && !(m->d_frames = copy_lengths(enc_frames, n_utts)))
+            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_decode: host allocation");
+        if (!st) st = pkcu_decoder_buffers(m->d_dec, &m->d_dc.go, &m->d_dc.gi);
+        if (st) {
+            asr_release_decoder(m);
+            return st;
+        }
+        m->d_n = n_utts;
+    }
     long long F = 0;
     for (int i = 0; i < n_utts; i++) F += enc_frames[i];
-    pkcu_decoder *dec = NULL;
-    int st = pkcu_decoder_create(enc_frames, n_utts, &dec);
-    DecCtx dc = {.m = m};
-    if (!st) {
-        st = pkcu_decoder_buffers(dec, &dc.go, &dc.gi);
-        dc.x = x;
-        dc.F = F;
-        dc.B = n_utts;
-    }
-    if (!st && m->decode_mode == PKCU_ASR_DECODE_FUSED) {
-        const pkcu_dec_weights dw = {m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
-        st = pkcu_decoder_set_weights(dec, &dw, stream);
-        if (!st) st = dec_hook(&dc, -1, PKCU_GEMM_DEC_ENC, stream);
+    DecCtx *dc = &m->d_dc;
+    dc->m = m;
+    dc->x = x;
+    dc->F = F;
+    dc->B = n_utts;
+    pkcu_decoder *dec = m->d_dec;
+    if (m->decode_mode == PKCU_ASR_DECODE_FUSED) {
+        if (!m->d_weights) {
+            const pkcu_dec_weights dw = {m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
+            st = pkcu_decoder_set_weights(dec, &dw, stream);
+            m->d_weights = !st;
+        }
+        if (!st) st = dec_hook(dc, -1, PKCU_GEMM_DEC_ENC, stream);
         if (!st) st = pkcu_greedy_decode_fused(dec, &m->dec, stream);
-    } else if (!st) {
+    } else {
         st = m->decode_mode == PKCU_ASR_DECODE_EAGER
-                 ? pkcu_greedy_decode(dec, &m->dec, dec_hook, &dc, stream)
-                 : pkcu_greedy_decode_graph(dec, &m->dec, dec_hook, &dc, stream);
+                 ? pkcu_greedy_decode(dec, &m->dec, dec_hook, dc, stream)
+                 : pkcu_greedy_decode_graph(dec, &m->dec, dec_hook, dc, stream);
     }
     if (!st) st = pkcu_decoder_results(dec, n_tokens, NULL, tokens, stream);
-    pkcu_decoder_destroy(dec);
     return st;
 }
 
@@ -505,48 +571,56 @@ int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, in
 {
     if (!m || !mel || !mel_frames || n_utts <= 0 || !tokens || !n_tokens)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: bad argument");
-    pkcu_pre_plan *plan = NULL;
-    pkcu_encoder_ws *ws = NULL;
-    float *pre = NULL;
-    int *enc_frames = NULL;
-    int st = pkcu_pre_plan_create(mel_frames, n_utts, &plan);
-    PreCtx pc = {.m = m};
-    if (!st) {
-        pc.P2 = pkcu_pre_plan_p2(plan);
-        pc.P3 = pkcu_pre_plan_p3(plan);
-        pc.F = pkcu_pre_plan_frames(plan);
-        const long long n2 = 256 * pc.P2, n3 = 256 * pc.P3;
-        const long long total = 2 * n2 + 2 * n3 + pc.F * 4096 + pc.F * PK_D;
-        if (cudaMalloc((void **)&pre, sizeof(float) * (size_t)total) != cudaSuccess) {
-            cudaGetLastError();
-            pre = NULL;
-            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: pre-encode buffers");
-        } else {
-            pc.gi.s2d = pre;
-            pc.go.pw1 = pre + n2;
-            pc.gi.s3d = pre + 2 * n2;
-            pc.go.pw2 = pre + 2 * n2 + n3;
-            pc.gi.flat = pre + 2 * n2 + 2 * n3;
-            pc.go.proj = pc.gi.flat + pc.F * 4096;
+    int st = PKCU_OK;
+    PreCtx *pc = &m->t_pc;
+    if (!same_lengths(m->t_n, m->t_frames, n_utts, mel_frames)) {
+        asr_release_transcribe(m);
+        st = pkcu_pre_plan_create(mel_frames, n_utts, &m->t_plan);
+        if (!st && !(m->t_frames = copy_lengths(mel_frames, n_utts)))
+            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: host allocation");
+        if (!st) {
+            memset(pc, 0, sizeof(*pc));
+            pc->m = m;
+            pc->P2 = pkcu_pre_plan_p2(m->t_plan);
+            pc->P3 = pkcu_pre_plan_p3(m->t_plan);
+            pc->F = pkcu_pre_plan_frames(m->t_plan);
+            const long long n2 = 256 * pc->P2, n3 = 256 * pc->P3;
+            const long long total = 2 * n2 + 2 * n3 + pc->F * 4096 + pc->F * PK_D;
+            if (cudaMalloc((void **)&m->t_pre, sizeof(float) * (size_t)total) != cudaSuccess) {
+                cudaGetLastError();
+                m->t_pre = NULL;
+                st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: pre-encode buffers");
+            } else {
+                float *pre = m->t_pre;
+                pc->gi.s2d = pre;
+                pc->go.pw1 = pre + n2;
+                pc->gi.s3d = pre + 2 * n2;
+                pc->go.pw2 = pre + 2 * n2 + n3;
+                pc->gi.flat = pre + 2 * n2 + 2 * n3;
+                pc->go.proj = pc->gi.flat + pc->F * 4096;
+            }
         }
+        if (!st) st = pkcu_encoder_ws_create(pkcu_pre_plan_out_seq(m->t_plan), 1, &m->t_ws);
+        if (st) {
+            asr_release_transcribe(m);
+            return st;
+        }
+        m->t_n = n_utts;
     }
-    const pkcu_seq *seq = plan ? pkcu_pre_plan_out_seq(plan) : NULL;
+    const pkcu_seq *seq = pkcu_pre_plan_out_seq(m->t_plan);
     float *x = NULL;
     pkcu_gemm_outputs go;
     pkcu_gemm_inputs gi;
-    if (!st) st = pkcu_encoder_ws_create(seq, 1, &ws);
-    if (!st) st = pkcu_encoder_ws_device(ws, &x, &go, &gi);
-    if (!st) st = pkcu_pre_encode(mel, &m->pre, &pc.go, &pc.gi, x, plan, pre_hook, &pc, stream);
+    st = pkcu_encoder_ws_device(m->t_ws, &x, &go, &gi);
+    if (!st) st = pkcu_pre_encode(mel, &m->pre, &pc->go, &pc->gi, x, m->t_plan, pre_hook, pc, stream);
     if (!st) st = pkcu_encoder_forward(m->enc, x, &go, &gi, seq, stream);
+    int *enc_frames = NULL;
     if (!st) {
         enc_frames = (int *)malloc(sizeof(int) * (size_t)n_utts);
         if (!enc_frames) st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: host allocation");
         for (int i = 0; i < n_utts && !st; i++) enc_frames[i] = pkcu_asr_encoder_frames(mel_frames[i]);
     }
     if (!st) st = asr_decode(m, x, enc_frames, n_utts, tokens, n_tokens, stream);
-    pkcu_encoder_ws_destroy(ws);
-    pkcu_pre_plan_destroy(plan);
-    if (pre) cudaFree(pre);
     free(enc_frames);
     return st;
 }

@@ -309,6 +309,12 @@ def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):
                 got.append(asr.transcribe(mels, frames))
                 # the decode alone, on the reference's own encoder outputs
                 got.append(asr.decode(ref_enc, [e.shape[0] for e in enc]))
+            # other lengths replace the kept buffers and decoder, the first lengths again
+            # rebuild them
+            alone = asr.transcribe(dev(mel.reshape(-1)), [mel.shape[1]])
+            again = asr.transcribe(mels, frames)
+    assert len(alone) == 1 and (alone[0] == want[0]).all()
+    got.append(again)
     for b in range(2):
         for g in got:
             assert len(g[b]) == len(want[b]) and (g[b] == want[b]).all(), \
