@@ -142,30 +142,47 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * SEL_ROWS + (threadIdx.x >> 5);
   if (b >= B) return;
-  if (cm.h0 && st.pending[b]) {
-    const long long r = (long long)b * DEC_H;
-#pragma unroll
-    for (int k = 0; k < DEC_H4 / 32; k++) {
-      st4(cm.h0 + r + 4 * (lane + 32 * k), ld4(cm.h0n + r + 4 * (lane + 32 * k)));
-      st4(cm.h1 + r + 4 * (lane + 32 * k), ld4(cm.h1n + r + 4 * (lane + 32 * k)));
-    }
-  }
+  // every load this row needs before its argmax is issued here, together: the
+  // row state, this lane's logits and, for a commit, the new LSTM states
   const int T = seq_T(seq, b);
   const int tb = st.t[b];
-  if (tb >= T) {                       // finished: its last decoder step (if any) has run
+  const bool active = tb < T;
+  const bool commit = cm.h0 && st.pending[b];
+  int s_in = 0, ntok_in = 0, evals_in = 0;
+  if (lane == 0 && active) {
+    s_in = st.s[b];
+    ntok_in = st.ntok[b];
+    evals_in = st.evals[b];
+  }
+  const float *l = out + (long long)b * DEC_V;
+  constexpr int NV = (DEC_V + 31) / 32;
+  float xv[NV];
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int v = lane + 32 * i;
+      xv[i] = v < DEC_V ? l[v] + __ldg(out_b + v) : 0.f;
+    }
+  }
+  if (commit) {
+    const long long r = (long long)b * DEC_H;
+    float4 n0[DEC_H4 / 32], n1[DEC_H4 / 32];
+#pragma unroll
+    for (int k = 0; k < DEC_H4 / 32; k++) {
+      n0[k] = ld4(cm.h0n + r + 4 * (lane + 32 * k));
+      n1[k] = ld4(cm.h1n + r + 4 * (lane + 32 * k));
+    }
+#pragma unroll
+    for (int k = 0; k < DEC_H4 / 32; k++) {
+      st4(cm.h0 + r + 4 * (lane + 32 * k), n0[k]);
+      st4(cm.h1 + r + 4 * (lane + 32 * k), n1[k]);
+    }
+  }
+  if (!active) {                       // finished: its last decoder step (if any) has run
     if (lane == 0) st.pending[b] = 0;
     return;
   }
-  const float *l = out + (long long)b * DEC_V;
-  // all of this lane's logits first (independent loads in flight), then the
-  // comparisons in index order
-  constexpr int NV = (DEC_V + 31) / 32;
-  float xv[NV];
-#pragma unroll
-  for (int i = 0; i < NV; i++) {
-    const int v = lane + 32 * i;
-    xv[i] = v < DEC_V ? l[v] + __ldg(out_b + v) : 0.f;
-  }
+  // the comparisons in index order
   float bv = -INFINITY;
   int bi = INT_MAX;
 #pragma unroll
@@ -179,20 +196,21 @@ dec_select_kernel(const float *__restrict__ out, const float *__restrict__ out_b
     const int oi = __shfl_xor_sync(PK_FULL_MASK, bi, o);
     if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
   }
-  const int best = (isnan(l[0] + __ldg(out_b)) || bi == INT_MAX) ? 0 : bi;
+  const float first = __shfl_sync(PK_FULL_MASK, xv[0], 0);   // logit 0 + its bias (lane 0's v = 0)
+  const int best = (isnan(first) || bi == INT_MAX) ? 0 : bi;
   if (best != DEC_BLANK) {             // the next decoder step's input (csrc/decoder.c:19)
     const float4 *src = reinterpret_cast<const float4 *>(embed + (long long)best * DEC_H);
     float4 *dst = reinterpret_cast<float4 *>(x0 + (long long)b * DEC_H);
     for (int j = lane; j < DEC_H4; j += 32) dst[j] = __ldg(src + j);
   }
   if (lane != 0) return;
-  st.evals[b] += 1;
-  int t = tb, s = st.s[b], pend = 0;
+  st.evals[b] = evals_in + 1;
+  int t = tb, s = s_in, pend = 0;
   if (best == DEC_BLANK) {
     t += 1;
     s = 0;
   } else {
-    const int n = st.ntok[b];
+    const int n = ntok_in;
     tokens[DEC_MAX_SYM * seq_frame_off(seq, b) + n] = best;
     st.ntok[b] = n + 1;
     st.last[b] = best;
