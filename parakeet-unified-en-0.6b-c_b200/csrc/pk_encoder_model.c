@@ -18,6 +18,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <stdint.h>
+
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
@@ -38,6 +40,13 @@ static const long long W_ELEMS[W_N] = {
     (long long)PK_D * PK_D, (long long)PK_D * PK_D, 2LL * PK_D * PK_D, (long long)PK_D * PK_D,
     (long long)PK_D * PK_FF, (long long)PK_FF * PK_D};
 
+/* [K, N] of each weight as the product x W reads it (row-major, [in, out]). */
+static const int W_K[W_N] = {PK_D, PK_FF, PK_D, PK_D, PK_D, PK_D, PK_D, PK_D, PK_FF};
+static const int W_COLS[W_N] = {PK_FF, PK_D, 3 * PK_D, PK_D, PK_D, 2 * PK_D, PK_D, PK_FF, PK_D};
+/* The row-major projections, done as three bf16 GEMMs on split operands
+ * (k_split.cu); the pointwise convolutions keep fp32 SGEMM. */
+static const int W_SPLIT[W_N] = {1, 1, 1, 1, 1, 0, 0, 1, 1};
+
 struct pkcu_encoder_model {
     int device, n_blocks;
     cublasHandle_t blas;
@@ -45,6 +54,10 @@ struct pkcu_encoder_model {
     const float *w[64][W_N];
     pkcu_block_params params[64];
     const float *pe;                   /* pos_encoding.pe_table [9999, 1024] */
+    void *stacks;                      /* bf16 part stacks [3K, N] of the W_SPLIT weights */
+    const void *stack[64][W_N];        /* NULL: that product runs on the fp32 path */
+    void *split_ws;                    /* activation parts [rows, 3K] bf16, grown per forward */
+    size_t split_cap;                  /* its bytes */
 };
 
 void pkcu_encoder_model_destroy(pkcu_encoder_model *m)
@@ -52,7 +65,37 @@ void pkcu_encoder_model_destroy(pkcu_encoder_model *m)
     if (!m) return;
     if (m->blas) cublasDestroy(m->blas);
     if (m->arena) cudaFree(m->arena);
+    if (m->stacks) cudaFree(m->stacks);
+    if (m->split_ws) cudaFree(m->split_ws);
     free(m);
+}
+
+/* The bf16 part stacks of every W_SPLIT weight (3 parts x 2 bytes per
+ * element). Without the memory for them the model keeps the fp32 path. */
+static int build_stacks(pkcu_encoder_model *m, long long per, pkcu_stream_t stream)
+{
+    long long elems = 0;
+    for (int k = 0; k < W_N; k++)
+        if (W_SPLIT[k]) elems += 3 * W_ELEMS[k];
+    if (cudaMalloc(&m->stacks, 2 * (size_t)(elems * m->n_blocks)) != cudaSuccess) {
+        cudaGetLastError();
+        m->stacks = NULL;
+        return PKCU_OK;
+    }
+    char *p = (char *)m->stacks;
+    for (int b = 0; b < m->n_blocks; b++) {
+        const float *src = m->arena + per * b;
+        for (int k = 0; k < W_N; k++) {
+            if (W_SPLIT[k]) {
+                const int st = pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream);
+                if (st) return st;
+                m->stack[b][k] = p;
+                p += 2 * 3 * W_ELEMS[k];
+            }
+            src += W_ELEMS[k];
+        }
+    }
+    return PKCU_OK;
 }
 
 static long long block_elems(void)
@@ -132,6 +175,11 @@ int pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_
             return st;
         }
     }
+    st = build_stacks(m, per, stream);
+    if (st) {
+        pkcu_encoder_model_destroy(m);
+        return st;
+    }
     if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) {
         pkcu_encoder_model_destroy(m);
         return pkcu_launch_status("pkcu_encoder_model_create");
@@ -180,6 +228,57 @@ static int proj(cublasHandle_t h, int M, int N, int K, const float *A, const flo
     return rm_gemm(h, M, N, K, A, K, 0, B, N, 0, 0, C, N, 0, 1);
 }
 
+/* C[M, N] = A[M, K] W[K, N] from the split operands: the activation parts
+ * [a0 | a1 | a2] into the model's workspace, then cuBLAS bf16 GEMMs (fp32
+ * accumulation and output) band by band, smallest band first, the later ones
+ * added through beta = 1 (stack = [w2; w1; w0], k_split.cu):
+ *   C = [a0 a1 a2] [w2; w1; w0];  C += [a0 a1] [w1; w0];  C += a0 w0 (in K chunks)
+ * Row-major through the column-major library as C^T = W^T A^T. */
+static int proj_split(pkcu_encoder_model *m, cublasHandle_t h, int M, int N, int K, const float *A,
+                      const void *stack, float *C, pkcu_stream_t stream)
+{
+    if ((size_t)M * 3 * K * 2 > m->split_cap)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: split workspace too small");
+    int st = pk_split_rows_bf16x3(A, m->split_ws, M, K, stream);
+    if (st) return st;
+    const uint16_t *S = (const uint16_t *)stack;   /* bf16 elements */
+    const uint16_t *Ap = (const uint16_t *)m->split_ws;
+    static const float one = 1.0f, zero = 0.0f;
+    /* (k, first stack row, first activation column, beta): bands 2 and 1,
+     * then band 0 in chunks of at most SPLIT_CHUNK along K -- the tensor
+     * cores' accumulation rounds less exactly than an fp32 add, so the
+     * largest band is summed in short runs joined by the GEMM's fp32 epilogue */
+    enum { SPLIT_CHUNK = 512 };
+    struct { int k; long long srow, acol; const float *beta; } part[2 + PK_FF / SPLIT_CHUNK];
+    int np = 0;
+    part[np].k = 3 * K; part[np].srow = 0; part[np].acol = 0; part[np++].beta = &zero;
+    part[np].k = 2 * K; part[np].srow = K; part[np].acol = 0; part[np++].beta = &one;
+    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
+        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
+        part[np].srow = 2LL * K + k0;
+        part[np].acol = k0;
+        part[np++].beta = &one;
+    }
+    for (int i = 0; i < np; i++) {
+        const cublasStatus_t cs = cublasGemmEx(
+            h, CUBLAS_OP_N, CUBLAS_OP_N, N, M, part[i].k, &one, S + part[i].srow * N, CUDA_R_16BF, N,
+            Ap + part[i].acol, CUDA_R_16BF, 3 * K, part[i].beta, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
+            CUBLAS_GEMM_DEFAULT);
+        if (cs != CUBLAS_STATUS_SUCCESS)
+            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
+    }
+    return PKCU_OK;
+}
+
+/* The block's row-major projection: split operands when the model has the
+ * weight's part stack, the fp32 tensor-core GEMM otherwise. */
+static int proj_w(pkcu_encoder_model *m, cublasHandle_t h, int b, int k, int M, const float *A, float *C,
+                  pkcu_stream_t stream)
+{
+    if (m->stack[b][k]) return proj_split(m, h, M, W_COLS[k], W_K[k], A, m->stack[b][k], C, stream);
+    return proj(h, M, W_COLS[k], W_K[k], A, m->w[b][k], C, stream);
+}
+
 static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
 {
     Fwd *f = (Fwd *)user;
@@ -192,12 +291,12 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     const int n = f->seq->dev.n_items, uni = f->seq->dev.uniform_T;
     const long long F = f->seq->frames;
     switch (gemm) {   /* the row-major projections of the whole batch */
-    case PKCU_GEMM_FF1_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff1, W[W_FF1_1], gemm_dst(go->ff1_h), stream);
-    case PKCU_GEMM_FF1_2: return proj(h, (int)F, PK_D, PK_FF, gi->h1, W[W_FF1_2], gemm_dst(go->ff1_out), stream);
-    case PKCU_GEMM_QKV:   return proj(h, (int)F, 3 * PK_D, PK_D, gi->ln_sa, W[W_QKV], gemm_dst(go->qkv), stream);
-    case PKCU_GEMM_OUT:   return proj(h, (int)F, PK_D, PK_D, gi->attn, W[W_OUT], gemm_dst(go->att_out), stream);
-    case PKCU_GEMM_FF2_1: return proj(h, (int)F, PK_FF, PK_D, gi->ln_ff2, W[W_FF2_1], gemm_dst(go->ff2_h), stream);
-    case PKCU_GEMM_FF2_2: return proj(h, (int)F, PK_D, PK_FF, gi->h2, W[W_FF2_2], gemm_dst(go->ff2_out), stream);
+    case PKCU_GEMM_FF1_1: return proj_w(f->m, h, b, W_FF1_1, (int)F, gi->ln_ff1, gemm_dst(go->ff1_h), stream);
+    case PKCU_GEMM_FF1_2: return proj_w(f->m, h, b, W_FF1_2, (int)F, gi->h1, gemm_dst(go->ff1_out), stream);
+    case PKCU_GEMM_QKV:   return proj_w(f->m, h, b, W_QKV, (int)F, gi->ln_sa, gemm_dst(go->qkv), stream);
+    case PKCU_GEMM_OUT:   return proj_w(f->m, h, b, W_OUT, (int)F, gi->attn, gemm_dst(go->att_out), stream);
+    case PKCU_GEMM_FF2_1: return proj_w(f->m, h, b, W_FF2_1, (int)F, gi->ln_ff2, gemm_dst(go->ff2_h), stream);
+    case PKCU_GEMM_FF2_2: return proj_w(f->m, h, b, W_FF2_2, (int)F, gi->h2, gemm_dst(go->ff2_out), stream);
     default: break;
     }
     if (gemm == PKCU_GEMM_POS) {
@@ -215,7 +314,7 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
                          ? PKCU_OK : pkcu_fail(PKCU_ERR_CUDA, "pkcu_encoder_forward: positional copy");
             } else {
                 const float *pe = f->m->pe + (long long)(PE_CENTER - T + 1) * PK_D;
-                st = proj(h, L, PK_D, PK_D, pe, W[W_POS], dst, stream);
+                st = proj_w(f->m, h, b, W_POS, L, pe, dst, stream);
             }
             if (st) return st;
         }
@@ -280,6 +379,27 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
         acc[1] += 2 * T - 1;
         acc[2] += (long long)PK_H * T * T;
         acc[3] += (long long)PK_H * T * (2 * T - 1);
+    }
+    /* the activation parts of the largest projection: F rows of K = 4096, or
+     * 2T - 1 positional rows of K = 1024 */
+    long long rows_ff = 0, rows_pos = 0;
+    for (int i = 0; i < n; i++) {
+        rows_ff += seq->lengths[i];
+        if (2LL * seq->lengths[i] - 1 > rows_pos) rows_pos = 2LL * seq->lengths[i] - 1;
+    }
+    size_t need = (size_t)rows_ff * 3 * PK_FF * 2;
+    if ((size_t)rows_pos * 3 * PK_D * 2 > need) need = (size_t)rows_pos * 3 * PK_D * 2;
+    if (m->stacks && need > m->split_cap) {
+        if (m->split_ws) cudaFree(m->split_ws);
+        m->split_ws = NULL;
+        m->split_cap = 0;
+        if (cudaMalloc(&m->split_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            m->split_ws = NULL;
+            free(off);
+            return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_encoder_forward: %zu bytes of split workspace", need);
+        }
+        m->split_cap = need;
     }
     Fwd f = {m, gemm_out, gemm_in, seq, off};
     const int st = pkcu_encoder_nongemm(x, m->params, m->n_blocks, gemm_out, gemm_in, seq, fwd_hook,

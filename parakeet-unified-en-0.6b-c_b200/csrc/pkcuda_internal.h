@@ -61,6 +61,12 @@ int pk_conv_wait_timeouts(unsigned *count, int reset);
 int pk_gemm_f32_rm(const float *A, const float *B, float *C, int M, int N, int K,
                    pkcu_stream_t stream);
 
+/* fp32 operands as three bf16 parts (k_split.cu): rows of A [M, K] to
+ * out [M, 3K] = [a0 | a1 | a2]; W [K, N] to the stack S [3K, N] =
+ * [w2; w1; w0] (K resp. N a multiple of 4, 16-byte aligned). */
+int pk_split_rows_bf16x3(const float *A, void *out, long long M, int K, pkcu_stream_t stream);
+int pk_split_stack_bf16x3(const float *W, void *S, int K, int N, pkcu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
