@@ -670,8 +670,9 @@ def time_asr_decode(stream, reps, n_utts=256, T=375, cpu=True):
             out[name] = r
         finally:
             shutil.rmtree(d, ignore_errors=True)
-    out["note"] = ("host wall clock of the synchronous call: decoder set-up, the encoder projection, "
-                   "the decode graph, tokens copied to the host")
+    out["note"] = ("host wall clock of the synchronous call after a first call with the same lengths "
+                   "(which creates the decoder and captures its graph): the encoder projection, the "
+                   "decode graph, tokens copied to the host")
     return out
 
 
@@ -772,14 +773,16 @@ def cpu_encoder_baseline(T=375):
 ASR_UTTS, ASR_MEL = 32, 3000
 
 
-def time_asr(stream, reps, n_utts=ASR_UTTS, mel_frames=ASR_MEL):
+def time_asr(stream, reps, n_utts=ASR_UTTS, mel_frames=ASR_MEL, blank_bias=0.0):
     """pkcu_asr_transcribe: n_utts spectrograms of 3000 mel frames (30 s each)
     to tokens -- pre-encode, 24 blocks, greedy decode, every GEMM done by the
-    library -- on a synthetic checkpoint in the reference's format."""
+    library -- on a synthetic checkpoint in the reference's format (blank bias
+    0: its random weights emit the 10-symbol cap on every frame, the decode's
+    worst case)."""
     import shutil
     import torch
     import pkcuda
-    d, bp, jp = _synthetic_checkpoint()
+    d, bp, jp = _synthetic_checkpoint(blank_bias=blank_bias)
     try:
         with pkcuda.Weights(bp, jp) as w:
             w.upload(stream)
@@ -799,10 +802,12 @@ def time_asr(stream, reps, n_utts=ASR_UTTS, mel_frames=ASR_MEL):
     finally:
         shutil.rmtree(d, ignore_errors=True)
     enc = n_utts * (((mel_frames + 1) // 2 + 1) // 2 + 1) // 2
-    return {"utterances": n_utts, "mel_frames": mel_frames, "seconds_per_call": round(dt, 4),
+    ntok = int(sum(len(o) for o in out))
+    return {"utterances": n_utts, "mel_frames": mel_frames, "blank_bias": blank_bias,
+            "seconds_per_call": round(dt, 4),
             "utterances_per_s": round(n_utts / dt, 2), "encoder_frames_per_s": round(enc / dt),
             "audio_seconds_per_s": round(n_utts * mel_frames / 100.0 / dt, 1),
-            "tokens": int(sum(len(o) for o in out)),
+            "tokens": ntok, "tokens_per_frame": round(ntok / enc, 3),
             "first_call_s": round(first, 4),
             "note": "host wall clock of the synchronous call with spectrograms on the device; after the "
                     "first call (which allocates the working buffers and captures the decode graph) "
@@ -1022,6 +1027,7 @@ def aux_only(args, local_rank):
             return
         if args.asr_only:
             asr = time_asr(stream, args.aux_reps)
+            asr["every_frame_blank"] = time_asr(stream, args.aux_reps, blank_bias=6.0)
             if not args.no_cpu_baseline:
                 asr["cpu_baseline"] = cpu_asr_baseline()
             print(json.dumps({"asr": asr}), flush=True)
@@ -1126,6 +1132,12 @@ def _ours(args, rank, world, local_rank, stream):
         gemms = time_fused_gemms(stream, 3)
         forward = time_encoder_forward(stream, 2)
         asr = time_asr(stream, 1)
+        # the same with a blank bias that makes every evaluation blank: the
+        # decode's lightest case (the synthetic model's outputs flip between
+        # the two extremes; a trained model lies between them)
+        asr["every_frame_blank"] = {k: v for k, v in time_asr(stream, 1, blank_bias=6.0).items()
+                                    if k in ("blank_bias", "seconds_per_call", "utterances_per_s",
+                                             "audio_seconds_per_s", "tokens_per_frame")}
         asr_dec = time_asr_decode(stream, 2, cpu=world == 1 and not args.no_cpu_baseline)
         dec_fused = {"10_tokens_every_frame": time_decode_fused(stream, 2, 256, 40, 0.0),
                      "sparse_decoder_steps": time_decode_fused(stream, 2, 256, 200, 3.5)}
