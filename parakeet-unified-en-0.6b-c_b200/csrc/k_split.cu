@@ -75,6 +75,37 @@ __global__ void split_stack_kernel(const float *__restrict__ W, __nv_bfloat16 *_
   }
 }
 
+// items x [K, T] fp32 (channel-first) -> items x [3K, Tp] bf16 = [x2; x1; x0]
+// per item, rows padded to the pitch Tp >= T (the pad columns are left as they
+// are: they only feed output columns that are dropped).
+__global__ void split_cols_kernel(const float *__restrict__ X, __nv_bfloat16 *__restrict__ out, long long items,
+                                  int K, int T, int Tp) {
+  const long long per = (long long)K * T, per_out = (long long)K * Tp;
+  const long long n = items * per;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long it = e / per, r = e - it * per;
+    const long long k = r / T, t = r - k * T;
+    __nv_bfloat16 p0, p1, p2;
+    split3(__ldg(X + e), p0, p1, p2);
+    __nv_bfloat16 *o = out + it * 3 * per_out + k * Tp + t;
+    o[0] = p2;
+    o[per_out] = p1;
+    o[2 * per_out] = p0;
+  }
+}
+
+// rows x [Tp] -> rows x [T]: drops the pad columns.
+__global__ void depad_kernel(const float *__restrict__ src, float *__restrict__ dst, long long rows, int T,
+                             int Tp) {
+  const long long n = rows * T;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long r = e / T, t = e - r * T;
+    dst[e] = __ldg(src + r * Tp + t);
+  }
+}
+
 static unsigned split_grid(long long work) {
   long long g = (work + 255) / 256;
   const long long cap = (long long)pkcu_sm_count() * 16;
@@ -100,4 +131,19 @@ extern "C" int pk_split_stack_bf16x3(const float *W, void *S, int K, int N, pkcu
   split_stack_kernel<<<split_grid((long long)K * (N / 4)), 256, 0, (cudaStream_t)stream>>>(
       W, static_cast<__nv_bfloat16 *>(S), K, N);
   return pkcu_launch_status("pk_split_stack_bf16x3");
+}
+
+extern "C" int pk_split_cols_bf16x3(const float *X, void *out, long long items, int K, int T, int Tp,
+                                    pkcu_stream_t stream) {
+  if (!X || !out || items <= 0 || K <= 0 || T <= 0 || Tp < T)
+    return pkcu_fail(PKCU_ERR_ARG, "pk_split_cols_bf16x3: bad argument");
+  split_cols_kernel<<<split_grid(items * K * (long long)T), 256, 0, (cudaStream_t)stream>>>(
+      X, static_cast<__nv_bfloat16 *>(out), items, K, T, Tp);
+  return pkcu_launch_status("pk_split_cols_bf16x3");
+}
+
+extern "C" int pk_depad_rows(const float *src, float *dst, long long rows, int T, int Tp, pkcu_stream_t stream) {
+  if (!src || !dst || rows <= 0 || T <= 0 || Tp < T) return pkcu_fail(PKCU_ERR_ARG, "pk_depad_rows: bad argument");
+  depad_kernel<<<split_grid(rows * T), 256, 0, (cudaStream_t)stream>>>(src, dst, rows, T, Tp);
+  return pkcu_launch_status("pk_depad_rows");
 }

@@ -43,9 +43,10 @@ static const long long W_ELEMS[W_N] = {
 /* [K, N] of each weight as the product x W reads it (row-major, [in, out]). */
 static const int W_K[W_N] = {PK_D, PK_FF, PK_D, PK_D, PK_D, PK_D, PK_D, PK_D, PK_FF};
 static const int W_COLS[W_N] = {PK_FF, PK_D, 3 * PK_D, PK_D, PK_D, 2 * PK_D, PK_D, PK_FF, PK_D};
-/* The row-major projections, done as three bf16 GEMMs on split operands
- * (k_split.cu); the pointwise convolutions keep fp32 SGEMM. */
-static const int W_SPLIT[W_N] = {1, 1, 1, 1, 1, 0, 0, 1, 1};
+/* Every block weight runs on split operands (k_split.cu): 1 = the right-hand
+ * operand of a row-major projection, kept as the stack [w2; w1; w0]; 2 = the
+ * left-hand operand of a pointwise convolution, kept as rows [w0 | w1 | w2]. */
+static const int W_SPLIT[W_N] = {1, 1, 1, 1, 1, 2, 2, 1, 1};
 
 struct pkcu_encoder_model {
     int device, n_blocks;
@@ -87,7 +88,9 @@ static int build_stacks(pkcu_encoder_model *m, long long per, pkcu_stream_t stre
         const float *src = m->arena + per * b;
         for (int k = 0; k < W_N; k++) {
             if (W_SPLIT[k]) {
-                const int st = pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream);
+                /* a pointwise weight is [out channels, 1024]: W_COLS x W_K */
+                const int st = W_SPLIT[k] == 1 ? pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream)
+                                               : pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
                 if (st) return st;
                 m->stack[b][k] = p;
                 p += 2 * 3 * W_ELEMS[k];
@@ -270,6 +273,53 @@ static int proj_split(pkcu_encoder_model *m, cublasHandle_t h, int M, int N, int
     return PKCU_OK;
 }
 
+/* The pointwise convolution C[Mo, T] = W[Mo, K] X[K, T] of `items`
+ * consecutive utterances of T frames (channel-first) from split operands,
+ * when the workspace holds them (else the fp32 SGEMM path, return 1): X's
+ * parts as [x2; x1; x0] per utterance at the padded pitch Tp (T rounded up
+ * to 8, so every row starts 16-byte aligned) into the workspace, W's as
+ * [w0 | w1 | w2] (model load), one strided-batched bf16 GEMM per band as in
+ * proj_split (band 0 in K chunks) into a padded fp32 product behind them, then
+ * the pad columns dropped into C. */
+static int pw_split(pkcu_encoder_model *m, cublasHandle_t h, int Mo, int T, int items, const void *wrows,
+                    const float *X, float *C, pkcu_stream_t stream, int *fallback)
+{
+    const int K = PK_D, Tp = (T + 7) & ~7;
+    const size_t xbytes = ((size_t)items * 3 * K * Tp * 2 + 255) & ~(size_t)255;
+    const size_t cbytes = (size_t)items * Mo * Tp * 4;
+    *fallback = 0;
+    if (xbytes + cbytes > m->split_cap) {
+        *fallback = 1;
+        return PKCU_OK;
+    }
+    const uint16_t *Xp = (const uint16_t *)m->split_ws;   /* bf16 elements */
+    float *Cp = (float *)((char *)m->split_ws + xbytes);
+    int st = pk_split_cols_bf16x3(X, m->split_ws, items, K, T, Tp, stream);
+    if (st) return st;
+    const uint16_t *Wp = (const uint16_t *)wrows;
+    static const float one = 1.0f, zero = 0.0f;
+    enum { SPLIT_CHUNK = 512 };
+    struct { int k; long long wcol, xrow; const float *beta; } part[2 + PK_D / SPLIT_CHUNK];
+    int np = 0;
+    part[np].k = 3 * K; part[np].wcol = 0; part[np].xrow = 0; part[np++].beta = &zero;
+    part[np].k = 2 * K; part[np].wcol = 0; part[np].xrow = K; part[np++].beta = &one;
+    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
+        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
+        part[np].wcol = k0;
+        part[np].xrow = 2LL * K + k0;
+        part[np++].beta = &one;
+    }
+    for (int i = 0; i < np; i++) {
+        const cublasStatus_t cs = cublasGemmStridedBatchedEx(
+            h, CUBLAS_OP_N, CUBLAS_OP_N, Tp, Mo, part[i].k, &one, Xp + part[i].xrow * Tp, CUDA_R_16BF, Tp,
+            3LL * K * Tp, Wp + part[i].wcol, CUDA_R_16BF, 3 * K, 0, part[i].beta, Cp, CUDA_R_32F, Tp,
+            (long long)Mo * Tp, items, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (cs != CUBLAS_STATUS_SUCCESS)
+            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
+    }
+    return pk_depad_rows(Cp, C, (long long)items * Mo, T, Tp, stream);
+}
+
 /* The block's row-major projection: split operands when the model has the
  * weight's part stack, the fp32 tensor-core GEMM otherwise. */
 static int proj_w(pkcu_encoder_model *m, cublasHandle_t h, int b, int k, int M, const float *A, float *C,
@@ -342,14 +392,26 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
             st = rm_gemm(h, T, PK_DH, T, gi->S + so, T, (long long)T * T, gi->V + fo * PK_D, PK_DH,
                          (long long)T * PK_DH, 0, gemm_dst(go->attn_h) + fo * PK_D, PK_DH, (long long)T * PK_DH, Hb);
             break;
-        case PKCU_GEMM_PW1:   /* [2048, T] = W_pw1 [2048, 1024] x cf [1024, T] */
-            st = rm_gemm(h, 2 * PK_D, T, PK_D, W[W_PW1], PK_D, 0, gi->cf + fo * PK_D, T,
-                         (long long)PK_D * T, 0, gemm_dst(go->pw1) + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
+        case PKCU_GEMM_PW1: { /* [2048, T] = W_pw1 [2048, 1024] x cf [1024, T] */
+            int fb = 1;
+            if (f->m->stack[b][W_PW1])
+                st = pw_split(f->m, h, 2 * PK_D, T, per, f->m->stack[b][W_PW1], gi->cf + fo * PK_D,
+                              gemm_dst(go->pw1) + fo * 2 * PK_D, stream, &fb);
+            if (!st && fb)
+                st = rm_gemm(h, 2 * PK_D, T, PK_D, W[W_PW1], PK_D, 0, gi->cf + fo * PK_D, T,
+                             (long long)PK_D * T, 0, gemm_dst(go->pw1) + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
             break;
-        case PKCU_GEMM_PW2:   /* [1024, T] = W_pw2 x dw [1024, T] */
-            st = rm_gemm(h, PK_D, T, PK_D, W[W_PW2], PK_D, 0, gi->dw + fo * PK_D, T,
-                         (long long)PK_D * T, 0, gemm_dst(go->pw2) + fo * PK_D, T, (long long)PK_D * T, per);
+        }
+        case PKCU_GEMM_PW2: { /* [1024, T] = W_pw2 x dw [1024, T] */
+            int fb = 1;
+            if (f->m->stack[b][W_PW2])
+                st = pw_split(f->m, h, PK_D, T, per, f->m->stack[b][W_PW2], gi->dw + fo * PK_D,
+                              gemm_dst(go->pw2) + fo * PK_D, stream, &fb);
+            if (!st && fb)
+                st = rm_gemm(h, PK_D, T, PK_D, W[W_PW2], PK_D, 0, gi->dw + fo * PK_D, T,
+                             (long long)PK_D * T, 0, gemm_dst(go->pw2) + fo * PK_D, T, (long long)PK_D * T, per);
             break;
+        }
         default:
             return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: unknown GEMM %d", gemm);
         }

@@ -66,6 +66,11 @@ int pk_gemm_f32_rm(const float *A, const float *B, float *C, int M, int N, int K
  * [w2; w1; w0] (K resp. N a multiple of 4, 16-byte aligned). */
 int pk_split_rows_bf16x3(const float *A, void *out, long long M, int K, pkcu_stream_t stream);
 int pk_split_stack_bf16x3(const float *W, void *S, int K, int N, pkcu_stream_t stream);
+/* items x [K, T] (any T) to items x [3K, Tp] = [x2; x1; x0], rows at pitch
+ * Tp >= T; pk_depad_rows copies rows x [Tp] to rows x [T]. */
+int pk_split_cols_bf16x3(const float *X, void *out, long long items, int K, int T, int Tp,
+                         pkcu_stream_t stream);
+int pk_depad_rows(const float *src, float *dst, long long rows, int T, int Tp, pkcu_stream_t stream);
 
 #ifdef __cplusplus
 }
