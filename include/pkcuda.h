@@ -409,9 +409,14 @@ int pkcu_gemm_bias_residual(const float *A, const float *W, const float *bias, f
  * Replaces encode_blocks (csrc/encoder.c:495-512) for a batch: fp32 device
  * copies of every block's GEMM weights from an uploaded checkpoint (int8 /
  * int4 dequantised once, the fused QKV as the reference's loader builds it),
- * then pkcu_encoder_nongemm with its twelve GEMM points done by the library
- * (cuBLAS single-precision GEMMs, no TF32; the positional projection of each
- * utterance's slice of pos_encoding.pe_table, csrc/encoder.c:220-227). */
+ * then pkcu_encoder_nongemm with its twelve GEMM points done by the library,
+ * fp32-accurate: the projections (the positional one on each distinct
+ * utterance length's slice of pos_encoding.pe_table, csrc/encoder.c:220-227)
+ * and the pointwise convolutions as bf16 tensor-core GEMMs on operands split
+ * into three bf16 parts (the weights' parts made once here), the per-head
+ * products as cuBLAS single-precision GEMMs (no TF32). A model keeps a working
+ * buffer for the split operands (grown by the largest forward so far), so one
+ * model serves one forward at a time. */
 typedef struct pkcu_weights pkcu_weights;   /* a loaded checkpoint (section 4 below) */
 typedef struct pkcu_encoder_model pkcu_encoder_model;
 int  pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_encoder_model **out);
@@ -427,7 +432,8 @@ int  pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_outpu
  * pre_encode_and_scale + encode_blocks + pk_greedy_decode (csrc/encoder.c:
  * 578-593, 495-512; csrc/decoder.c:80-132) for a batch of utterances, every
  * GEMM done by the library (fp32-accurate tensor-core GEMMs where the shape
- * suits them, cuBLAS single precision elsewhere). */
+ * suits them, cuBLAS single precision elsewhere). One pkcu_asr serves one call
+ * at a time: its calls share the kept working buffers and decoder. */
 typedef struct pkcu_asr pkcu_asr;
 int  pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out);
 void pkcu_asr_destroy(pkcu_asr *m);
