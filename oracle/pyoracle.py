@@ -796,3 +796,39 @@ def reference_transcribe(bin_path, json_path, mel):
                                      C.byref(nt))
     assert got > 0, "reference failed to load the checkpoint"
     return enc[:got].copy(), tok[:nt.value].copy()
+
+
+# ── fp32 operands as three bf16 parts (the library's split-operand GEMMs) ────
+
+def bf16_rn(x):
+    """float32 -> bfloat16 bits (uint16), round to nearest, ties to even (the
+    conversion the split kernels use; values here are finite)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def bf16_to_f32(h):
+    return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def split3_bf16(x):
+    """x = x0 + x1 + x2 with x0 = bf16(x), x1 = bf16(x - x0), x2 =
+    bf16(x - x0 - x1), each difference exact in fp32 (the parts as uint16
+    bits, in that order)."""
+    x = np.ascontiguousarray(x, np.float32)
+    p0 = bf16_rn(x)
+    r1 = (x - bf16_to_f32(p0)).astype(np.float32)
+    p1 = bf16_rn(r1)
+    r2 = (r1 - bf16_to_f32(p1)).astype(np.float32)
+    return p0, p1, bf16_rn(r2)
+
+
+def split_band_product(a, w):
+    """A [M, K] x W [K, N] from the six part products with i + j <= 2, each
+    band summed on its own and the bands added smallest first (float64
+    accumulation: the arithmetic the split GEMMs approximate)."""
+    pa = [bf16_to_f32(p).astype(np.float64) for p in split3_bf16(a)]
+    pw = [bf16_to_f32(p).astype(np.float64) for p in split3_bf16(w)]
+    band = lambda k: sum(pa[i] @ pw[k - i] for i in range(k + 1))
+    return (band(2) + band(1)) + band(0)

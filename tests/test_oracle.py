@@ -278,3 +278,21 @@ def test_kat_exp_poly_exact_points(oracle):
     # degree-5 Taylor on |r| <= ln2/2: relative error below 2e-6 (r^6/720 at the edge)
     for x in (1.0, -3.5, 10.0, -20.25):
         assert abs(oracle.exp_poly(x) / np.exp(np.float64(x)) - 1) < 2e-6
+
+
+def test_split3_bf16_properties():
+    """The three-part bf16 split behind the split-operand GEMMs: the parts sum
+    back to the fp32 value exactly, and the six kept part products of a
+    1024-long product are within a few fp32 units of the float64 product
+    (the three dropped ones are below 2^-23 of |a||w|)."""
+    rng = np.random.default_rng(41)
+    x = (rng.standard_normal(100000) * np.exp(rng.uniform(-20, 20, 100000))).astype(np.float32)
+    p0, p1, p2 = po.split3_bf16(x)
+    back = (po.bf16_to_f32(p0).astype(np.float64) + po.bf16_to_f32(p1) + po.bf16_to_f32(p2))
+    assert (back == x.astype(np.float64)).all()
+    a = rng.standard_normal((64, 1024)).astype(np.float32)
+    w = (rng.standard_normal((1024, 96)) / 32).astype(np.float32)
+    exact = a.astype(np.float64) @ w.astype(np.float64)
+    bound = np.abs(a).astype(np.float64) @ np.abs(w).astype(np.float64)
+    err = np.abs(po.split_band_product(a, w) - exact) / bound
+    assert err.max() < 2.0 ** -22, err.max()
