@@ -413,7 +413,8 @@ int pkcu_gemm_bias_residual(const float *A, const float *W, const float *bias, f
  * fp32-accurate: the projections (the positional one on each distinct
  * utterance length's slice of pos_encoding.pe_table, csrc/encoder.c:220-227)
  * and the pointwise convolutions as bf16 tensor-core GEMMs on operands split
- * into three bf16 parts (the weights' parts made once here), the per-head
+ * into three bf16 parts (the weights' parts made once here; an int8 weight
+ * with a per-tensor scale is used as stored, q exact in bf16), the per-head
  * products as cuBLAS single-precision GEMMs (no TF32). A model keeps a working
  * buffer for the split operands (grown by the largest forward so far), so one
  * model serves one forward at a time. */

@@ -95,6 +95,13 @@ __global__ void split_cols_kernel(const float *__restrict__ X, __nv_bfloat16 *__
   }
 }
 
+// int8 -> bf16 (exact: |q| <= 128 fits the 8-bit significand).
+__global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, long long n) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (long long)gridDim.x * blockDim.x)
+    out[e] = __float2bfloat16_rn((float)q[e]);
+}
+
 // rows x [Tp] -> rows x [T]: drops the pad columns.
 __global__ void depad_kernel(const float *__restrict__ src, float *__restrict__ dst, long long rows, int T,
                              int Tp) {
@@ -146,4 +153,10 @@ extern "C" int pk_depad_rows(const float *src, float *dst, long long rows, int T
   if (!src || !dst || rows <= 0 || T <= 0 || Tp < T) return pkcu_fail(PKCU_ERR_ARG, "pk_depad_rows: bad argument");
   depad_kernel<<<split_grid(rows * T), 256, 0, (cudaStream_t)stream>>>(src, dst, rows, T, Tp);
   return pkcu_launch_status("pk_depad_rows");
+}
+
+extern "C" int pk_i8_to_bf16(const int8_t *q, void *out, long long n, pkcu_stream_t stream) {
+  if (!q || !out || n <= 0) return pkcu_fail(PKCU_ERR_ARG, "pk_i8_to_bf16: bad argument");
+  i8_to_bf16_kernel<<<split_grid(n), 256, 0, (cudaStream_t)stream>>>(q, static_cast<__nv_bfloat16 *>(out), n);
+  return pkcu_launch_status("pk_i8_to_bf16");
 }

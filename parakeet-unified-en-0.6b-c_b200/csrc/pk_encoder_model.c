@@ -57,6 +57,7 @@ struct pkcu_encoder_model {
     const float *pe;                   /* pos_encoding.pe_table [9999, 1024] */
     void *stacks;                      /* bf16 part stacks [3K, N] of the W_SPLIT weights */
     const void *stack[64][W_N];        /* NULL: that product runs on the fp32 path */
+    float qscale[64][W_N];             /* > 0: stack holds the int8 weight q as bf16 [K, N], w = q x this */
     void *split_ws;                    /* activation parts [rows, 3K] bf16, grown per forward */
     size_t split_cap;                  /* its bytes */
 };
@@ -71,14 +72,50 @@ void pkcu_encoder_model_destroy(pkcu_encoder_model *m)
     free(m);
 }
 
-/* The bf16 part stacks of every W_SPLIT weight (3 parts x 2 bytes per
- * element). Without the memory for them the model keeps the fp32 path. */
-static int build_stacks(pkcu_encoder_model *m, long long per, pkcu_stream_t stream)
+static long long block_elems(void)
 {
-    long long elems = 0;
-    for (int k = 0; k < W_N; k++)
-        if (W_SPLIT[k]) elems += 3 * W_ELEMS[k];
-    if (cudaMalloc(&m->stacks, 2 * (size_t)(elems * m->n_blocks)) != cudaSuccess) {
+    long long n = 0;
+    for (int k = 0; k < W_N; k++) n += W_ELEMS[k];
+    return n;
+}
+
+/* Block b's weight k as stored when it is int8 with one per-tensor scale (the
+ * reference's int8 projections; the fused QKV at its common scale): the device
+ * int8 [K, N] and the scale, else NULL. */
+static const int8_t *int8_source(const pkcu_weights *w, int b, int k, float *scale)
+{
+    if (k == W_QKV) {
+        const void *qw;
+        int bits;
+        const float *qb;
+        if (pkcu_weights_fused_qkv(w, b, &qw, &bits, scale, &qb) == PKCU_OK && bits == 8)
+            return (const int8_t *)qw;
+        return NULL;
+    }
+    char name[128];
+    pkcu_tensor t;
+    snprintf(name, sizeof(name), "layers.%d.%s", b, W_NAME[k]);
+    if (pkcu_weights_find(w, name, &t) == PKCU_OK && t.dtype == PKCU_DTYPE_I8 && t.dev &&
+        t.numel == W_ELEMS[k] && t.scale > 0.f) {
+        *scale = t.scale;
+        return (const int8_t *)t.dev;
+    }
+    return NULL;
+}
+
+/* The bf16 operands of the split-operand GEMMs: an int8 projection weight as
+ * its q (exact in bf16, 2 bytes per element; the scale goes into the GEMM's
+ * alpha), any other W_SPLIT weight as its three parts (6 bytes per element).
+ * Without the memory for them the model keeps the fp32 path. */
+static int build_stacks(pkcu_encoder_model *m, const pkcu_weights *w, long long per, pkcu_stream_t stream)
+{
+    long long bytes = 0;
+    for (int b = 0; b < m->n_blocks; b++)
+        for (int k = 0; k < W_N; k++) {
+            float sc;
+            if (W_SPLIT[k]) bytes += (W_SPLIT[k] == 1 && int8_source(w, b, k, &sc) ? 2 : 6) * W_ELEMS[k];
+        }
+    if (cudaMalloc(&m->stacks, (size_t)bytes) != cudaSuccess) {
         cudaGetLastError();
         m->stacks = NULL;
         return PKCU_OK;
@@ -88,24 +125,25 @@ static int build_stacks(pkcu_encoder_model *m, long long per, pkcu_stream_t stre
         const float *src = m->arena + per * b;
         for (int k = 0; k < W_N; k++) {
             if (W_SPLIT[k]) {
-                /* a pointwise weight is [out channels, 1024]: W_COLS x W_K */
-                const int st = W_SPLIT[k] == 1 ? pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream)
-                                               : pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
+                float sc = 0.f;
+                const int8_t *q = W_SPLIT[k] == 1 ? int8_source(w, b, k, &sc) : NULL;
+                int st;
+                if (q) {
+                    st = pk_i8_to_bf16(q, p, W_ELEMS[k], stream);
+                    m->qscale[b][k] = sc;
+                } else {
+                    /* a pointwise weight is [out channels, 1024]: W_COLS x W_K */
+                    st = W_SPLIT[k] == 1 ? pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream)
+                                         : pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
+                }
                 if (st) return st;
                 m->stack[b][k] = p;
-                p += 2 * 3 * W_ELEMS[k];
+                p += (q ? 2 : 6) * W_ELEMS[k];
             }
             src += W_ELEMS[k];
         }
     }
     return PKCU_OK;
-}
-
-static long long block_elems(void)
-{
-    long long n = 0;
-    for (int k = 0; k < W_N; k++) n += W_ELEMS[k];
-    return n;
 }
 
 int pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_encoder_model **out)
@@ -178,7 +216,7 @@ int pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_
             return st;
         }
     }
-    st = build_stacks(m, per, stream);
+    st = build_stacks(m, w, per, stream);
     if (st) {
         pkcu_encoder_model_destroy(m);
         return st;
@@ -320,11 +358,50 @@ static int pw_split(pkcu_encoder_model *m, cublasHandle_t h, int Mo, int T, int 
     return pk_depad_rows(Cp, C, (long long)items * Mo, T, Tp, stream);
 }
 
-/* The block's row-major projection: split operands when the model has the
- * weight's part stack, the fp32 tensor-core GEMM otherwise. */
+/* C[M, N] = A[M, K] (s Q[K, N]) for an int8 weight w = s q: q is exact in
+ * bf16, so the product needs only the activation's three parts, a band each
+ * (smallest first, a0 in K chunks), every GEMM scaled by s through alpha:
+ *   C = s a2 q;  C += s a1 q;  C += s a0 q (in K chunks) */
+static int proj_q(pkcu_encoder_model *m, cublasHandle_t h, int M, int N, int K, const float *A, const void *Q,
+                  float s, float *C, pkcu_stream_t stream)
+{
+    if ((size_t)M * 3 * K * 2 > m->split_cap)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: split workspace too small");
+    int st = pk_split_rows_bf16x3(A, m->split_ws, M, K, stream);
+    if (st) return st;
+    const uint16_t *Qp = (const uint16_t *)Q;   /* bf16 elements */
+    const uint16_t *Ap = (const uint16_t *)m->split_ws;
+    static const float one = 1.0f, zero = 0.0f;
+    enum { SPLIT_CHUNK = 512 };
+    struct { int k; long long acol, qrow; const float *beta; } part[2 + PK_FF / SPLIT_CHUNK];
+    int np = 0;
+    part[np].k = K; part[np].acol = 2LL * K; part[np].qrow = 0; part[np++].beta = &zero;
+    part[np].k = K; part[np].acol = K; part[np].qrow = 0; part[np++].beta = &one;
+    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
+        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
+        part[np].acol = k0;
+        part[np].qrow = k0;
+        part[np++].beta = &one;
+    }
+    for (int i = 0; i < np; i++) {
+        const cublasStatus_t cs = cublasGemmEx(
+            h, CUBLAS_OP_N, CUBLAS_OP_N, N, M, part[i].k, &s, Qp + part[i].qrow * N, CUDA_R_16BF, N,
+            Ap + part[i].acol, CUDA_R_16BF, 3 * K, part[i].beta, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
+            CUBLAS_GEMM_DEFAULT);
+        if (cs != CUBLAS_STATUS_SUCCESS)
+            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
+    }
+    return PKCU_OK;
+}
+
+/* The block's row-major projection: on the int8 weight directly, else on split
+ * operands when the model has the weight's part stack, else the fp32
+ * tensor-core GEMM. */
 static int proj_w(pkcu_encoder_model *m, cublasHandle_t h, int b, int k, int M, const float *A, float *C,
                   pkcu_stream_t stream)
 {
+    if (m->stack[b][k] && m->qscale[b][k] > 0.f)
+        return proj_q(m, h, M, W_COLS[k], W_K[k], A, m->stack[b][k], m->qscale[b][k], C, stream);
     if (m->stack[b][k]) return proj_split(m, h, M, W_COLS[k], W_K[k], A, m->stack[b][k], C, stream);
     return proj(h, M, W_COLS[k], W_K[k], A, m->w[b][k], C, stream);
 }

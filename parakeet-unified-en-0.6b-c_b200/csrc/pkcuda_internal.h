@@ -71,6 +71,8 @@ int pk_split_stack_bf16x3(const float *W, void *S, int K, int N, pkcu_stream_t s
 int pk_split_cols_bf16x3(const float *X, void *out, long long items, int K, int T, int Tp,
                          pkcu_stream_t stream);
 int pk_depad_rows(const float *src, float *dst, long long rows, int T, int Tp, pkcu_stream_t stream);
+/* int8 -> bf16, exact (an int8 weight's single part). */
+int pk_i8_to_bf16(const int8_t *q, void *out, long long n, pkcu_stream_t stream);
 
 #ifdef __cplusplus
 }
