@@ -251,16 +251,9 @@ def test_pipeline_matches_reference_engine(cuda, model, tmp_path):
     assert len(tok) == len(tok_ref) and (tok == tok_ref).all(), (len(tok), len(tok_ref))
 
 
-def test_encoder_forward_matches_reference_engine(cuda, model, tmp_path):
-    """The encoder stack through pkcu_encoder_forward -- the library's own GEMMs
-    (cuBLAS fp32) on the fp32 weights pkcu_encoder_model_create made from the
-    uploaded checkpoint -- after pkcu_pre_encode, against the reference's
-    pk_encoder on the same checkpoint and spectrogram."""
-    if not po.ref_full_available():
-        pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
+def _forward(cuda, bp, jp, mel):
+    """pre-encode (torch GEMMs at the hooks) then pkcu_encoder_forward."""
     import torch
-    tensors, bp, jp, mel = model
-    enc_ref, _ = reference_run(bp, jp, mel, tmp_path)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
@@ -277,9 +270,30 @@ def test_encoder_forward_matches_reference_engine(cuda, model, tmp_path):
                 ws.close()
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
-    err = np.abs(enc.astype(np.float64) - enc_ref).max()
-    print(f"pkcu_encoder_forward: max |gpu - reference| = {err:.3e}")
-    assert err <= 5e-5, f"encoder output differs by {err:.3e}"
+    return enc
+
+
+def test_encoder_forward_matches_reference_engine(cuda, model, tmp_path):
+    """The encoder stack through pkcu_encoder_forward -- the library's own
+    fp32-accurate GEMMs on the weights pkcu_encoder_model_create prepared from
+    the uploaded checkpoint -- after pkcu_pre_encode, against the reference's
+    pk_encoder on the same checkpoint and spectrogram. Twice: with the
+    projections stored int8 (used as stored, q exact in bf16) and stored as
+    float32 with the same values (split into three bf16 parts); the reference
+    dequantises both to the same fp32 weights."""
+    if not po.ref_full_available():
+        pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
+    tensors, bp, jp, mel = model
+    enc_ref, _ = reference_run(bp, jp, mel, tmp_path)
+    d = tmp_path / "fp32_ckpt"
+    d.mkdir()
+    _, bp32, jp32 = wf.write_full_checkpoint(str(d), np.random.default_rng(5), enc_gain=1.0,
+                                             blank_bias=0.0, fp32_matrices=True)
+    for what, (b, j) in (("int8 projections", (bp, jp)), ("fp32 projections", (bp32, jp32))):
+        enc = _forward(cuda, b, j, mel)
+        err = np.abs(enc.astype(np.float64) - enc_ref).max()
+        print(f"pkcu_encoder_forward ({what}): max |gpu - reference| = {err:.3e}")
+        assert err <= 5e-5, f"encoder output ({what}) differs by {err:.3e}"
 
 
 def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):

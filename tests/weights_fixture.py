@@ -163,11 +163,14 @@ def _f32(a):
     return {"data": np.ascontiguousarray(a, np.float32), "scale": None, "scales": None}
 
 
-def full_model_tensors(rng, enc_gain: float = 1.0, blank_bias: float = 1.5) -> dict:
+def full_model_tensors(rng, enc_gain: float = 1.0, blank_bias: float = 1.5,
+                       fp32_matrices: bool = False) -> dict:
     """Every tensor pk_load_weights looks up (csrc/weights.c:309-396) for one
     conformer block plus the pre-encode, positional table and decoder:
     attention, feed-forward and pre-encode projections int8 (the reference's
-    int8 manifest), everything else float32. Scales keep activations O(1)."""
+    int8 manifest), everything else float32. Scales keep activations O(1).
+    fp32_matrices: the block's projections stored instead as float32 holding
+    the same values (float32(q) * scale, the reference's dequantisation)."""
     t = {}
     for role, nm in PRE_NAMES.items():
         shape = (256, 1, 3, 3) if role.endswith("_w") else (D if role == "out_b" else 256,)
@@ -192,7 +195,10 @@ def full_model_tensors(rng, enc_gain: float = 1.0, blank_bias: float = 1.5) -> d
     for m in QKV:
         t[f"layers.0.self_attn.linear_{m}.bias"] = _f32(0.1 * rng.standard_normal(D))
     for nm, (K, N) in MATRICES.items():
-        t[f"layers.0.{nm}"] = _int8(rng, K, N)
+        q = _int8(rng, K, N)
+        if fp32_matrices:
+            q = _f32(q["data"].astype(np.float32) * np.float32(q["scale"]))
+        t[f"layers.0.{nm}"] = q
     t["layers.0.conv.pointwise_conv1.weight"] = _f32(rng.standard_normal((2 * D, D, 1)) / 32.0)
     t["layers.0.conv.pointwise_conv2.weight"] = _f32(rng.standard_normal((D, D, 1)) / 32.0)
     Hd, V = 640, 1025
