@@ -77,21 +77,37 @@ __global__ void split_stack_kernel(const float *__restrict__ W, __nv_bfloat16 *_
 
 // items x [K, T] fp32 (channel-first) -> items x [3K, Tp] bf16 = [x2; x1; x0]
 // per item, rows padded to the pitch Tp >= T (the pad columns are left as they
-// are: they only feed output columns that are dropped).
+// are: they only feed output columns that are dropped). A warp per channel row
+// (rows of T floats are not 16-byte aligned): lane-strided, coalesced loads and
+// stores, four in flight.
 __global__ void split_cols_kernel(const float *__restrict__ X, __nv_bfloat16 *__restrict__ out, long long items,
                                   int K, int T, int Tp) {
-  const long long per = (long long)K * T, per_out = (long long)K * Tp;
-  const long long n = items * per;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long it = e / per, r = e - it * per;
-    const long long k = r / T, t = r - k * T;
-    __nv_bfloat16 p0, p1, p2;
-    split3(__ldg(X + e), p0, p1, p2);
-    __nv_bfloat16 *o = out + it * 3 * per_out + k * Tp + t;
-    o[0] = p2;
-    o[per_out] = p1;
-    o[2 * per_out] = p0;
+  const int lane = threadIdx.x & 31;
+  const long long rows = items * K, part = (long long)K * Tp;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    const long long it = r / K, k = r - it * K;
+    const float *src = X + r * T;
+    __nv_bfloat16 *o = out + it * 3 * part + k * Tp;
+    for (int t0 = 0; t0 < T; t0 += 128) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + 32 * u + lane;
+        x[u] = t < T ? __ldg(src + t) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + 32 * u + lane;
+        if (t < T) {
+          __nv_bfloat16 p0, p1, p2;
+          split3(x[u], p0, p1, p2);
+          o[t] = p2;
+          o[part + t] = p1;
+          o[2 * part + t] = p0;
+        }
+      }
+    }
   }
 }
 
@@ -102,14 +118,28 @@ __global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *_
     out[e] = __float2bfloat16_rn((float)q[e]);
 }
 
-// rows x [Tp] -> rows x [T]: drops the pad columns.
+// rows x [Tp] -> rows x [T]: drops the pad columns; a warp per row, four
+// accesses in flight per lane.
 __global__ void depad_kernel(const float *__restrict__ src, float *__restrict__ dst, long long rows, int T,
                              int Tp) {
-  const long long n = rows * T;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long r = e / T, t = e - r * T;
-    dst[e] = __ldg(src + r * Tp + t);
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    const float *s = src + r * Tp;
+    float *d = dst + r * T;
+    for (int t0 = 0; t0 < T; t0 += 128) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + 32 * u + lane;
+        v[u] = t < T ? __ldg(s + t) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int t = t0 + 32 * u + lane;
+        if (t < T) d[t] = v[u];
+      }
+    }
   }
 }
 
@@ -144,14 +174,14 @@ extern "C" int pk_split_cols_bf16x3(const float *X, void *out, long long items, 
                                     pkcu_stream_t stream) {
   if (!X || !out || items <= 0 || K <= 0 || T <= 0 || Tp < T)
     return pkcu_fail(PKCU_ERR_ARG, "pk_split_cols_bf16x3: bad argument");
-  split_cols_kernel<<<split_grid(items * K * (long long)T), 256, 0, (cudaStream_t)stream>>>(
+  split_cols_kernel<<<split_grid(items * K * 32), 256, 0, (cudaStream_t)stream>>>(
       X, static_cast<__nv_bfloat16 *>(out), items, K, T, Tp);
   return pkcu_launch_status("pk_split_cols_bf16x3");
 }
 
 extern "C" int pk_depad_rows(const float *src, float *dst, long long rows, int T, int Tp, pkcu_stream_t stream) {
   if (!src || !dst || rows <= 0 || T <= 0 || Tp < T) return pkcu_fail(PKCU_ERR_ARG, "pk_depad_rows: bad argument");
-  depad_kernel<<<split_grid(rows * T), 256, 0, (cudaStream_t)stream>>>(src, dst, rows, T, Tp);
+  depad_kernel<<<split_grid(rows * 32), 256, 0, (cudaStream_t)stream>>>(src, dst, rows, T, Tp);
   return pkcu_launch_status("pk_depad_rows");
 }
 
