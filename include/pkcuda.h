@@ -513,9 +513,10 @@ int  pkcu_greedy_decode(pkcu_decoder *dec, const pkcu_dec_params *params, pkcu_g
  * CUDA graph of 8 iterations: the hook must be capture-safe (only stream-
  * ordered work on the stream it is given, e.g. cuBLAS calls, no synchronisation
  * or allocation) and its work must not depend on the iteration. It is called
- * 8 times per product while the graph is captured, and again only when the
- * hook, its user pointer or the parameter pointers change; DEC_ENC is called
- * once per decode outside the graph. */
+ * 8 times per product for each of the decoder's two graphs while they are
+ * captured (the host launches one while it reads the other's live count), and
+ * again only when the hook, its user pointer or the parameter pointers change;
+ * DEC_ENC is called once per decode outside the graphs. */
 int  pkcu_greedy_decode_graph(pkcu_decoder *dec, const pkcu_dec_params *params,
                               pkcu_gemm_hook hook, void *hook_user, pkcu_stream_t stream);
 /* The decode with its own products: the decoder's weights in the reference's

@@ -598,7 +598,7 @@ struct pkcu_decoder {
   float *x0, *hidden;      // [B, 640]
   float *encp, *pred, *out, *g0i, *g0r, *g1i, *g1r;
   int *tokens;             // [10 F]: utterance b's tokens from 10 * frame_off(b)
-  int *live_host;          // page-locked poll target
+  int *live_host;          // page-locked poll targets, one per graph
   int iterations;          // of the last decode
   int device;
   // Without a hook (or with a capture-safe one, pkcu_greedy_decode_graph),
@@ -606,8 +606,8 @@ struct pkcu_decoder {
   // for the parameter pointers in `gp` and the hook in `ghook` / `guser`, and
   // replayed.
   cudaStream_t gs;
-  cudaEvent_t ev_in, ev_out;
-  cudaGraphExec_t graph;
+  cudaEvent_t ev_in, ev_out, ev_done[2];
+  cudaGraphExec_t graph[2];   // the same iterations; each copies the live count to its own slot
   pkcu_dec_params gp;
   pkcu_gemm_hook ghook;
   void *guser;
@@ -622,7 +622,10 @@ struct pkcu_decoder {
 
 extern "C" void pkcu_decoder_destroy(pkcu_decoder *d) {
   if (!d) return;
-  if (d->graph) cudaGraphExecDestroy(d->graph);
+  for (int c = 0; c < 2; c++) {
+    if (d->graph[c]) cudaGraphExecDestroy(d->graph[c]);
+    if (d->ev_done[c]) cudaEventDestroy(d->ev_done[c]);
+  }
   if (d->ev_in) cudaEventDestroy(d->ev_in);
   if (d->ev_out) cudaEventDestroy(d->ev_out);
   if (d->gs) cudaStreamDestroy(d->gs);
@@ -664,7 +667,7 @@ extern "C" int pkcu_decoder_create(const int *frames, int n_utts, pkcu_decoder *
     pkcu_decoder_destroy(d);
     return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_decoder_create: device allocation of %zu bytes", total);
   }
-  if (cudaMallocHost(&d->live_host, sizeof(int)) != cudaSuccess) {
+  if (cudaMallocHost(&d->live_host, 2 * sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
     d->live_host = nullptr;
     pkcu_decoder_destroy(d);
@@ -788,7 +791,8 @@ static int dec_iteration_fused(pkcu_decoder *d, const pkcu_dec_params *prm, cuda
 }
 
 // Captures DEC_POLL iterations (hook form, with the hook's GEMMs if any, or
-// the fused form) + the copy of the live count into d->graph.
+// the fused form) + the copy of the live count, twice: graph[c] copies into
+// live_host[c], so the host can read one batch's count while the next runs.
 static int g_dec_flags[3][64];
 
 static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
@@ -798,30 +802,35 @@ static int dec_capture(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_ho
     smem_optin(dec_pred_joint_kernel, DEC_ROW_SMEM, g_dec_flags[1]);
     smem_optin(dec_out_kernel, DEC_ROW_SMEM, g_dec_flags[2]);
   }
-  if (d->graph) {
-    cudaGraphExecDestroy(d->graph);
-    d->graph = nullptr;
-  }
+  for (int c = 0; c < 2; c++)
+    if (d->graph[c]) {
+      cudaGraphExecDestroy(d->graph[c]);
+      d->graph[c] = nullptr;
+    }
   if (!d->gs && (cudaStreamCreateWithFlags(&d->gs, cudaStreamNonBlocking) != cudaSuccess ||
                  cudaEventCreateWithFlags(&d->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-                 cudaEventCreateWithFlags(&d->ev_out, cudaEventDisableTiming) != cudaSuccess))
+                 cudaEventCreateWithFlags(&d->ev_out, cudaEventDisableTiming) != cudaSuccess ||
+                 cudaEventCreateWithFlags(&d->ev_done[0], cudaEventDisableTiming) != cudaSuccess ||
+                 cudaEventCreateWithFlags(&d->ev_done[1], cudaEventDisableTiming) != cudaSuccess))
     return pkcu_launch_status("pkcu_greedy_decode: graph stream");
-  if (cudaStreamBeginCapture(d->gs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-    return pkcu_launch_status("pkcu_greedy_decode: begin capture");
   int st = PKCU_OK;
-  for (int i = 0; i < DEC_POLL && !st; i++)
-    st = fused ? dec_iteration_fused(d, prm, d->gs) : dec_iteration(d, prm, hook, hook_user, d->gs);
-  if (!st && cudaMemcpyAsync(d->live_host, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, d->gs) !=
-                 cudaSuccess)
-    st = pkcu_launch_status("pkcu_greedy_decode: capture poll copy");
-  cudaGraph_t g = nullptr;
-  const cudaError_t ce = cudaStreamEndCapture(d->gs, &g);
-  if (!st && ce != cudaSuccess) st = pkcu_launch_status("pkcu_greedy_decode: end capture");
-  if (!st && cudaGraphInstantiate(&d->graph, g, 0) != cudaSuccess) {
-    d->graph = nullptr;
-    st = pkcu_launch_status("pkcu_greedy_decode: instantiate");
+  for (int c = 0; c < 2 && !st; c++) {
+    if (cudaStreamBeginCapture(d->gs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+      return pkcu_launch_status("pkcu_greedy_decode: begin capture");
+    for (int i = 0; i < DEC_POLL && !st; i++)
+      st = fused ? dec_iteration_fused(d, prm, d->gs) : dec_iteration(d, prm, hook, hook_user, d->gs);
+    if (!st && cudaMemcpyAsync(d->live_host + c, d->st.live, sizeof(int), cudaMemcpyDeviceToHost, d->gs) !=
+                   cudaSuccess)
+      st = pkcu_launch_status("pkcu_greedy_decode: capture poll copy");
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(d->gs, &g);
+    if (!st && ce != cudaSuccess) st = pkcu_launch_status("pkcu_greedy_decode: end capture");
+    if (!st && cudaGraphInstantiate(&d->graph[c], g, 0) != cudaSuccess) {
+      d->graph[c] = nullptr;
+      st = pkcu_launch_status("pkcu_greedy_decode: instantiate");
+    }
+    if (g) cudaGraphDestroy(g);
   }
-  if (g) cudaGraphDestroy(g);
   if (!st) {
     d->gp = *prm;
     d->ghook = hook;
@@ -861,23 +870,33 @@ static int dec_start(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook
   return st;
 }
 
-// Replays the captured DEC_POLL-iteration graph on d->gs until no utterance
-// is live, joined to the caller's stream on both sides.
+// Replays the captured DEC_POLL-iteration graphs on d->gs until no utterance
+// is live, joined to the caller's stream on both sides. The host keeps one
+// batch ahead: batch k + 1 is launched before batch k's live count is read, so
+// the GPU never waits for the host's check. When batch k's count is zero the
+// batch already launched after it does nothing (finished rows are skipped by
+// every kernel); the iterations reported end with batch k, as without it.
 static int dec_replay(pkcu_decoder *d, const pkcu_dec_params *prm, pkcu_gemm_hook hook,
                       void *hook_user, int fused, cudaStream_t s) {
   int st = PKCU_OK;
-  if (!d->graph || !same_params(d->gp, *prm) || d->ghook != hook || d->guser != hook_user ||
-      d->gfused != fused || (fused && d->gwgen != d->wgen))
+  if (!d->graph[0] || !d->graph[1] || !same_params(d->gp, *prm) || d->ghook != hook ||
+      d->guser != hook_user || d->gfused != fused || (fused && d->gwgen != d->wgen))
     st = dec_capture(d, prm, hook, hook_user, fused);
   if (st) return st;
   if (cudaEventRecord(d->ev_in, s) != cudaSuccess || cudaStreamWaitEvent(d->gs, d->ev_in, 0) != cudaSuccess)
     return pkcu_launch_status("pkcu_greedy_decode: join");
   const long long max_iters = max_iterations(d);
-  for (long long it = 0; it < max_iters; it += DEC_POLL) {
-    if (cudaGraphLaunch(d->graph, d->gs) != cudaSuccess || cudaStreamSynchronize(d->gs) != cudaSuccess)
+  if (cudaGraphLaunch(d->graph[0], d->gs) != cudaSuccess || cudaEventRecord(d->ev_done[0], d->gs) != cudaSuccess)
+    return pkcu_launch_status("pkcu_greedy_decode: graph");
+  for (long long k = 0;; k++) {
+    const int cur = (int)(k & 1), next = cur ^ 1;
+    if ((k + 1) * DEC_POLL < max_iters &&
+        (cudaGraphLaunch(d->graph[next], d->gs) != cudaSuccess ||
+         cudaEventRecord(d->ev_done[next], d->gs) != cudaSuccess))
       return pkcu_launch_status("pkcu_greedy_decode: graph");
-    d->iterations += DEC_POLL;
-    if (*d->live_host == 0) break;
+    if (cudaEventSynchronize(d->ev_done[cur]) != cudaSuccess) return pkcu_launch_status("pkcu_greedy_decode: graph");
+    d->iterations = (int)((k + 1) * DEC_POLL);
+    if (d->live_host[cur] == 0 || (k + 1) * DEC_POLL >= max_iters) break;
   }
   if (cudaEventRecord(d->ev_out, d->gs) != cudaSuccess || cudaStreamWaitEvent(s, d->ev_out, 0) != cudaSuccess)
     return pkcu_launch_status("pkcu_greedy_decode: join");

@@ -172,10 +172,10 @@ def test_decode_graph_no_hook(cuda):
 
 def test_decode_graph_with_hook(cuda):
     """pkcu_greedy_decode_graph: the hook's products are captured into the
-    8-iteration graph (here device-to-device copies of one fixed row per
-    utterance, as in the test above); the hook is called 8 times per product
-    while capturing and, on the second decode with the same hook, only for
-    DEC_ENC."""
+    decoder's two 8-iteration graphs (here device-to-device copies of one fixed
+    row per utterance, as in the test above); the hook is called 8 times per
+    product for each graph while capturing and, on the second decode with the
+    same hook, only for DEC_ENC."""
     import torch
     frames = [4, 9, 2, 6]
     emits = [False, True, True, False]
@@ -220,7 +220,7 @@ def test_decode_graph_with_hook(cuda):
             calls.clear()
             dec.decode(dp, hook=fn, graph=True)
             n_tok, evals, tokens = dec.results()
-            want_calls = 1 + (6 * 8 if rep == 0 else 0)
+            want_calls = 1 + (6 * 16 if rep == 0 else 0)   # 8 iterations x 2 graphs
             assert len(calls) == want_calls and calls[0] == "enc", (rep, len(calls))
             need = max(10 * T + 1 if em else T for T, em in zip(frames, emits))
             assert dec.iterations % 8 == 0 and need <= dec.iterations < need + 8
