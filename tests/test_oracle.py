@@ -296,3 +296,27 @@ def test_split3_bf16_properties():
     bound = np.abs(a).astype(np.float64) @ np.abs(w).astype(np.float64)
     err = np.abs(po.split_band_product(a, w) - exact) / bound
     assert err.max() < 2.0 ** -22, err.max()
+
+
+def test_decode_restatement_matches_reference_with_weight_products():
+    """The greedy-decode restatement against the reference's own
+    pk_greedy_decode, both fed every product computed in float64 from the same
+    seeded decoder weights (the oracle the fused decode is checked against):
+    tokens and joint evaluations identical, on utterances that mix blanks,
+    emissions and the 10-symbol cap."""
+    if not po.ref_dec_available():
+        pytest.skip("oracle/_ref/libpkref_dec.so not built (reference tree absent)")
+    rng = np.random.default_rng(91)
+    params = po.random_dec_params(rng)
+    weights = po.random_dec_weights(rng)
+    seen = set()
+    for shift, T in ((3.5, 17), (3.5, 1), (0.0, 6), (8.0, 9)):
+        p = dict(params)
+        p["out_b"] = params["out_b"].copy()
+        p["out_b"][po.DEC_BLANK] += shift
+        enc = rng.standard_normal((T, po.DEC_H)).astype(np.float32)
+        tok_o, it_o, _ = po.oracle_greedy_decode(T, p, po.WeightProducts(weights, enc, p["out_b"]))
+        tok_r, it_r = po.reference_greedy_decode(T, p, po.WeightProducts(weights, enc, p["out_b"]))
+        assert it_o == it_r and len(tok_o) == len(tok_r) and (tok_o == tok_r).all(), (shift, T)
+        seen.add("cap" if len(tok_o) == 10 * T else "none" if len(tok_o) == 0 else "mixed")
+    assert seen == {"cap", "none", "mixed"}, seen
