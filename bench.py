@@ -601,15 +601,18 @@ def time_decode_fused(stream, reps, n_utts=256, T=40, blank_shift=0.0):
     import numpy as np
     import torch
     import pkcuda
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import pyoracle as po
     rng = np.random.default_rng(5)
-    params = po.random_dec_params(rng)
-    params["out_b"][po.DEC_BLANK] += blank_shift
-    w = {k: torch.from_numpy(v).cuda() for k, v in po.random_dec_weights(rng).items()}
-    dp = {"embed": params["embed"], "lstm0_b": params["B0"], "lstm1_b": params["B1"],
-          "joint_enc_b": params["enc_b"], "joint_pred_b": params["pred_b"], "joint_out_b": params["out_b"]}
-    dp = {k: torch.from_numpy(v).cuda() for k, v in dp.items()}
+    Hd, V = 640, 1025
+    g = lambda *shape, sd=1.0: torch.from_numpy((sd * rng.standard_normal(shape)).astype(np.float32)).cuda()
+    # decoder parameters and weights in the reference's layouts (embedding
+    # [1025, 640], LSTM biases [5120], joint biases; W_i / W_r [2560, 640],
+    # joint.pred [640, 640], joint.out [640, 1025] as (in, out))
+    dp = {"embed": g(V, Hd, sd=0.5), "lstm0_b": g(8 * Hd, sd=0.1), "lstm1_b": g(8 * Hd, sd=0.1),
+          "joint_enc_b": g(Hd, sd=0.1), "joint_pred_b": g(Hd, sd=0.1), "joint_out_b": g(V, sd=0.1)}
+    dp["joint_out_b"][V - 1] += blank_shift   # the blank token's bias
+    s = 1.0 / np.sqrt(Hd)
+    w = {"lstm0_wi": g(4 * Hd, Hd, sd=s), "lstm0_wr": g(4 * Hd, Hd, sd=s), "lstm1_wi": g(4 * Hd, Hd, sd=s),
+         "lstm1_wr": g(4 * Hd, Hd, sd=s), "joint_pred": g(Hd, Hd, sd=s), "joint_out": g(Hd, V, sd=s)}
     with pkcuda.Decoder([T] * n_utts) as dec:
         enc = torch.as_tensor(_DevView(dec.gemm_out["enc"], n_utts * T * 640), device="cuda")
         enc.copy_(torch.randn(n_utts * T * 640, generator=torch.Generator(device="cuda").manual_seed(7),
