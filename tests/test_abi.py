@@ -167,3 +167,14 @@ def test_fused_decode_argument_checks():
     tok = (C.c_int * 80)()
     cnt = (C.c_int * 1)()
     assert L.pkcu_asr_decode(None, None, frames, 1, tok, cnt, None) == ERR_ARG
+
+
+def test_asr_encoder_frames_follow_the_pre_encode_convolutions():
+    """pkcu_asr_encoder_frames (host arithmetic, no GPU) gives the frame count of
+    the restatement's three stride-2 convolutions (kernel 3, padding 1) for
+    every length up to 5000 mel frames."""
+    import pkcuda
+    import pyoracle as po
+    L = pkcuda.lib()
+    for T in range(1, 5001):
+        assert L.pkcu_asr_encoder_frames(T) == po.pre_dims(T)["H3"], T
