@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <mutex>
 #include <stdint.h>
 
 #include "pkcuda_internal.h"
@@ -419,13 +420,24 @@ __device__ __forceinline__ void span_issue(float *dst, const float *src, const S
 
 // Raises a kernel's dynamic shared-memory limit once per device (the first
 // launch on each device; later launches, including ones under stream
-// capture, make no attribute call). `flags` is a per-kernel static array.
+// capture, make no attribute call). `flags` is a per-kernel static array of
+// the size raised so far per device: read atomically on the fast path, raised
+// under one process-wide lock so that concurrent first calls from several
+// host threads never leave a smaller limit recorded than set.
+inline std::mutex &smem_optin_lock() {
+  static std::mutex m;
+  return m;
+}
 template <typename K>
 inline void smem_optin(K kernel, size_t bytes, int *flags) {
   const int dev = pkcu_device();
+  if (dev < 64 && __atomic_load_n(&flags[dev], __ATOMIC_ACQUIRE) >= (int)bytes) return;
+  std::lock_guard<std::mutex> lock(smem_optin_lock());
   if (dev < 64 && flags[dev] >= (int)bytes) return;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (dev < 64) flags[dev] = (int)bytes;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+      cudaSuccess)
+    return;   // the launch that follows reports the error
+  if (dev < 64) __atomic_store_n(&flags[dev], (int)bytes, __ATOMIC_RELEASE);
 }
 
 }  // namespace pk

@@ -246,5 +246,6 @@ int pkcu_encoder_nongemm_host(pkcu_encoder_ws *ws, float *x_host, const pkcu_gem
     if (!st && (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess))
         st = pkcu_fail(PKCU_ERR_CUDA, "pkcu_encoder_nongemm_host: %s",
                        cudaGetErrorString(e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3)));
+    if (!st) st = pk_check_wait_timeouts("pkcu_encoder_nongemm_host");
     return st;
 }

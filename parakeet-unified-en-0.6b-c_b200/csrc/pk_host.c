@@ -72,6 +72,19 @@ int pkcu_wait_timeouts(unsigned *count, int reset)
     return PKCU_OK;
 }
 
+int pk_check_wait_timeouts(const char *what)
+{
+    unsigned a = 0, b = 0;
+    if (pk_softmax_wait_timeouts(&a, 1) != PKCU_OK || pk_conv_wait_timeouts(&b, 1) != PKCU_OK) {
+        cudaGetLastError();
+        return pkcu_fail(PKCU_ERR_CUDA, "%s: reading the device wait counters failed", what);
+    }
+    if (a + b)
+        return pkcu_fail(PKCU_ERR_CUDA, "%s: %u bounded device wait(s) ran out; outputs are incomplete",
+                         what, a + b);
+    return PKCU_OK;
+}
+
 int pkcu_sm_count(void)
 {
     int dev = 0;
@@ -270,7 +283,7 @@ static int d2h_sync(void *h, const void *d, size_t bytes, cudaStream_t s)
         return pkcu_fail(PKCU_ERR_CUDA, "device to host copy: %s", cudaGetErrorString(cudaGetLastError()));
     if (cudaStreamSynchronize(s) != cudaSuccess)
         return pkcu_fail(PKCU_ERR_CUDA, "stream synchronize: %s", cudaGetErrorString(cudaGetLastError()));
-    return PKCU_OK;
+    return pk_check_wait_timeouts("drop-in call");
 }
 
 /* Row LayerNorm of n_rows x D host floats: x (and out, possibly == x). */

@@ -52,6 +52,11 @@ int pkcu_device(void);
  * k_conv.cu); read and optionally reset on the current device. */
 int pk_softmax_wait_timeouts(unsigned *count, int reset);
 int pk_conv_wait_timeouts(unsigned *count, int reset);
+/* For synchronous entry points, after their final synchronisation: reads and
+ * resets both counters and returns PKCU_ERR_CUDA (with a message naming what)
+ * when any wait ran out since the last reset, anywhere in the process on this
+ * device. */
+int pk_check_wait_timeouts(const char *what);
 
 #define PK_ALIGNED16(p) ((((uintptr_t)(p)) & 15u) == 0)
 
