@@ -55,6 +55,10 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-aux", action="store_true", help="skip the standalone-kernel table")
+    ap.add_argument("--extras", action="store_true",
+                    help="also time the steps beyond the non-GEMM path (fused GEMMs, encoder "
+                         "with GEMMs, decode, mel-to-tokens) and print them as one JSON line "
+                         "before the bench line")
     ap.add_argument("--aux-only", action="store_true",
                     help="time only the standalone kernels (one JSON object), e.g. for ncu")
     ap.add_argument("--pre-only", action="store_true",
@@ -262,12 +266,17 @@ def reference_arm(args, rank, world):
     value = frames / secs
     sample = (f"{args.steps} steps x 1 utterance x T={args.T} x {args.blocks} blocks through the "
               f"reference's conformer_block with GEMMs as no-ops, PK_THREADS={threads}")
+    config = config_dict(args, world)
+    config["workload"] = (f"config 4 sampled: each step 1 utterance x T={args.T} through the "
+                          f"{args.blocks}-block non-GEMM op sequence (utterances are independent, "
+                          f"so frames/s does not depend on how many run), fp32")
+    config["utterances_per_step"] = 1
     line = {
         "metric": METRIC, "value": value, "unit": "frames/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * secs / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args, world),
+        "config": config,
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -292,25 +301,21 @@ def setup_device(args, rank, world):
     mine = shard(rank, world, args.utts)
     seq = pkcuda.Seq([args.T] * len(mine))
     ws = pkcuda.EncoderWorkspace(seq, args.groups)
-    x_addr, gout, gin = ws.device()
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1234 + mine.start)   # this rank's own utterances
-    F = seq.frames
-    # Fill x and the stand-in GEMM outputs with N(0,1) (views of the workspace).
-    total = ws.device_bytes // 4
-    base = torch.empty(0, device="cuda")
-    del base
-    fills = [(x_addr, F * D)]
-    ext = {"ff1_h": F * FF, "ff1_out": F * D, "qkv": 3 * F * D, "P": seq.pos_rows * D,
-           "ac": seq.score_elems, "bd": seq.bd_elems, "attn_h": F * D, "att_out": F * D,
-           "pw1": 2 * F * D, "pw2": F * D, "ff2_h": F * FF, "ff2_out": F * D}
-    for f in pkcuda.GEMM_OUT_FIELDS:
-        fills.append((getattr(gout, f), ext[f]))
-    for addr, n in fills:
-        t = tensor_at(addr, n)
-        t.normal_(generator=gen)
+    x_addr, gout, gin = fill_workspace(ws, seq, gen)
+    blocks = random_block_params(args.blocks, gen)
+    arr = pkcuda.block_params_array(blocks)
+    return seq, ws, x_addr, gout, gin, blocks, arr
+
+
+def random_block_params(n_blocks, gen):
+    """Device block parameters: LN gamma ~ N(1, 0.1), depthwise taps 0.3 N(0,1),
+    the rest 0.1 N(0,1)."""
+    import torch
+    import pkcuda
     blocks = []
-    for _ in range(args.blocks):
+    for _ in range(n_blocks):
         p = {}
         for f in pkcuda.BLOCK_PARAM_FIELDS:
             n = {"ff1_b1": FF, "ff2_b1": FF, "qkv_b": 3 * D, "pw1_b": 2 * D, "dw_w": 9 * D,
@@ -324,9 +329,136 @@ def setup_device(args, rank, world):
                 t = 0.1 * t
             p[f] = t.contiguous()
         blocks.append(p)
-    arr = pkcuda.block_params_array(blocks)
-    del total
-    return seq, ws, x_addr, gout, gin, blocks, arr
+    return blocks
+
+
+def fill_workspace(ws, seq, gen):
+    """N(0,1) in x and every stand-in GEMM output of a workspace."""
+    import pkcuda
+    x_addr, gout, gin = ws.device()
+    F = seq.frames
+    ext = {"ff1_h": F * FF, "ff1_out": F * D, "qkv": 3 * F * D, "P": seq.pos_rows * D,
+           "ac": seq.score_elems, "bd": seq.bd_elems, "attn_h": F * D, "att_out": F * D,
+           "pw1": 2 * F * D, "pw2": F * D, "ff2_h": F * FF, "ff2_out": F * D}
+    tensor_at(x_addr, F * D).normal_(generator=gen)
+    for f in pkcuda.GEMM_OUT_FIELDS:
+        tensor_at(getattr(gout, f), ext[f]).normal_(generator=gen)
+    return x_addr, gout, gin
+
+
+CONFIG3_LENGTHS = [408] + [416] * 6 + [408]
+
+
+def ragged_step_bytes(lengths, n_blocks):
+    """Algorithmic bytes of the sequence over a ragged batch: every term of
+    step_bytes is a sum over items, so the batch total is the items' sum."""
+    return sum(step_bytes(T, T, 1, n_blocks) for T in lengths)
+
+
+def time_config3(args, stream, reps=10):
+    """BASELINE config 3 as configured: 3200 frames of long audio as 8 chunks
+    of 400 frames plus 8-frame overlaps (edge chunks 408 frames, interior ones
+    416, csrc/encoder.c:531-543), one ragged batch through the 24-block
+    sequence; GEMM outputs are N(0,1) stand-ins (about 375 MB, above the L2).
+    CUDA-graph replays timed with CUDA events on the bench stream."""
+    import torch
+    import pkcuda
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3200)
+    seq = pkcuda.Seq(CONFIG3_LENGTHS)
+    ws = pkcuda.EncoderWorkspace(seq, 1)
+    try:
+        x_addr, gout, gin = fill_workspace(ws, seq, gen)
+        blocks = random_block_params(args.blocks, gen)
+        arr = pkcuda.block_params_array(blocks)
+
+        def step():
+            pkcuda.call("pkcu_encoder_nongemm", x_addr, C.cast(arr, pkcuda.VP), args.blocks,
+                        C.byref(gout), C.byref(gin), seq.handle, None, None, stream.cuda_stream)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        del graph
+    finally:
+        ws.close()
+        seq.close()
+    frames = sum(CONFIG3_LENGTHS)
+    nb = ragged_step_bytes(CONFIG3_LENGTHS, args.blocks)
+    return {"chunks": "408,416x6,408", "frames": frames, "ms": round(ms, 4),
+            "frames_per_s": round(frames / (ms * 1e-3)), "gbs": round(nb / (ms * 1e-3) / 1e9, 1)}
+
+
+def time_config5(stream, reps=20):
+    """BASELINE config 5 as configured, each op timed launch by launch with an
+    L2 flush (a 512 MB device write) between launches, since these sizes fit
+    in the 126 MB L2: GPTQ int4 dequant of FF1 [1024, 4096] and FF2
+    [4096, 1024] with G = 128 along K; int8 dequant of the fused QKV
+    [1024, 3072] and out-proj [1024, 1024] weights; the RNN-T joint add + tanh
+    at B = 32 x T = 416 x J = 640 and the argmax over [13312, 1025] logits.
+    Algorithmic bytes as in kernel_table's notes (each input read once, each
+    output written once)."""
+    import torch
+    import pkcuda
+    sh = stream.cuda_stream
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    f32 = dict(device=dev, dtype=torch.float32)
+    flush = torch.empty(128 << 20, **f32)
+    out = {}
+
+    def timed(name, nbytes, fn):
+        fn()
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        ms = total / reps
+        out[name] = {"us": round(1000 * ms, 2), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+
+    G = 128
+    for tag, K, N in (("dequant_i4_ff1_g128_k", 1024, 4096), ("dequant_i4_ff2_g128_k", 4096, 1024)):
+        pk = torch.randint(0, 256, (K * N // 2,), generator=g, device=dev, dtype=torch.uint8)
+        sc = 1e-3 + 1.9e-2 * torch.rand(K * N // G, generator=g, **f32)
+        o = torch.empty(K * N, **f32)
+        timed(tag, K * N // 2 + 4 * K * N // G + 4 * K * N,
+              lambda: pkcuda.call("pkcu_dequant_i4", pk.data_ptr(), sc.data_ptr(), o.data_ptr(), K, N, G,
+                                  pkcuda.PKCU_GROUP_ALONG_K, sh))
+    for tag, n in (("dequant_i8_qkv", 1024 * 3072), ("dequant_i8_out", 1024 * 1024)):
+        q = torch.randint(-127, 128, (n,), generator=g, device=dev, dtype=torch.int8)
+        o = torch.empty(n, **f32)
+        timed(tag, 5 * n, lambda: pkcuda.call("pkcu_dequant_i8", q.data_ptr(), 5e-3, o.data_ptr(), n, sh))
+    B, T, J, V = 32, 416, 640, 1025
+    enc = torch.randn(B * T * J, generator=g, **f32)
+    pred = torch.randn(B * J, generator=g, **f32)
+    jo = torch.empty_like(enc)
+    timed("joint_add_tanh", 8 * B * T * J + 4 * B * J,
+          lambda: pkcuda.call("pkcu_joint_add_act", enc.data_ptr(), pred.data_ptr(), jo.data_ptr(),
+                              B, T, J, pkcuda.PKCU_ACT_TANH, sh))
+    logits = torch.randn(B * T * V, generator=g, **f32)
+    am = torch.empty(B * T, device=dev, dtype=torch.int32)
+    timed("argmax_rows", 4 * B * T * V + 4 * B * T,
+          lambda: pkcuda.call("pkcu_argmax_rows", logits.data_ptr(), am.data_ptr(), B * T, V, sh))
+    torch.cuda.synchronize()
+    return out
 
 
 def tensor_at(addr, n):
@@ -1128,27 +1260,13 @@ def _ours(args, rank, world, local_rank, stream):
 
     used_graph = graph is not None
     del graph
-    aux = decode = gemms = forward = asr = asr_dec = dec_fused = None
+    aux = cfg3 = cfg5 = None
     if rank == 0 and not args.no_aux:
         aux = time_aux_kernels(stream)
-        decode = time_decode(stream, 3)
-        gemms = time_fused_gemms(stream, 3)
-        forward = time_encoder_forward(stream, 2)
-        asr = time_asr(stream, 1)
-        # the same with a blank bias that makes every evaluation blank: the
-        # decode's lightest case (the synthetic model's outputs flip between
-        # the two extremes; a trained model lies between them)
-        asr["every_frame_blank"] = {k: v for k, v in time_asr(stream, 1, blank_bias=6.0).items()
-                                    if k in ("blank_bias", "seconds_per_call", "utterances_per_s",
-                                             "audio_seconds_per_s", "tokens_per_frame")}
-        asr_dec = time_asr_decode(stream, 2, cpu=world == 1 and not args.no_cpu_baseline)
-        dec_fused = {"10_tokens_every_frame": time_decode_fused(stream, 2, 256, 40, 0.0),
-                     "sparse_decoder_steps": time_decode_fused(stream, 2, 256, 200, 3.5)}
-        if world == 1 and not args.no_cpu_baseline:
-            forward["cpu_baseline"] = cpu_encoder_baseline()
-            asr["cpu_baseline"] = cpu_asr_baseline()
-        if world == 1 and not args.no_cpu_baseline:
-            decode["cpu_baseline"] = cpu_decode_baseline()
+        cfg3 = time_config3(args, stream)
+        cfg5 = time_config5(stream)
+    if rank == 0 and args.extras:
+        print(json.dumps({"extras": run_extras(args, stream, world)}), flush=True)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = RefRunner(args.T, args.blocks)
@@ -1163,38 +1281,57 @@ def _ours(args, rank, world, local_rank, stream):
     dom = max(table, key=lambda k: table[k]["ms"] * table[k]["launches_per_step"])
     d = table[dom]
     traffic = ncu_traffic(dom)
+    fr = lambda gbs: round(gbs / peak, 3)
     line = {
         "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) GEMM outputs and inputs, random block parameters)",
         "config": config_dict(args, world),
-        "hbm": {"algorithmic_bytes_per_step": bytes_step, "achieved_gbs_per_gpu": hbm_gbs,
-                "peak_gbs": peak, "frac": hbm_gbs / peak, "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
-                     "unit": "GB/s", "frac": d["gbs"] / peak, "traffic": traffic,
-                     "peak_kind": peak_kind},
-        "kernels": {k: {"ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
-                        "frac": round(v["gbs"] / peak, 3), "launches_per_step": v["launches_per_step"]}
-                    for k, v in table.items()},
-        "kernels_aux": None if aux is None else {
-            k: {"shape": v["shape"], "ms": round(v["ms"], 4), "gbs": round(v["gbs"], 1),
-                "frac": round(v["gbs"] / peak, 3),
-                **({"frames_per_s": round(v["frames_per_s"])} if "frames_per_s" in v else {})}
-            for k, v in aux.items()},
-        "decode": decode,
-        "fused_gemms": gemms,
-        "encoder_forward": forward,
-        "asr": asr,
-        "asr_decode": asr_dec,
-        "decode_fused": dec_fused,
         "gpu_launches": pkcuda.lib().pkcu_encoder_nongemm_launches(args.blocks) * args.steps,
         "graph": used_graph,
         "clocks": clocks,
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "hbm": {"bytes_per_step": bytes_step, "gbs": round(hbm_gbs, 1), "frac": round(hbm_gbs / peak, 3)},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": d["gbs"] / peak, "traffic": traffic,
+                     "peak_kind": peak_kind},
     }
+    if cfg3 is not None:
+        line["config3"] = {**cfg3, "frac": fr(cfg3["gbs"])}
+    if cfg5 is not None:
+        line["config5_frac"] = {k: fr(v["gbs"]) for k, v in cfg5.items()}
+        line["config5_us"] = {k: v["us"] for k, v in cfg5.items()}
+    if aux is not None:
+        # standalone entry points at sizes above the L2: fraction of the measured copy peak
+        line["kernels_aux_frac"] = {k: fr(v["gbs"]) for k, v in aux.items() if v.get("gbs")}
+    # the sequence's kernels, each alone over the full batch: [ms, GB/s, fraction]
+    line["kernels"] = {k: [round(v["ms"], 3), round(v["gbs"]), fr(v["gbs"])] for k, v in table.items()}
     print(json.dumps(line), flush=True)
+
+
+def run_extras(args, stream, world):
+    """The steps beyond the non-GEMM path, on rank 0 after the timed region:
+    batched greedy decode, fused-epilogue GEMMs, the encoder with its GEMMs,
+    mel-to-tokens and the decode alone, each beside the reference's own code
+    on the host where one exists."""
+    cpu = world == 1 and not args.no_cpu_baseline
+    ex = {"decode": time_decode(stream, 3), "fused_gemms": time_fused_gemms(stream, 3),
+          "encoder_forward": time_encoder_forward(stream, 2)}
+    asr = time_asr(stream, 1)
+    asr["every_frame_blank"] = {k: v for k, v in time_asr(stream, 1, blank_bias=6.0).items()
+                                if k in ("blank_bias", "seconds_per_call", "utterances_per_s",
+                                         "audio_seconds_per_s", "tokens_per_frame")}
+    ex["asr"] = asr
+    ex["asr_decode"] = time_asr_decode(stream, 2, cpu=cpu)
+    ex["decode_fused"] = {"10_tokens_every_frame": time_decode_fused(stream, 2, 256, 40, 0.0),
+                          "sparse_decoder_steps": time_decode_fused(stream, 2, 256, 200, 3.5)}
+    if cpu:
+        ex["encoder_forward"]["cpu_baseline"] = cpu_encoder_baseline()
+        ex["asr"]["cpu_baseline"] = cpu_asr_baseline()
+        ex["decode"]["cpu_baseline"] = cpu_decode_baseline()
+    return ex
 
 
 def run_e2e(args, ws, arr, gout, x_addr, stream, world):
@@ -1242,8 +1379,8 @@ def run_e2e(args, ws, arr, gout, x_addr, stream, world):
     return {"value": F * steps * world / secs, "unit": "frames/s", "steps": steps,
             "h2d_bytes_per_step": ws.h2d_bytes, "d2h_bytes_per_step": ws.d2h_bytes,
             "pipeline_groups": args.groups,
-            "note": "pkcu_encoder_nongemm_host: H2D of x + GEMM outputs, 24 blocks, D2H of x, "
-                    "host wall clock per call (synchronous API), max over ranks"}
+            "h2d_gbs_per_rank": round(ws.h2d_bytes * steps / secs / 1e9, 1),
+            "note": "pkcu_encoder_nongemm_host, host clock, max over ranks"}
 
 
 def main():

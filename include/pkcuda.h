@@ -61,7 +61,12 @@ int pkcu_selftest(unsigned long long *mismatches);
  * rows with bulk asynchronous copies wait for them at most 1 s; a wait that
  * runs out makes the kernel abandon that part of its output and is counted.
  * *count receives the number of such waits on the current device since the
- * last reset (0 in correct operation); reset != 0 clears it. Synchronous. */
+ * last reset (0 in correct operation); reset != 0 clears it. Synchronous.
+ * The asynchronous pkcu_* calls report such timeouts only through this
+ * counter; the synchronous host-buffer calls (the drop-ins,
+ * pkcu_encoder_nongemm_host, pkcu_asr_transcribe / pkcu_asr_decode) read and
+ * reset it after their final synchronisation and return PKCU_ERR_CUDA when
+ * it is not 0. */
 int pkcu_wait_timeouts(unsigned *count, int reset);
 /* Self-test of that bound: one warp waits 20 ms on a barrier whose copy never
  * comes; *timed_out receives 1 when the wait gave up as designed. */
@@ -116,13 +121,15 @@ void pk_depthwise_conv1d(const float *x, const float *w, const float *b, float *
                          int T, int K);
 /* No counterpart in the reference. pk_softmax_rows for callers that cannot let
  * the library allocate device memory (a real-time callback that must not wait
- * on the allocator, a process that pre-assigns all device memory to its own
- * pool, code running during CUDA graph capture): the rows are staged in a
- * fixed 16 MiB array that every device loading the library holds until exit,
- * so n_rows * len may be at most 4,194,304 (larger sizes return
- * PKCU_ERR_ARG). The first call on a device looks up the array's address --
- * make it before any stream capture. Calls share the array; calls whose GPU
- * work overlaps race on it. Returns PKCU_OK or an error code. */
+ * on cudaMalloc, which can synchronise the device; a process that pre-assigns
+ * all device memory to its own pool): the rows are staged in a fixed 16 MiB
+ * array that every device loading the library holds until exit, so
+ * n_rows * len may be at most 4,194,304 (larger sizes return PKCU_ERR_ARG).
+ * The first call on a device looks up the array's address -- make it before
+ * any stream capture; the looked-up address does not survive cudaDeviceReset.
+ * Calls share the array; calls whose GPU work overlaps race on it. An empty
+ * call (n_rows or len 0) does nothing and accepts a NULL x. Returns PKCU_OK or
+ * an error code. */
 int pk_softmax_rows_noalloc(float *x, int n_rows, int len);
 /* Status of the calling thread's last drop-in call: PKCU_OK or an error code
  * (the message is in pkcu_last_error()). A failing drop-in also prints one
@@ -429,6 +436,50 @@ int  pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_outpu
                           const pkcu_gemm_inputs *gemm_in, const pkcu_seq *seq,
                           pkcu_stream_t stream);
 
+/* ── long audio: the chunked encoder (csrc/encoder.c:514-575, 597-633) ──────
+ * The reference encodes an utterance of more than PK_CHUNK_THRESHOLD encoder
+ * frames in chunks: chunk c owns frames [400c, min(400c + 400, T)) and runs the
+ * blocks over them plus up to 8 frames of overlap each side (clipped to the
+ * utterance), with the positional encoding of its own input length; only the
+ * owned frames are kept. A chunk plan lays the chunks of a batch of
+ * utterances out as one ragged batch (pkcu_chunk_plan_seq; an utterance that
+ * is not chunked is one item of its full length), so one pkcu_encoder_forward
+ * or pkcu_encoder_nongemm call encodes them all:
+ *   pkcu_chunk_split (x [sum T, 1024] -> xc [chunk frames, 1024]),
+ *   the blocks on xc with the plan's seq, pkcu_chunk_stitch (xc -> x).
+ * pkcu_encoder_forward itself never chunks (it is encode_blocks);
+ * pkcu_asr_transcribe chunks as pk_encoder does. */
+#define PKCU_CHUNK_SIZE      400   /* csrc/parakeet.h:132 */
+#define PKCU_CHUNK_OVERLAP   8     /* csrc/parakeet.h:133 */
+#define PKCU_CHUNK_THRESHOLD 500   /* csrc/parakeet.h:134 */
+/* AUTO: should_chunk (csrc/encoder.c:602-610) -- the PK_CHUNK environment
+ * variable ("0"/"off": never, "1"/"on": always), else T > 500; OFF / ON: never
+ * / always, whatever the environment says. */
+#define PKCU_CHUNK_AUTO 0
+#define PKCU_CHUNK_OFF  1
+#define PKCU_CHUNK_ON   2
+int  pkcu_should_chunk(int frames, int mode);
+/* Chunk bounds of one utterance (host only, no CUDA call): chunk c reads
+ * in_len[c] frames from in_start[c] and owns out_len[c] frames from
+ * out_start[c]; an utterance that is not chunked is one chunk of all its
+ * frames. Returns the number of chunks; with every array NULL it only counts,
+ * else -1 when that exceeds cap (or frames <= 0). */
+int  pkcu_chunk_bounds(int frames, int mode, int cap, int *in_start, int *in_len, int *out_start,
+                       int *out_len);
+typedef struct pkcu_chunk_plan pkcu_chunk_plan;
+int  pkcu_chunk_plan_create(const int *frames, int n_utts, int mode, pkcu_chunk_plan **out);
+void pkcu_chunk_plan_destroy(pkcu_chunk_plan *p);
+const pkcu_seq *pkcu_chunk_plan_seq(const pkcu_chunk_plan *p);   /* the chunk batch */
+int  pkcu_chunk_plan_chunked(const pkcu_chunk_plan *p);          /* utterances split */
+int  pkcu_chunk_plan_items(const pkcu_chunk_plan *p);            /* items of the chunk batch */
+/* Item `item` of the chunk batch: its utterance, its first input frame in that
+ * utterance and its frame count (any pointer may be NULL). */
+int  pkcu_chunk_plan_item(const pkcu_chunk_plan *p, int item, int *utt, int *first_frame,
+                          int *frames);
+/* Device arrays, 16-byte aligned; asynchronous on stream. */
+int  pkcu_chunk_split(const pkcu_chunk_plan *p, const float *x, float *xc, pkcu_stream_t stream);
+int  pkcu_chunk_stitch(const pkcu_chunk_plan *p, const float *xc, float *x, pkcu_stream_t stream);
+
 /* ── mel spectrograms to tokens on the GPU ─────────────────────────────────
  * pre_encode_and_scale + encode_blocks + pk_greedy_decode (csrc/encoder.c:
  * 578-593, 495-512; csrc/decoder.c:80-132) for a batch of utterances, every
@@ -448,6 +499,14 @@ int  pkcu_asr_encoder_frames(int mel_frames);
  * (a call with other lengths replaces them; pkcu_asr_destroy frees them). */
 int  pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
                          int *tokens, int *n_tokens, pkcu_stream_t stream);
+/* pk_encoder (csrc/encoder.c:612-633) for a batch: pre-encode and the blocks,
+ * utterances above the chunk threshold encoded in chunks (the model's chunk
+ * mode, PKCU_CHUNK_AUTO by default: the reference's should_chunk, PK_CHUNK
+ * included). enc (device) receives [sum encoder frames, 1024], utterance
+ * after utterance. Synchronous; pkcu_asr_transcribe encodes the same way. */
+int  pkcu_asr_encode(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
+                     float *enc, pkcu_stream_t stream);
+int  pkcu_asr_set_chunk_mode(pkcu_asr *m, int mode);   /* PKCU_CHUNK_AUTO / _OFF / _ON */
 /* The decode alone, a batched pk_greedy_decode (csrc/decoder.c:80-132) with
  * the model's decoder: enc (device, 16-byte aligned) holds the encoder
  * outputs [enc_frames[b], 1024] of n_utts utterances one after another;

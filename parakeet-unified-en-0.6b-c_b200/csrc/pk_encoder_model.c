@@ -585,7 +585,11 @@ struct pkcu_asr {
     int t_n, *t_frames;                /* mel frames the transcribe buffers were made for */
     pkcu_pre_plan *t_plan;
     float *t_pre;
-    pkcu_encoder_ws *t_ws;
+    pkcu_encoder_ws *t_ws;             /* the blocks' batch: utterances, or their chunks */
+    int *t_chunked;                    /* per utterance: chunked (the decisions t_ws was made for) */
+    pkcu_chunk_plan *t_chunk;          /* NULL when no utterance is chunked */
+    float *t_x;                        /* utterance-layout x of a chunked batch (in t_pre) */
+    int chunk_mode;                    /* PKCU_CHUNK_* */
     PreCtx t_pc;
     int d_n, *d_frames;                /* encoder frames the decoder was made for */
     pkcu_decoder *d_dec;
@@ -597,8 +601,13 @@ static void asr_release_transcribe(pkcu_asr *m)
 {
     pkcu_encoder_ws_destroy(m->t_ws);
     pkcu_pre_plan_destroy(m->t_plan);
+    pkcu_chunk_plan_destroy(m->t_chunk);
     if (m->t_pre) cudaFree(m->t_pre);
     free(m->t_frames);
+    free(m->t_chunked);
+    m->t_chunk = NULL;
+    m->t_chunked = NULL;
+    m->t_x = NULL;
     m->t_ws = NULL;
     m->t_plan = NULL;
     m->t_pre = NULL;
@@ -813,6 +822,7 @@ static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_
                  : pkcu_greedy_decode_graph(dec, &m->dec, dec_hook, dc, stream);
     }
     if (!st) st = pkcu_decoder_results(dec, n_tokens, NULL, tokens, stream);
+    if (!st) st = pk_check_wait_timeouts("pkcu_asr");
     return st;
 }
 
@@ -825,18 +835,40 @@ int pkcu_asr_decode(pkcu_asr *m, const float *enc, const int *enc_frames, int n_
     return asr_decode(m, enc, enc_frames, n_utts, tokens, n_tokens, stream);
 }
 
-int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
-                        int *tokens, int *n_tokens, pkcu_stream_t stream)
+/* Chunking decision of each utterance of this call (PK_CHUNK is read per
+ * call, as the reference's should_chunk does); *any: one or more chunked. */
+static int *chunk_decisions(const pkcu_asr *m, const int *mel_frames, int n_utts, int *any)
 {
-    if (!m || !mel || !mel_frames || n_utts <= 0 || !tokens || !n_tokens)
-        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: bad argument");
-    int st = PKCU_OK;
+    int *d = (int *)malloc(sizeof(int) * (size_t)n_utts);
+    *any = 0;
+    if (!d) return NULL;
+    for (int i = 0; i < n_utts; i++) {
+        d[i] = pkcu_should_chunk(pkcu_asr_encoder_frames(mel_frames[i]), m->chunk_mode);
+        *any |= d[i];
+    }
+    return d;
+}
+
+/* pre_encode_and_scale + the 24 blocks, chunked as pk_encoder chunks
+ * (csrc/encoder.c:612-633): on success *x_out is the encoder output
+ * [sum encoder frames, 1024], utterance after utterance, in a kept buffer. */
+static int asr_encode(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
+                      float **x_out, pkcu_stream_t stream)
+{
+    int st = PKCU_OK, any = 0;
     PreCtx *pc = &m->t_pc;
-    if (!same_lengths(m->t_n, m->t_frames, n_utts, mel_frames)) {
+    int *dec = chunk_decisions(m, mel_frames, n_utts, &any);
+    if (!dec) return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr: host allocation");
+    if (!same_lengths(m->t_n, m->t_frames, n_utts, mel_frames) ||
+        !same_lengths(m->t_n, m->t_chunked, n_utts, dec)) {
         asr_release_transcribe(m);
         st = pkcu_pre_plan_create(mel_frames, n_utts, &m->t_plan);
         if (!st && !(m->t_frames = copy_lengths(mel_frames, n_utts)))
-            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: host allocation");
+            st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr: host allocation");
+        if (!st) {
+            m->t_chunked = dec;
+            dec = NULL;
+        }
         if (!st) {
             memset(pc, 0, sizeof(*pc));
             pc->m = m;
@@ -844,11 +876,12 @@ int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, in
             pc->P3 = pkcu_pre_plan_p3(m->t_plan);
             pc->F = pkcu_pre_plan_frames(m->t_plan);
             const long long n2 = 256 * pc->P2, n3 = 256 * pc->P3;
-            const long long total = 2 * n2 + 2 * n3 + pc->F * 4096 + pc->F * PK_D;
+            /* + the utterance-layout x of a chunked batch */
+            const long long total = 2 * n2 + 2 * n3 + pc->F * 4096 + pc->F * PK_D + (any ? pc->F * PK_D : 0);
             if (cudaMalloc((void **)&m->t_pre, sizeof(float) * (size_t)total) != cudaSuccess) {
                 cudaGetLastError();
                 m->t_pre = NULL;
-                st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr_transcribe: pre-encode buffers");
+                st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr: pre-encode buffers");
             } else {
                 float *pre = m->t_pre;
                 pc->gi.s2d = pre;
@@ -857,22 +890,74 @@ int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, in
                 pc->go.pw2 = pre + 2 * n2 + n3;
                 pc->gi.flat = pre + 2 * n2 + 2 * n3;
                 pc->go.proj = pc->gi.flat + pc->F * 4096;
+                m->t_x = any ? pc->go.proj + pc->F * PK_D : NULL;
             }
         }
-        if (!st) st = pkcu_encoder_ws_create(pkcu_pre_plan_out_seq(m->t_plan), 1, &m->t_ws);
+        if (!st && any) {
+            int *ef = (int *)malloc(sizeof(int) * (size_t)n_utts);
+            if (!ef) st = pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr: host allocation");
+            for (int i = 0; i < n_utts && !st; i++) ef[i] = pkcu_asr_encoder_frames(mel_frames[i]);
+            if (!st) st = pkcu_chunk_plan_create(ef, n_utts, m->chunk_mode, &m->t_chunk);
+            free(ef);
+        }
+        if (!st)
+            st = pkcu_encoder_ws_create(m->t_chunk ? pkcu_chunk_plan_seq(m->t_chunk)
+                                                   : pkcu_pre_plan_out_seq(m->t_plan), 1, &m->t_ws);
         if (st) {
+            free(dec);
             asr_release_transcribe(m);
             return st;
         }
         m->t_n = n_utts;
     }
-    const pkcu_seq *seq = pkcu_pre_plan_out_seq(m->t_plan);
-    float *x = NULL;
+    free(dec);
+    const pkcu_seq *seq = m->t_chunk ? pkcu_chunk_plan_seq(m->t_chunk) : pkcu_pre_plan_out_seq(m->t_plan);
+    float *xb = NULL;
     pkcu_gemm_outputs go;
     pkcu_gemm_inputs gi;
-    st = pkcu_encoder_ws_device(m->t_ws, &x, &go, &gi);
-    if (!st) st = pkcu_pre_encode(mel, &m->pre, &pc->go, &pc->gi, x, m->t_plan, pre_hook, pc, stream);
-    if (!st) st = pkcu_encoder_forward(m->enc, x, &go, &gi, seq, stream);
+    st = pkcu_encoder_ws_device(m->t_ws, &xb, &go, &gi);
+    float *xu = m->t_chunk ? m->t_x : xb;   /* utterance layout */
+    if (!st) st = pkcu_pre_encode(mel, &m->pre, &pc->go, &pc->gi, xu, m->t_plan, pre_hook, pc, stream);
+    if (!st && m->t_chunk) st = pkcu_chunk_split(m->t_chunk, xu, xb, stream);
+    if (!st) st = pkcu_encoder_forward(m->enc, xb, &go, &gi, seq, stream);
+    if (!st && m->t_chunk) st = pkcu_chunk_stitch(m->t_chunk, xb, xu, stream);
+    if (!st) *x_out = xu;
+    return st;
+}
+
+int pkcu_asr_set_chunk_mode(pkcu_asr *m, int mode)
+{
+    if (!m) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_chunk_mode: NULL model");
+    if (mode != PKCU_CHUNK_AUTO && mode != PKCU_CHUNK_OFF && mode != PKCU_CHUNK_ON)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_chunk_mode: unknown mode %d", mode);
+    m->chunk_mode = mode;
+    return PKCU_OK;
+}
+
+int pkcu_asr_encode(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts, float *enc,
+                    pkcu_stream_t stream)
+{
+    if (!m || !mel || !mel_frames || n_utts <= 0 || !enc)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_encode: bad argument");
+    float *x = NULL;
+    int st = asr_encode(m, mel, mel_frames, n_utts, &x, stream);
+    if (st) return st;
+    long long F = 0;
+    for (int i = 0; i < n_utts; i++) F += pkcu_asr_encoder_frames(mel_frames[i]);
+    if (cudaMemcpyAsync(enc, x, sizeof(float) * (size_t)(F * PK_D), cudaMemcpyDeviceToDevice,
+                        (cudaStream_t)stream) != cudaSuccess ||
+        cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+        return pkcu_fail(PKCU_ERR_CUDA, "pkcu_asr_encode: %s", cudaGetErrorString(cudaGetLastError()));
+    return pk_check_wait_timeouts("pkcu_asr_encode");
+}
+
+int pkcu_asr_transcribe(pkcu_asr *m, const float *mel, const int *mel_frames, int n_utts,
+                        int *tokens, int *n_tokens, pkcu_stream_t stream)
+{
+    if (!m || !mel || !mel_frames || n_utts <= 0 || !tokens || !n_tokens)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: bad argument");
+    float *x = NULL;
+    int st = asr_encode(m, mel, mel_frames, n_utts, &x, stream);
     int *enc_frames = NULL;
     if (!st) {
         enc_frames = (int *)malloc(sizeof(int) * (size_t)n_utts);

@@ -20,6 +20,9 @@ D, H, DH, FF = 1024, 8, 128, 4096
 PKCU_CHANNEL_FIRST, PKCU_TIME_FIRST = 0, 1
 PKCU_GROUP_ALONG_K, PKCU_GROUP_ALONG_N = 0, 1
 PKCU_ACT_RELU, PKCU_ACT_TANH = 0, 1
+PKCU_CHUNK_AUTO, PKCU_CHUNK_OFF, PKCU_CHUNK_ON = 0, 1, 2
+PKCU_OK, PKCU_ERR_ARG, PKCU_ERR_CUDA, PKCU_ERR_NOMEM = 0, 1, 2, 3
+PKCU_CHUNK_SIZE, PKCU_CHUNK_OVERLAP, PKCU_CHUNK_THRESHOLD = 400, 8, 500
 
 # Symbols declared by include/pkcuda.h (checked by the CPU test suite).
 EXPORTED = (
@@ -55,6 +58,9 @@ EXPORTED = (
     "pkcu_encoder_forward", "pkcu_asr_create", "pkcu_asr_destroy", "pkcu_asr_encoder_frames",
     "pkcu_asr_transcribe", "pkcu_asr_set_decode_mode", "pkcu_greedy_decode_graph",
     "pkcu_decoder_set_weights", "pkcu_greedy_decode_fused", "pkcu_asr_decode",
+    "pkcu_should_chunk", "pkcu_chunk_bounds", "pkcu_chunk_plan_create", "pkcu_chunk_plan_destroy", "pkcu_chunk_plan_seq",
+    "pkcu_chunk_plan_chunked", "pkcu_chunk_plan_items", "pkcu_chunk_plan_item", "pkcu_chunk_split",
+    "pkcu_chunk_stitch", "pkcu_asr_encode", "pkcu_asr_set_chunk_mode",
 )
 
 
@@ -167,6 +173,18 @@ _SIGS = {
     "pkcu_encoder_ws_h2d_bytes": (LL, [VP]),
     "pkcu_encoder_ws_d2h_bytes": (LL, [VP]),
     "pkcu_encoder_nongemm_host": (I, [VP, VP, VP, VP, I, VP]),
+    "pkcu_should_chunk": (I, [I, I]),
+    "pkcu_chunk_bounds": (I, [I, I, I, VP, VP, VP, VP]),
+    "pkcu_chunk_plan_create": (I, [C.POINTER(I), I, I, C.POINTER(VP)]),
+    "pkcu_chunk_plan_destroy": (None, [VP]),
+    "pkcu_chunk_plan_seq": (VP, [VP]),
+    "pkcu_chunk_plan_chunked": (I, [VP]),
+    "pkcu_chunk_plan_items": (I, [VP]),
+    "pkcu_chunk_plan_item": (I, [VP, I, C.POINTER(I), C.POINTER(I), C.POINTER(I)]),
+    "pkcu_chunk_split": (I, [VP, VP, VP, VP]),
+    "pkcu_chunk_stitch": (I, [VP, VP, VP, VP]),
+    "pkcu_asr_encode": (I, [VP, VP, C.POINTER(I), I, VP, VP]),
+    "pkcu_asr_set_chunk_mode": (I, [VP, I]),
 }
 
 _lib = None
@@ -282,6 +300,55 @@ GEMM_OUT_FIELDS = ("ff1_h", "ff1_out", "qkv", "P", "ac", "bd", "attn_h", "att_ou
                    "ff2_h", "ff2_out")
 GEMM_IN_FIELDS = ("ln_ff1", "h1", "ln_sa", "Qu", "K", "Qv", "P_h", "S", "V", "attn", "cf", "dw",
                   "ln_ff2", "h2", "gated")
+
+
+class ChunkPlan:
+    """pkcu_chunk_plan: the chunk batch of the reference's chunked encoder."""
+
+    def __init__(self, frames, mode=PKCU_CHUNK_AUTO):
+        n = len(frames)
+        arr = (I * n)(*[int(t) for t in frames])
+        h = VP()
+        check(lib().pkcu_chunk_plan_create(arr, n, int(mode), C.byref(h)), "pkcu_chunk_plan_create")
+        self.handle = h
+        L = lib()
+        self.n_items = L.pkcu_chunk_plan_items(h)
+        self.chunked = L.pkcu_chunk_plan_chunked(h)
+        self.items = []
+        for i in range(self.n_items):
+            u, f0, nf = I(), I(), I()
+            check(L.pkcu_chunk_plan_item(h, i, C.byref(u), C.byref(f0), C.byref(nf)), "pkcu_chunk_plan_item")
+            self.items.append((u.value, f0.value, nf.value))
+        self.seq_handle = L.pkcu_chunk_plan_seq(h)
+
+    @property
+    def lengths(self):
+        return [nf for _, _, nf in self.items]
+
+    def split(self, x, xc, stream=None):
+        call("pkcu_chunk_split", self.handle, x if isinstance(x, int) else ptr(x),
+             xc if isinstance(xc, int) else ptr(xc), stream_handle(stream))
+
+    def stitch(self, xc, x, stream=None):
+        call("pkcu_chunk_stitch", self.handle, xc if isinstance(xc, int) else ptr(xc),
+             x if isinstance(x, int) else ptr(x), stream_handle(stream))
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_chunk_plan_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class BlockParams(C.Structure):
@@ -433,10 +500,11 @@ class EncoderWorkspace:
 
 
 def encoder_nongemm(x, blocks_arr, n_blocks, gout: GemmOutputs, gin: GemmInputs, seq: Seq,
-                    stream=None) -> None:
+                    stream=None, hook=None) -> None:
+    """hook: a GEMM_HOOK (called at every GEMM point of every block) or None."""
     call("pkcu_encoder_nongemm", x if isinstance(x, int) else ptr(x), C.cast(blocks_arr, VP), n_blocks,
-         C.cast(C.pointer(gout), VP), C.cast(C.pointer(gin), VP), seq.handle, None, None,
-         stream_handle(stream))
+         C.cast(C.pointer(gout), VP), C.cast(C.pointer(gin), VP), seq.handle,
+         C.cast(hook, VP) if hook is not None else None, None, stream_handle(stream))
 
 
 # ── pre-encode subsampling (pkcu_pre_encode) ────────────────────────────────
@@ -663,6 +731,17 @@ class ASR:
 
     def set_decode_mode(self, mode: int) -> None:
         call("pkcu_asr_set_decode_mode", self.handle, int(mode))
+
+    def set_chunk_mode(self, mode: int) -> None:
+        call("pkcu_asr_set_chunk_mode", self.handle, int(mode))
+
+    def encode(self, mel, mel_frames, out, stream=None) -> None:
+        """pk_encoder for a batch: out (device) receives the encoder outputs
+        [sum encoder frames, 1024], utterance after utterance."""
+        n = len(mel_frames)
+        mf = (I * n)(*[int(t) for t in mel_frames])
+        call("pkcu_asr_encode", self.handle, mel if isinstance(mel, int) else ptr(mel), mf, n,
+             out if isinstance(out, int) else ptr(out), stream_handle(stream))
 
     def transcribe(self, mel, mel_frames, stream=None):
         """mel: device tensor of the spectrograms [128, T_b] one after another;

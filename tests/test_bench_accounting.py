@@ -26,3 +26,12 @@ def test_decode_multiply_adds():
     assert bench.decode_fmas(1, 0) == 2 * 2 * 2560 * 640          # both LSTM layers' gate products
     assert bench.decode_fmas(0, 1) == 640 * 640 + 640 * 1025      # pred + out products
     assert bench.decode_fmas(256, 256) == 256 * (6_553_600 + 1_065_600)
+
+
+def test_ragged_bytes_are_the_items_sum():
+    # a uniform batch counted item by item equals the batch formula
+    assert bench.ragged_step_bytes([375] * 256, 24) == bench.step_bytes(256 * 375, 375, 256, 24)
+    # config 3: 8 chunks (408, 416 x 6, 408) x 24 blocks
+    lens = bench.CONFIG3_LENGTHS
+    assert sum(lens) == 3312 and len(lens) == 8
+    assert bench.ragged_step_bytes(lens, 24) == sum(bench.step_bytes(T, T, 1, 24) for T in lens)
