@@ -330,6 +330,20 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
                          const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
                          pkcu_stream_t stream);
 
+/* The same sequence with some GEMM epilogues done by the hook's GEMMs
+ * (pkcu_encoder_forward uses this with its tcgen05 GEMMs):
+ *   PKCU_FUSED_FF_SWISH -- the FF1_1 / FF2_1 hooks write Swish(x W + b1) into
+ *     gemm_in->h1 / h2 themselves; the sequence's bias+Swish steps are skipped;
+ *   PKCU_FUSED_QKV -- the QKV hook writes Qu, Qv, K, V (bias, head split and
+ *     pos_bias_u / v, as pkcu_qkv_split_uv) itself; that step is skipped.
+ * The skipped GEMM outputs (ff1_h, ff2_h, qkv) are then not read. */
+#define PKCU_FUSED_FF_SWISH 1u
+#define PKCU_FUSED_QKV      2u
+int pkcu_encoder_nongemm_fused(float *x, const pkcu_block_params *blocks, int n_blocks,
+                               const pkcu_gemm_outputs *gemm_out, const pkcu_gemm_inputs *gemm_in,
+                               const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
+                               unsigned fused, pkcu_stream_t stream);
+
 /* Number of kernel launches pkcu_encoder_nongemm makes for n_blocks blocks. */
 int pkcu_encoder_nongemm_launches(int n_blocks);
 
@@ -411,6 +425,49 @@ int pkcu_gemm_bias_swish(const float *A, const float *W, const float *bias, floa
  * residual (:418-434, scale 1). */
 int pkcu_gemm_bias_residual(const float *A, const float *W, const float *bias, float *X,
                             float scale, int M, int N, int K, pkcu_stream_t stream);
+
+/* ── weight products on the library's own tcgen05 GEMM ───────────────────────
+ * pk_wmatmul (csrc/tensor_ops.c:50-61) and the epilogues that follow it in a
+ * block, for the reference's three weight storages (Weight, csrc/parakeet.h:
+ * 52-57): float32 (cblas_sgemm_st), int8 with one per-tensor scale
+ * (cblas_sgemm_qb, csrc/blas.c:759, dequantised while packing :526-558) and
+ * GPTQ int4 with group scales (cblas_sgemm_q4b, :950, :780-843). fp32
+ * accurate on the bf16 tensor cores: the activation as three bf16 parts, an
+ * int8 weight as its q (exact in bf16, the scale applied to the sum), a float32
+ * or int4 weight as the three bf16 parts of its fp32 values (int4: (float)q *
+ * scale first, bit for bit); tcgen05.mma with TMEM accumulators drained to
+ * fp32 every 24 MMAs.
+ * A weight is prepared once (synchronous): data is device memory, [K, N]
+ * row-major for bits 32 / 8, packed [K, N/2] bytes + scales for bits 4 (group /
+ * axis as pkcu_dequant_i4; the reference's layout is 32, PKCU_GROUP_ALONG_N);
+ * K and N multiples of 32. Every call needs a work buffer of
+ * pkcu_wmatmul_work_bytes(M, K) bytes (the activation's parts), 16-byte
+ * aligned; calls sharing one run one at a time. All arrays are device
+ * memory, 16-byte aligned, rows packed. */
+typedef struct pkcu_weight pkcu_weight;
+int  pkcu_weight_create(const void *data, int bits, float scale, const float *scales, int group,
+                        int axis, int K, int N, pkcu_stream_t stream, pkcu_weight **out);
+void pkcu_weight_destroy(pkcu_weight *w);
+long long pkcu_wmatmul_work_bytes(int M, int K);
+/* C[M, N] = alpha A[M, K] W + beta C (pk_wmatmul). */
+int pkcu_wmatmul(const float *A, const pkcu_weight *W, float *C, int M, float alpha, float beta,
+                 void *work, pkcu_stream_t stream);
+/* D = Swish(A W + bias): feed_forward's linear1 + pk_bias_add + pk_swish
+ * (csrc/encoder.c:193-196), Swish the reference's polynomial form. */
+int pkcu_wmatmul_bias_swish(const float *A, const pkcu_weight *W, const float *bias, float *D,
+                            int M, void *work, pkcu_stream_t stream);
+/* X += scale (A W + bias), one fused multiply-add per entry: linear2 + the
+ * 0.5 macaron residual (csrc/encoder.c:198-216), the output projection + the
+ * attention residual (scale 1, :418-434). */
+int pkcu_wmatmul_bias_residual(const float *A, const pkcu_weight *W, const float *bias, float *X,
+                               float scale, int M, void *work, pkcu_stream_t stream);
+/* The fused QKV projection with its bias, head split and pos_bias_u / v
+ * (csrc/encoder.c:313-356) in the epilogue: A = the batch's LN_sa rows
+ * [frames, 1024], W the fused [1024, 3072] weight, outputs as
+ * pkcu_qkv_split_uv writes them (per item [8, T, 128]). */
+int pkcu_wmatmul_qkv(const float *A, const pkcu_weight *W, const float *bqkv, const float *u,
+                     const float *v, float *Qu, float *Qv, float *K, float *V, const pkcu_seq *seq,
+                     void *work, pkcu_stream_t stream);
 
 /* ── the encoder stack on the GPU, GEMMs included ──────────────────────────
  * Replaces encode_blocks (csrc/encoder.c:495-512) for a batch: fp32 device

@@ -561,15 +561,22 @@ class Reference:
         assert rc == 0 and bits.value == 8, (rc, bits.value)
         return out, scales
 
-    def wmatmul(self, A, W):
-        """A [M, K] x W [K, N] through the reference's pk_wmatmul with an fp32
-        Weight (csrc/tensor_ops.c:50-61)."""
-        A, W = f32(A), f32(W)
+    def wmatmul(self, A, W, scale=None, alpha=1.0, beta=0.0, C_in=None):
+        """A [M, K] x W [K, N] through the reference's pk_wmatmul
+        (csrc/tensor_ops.c:50-61): an fp32 Weight, or with scale given an int8
+        Weight (W int8 [K, N], per-tensor scale: cblas_sgemm_qb, dequantised
+        while packing, csrc/blas.c:526-558, 759); C = alpha A W + beta C_in."""
+        A = f32(A)
         M, K = A.shape
         N = W.shape[1]
-        w = RefWeight(W.ctypes.data, 0.0, FP(), 32)
-        out = np.empty((M, N), np.float32)
-        self.L.pk_wmatmul(_fp(A), C.byref(w), _fp(out), M, N, K, 1.0, 0.0)
+        if scale is None:
+            W = f32(W)
+            w = RefWeight(W.ctypes.data, 0.0, FP(), 32)
+        else:
+            W = np.ascontiguousarray(W, np.int8)
+            w = RefWeight(W.ctypes.data, float(scale), FP(), 8)
+        out = np.zeros((M, N), np.float32) if C_in is None else f32(C_in).copy()
+        self.L.pk_wmatmul(_fp(A), C.byref(w), _fp(out), M, N, K, float(alpha), float(beta))
         return out
 
     def ff_linear1(self, A, W, b):

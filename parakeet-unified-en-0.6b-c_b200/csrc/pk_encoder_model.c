@@ -8,12 +8,14 @@
  * forward pass is fp32 throughout like the reference's (csrc/encoder.c). The
  * row-major projections of the block (FF, QKV, output, and the positional
  * projection of the sinusoidal table's slice, csrc/encoder.c:220-227, once per
- * distinct utterance length) run on the tensor cores with fp32 accuracy
- * (k_gemm.cu: three bf16 parts per operand, nine MMAs per product); the other
- * products are cuBLAS single-precision GEMMs (no TF32): the per-head score,
- * positional-score and context products and the two pointwise convolutions,
- * as strided batches over heads (and over utterances when the batch is
- * uniform). */
+ * distinct utterance length) run on the library's tcgen05 GEMM (k_tcgemm.cu)
+ * with fp32 accuracy: an int8 weight used as stored (q exact in bf16, its
+ * scale applied to the sum), any other as the three bf16 parts of its fp32
+ * values, the activation as three bf16 parts. The pointwise convolutions run
+ * on split operands through cuBLAS bf16 GEMMs band by band, and the per-head
+ * score, positional-score and context products as cuBLAS single-precision
+ * GEMMs (no TF32), strided batches over heads (and over utterances when the
+ * batch is uniform). */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -43,9 +45,10 @@ static const long long W_ELEMS[W_N] = {
 /* [K, N] of each weight as the product x W reads it (row-major, [in, out]). */
 static const int W_K[W_N] = {PK_D, PK_FF, PK_D, PK_D, PK_D, PK_D, PK_D, PK_D, PK_FF};
 static const int W_COLS[W_N] = {PK_FF, PK_D, 3 * PK_D, PK_D, PK_D, 2 * PK_D, PK_D, PK_FF, PK_D};
-/* Every block weight runs on split operands (k_split.cu): 1 = the right-hand
- * operand of a row-major projection, kept as the stack [w2; w1; w0]; 2 = the
- * left-hand operand of a pointwise convolution, kept as rows [w0 | w1 | w2]. */
+/* Every block weight runs on split operands: 1 = the right-hand operand of a
+ * row-major projection, kept as K-major planes for the tcgen05 GEMM
+ * (k_tcgemm.cu); 2 = the left-hand operand of a pointwise convolution, kept as
+ * rows [w0 | w1 | w2] (k_split.cu). */
 static const int W_SPLIT[W_N] = {1, 1, 1, 1, 1, 2, 2, 1, 1};
 
 struct pkcu_encoder_model {
@@ -55,9 +58,10 @@ struct pkcu_encoder_model {
     const float *w[64][W_N];
     pkcu_block_params params[64];
     const float *pe;                   /* pos_encoding.pe_table [9999, 1024] */
-    void *stacks;                      /* bf16 part stacks [3K, N] of the W_SPLIT weights */
-    const void *stack[64][W_N];        /* NULL: that product runs on the fp32 path */
-    float qscale[64][W_N];             /* > 0: stack holds the int8 weight q as bf16 [K, N], w = q x this */
+    void *stacks;                      /* bf16 operands of the W_SPLIT weights */
+    const void *stack[64][W_N];        /* projections: K-major planes [N, K] (int8 q) or [N, 3K] (parts);
+                                          pointwise: rows [w0 | w1 | w2]; NULL: the fp32 path */
+    float qscale[64][W_N];             /* > 0: the int8 weight's scale, w = q x this */
     void *split_ws;                    /* activation parts [rows, 3K] bf16, grown per forward */
     size_t split_cap;                  /* its bytes */
 };
@@ -128,13 +132,17 @@ static int build_stacks(pkcu_encoder_model *m, const pkcu_weights *w, long long 
                 float sc = 0.f;
                 const int8_t *q = W_SPLIT[k] == 1 ? int8_source(w, b, k, &sc) : NULL;
                 int st;
-                if (q) {
-                    st = pk_i8_to_bf16(q, p, W_ELEMS[k], stream);
-                    m->qscale[b][k] = sc;
+                if (W_SPLIT[k] == 1) {
+                    /* K-major planes for the library's tcgen05 GEMM: q of an
+                     * int8 weight (its scale as the GEMM's alpha), else the
+                     * three parts of the fp32 values */
+                    float alpha = 1.0f;
+                    st = q ? pk_tc_prepare(q, 8, sc, W_K[k], W_COLS[k], p, &alpha, stream)
+                           : pk_tc_prepare(src, 32, 0.0f, W_K[k], W_COLS[k], p, &alpha, stream);
+                    m->qscale[b][k] = q ? alpha : 0.0f;
                 } else {
                     /* a pointwise weight is [out channels, 1024]: W_COLS x W_K */
-                    st = W_SPLIT[k] == 1 ? pk_split_stack_bf16x3(src, p, W_K[k], W_COLS[k], stream)
-                                         : pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
+                    st = pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
                 }
                 if (st) return st;
                 m->stack[b][k] = p;
@@ -239,6 +247,7 @@ typedef struct {
     const pkcu_gemm_inputs *gi;
     const pkcu_seq *seq;
     long long *off;   /* per item: frame, pos row, score, bd element offsets (4 x n_items) */
+    unsigned fused;   /* PKCU_FUSED_* epilogues the hook's GEMMs apply */
 } Fwd;
 
 static const float ONE = 1.0f, ZERO = 0.0f;
@@ -269,56 +278,16 @@ static int proj(cublasHandle_t h, int M, int N, int K, const float *A, const flo
     return rm_gemm(h, M, N, K, A, K, 0, B, N, 0, 0, C, N, 0, 1);
 }
 
-/* C[M, N] = A[M, K] W[K, N] from the split operands: the activation parts
- * [a0 | a1 | a2] into the model's workspace, then cuBLAS bf16 GEMMs (fp32
- * accumulation and output) band by band, smallest band first, the later ones
- * added through beta = 1 (stack = [w2; w1; w0], k_split.cu):
- *   C = [a0 a1 a2] [w2; w1; w0];  C += [a0 a1] [w1; w0];  C += a0 w0 (in K chunks)
- * Row-major through the column-major library as C^T = W^T A^T. */
-static int proj_split(pkcu_encoder_model *m, cublasHandle_t h, int M, int N, int K, const float *A,
-                      const void *stack, float *C, pkcu_stream_t stream)
-{
-    if ((size_t)M * 3 * K * 2 > m->split_cap)
-        return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: split workspace too small");
-    int st = pk_split_rows_bf16x3(A, m->split_ws, M, K, stream);
-    if (st) return st;
-    const uint16_t *S = (const uint16_t *)stack;   /* bf16 elements */
-    const uint16_t *Ap = (const uint16_t *)m->split_ws;
-    static const float one = 1.0f, zero = 0.0f;
-    /* (k, first stack row, first activation column, beta): bands 2 and 1,
-     * then band 0 in chunks of at most SPLIT_CHUNK along K -- the tensor
-     * cores' accumulation rounds less exactly than an fp32 add, so the
-     * largest band is summed in short runs joined by the GEMM's fp32 epilogue */
-    enum { SPLIT_CHUNK = 512 };
-    struct { int k; long long srow, acol; const float *beta; } part[2 + PK_FF / SPLIT_CHUNK];
-    int np = 0;
-    part[np].k = 3 * K; part[np].srow = 0; part[np].acol = 0; part[np++].beta = &zero;
-    part[np].k = 2 * K; part[np].srow = K; part[np].acol = 0; part[np++].beta = &one;
-    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
-        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
-        part[np].srow = 2LL * K + k0;
-        part[np].acol = k0;
-        part[np++].beta = &one;
-    }
-    for (int i = 0; i < np; i++) {
-        const cublasStatus_t cs = cublasGemmEx(
-            h, CUBLAS_OP_N, CUBLAS_OP_N, N, M, part[i].k, &one, S + part[i].srow * N, CUDA_R_16BF, N,
-            Ap + part[i].acol, CUDA_R_16BF, 3 * K, part[i].beta, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
-            CUBLAS_GEMM_DEFAULT);
-        if (cs != CUBLAS_STATUS_SUCCESS)
-            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
-    }
-    return PKCU_OK;
-}
-
 /* The pointwise convolution C[Mo, T] = W[Mo, K] X[K, T] of `items`
  * consecutive utterances of T frames (channel-first) from split operands,
  * when the workspace holds them (else the fp32 SGEMM path, return 1): X's
  * parts as [x2; x1; x0] per utterance at the padded pitch Tp (T rounded up
  * to 8, so every row starts 16-byte aligned) into the workspace, W's as
- * [w0 | w1 | w2] (model load), one strided-batched bf16 GEMM per band as in
- * proj_split (band 0 in K chunks) into a padded fp32 product behind them, then
- * the pad columns dropped into C. */
+ * [w0 | w1 | w2] (model load), one strided-batched bf16 GEMM per band
+ * (smallest first, the later ones added through beta = 1; band 0 in K chunks
+ * of 512, because the tensor cores' accumulation rounds less exactly than an
+ * fp32 add) into a padded fp32 product behind them, then the pad columns
+ * dropped into C. */
 static int pw_split(pkcu_encoder_model *m, cublasHandle_t h, int Mo, int T, int items, const void *wrows,
                     const float *X, float *C, pkcu_stream_t stream, int *fallback)
 {
@@ -358,52 +327,44 @@ static int pw_split(pkcu_encoder_model *m, cublasHandle_t h, int Mo, int T, int 
     return pk_depad_rows(Cp, C, (long long)items * Mo, T, Tp, stream);
 }
 
-/* C[M, N] = A[M, K] (s Q[K, N]) for an int8 weight w = s q: q is exact in
- * bf16, so the product needs only the activation's three parts, a band each
- * (smallest first, a0 in K chunks), every GEMM scaled by s through alpha:
- *   C = s a2 q;  C += s a1 q;  C += s a0 q (in K chunks) */
-static int proj_q(pkcu_encoder_model *m, cublasHandle_t h, int M, int N, int K, const float *A, const void *Q,
-                  float s, float *C, pkcu_stream_t stream)
+/* The block's row-major projection on the library's tcgen05 GEMM: the
+ * activation's three parts into the model's workspace, then the product with
+ * the weight's K-major planes (an int8 weight's q with its scale as alpha, or
+ * the three parts of fp32 values); the fp32 tensor-core GEMM when the model
+ * could not hold the planes. */
+static int proj_tc(pkcu_encoder_model *m, int b, int k, int M, const float *A, pk_tc_epi *e,
+                   pkcu_stream_t stream)
 {
-    if ((size_t)M * 3 * K * 2 > m->split_cap)
+    if ((size_t)M * 3 * W_K[k] * 2 > m->split_cap)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: split workspace too small");
-    int st = pk_split_rows_bf16x3(A, m->split_ws, M, K, stream);
+    int st = pk_split_rows_bf16x3(A, m->split_ws, M, W_K[k], stream);
     if (st) return st;
-    const uint16_t *Qp = (const uint16_t *)Q;   /* bf16 elements */
-    const uint16_t *Ap = (const uint16_t *)m->split_ws;
-    static const float one = 1.0f, zero = 0.0f;
-    enum { SPLIT_CHUNK = 512 };
-    struct { int k; long long acol, qrow; const float *beta; } part[2 + PK_FF / SPLIT_CHUNK];
-    int np = 0;
-    part[np].k = K; part[np].acol = 2LL * K; part[np].qrow = 0; part[np++].beta = &zero;
-    part[np].k = K; part[np].acol = K; part[np].qrow = 0; part[np++].beta = &one;
-    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
-        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
-        part[np].acol = k0;
-        part[np].qrow = k0;
-        part[np++].beta = &one;
-    }
-    for (int i = 0; i < np; i++) {
-        const cublasStatus_t cs = cublasGemmEx(
-            h, CUBLAS_OP_N, CUBLAS_OP_N, N, M, part[i].k, &s, Qp + part[i].qrow * N, CUDA_R_16BF, N,
-            Ap + part[i].acol, CUDA_R_16BF, 3 * K, part[i].beta, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
-            CUBLAS_GEMM_DEFAULT);
-        if (cs != CUBLAS_STATUS_SUCCESS)
-            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
-    }
-    return PKCU_OK;
+    e->alpha = m->qscale[b][k] > 0.f ? m->qscale[b][k] : 1.0f;
+    return pk_tc_gemm(m->split_ws, m->stack[b][k], m->qscale[b][k] > 0.f ? 1 : 3, M, W_COLS[k], W_K[k], e,
+                      stream);
 }
 
-/* The block's row-major projection: on the int8 weight directly, else on split
- * operands when the model has the weight's part stack, else the fp32
- * tensor-core GEMM. */
 static int proj_w(pkcu_encoder_model *m, cublasHandle_t h, int b, int k, int M, const float *A, float *C,
                   pkcu_stream_t stream)
 {
-    if (m->stack[b][k] && m->qscale[b][k] > 0.f)
-        return proj_q(m, h, M, W_COLS[k], W_K[k], A, m->stack[b][k], m->qscale[b][k], C, stream);
-    if (m->stack[b][k]) return proj_split(m, h, M, W_COLS[k], W_K[k], A, m->stack[b][k], C, stream);
-    return proj(h, M, W_COLS[k], W_K[k], A, m->w[b][k], C, stream);
+    if (!m->stack[b][k]) return proj(h, M, W_COLS[k], W_K[k], A, m->w[b][k], C, stream);
+    pk_tc_epi e;
+    memset(&e, 0, sizeof(e));
+    e.mode = PK_TC_STORE;
+    e.C = C;
+    return proj_tc(m, b, k, M, A, &e, stream);
+}
+
+/* FF linear1 with its bias and Swish in the GEMM's epilogue: h = Swish(A W + b1). */
+static int proj_swish(pkcu_encoder_model *m, int b, int k, int M, const float *A, const float *b1, float *h,
+                      pkcu_stream_t stream)
+{
+    pk_tc_epi e;
+    memset(&e, 0, sizeof(e));
+    e.mode = PK_TC_SWISH;
+    e.bias = b1;
+    e.C = h;
+    return proj_tc(m, b, k, M, A, &e, stream);
 }
 
 static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
@@ -417,6 +378,28 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     const pkcu_gemm_inputs *gi = f->gi;
     const int n = f->seq->dev.n_items, uni = f->seq->dev.uniform_T;
     const long long F = f->seq->frames;
+    const pkcu_block_params *p = &f->m->params[b];
+    if (f->fused) {   /* the projections whose epilogues the sequence leaves to the GEMM */
+        switch (gemm) {
+        case PKCU_GEMM_FF1_1: return proj_swish(f->m, b, W_FF1_1, (int)F, gi->ln_ff1, p->ff1_b1, gi->h1, stream);
+        case PKCU_GEMM_FF2_1: return proj_swish(f->m, b, W_FF2_1, (int)F, gi->ln_ff2, p->ff2_b1, gi->h2, stream);
+        case PKCU_GEMM_QKV: {
+            pk_tc_epi e;
+            memset(&e, 0, sizeof(e));
+            e.mode = PK_TC_QKV;
+            e.bias = p->qkv_b;
+            e.u = p->pos_u;
+            e.v = p->pos_v;
+            e.Qu = gi->Qu;
+            e.Qv = gi->Qv;
+            e.K = gi->K;
+            e.V = gi->V;
+            e.seq = f->seq;
+            return proj_tc(f->m, b, W_QKV, (int)F, gi->ln_sa, &e, stream);
+        }
+        default: break;
+        }
+    }
     switch (gemm) {   /* the row-major projections of the whole batch */
     case PKCU_GEMM_FF1_1: return proj_w(f->m, h, b, W_FF1_1, (int)F, gi->ln_ff1, gemm_dst(go->ff1_h), stream);
     case PKCU_GEMM_FF1_2: return proj_w(f->m, h, b, W_FF1_2, (int)F, gi->h1, gemm_dst(go->ff1_out), stream);
@@ -540,9 +523,14 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
         }
         m->split_cap = need;
     }
-    Fwd f = {m, gemm_out, gemm_in, seq, off};
-    const int st = pkcu_encoder_nongemm(x, m->params, m->n_blocks, gemm_out, gemm_in, seq, fwd_hook,
-                                        &f, stream);
+    /* with every projection on the tcgen05 GEMM, bias+Swish and the QKV split
+     * run in its epilogues */
+    int all_tc = m->stacks != NULL;
+    for (int b = 0; b < m->n_blocks && all_tc; b++)
+        all_tc = m->stack[b][W_FF1_1] && m->stack[b][W_FF2_1] && m->stack[b][W_QKV];
+    Fwd f = {m, gemm_out, gemm_in, seq, off, all_tc ? (PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV) : 0u};
+    const int st = pkcu_encoder_nongemm_fused(x, m->params, m->n_blocks, gemm_out, gemm_in, seq, fwd_hook,
+                                              &f, f.fused, stream);
     free(off);
     return st;
 }

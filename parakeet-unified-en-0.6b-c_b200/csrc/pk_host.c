@@ -65,23 +65,25 @@ int pkcu_device(void)
 int pkcu_wait_timeouts(unsigned *count, int reset)
 {
     if (!count) return pkcu_fail(PKCU_ERR_ARG, "pkcu_wait_timeouts: NULL count");
-    unsigned a = 0, b = 0;
-    if (pk_softmax_wait_timeouts(&a, reset) != PKCU_OK || pk_conv_wait_timeouts(&b, reset) != PKCU_OK)
+    unsigned a = 0, b = 0, c = 0;
+    if (pk_softmax_wait_timeouts(&a, reset) != PKCU_OK || pk_conv_wait_timeouts(&b, reset) != PKCU_OK ||
+        pk_tc_wait_timeouts(&c, reset) != PKCU_OK)
         return pkcu_fail(PKCU_ERR_CUDA, "pkcu_wait_timeouts: reading the device counters failed");
-    *count = a + b;
+    *count = a + b + c;
     return PKCU_OK;
 }
 
 int pk_check_wait_timeouts(const char *what)
 {
-    unsigned a = 0, b = 0;
-    if (pk_softmax_wait_timeouts(&a, 1) != PKCU_OK || pk_conv_wait_timeouts(&b, 1) != PKCU_OK) {
+    unsigned a = 0, b = 0, c = 0;
+    if (pk_softmax_wait_timeouts(&a, 1) != PKCU_OK || pk_conv_wait_timeouts(&b, 1) != PKCU_OK ||
+        pk_tc_wait_timeouts(&c, 1) != PKCU_OK) {
         cudaGetLastError();
         return pkcu_fail(PKCU_ERR_CUDA, "%s: reading the device wait counters failed", what);
     }
-    if (a + b)
+    if (a + b + c)
         return pkcu_fail(PKCU_ERR_CUDA, "%s: %u bounded device wait(s) ran out; outputs are incomplete",
-                         what, a + b);
+                         what, a + b + c);
     return PKCU_OK;
 }
 
@@ -414,8 +416,20 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
                          const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
                          pkcu_stream_t stream)
 {
+    return pkcu_encoder_nongemm_fused(x, blocks, n_blocks, go, gi, seq, hook, hook_user, 0u, stream);
+}
+
+int pkcu_encoder_nongemm_fused(float *x, const pkcu_block_params *blocks, int n_blocks,
+                               const pkcu_gemm_outputs *go, const pkcu_gemm_inputs *gi,
+                               const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
+                               unsigned fused, pkcu_stream_t stream)
+{
     if (!x || !blocks || n_blocks < 0 || !go || !gi || !seq)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: NULL argument");
+    if (fused & ~(unsigned)(PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV))
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: unknown fusion flags 0x%x", fused);
+    if (fused && !hook)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: fusion flags without a GEMM hook");
     if (n_blocks == 0 || seq->frames == 0) return PKCU_OK;
     if (seq->frames > 0x7fffffffLL / PK_FF)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: too many frames in one call");
@@ -430,14 +444,16 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
         const pkcu_block_params *nx = (b + 1 < n_blocks) ? &blocks[b + 1] : NULL;
         /* FF1 (csrc/encoder.c:179-217) */
         PK_HOOK(b, PKCU_GEMM_FF1_1);
-        PK_TRY(pkcu_bias_swish_rows(go->ff1_h, p->ff1_b1, gi->h1, F, PK_FF, stream));
+        if (!(fused & PKCU_FUSED_FF_SWISH))
+            PK_TRY(pkcu_bias_swish_rows(go->ff1_h, p->ff1_b1, gi->h1, F, PK_FF, stream));
         PK_HOOK(b, PKCU_GEMM_FF1_2);
         PK_TRY(pkcu_residual_layer_norm(x, go->ff1_out, p->ff1_b2, 0.5f, p->norm_sa_w, p->norm_sa_b,
                                         gi->ln_sa, F, stream));
         /* self-attention (csrc/encoder.c:297-435) */
         PK_HOOK(b, PKCU_GEMM_QKV);
-        PK_TRY(pkcu_qkv_split_uv(go->qkv, p->qkv_b, p->pos_u, p->pos_v, gi->Qu, gi->Qv, gi->K, gi->V,
-                                 seq, stream));
+        if (!(fused & PKCU_FUSED_QKV))
+            PK_TRY(pkcu_qkv_split_uv(go->qkv, p->qkv_b, p->pos_u, p->pos_v, gi->Qu, gi->Qv, gi->K,
+                                     gi->V, seq, stream));
         PK_HOOK(b, PKCU_GEMM_POS);
         PK_TRY(pkcu_pos_head_split(go->P, gi->P_h, seq, stream));
         PK_HOOK(b, PKCU_GEMM_AC);
@@ -457,7 +473,8 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
                                              gi->ln_ff2, seq, stream));
         /* FF2 and the block's final LN (csrc/encoder.c:489-490) */
         PK_HOOK(b, PKCU_GEMM_FF2_1);
-        PK_TRY(pkcu_bias_swish_rows(go->ff2_h, p->ff2_b1, gi->h2, F, PK_FF, stream));
+        if (!(fused & PKCU_FUSED_FF_SWISH))
+            PK_TRY(pkcu_bias_swish_rows(go->ff2_h, p->ff2_b1, gi->h2, F, PK_FF, stream));
         PK_HOOK(b, PKCU_GEMM_FF2_2);
         PK_TRY(pkcu_residual_layer_norm2(x, go->ff2_out, p->ff2_b2, 0.5f, p->norm_out_w,
                                          p->norm_out_b, nx ? nx->norm_ff1_w : NULL,

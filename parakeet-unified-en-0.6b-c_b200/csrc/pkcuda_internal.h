@@ -52,6 +52,32 @@ int pkcu_device(void);
  * k_conv.cu); read and optionally reset on the current device. */
 int pk_softmax_wait_timeouts(unsigned *count, int reset);
 int pk_conv_wait_timeouts(unsigned *count, int reset);
+int pk_tc_wait_timeouts(unsigned *count, int reset);   /* k_tcgemm.cu */
+
+/* The library's tcgen05 GEMM (k_tcgemm.cu): C = epilogue(alpha * A W) with A
+ * given as its three bf16 parts [M, 3K] (pk_split_rows_bf16x3) and W as
+ * npb K-major bf16 planes [N, npb K] (pk_tc_prepare); K % 32 == 0, N % 32 == 0. */
+#define PK_TC_STORE 0   /* C = alpha A W (+ bias) (+ beta C)            */
+#define PK_TC_SWISH 1   /* C = Swish(alpha A W + bias)                  */
+#define PK_TC_RESID 2   /* C += rscale (alpha A W + bias), one FMA      */
+#define PK_TC_QKV   3   /* the QKV head split with pos_bias_u / v       */
+typedef struct {
+    int mode;
+    float alpha, beta, rscale;
+    const float *bias;
+    float *C;
+    long long ldc;                       /* 0: N */
+    const float *u, *v;                  /* QKV: pos_bias_u / v [8, 128] */
+    float *Qu, *Qv, *K, *V;              /* QKV: per-item [8, T, 128] outputs */
+    const pkcu_seq *seq;                 /* QKV: the batch (M = its frames) */
+} pk_tc_epi;
+/* W [K, N] (bits 32: fp32, 8: int8 with per-tensor scale) -> planes: one
+ * [N, K] plane of q for int8 (alpha = scale), else three [N, 3K] parts. */
+int pk_tc_prepare(const void *data, int bits, float scale, int K, int N, void *planes, float *alpha,
+                  pkcu_stream_t stream);
+int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
+               const pk_tc_epi *ep, pkcu_stream_t stream);
+
 /* For synchronous entry points, after their final synchronisation: reads and
  * resets both counters and returns PKCU_ERR_CUDA (with a message naming what)
  * when any wait ran out since the last reset, anywhere in the process on this

@@ -61,6 +61,9 @@ EXPORTED = (
     "pkcu_should_chunk", "pkcu_chunk_bounds", "pkcu_chunk_plan_create", "pkcu_chunk_plan_destroy", "pkcu_chunk_plan_seq",
     "pkcu_chunk_plan_chunked", "pkcu_chunk_plan_items", "pkcu_chunk_plan_item", "pkcu_chunk_split",
     "pkcu_chunk_stitch", "pkcu_asr_encode", "pkcu_asr_set_chunk_mode",
+    "pkcu_weight_create", "pkcu_weight_destroy", "pkcu_wmatmul_work_bytes", "pkcu_wmatmul",
+    "pkcu_wmatmul_bias_swish", "pkcu_wmatmul_bias_residual", "pkcu_wmatmul_qkv",
+    "pkcu_encoder_nongemm_fused",
 )
 
 
@@ -165,6 +168,7 @@ _SIGS = {
     "pkcu_joint_add_act": (I, [VP, VP, VP, I, I, I, I, VP]),
     "pkcu_argmax_rows": (I, [VP, VP, LL, I, VP]),
     "pkcu_encoder_nongemm": (I, [VP, VP, I, VP, VP, VP, VP, VP, VP]),
+    "pkcu_encoder_nongemm_fused": (I, [VP, VP, I, VP, VP, VP, VP, VP, C.c_uint, VP]),
     "pkcu_encoder_nongemm_launches": (I, [I]),
     "pkcu_encoder_ws_create": (I, [VP, I, C.POINTER(VP)]),
     "pkcu_encoder_ws_destroy": (None, [VP]),
@@ -185,6 +189,13 @@ _SIGS = {
     "pkcu_chunk_stitch": (I, [VP, VP, VP, VP]),
     "pkcu_asr_encode": (I, [VP, VP, C.POINTER(I), I, VP, VP]),
     "pkcu_asr_set_chunk_mode": (I, [VP, I]),
+    "pkcu_weight_create": (I, [VP, I, F, VP, I, I, I, I, VP, C.POINTER(VP)]),
+    "pkcu_weight_destroy": (None, [VP]),
+    "pkcu_wmatmul_work_bytes": (LL, [I, I]),
+    "pkcu_wmatmul": (I, [VP, VP, VP, I, F, F, VP, VP]),
+    "pkcu_wmatmul_bias_swish": (I, [VP, VP, VP, VP, I, VP, VP]),
+    "pkcu_wmatmul_bias_residual": (I, [VP, VP, VP, VP, F, I, VP, VP]),
+    "pkcu_wmatmul_qkv": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, VP]),
 }
 
 _lib = None
@@ -300,6 +311,37 @@ GEMM_OUT_FIELDS = ("ff1_h", "ff1_out", "qkv", "P", "ac", "bd", "attn_h", "att_ou
                    "ff2_h", "ff2_out")
 GEMM_IN_FIELDS = ("ln_ff1", "h1", "ln_sa", "Qu", "K", "Qv", "P_h", "S", "V", "attn", "cf", "dw",
                   "ln_ff2", "h2", "gated")
+
+
+class Weight:
+    """pkcu_weight: a GEMM weight prepared for the tcgen05 weight products
+    (bits 32: fp32 [K, N]; 8: int8 [K, N] with scale; 4: packed int4 [K, N/2]
+    with group scales)."""
+
+    def __init__(self, data, bits, K, N, scale=0.0, scales=None, group=32, axis=PKCU_GROUP_ALONG_N,
+                 stream=None):
+        h = VP()
+        call("pkcu_weight_create", data if isinstance(data, int) else ptr(data), int(bits), float(scale),
+             None if scales is None else (scales if isinstance(scales, int) else ptr(scales)), int(group),
+             int(axis), int(K), int(N), stream_handle(stream), C.byref(h))
+        self.handle, self.K, self.N = h, K, N
+
+    def close(self):
+        if self.handle:
+            lib().pkcu_weight_destroy(self.handle)
+            self.handle = VP()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class ChunkPlan:

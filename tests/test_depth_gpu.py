@@ -17,11 +17,10 @@ the data-movement outputs) holds at every depth:
     (csrc/encoder.c:531-543), one ragged batch.
 
 The free-running drift (GPU chain against the restatement's own chain, no
-teacher forcing) is measured in the same run and bounded by the drift of the
+teacher forcing) is measured in the same run beside the drift of the
 reference's own build against the same restatement over the same blocks
-(test_free_running_drift_tracks_reference_build): after 24 renormalised
-blocks both differ from the IEEE restatement by rounding-order growth of the
-same size."""
+(test_free_running_drift_tracks_reference_build): every block ends in a
+LayerNorm, so neither grows with depth (both stay near 1e-6 over 24 blocks)."""
 import numpy as np
 import pytest
 
@@ -141,7 +140,6 @@ def test_free_running_drift_tracks_reference_build(cuda, oracle, reference):
     print("block  |gpu - restatement|  |reference build - restatement|")
     for b, (a, c) in enumerate(zip(d_gpu, d_ref)):
         print(f"{b:5d}  {a:.3e}  {c:.3e}")
-    # the relaxed free-running bound (2e-5 abs / 1e-4 rel) that the 24-block
-    # chain tests use is of the same order as the reference build's own drift
-    assert max(d_gpu) <= max(4 * max(d_ref), 2e-5), (d_gpu, d_ref)
+    # within the north-star tolerance, like the reference build's own drift
+    assert max(d_gpu) <= max(2 * max(d_ref), 2e-6), (d_gpu, d_ref)
     assert np.isfinite(x_out).all()

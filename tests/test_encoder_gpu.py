@@ -122,10 +122,12 @@ def test_encoder_nongemm_host_buffers(cuda, oracle, lengths, n_groups):
         assert_close(L.frames_of(got, i), x, f"x item {i}")
 
 
-def test_encoder_nongemm_vs_reference_block(cuda, reference):
-    """One block against the reference's own conformer_block (csrc/encoder.c:482)."""
-    blocks, items = make_batch([41], 1, seed=4141)
-    L, gx, got = run_gpu(cuda, [41], blocks, items)
+@pytest.mark.parametrize("T", [41, 375])
+def test_encoder_nongemm_vs_reference_block(cuda, reference, T):
+    """One block against the reference's own conformer_block (csrc/encoder.c:482),
+    also at the bench's T = 375."""
+    blocks, items = make_batch([T], 1, seed=4100 + T)
+    L, gx, got = run_gpu(cuda, [T], blocks, items)
     si, x = items[0]
     xr, caps = reference.conformer_block(x, blocks[0], si)
     assert_close(gx, xr, "x")
@@ -144,11 +146,12 @@ def test_chunked_long_audio_24_blocks(cuda, oracle):
     for i, (si, x) in enumerate(items):
         for p in blocks:
             x, caps = oracle.conformer_block(x, p, si)
-        # 24 renormalised blocks: per-op rounding differences compound slightly
-        assert_close(L.frames_of(gx, i), x, f"x chunk {i}", atol=2e-5, rtol=1e-4)
+        # 24 free-running blocks: every block ends in a LayerNorm, so rounding
+        # differences do not compound (measured drift about 1.4e-6, as for the
+        # reference's own build against the restatement: test_depth_gpu.py)
+        assert_close(L.frames_of(gx, i), x, f"x chunk {i}")
         for role in ("S", "dw", "h2", "ln_ff2"):
-            assert_close(item_view(L, role, got[role], i), caps[role], f"{role} chunk {i}",
-                         atol=2e-5, rtol=1e-4)
+            assert_close(item_view(L, role, got[role], i), caps[role], f"{role} chunk {i}")
     assert np.isfinite(gx).all()
 
 
@@ -160,5 +163,5 @@ def test_encoder_nongemm_24_blocks_stays_bounded(cuda, oracle):
     si, x = items[0]
     for p in blocks:
         x, caps = oracle.conformer_block(x, p, si)
-    assert_close(gx, x, "x after 24 blocks", atol=2e-5, rtol=1e-4)
+    assert_close(gx, x, "x after 24 blocks")
     assert np.isfinite(gx).all()
