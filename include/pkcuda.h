@@ -335,10 +335,17 @@ int pkcu_encoder_nongemm(float *x, const pkcu_block_params *blocks, int n_blocks
  *   PKCU_FUSED_FF_SWISH -- the FF1_1 / FF2_1 hooks write Swish(x W + b1) into
  *     gemm_in->h1 / h2 themselves; the sequence's bias+Swish steps are skipped;
  *   PKCU_FUSED_QKV -- the QKV hook writes Qu, Qv, K, V (bias, head split and
- *     pos_bias_u / v, as pkcu_qkv_split_uv) itself; that step is skipped.
- * The skipped GEMM outputs (ff1_h, ff2_h, qkv) are then not read. */
+ *     pos_bias_u / v, as pkcu_qkv_split_uv) itself; that step is skipped;
+ *   PKCU_FUSED_CONV -- the conv module's GEMMs carry its epilogues: the
+ *     sequence writes LN_conv time-first ([frames, 1024]) into gemm_in->cf,
+ *     the PW1 hook writes the GLU output (bias included) into gemm_in->gated
+ *     (per item [1024, T]), the depthwise conv reads it, and the PW2 hook adds
+ *     pw2 + bias to x itself (the residual of csrc/encoder.c:475-477); the
+ *     sequence then takes LN_ff2 of x.
+ * The skipped GEMM outputs (ff1_h, ff2_h, qkv, pw1, pw2) are then not read. */
 #define PKCU_FUSED_FF_SWISH 1u
 #define PKCU_FUSED_QKV      2u
+#define PKCU_FUSED_CONV     4u
 int pkcu_encoder_nongemm_fused(float *x, const pkcu_block_params *blocks, int n_blocks,
                                const pkcu_gemm_outputs *gemm_out, const pkcu_gemm_inputs *gemm_in,
                                const pkcu_seq *seq, pkcu_gemm_hook hook, void *hook_user,
@@ -468,6 +475,21 @@ int pkcu_wmatmul_bias_residual(const float *A, const pkcu_weight *W, const float
 int pkcu_wmatmul_qkv(const float *A, const pkcu_weight *W, const float *bqkv, const float *u,
                      const float *v, float *Qu, float *Qv, float *K, float *V, const pkcu_seq *seq,
                      void *work, pkcu_stream_t stream);
+
+/* pk_pointwise_conv1d (csrc/tensor_ops.c:579-590) on the same GEMM: x [Cin, T]
+ * channel-first, W [Cout, Cin] (float32, as the reference stores it; prepared
+ * once, synchronous; glu != 0 prepares it for pkcu_pointwise_conv1d_glu),
+ * out [Cout, T] = W x + b[c]; b may be NULL. Work: pkcu_wmatmul_work_bytes(T,
+ * Cin) bytes. Cin a multiple of 32, Cout of 32 (64 with glu). */
+int pkcu_conv_weight_create(const float *w, int Cout, int Cin, int glu, pkcu_stream_t stream,
+                            pkcu_weight **out);
+int pkcu_pointwise_conv1d(const float *x, const pkcu_weight *W, const float *b, float *out, int T,
+                          void *work, pkcu_stream_t stream);
+/* The first pointwise convolution and the GLU after it (csrc/encoder.c:454-465)
+ * in one pass: gated [Cout/2, T] = a * 1/(1 + expf(-g)), a = rows [0, Cout/2)
+ * of W x + b, g = rows [Cout/2, Cout). */
+int pkcu_pointwise_conv1d_glu(const float *x, const pkcu_weight *W, const float *b, float *gated, int T,
+                              void *work, pkcu_stream_t stream);
 
 /* ── the encoder stack on the GPU, GEMMs included ──────────────────────────
  * Replaces encode_blocks (csrc/encoder.c:495-512) for a batch: fp32 device

@@ -140,6 +140,7 @@ _REF_SIGS = {
     "pkref_manifest_scales": (C.c_int, [C.c_char_p, C.POINTER(C.c_char_p), C.c_int, FP]),
     "pkref_pre_encode": (C.c_int, [FP, C.c_int, FPP, FP, FP, FP, FP, FP, FP, FP]),
     "pk_wmatmul": (None, [FP, C.c_void_p, FP, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float]),
+    "pk_pointwise_conv1d": (None, [FP, FP, FP, FP, C.c_int, C.c_int, C.c_int]),
 }
 
 
@@ -577,6 +578,17 @@ class Reference:
             w = RefWeight(W.ctypes.data, float(scale), FP(), 8)
         out = np.zeros((M, N), np.float32) if C_in is None else f32(C_in).copy()
         self.L.pk_wmatmul(_fp(A), C.byref(w), _fp(out), M, N, K, float(alpha), float(beta))
+        return out
+
+    def pointwise_conv1d(self, x, w, b):
+        """The reference's pk_pointwise_conv1d (csrc/tensor_ops.c:579-590):
+        out [Cout, T] = w [Cout, Cin] x [Cin, T] (cblas_sgemm) + b[c]."""
+        x, w = f32(x), f32(w)
+        Cin, T = x.shape
+        Cout = w.shape[0]
+        out = np.empty((Cout, T), np.float32)
+        self.L.pk_pointwise_conv1d(_fp(x), _fp(w), _fp(f32(b)) if b is not None else FP(), _fp(out),
+                                   Cin, Cout, T)
         return out
 
     def ff_linear1(self, A, W, b):

@@ -160,6 +160,7 @@ struct Epi {
   const float *u, *v;
   float *Qu, *Qv, *Kh, *Vh;
   SeqDev seq;
+  int channels;          // CF / GLU: output channels per frame (GLU: C, half of N)
 };
 
 // Item of frame r: a division for a uniform batch, else a binary search of
@@ -175,8 +176,45 @@ __device__ __forceinline__ int item_of_row(const Epi &e, long long r) {
   return lo;
 }
 
+// Channel-first store of 32 channels c0 .. c0 + 31 of frame r: each item's
+// output is [channels, T] (the pointwise convolutions' layout,
+// csrc/tensor_ops.c:579-590), at element f0 * channels; the lanes of a warp
+// hold consecutive frames, so each channel's 32 stores are contiguous.
+__device__ __forceinline__ void store_cf32(const Epi &e, long long r, int c0, int channels, const float (&v)[32]) {
+  const int item = item_of_row(e, r);
+  const long long f0 = seq_frame_off(e.seq, item);
+  const int T = seq_T(e.seq, item);
+  float *o = e.C + f0 * channels + (long long)c0 * T + (r - f0);
+#pragma unroll
+  for (int j = 0; j < 32; j++) o[(long long)j * T] = v[j];
+}
+
+// The GLU of the first pointwise convolution (csrc/encoder.c:454-465) on 32
+// channel pairs: a = the 32 "value" channels d0 .. d0 + 31, g = their gates
+// d0 + C .. (the weight's rows are interleaved in groups of 32 at
+// preparation, so both halves of a pair sit in one thread's columns);
+// bias as pk_pointwise_conv1d adds it, then a * 1/(1 + expf(-g)).
+__device__ __forceinline__ void epi_glu32(const Epi &e, long long r, int d0, int C, float (&a)[32],
+                                          const float (&g)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    const float va = e.bias ? a[j] + __ldg(e.bias + d0 + j) : a[j];
+    const float vb = e.bias ? g[j] + __ldg(e.bias + C + d0 + j) : g[j];
+    a[j] = va * sigmoid_libm(vb);
+  }
+  store_cf32(e, r, d0, C, a);
+}
+
 // Finishes 32 columns n0 .. n0 + 31 of row r (all < N when the row exists).
 __device__ __forceinline__ void epi_store32(const Epi &e, long long r, int n0, float (&v)[32]) {
+  if (e.mode == PK_TC_CF) {
+    if (e.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = v[j] + __ldg(e.bias + n0 + j);
+    }
+    store_cf32(e, r, n0, e.channels, v);
+    return;
+  }
   if (e.mode == PK_TC_QKV) {
     // n0 .. n0+31 lie in one head of one of Q, K, V (32 | 128)
     const int part = n0 >> 10, h = (n0 & 1023) >> 7, d0 = n0 & 127;
@@ -389,7 +427,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (lane == 0) mbar_arrive(acc_empty + buf);
     }
     const long long r = (long long)m0 + row;
-    if (ok && r < M) {
+    if (ok && r < M && epi.mode == PK_TC_GLU) {
+      // columns 64k .. 64k + 31 hold value channels 32k .., the next 32 their gates
+#pragma unroll
+      for (int c = 0; c < 4; c += 2) {
+        const int n = n0 + half * 128 + c * 32;
+        if (n < N) {
+          float a[32], g[32];
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            a[j] = sum[c * 32 + j] * epi.alpha;
+            g[j] = sum[(c + 1) * 32 + j] * epi.alpha;
+          }
+          epi_glu32(epi, r, n / 2, epi.channels, a, g);
+        }
+      }
+    } else if (ok && r < M) {
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         const int n = n0 + half * 128 + c * 32;
@@ -454,6 +507,68 @@ __global__ void prep_q8_t_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__
   for (int i = ty; i < 32; i += 8) {
     const int n = nb + i, k = k0 + tx;
     if (n < N && k < K) out[(long long)n * K + k] = __float2bfloat16_rn(tile[tx][i]);
+  }
+}
+
+// A pointwise-convolution weight W [N, K] (out channels x in channels, already
+// K-major) -> planes [N, 3K], row n' = [w0 | w1 | w2] of source row src(n').
+// With glu (N = 2C) the rows are interleaved in groups of 32: rows 64k .. 64k+31
+// are value channels 32k .., rows 64k+32 .. 64k+63 their gates C + 32k ..
+__global__ void prep_split_rows_kernel(const float *__restrict__ W, __nv_bfloat16 *__restrict__ out, int N, int K,
+                                       int glu) {
+  const long long total = (long long)N * K;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(e / K), k = (int)(e - (long long)n * K);
+    int src = n;
+    if (glu) {
+      const int blk = n >> 6, w = n & 63;
+      src = w < 32 ? blk * 32 + w : (N >> 1) + blk * 32 + (w - 32);
+    }
+    const float x = __ldg(W + (long long)src * K + k);
+    const __nv_bfloat16 p0 = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(p0);
+    const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+    __nv_bfloat16 *o = out + (long long)n * 3 * K + k;
+    o[0] = p0;
+    o[K] = p1;
+    o[2 * K] = p2;
+  }
+}
+
+// Channel-first items X [C, T_b] (item after item) -> time-first parts
+// [frames, 3C], row f0_b + t = [x0 | x1 | x2] of column t: the operand of a
+// pointwise convolution as a K-major matrix. 32 x 32 tiles through shared
+// memory; blockIdx.z = item.
+__global__ void split_cf_t_kernel(const float *__restrict__ X, __nv_bfloat16 *__restrict__ out, int C,
+                                  SeqDev seq) {
+  __shared__ float tile[32][33];
+  const int item = blockIdx.z;
+  const int T = seq_T(seq, item);
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  if (t0 >= T) return;
+  const long long f0 = seq_frame_off(seq, item);
+  const float *x = X + f0 * C;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + tx;
+    tile[i][tx] = (c < C && t < T) ? __ldg(x + (long long)c * T + t) : 0.0f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + tx;
+    if (t < T && c < C) {
+      const float v = tile[tx][i];
+      const __nv_bfloat16 p0 = __float2bfloat16_rn(v);
+      const float r1 = v - __bfloat162float(p0);
+      const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+      __nv_bfloat16 *o = out + (f0 + t) * 3 * C + c;
+      o[0] = p0;
+      o[C] = p1;
+      o[2 * C] = p2;
+    }
   }
 }
 
@@ -540,6 +655,22 @@ extern "C" int pk_tc_prepare(const void *data, int bits, float scale, int K, int
   return pkcu_launch_status("tcgen05 GEMM weight preparation");
 }
 
+extern "C" int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *planes, pkcu_stream_t stream) {
+  const long long total = (long long)N * K;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  tc::prep_split_rows_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(W, static_cast<__nv_bfloat16 *>(planes), N,
+                                                                       K, glu);
+  return pkcu_launch_status("tcgen05 GEMM pointwise weight preparation");
+}
+
+extern "C" int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream) {
+  if (!X || !parts || !seq || C <= 0) return pkcu_fail(PKCU_ERR_ARG, "pk_split_cf_t: bad argument");
+  const dim3 grid((unsigned)((seq->dev.max_T + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)seq->dev.n_items);
+  tc::split_cf_t_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(X, static_cast<__nv_bfloat16 *>(parts), C,
+                                                                seq->dev);
+  return pkcu_launch_status("pk_split_cf_t");
+}
+
 extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                           const pk_tc_epi *ep, pkcu_stream_t stream) {
   if (!a_parts || !planes || !ep || (npb != 1 && npb != 3) || M <= 0 || N <= 0 || K <= 0 ||
@@ -565,11 +696,16 @@ extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int 
   e.Vh = ep->V;
   if (ep->seq) e.seq = ep->seq->dev;
   else memset(&e.seq, 0, sizeof(e.seq));
+  e.channels = e.mode == PK_TC_GLU ? N / 2 : N;
+  if ((e.mode == PK_TC_CF || e.mode == PK_TC_GLU) &&
+      (!ep->seq || !e.C || M != ep->seq->frames || (e.mode == PK_TC_GLU && N % 64)))
+    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: a channel-first epilogue needs the batch and its output");
   if (e.mode == PK_TC_QKV &&
       (!ep->seq || !e.bias || !e.u || !e.v || !e.Qu || !e.Qv || !e.Kh || !e.Vh || N != 3 * PK_D ||
        M != ep->seq->frames))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the QKV epilogue needs the batch and its outputs");
-  if (e.mode != PK_TC_QKV && (!e.C || !PK_ALIGNED16(e.C) || e.ldc % 4))
+  if ((e.mode == PK_TC_STORE || e.mode == PK_TC_SWISH || e.mode == PK_TC_RESID) &&
+      (!e.C || !PK_ALIGNED16(e.C) || e.ldc % 4))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: output must be 16-byte aligned rows");
   return npb == 1 ? launch<1>(ma, mb, M, N, K, e, (cudaStream_t)stream)
                   : launch<3>(ma, mb, M, N, K, e, (cudaStream_t)stream);
@@ -581,6 +717,8 @@ struct pkcu_weight {
   int K, N, bits, npb;
   float alpha;      // the int8 scale (1 for the three-part planes)
   void *planes;     // [N, npb K] bf16
+  int conv;         // a pointwise-convolution weight (N = out channels, K = in channels)
+  int glu;          // its rows interleaved value / gate for the GLU epilogue
 };
 
 extern "C" void pkcu_weight_destroy(pkcu_weight *w) {
@@ -710,4 +848,85 @@ extern "C" int pkcu_wmatmul_qkv(const float *A, const pkcu_weight *W, const floa
   e.V = V;
   e.seq = seq;
   return wm_run("pkcu_wmatmul_qkv", A, W, (int)seq->frames, work, e, stream);
+}
+
+// ── public entry points: pointwise convolutions (csrc/tensor_ops.c:579-590) ──
+
+extern "C" int pkcu_conv_weight_create(const float *w, int Cout, int Cin, int glu, pkcu_stream_t stream,
+                                       pkcu_weight **out) {
+  if (!out) return pkcu_fail(PKCU_ERR_ARG, "pkcu_conv_weight_create: NULL out");
+  *out = nullptr;
+  if (!w || Cout <= 0 || Cin <= 0 || Cin % tc::BK || Cout % (glu ? 64 : 32))
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_conv_weight_create: Cin %d must be a multiple of 32, Cout %d of %d",
+                     Cin, Cout, glu ? 64 : 32);
+  pkcu_weight *p = (pkcu_weight *)calloc(1, sizeof(*p));
+  if (!p) return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_conv_weight_create: host allocation");
+  p->K = Cin;
+  p->N = Cout;
+  p->bits = 32;
+  p->npb = 3;
+  p->alpha = 1.0f;
+  p->conv = 1;
+  p->glu = glu != 0;
+  const size_t bytes = (size_t)3 * Cin * Cout * 2;
+  if (cudaMalloc(&p->planes, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    p->planes = nullptr;
+    pkcu_weight_destroy(p);
+    return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_conv_weight_create: %zu bytes", bytes);
+  }
+  int st = pk_tc_prepare_rows(w, Cout, Cin, p->glu, p->planes, stream);
+  if (!st && cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+    st = pkcu_fail(PKCU_ERR_CUDA, "pkcu_conv_weight_create: %s", cudaGetErrorString(cudaGetLastError()));
+  if (st) {
+    pkcu_weight_destroy(p);
+    return st;
+  }
+  *out = p;
+  return PKCU_OK;
+}
+
+namespace {
+
+// One utterance of T frames as a batch descriptor (uniform: no device arrays).
+pkcu_seq one_item(int T) {
+  pkcu_seq q;
+  memset(&q, 0, sizeof(q));
+  q.dev.n_items = 1;
+  q.dev.uniform_T = T;
+  q.dev.max_T = T;
+  q.frames = T;
+  return q;
+}
+
+int pw_run(const char *what, const float *x, const pkcu_weight *W, const float *b, float *out, int T,
+           int glu, void *work, pkcu_stream_t stream) {
+  if (!x || !W || !out || !work || T <= 0 || !W->conv)
+    return pkcu_fail(PKCU_ERR_ARG, "%s: bad argument (a pkcu_conv_weight_create weight)", what);
+  if (glu != W->glu)
+    return pkcu_fail(PKCU_ERR_ARG, "%s: the weight was prepared %s the GLU interleave", what,
+                     glu ? "without" : "with");
+  if (!PK_ALIGNED16(work)) return pkcu_fail(PKCU_ERR_ARG, "%s: work must be 16-byte aligned", what);
+  pkcu_seq q = one_item(T);
+  int st = pk_split_cf_t(x, work, W->K, &q, stream);
+  if (st) return st;
+  pk_tc_epi e = {};
+  e.mode = glu ? PK_TC_GLU : PK_TC_CF;
+  e.alpha = 1.0f;
+  e.bias = b;
+  e.C = out;
+  e.seq = &q;
+  return pk_tc_gemm(work, W->planes, 3, T, W->N, W->K, &e, stream);
+}
+
+}  // namespace
+
+extern "C" int pkcu_pointwise_conv1d(const float *x, const pkcu_weight *W, const float *b, float *out, int T,
+                                     void *work, pkcu_stream_t stream) {
+  return pw_run("pkcu_pointwise_conv1d", x, W, b, out, T, 0, work, stream);
+}
+
+extern "C" int pkcu_pointwise_conv1d_glu(const float *x, const pkcu_weight *W, const float *b, float *gated,
+                                         int T, void *work, pkcu_stream_t stream) {
+  return pw_run("pkcu_pointwise_conv1d_glu", x, W, b, gated, T, 1, work, stream);
 }

@@ -45,10 +45,10 @@ static const long long W_ELEMS[W_N] = {
 /* [K, N] of each weight as the product x W reads it (row-major, [in, out]). */
 static const int W_K[W_N] = {PK_D, PK_FF, PK_D, PK_D, PK_D, PK_D, PK_D, PK_D, PK_FF};
 static const int W_COLS[W_N] = {PK_FF, PK_D, 3 * PK_D, PK_D, PK_D, 2 * PK_D, PK_D, PK_FF, PK_D};
-/* Every block weight runs on split operands: 1 = the right-hand operand of a
- * row-major projection, kept as K-major planes for the tcgen05 GEMM
- * (k_tcgemm.cu); 2 = the left-hand operand of a pointwise convolution, kept as
- * rows [w0 | w1 | w2] (k_split.cu). */
+/* Every block weight runs on the tcgen05 GEMM (k_tcgemm.cu) as K-major bf16
+ * planes: 1 = a row-major projection's [K, N] weight, transposed to [N, K]
+ * (int8: q; else three parts); 2 = a pointwise convolution's [out, in] weight,
+ * three parts as it is (the first one's rows interleaved value / gate). */
 static const int W_SPLIT[W_N] = {1, 1, 1, 1, 1, 2, 2, 1, 1};
 
 struct pkcu_encoder_model {
@@ -59,8 +59,8 @@ struct pkcu_encoder_model {
     pkcu_block_params params[64];
     const float *pe;                   /* pos_encoding.pe_table [9999, 1024] */
     void *stacks;                      /* bf16 operands of the W_SPLIT weights */
-    const void *stack[64][W_N];        /* projections: K-major planes [N, K] (int8 q) or [N, 3K] (parts);
-                                          pointwise: rows [w0 | w1 | w2]; NULL: the fp32 path */
+    const void *stack[64][W_N];        /* K-major planes [N, K] (int8 q) or [N, 3K] (three parts);
+                                          NULL: the fp32 path */
     float qscale[64][W_N];             /* > 0: the int8 weight's scale, w = q x this */
     void *split_ws;                    /* activation parts [rows, 3K] bf16, grown per forward */
     size_t split_cap;                  /* its bytes */
@@ -141,8 +141,10 @@ static int build_stacks(pkcu_encoder_model *m, const pkcu_weights *w, long long 
                            : pk_tc_prepare(src, 32, 0.0f, W_K[k], W_COLS[k], p, &alpha, stream);
                     m->qscale[b][k] = q ? alpha : 0.0f;
                 } else {
-                    /* a pointwise weight is [out channels, 1024]: W_COLS x W_K */
-                    st = pk_split_rows_bf16x3(src, p, W_COLS[k], W_K[k], stream);
+                    /* a pointwise weight is [out channels, 1024] (W_COLS x W_K),
+                     * already K-major: three-part planes, the first conv's rows
+                     * interleaved value / gate for its GLU epilogue */
+                    st = pk_tc_prepare_rows(src, W_COLS[k], W_K[k], k == W_PW1, p, stream);
                 }
                 if (st) return st;
                 m->stack[b][k] = p;
@@ -248,6 +250,7 @@ typedef struct {
     const pkcu_seq *seq;
     long long *off;   /* per item: frame, pos row, score, bd element offsets (4 x n_items) */
     unsigned fused;   /* PKCU_FUSED_* epilogues the hook's GEMMs apply */
+    float *x;         /* the residual stream (the fused PW2 epilogue adds to it) */
 } Fwd;
 
 static const float ONE = 1.0f, ZERO = 0.0f;
@@ -276,55 +279,6 @@ static int proj(cublasHandle_t h, int M, int N, int K, const float *A, const flo
 {
     if (pk_gemm_f32_rm(A, B, C, M, N, K, stream) == PKCU_OK) return PKCU_OK;
     return rm_gemm(h, M, N, K, A, K, 0, B, N, 0, 0, C, N, 0, 1);
-}
-
-/* The pointwise convolution C[Mo, T] = W[Mo, K] X[K, T] of `items`
- * consecutive utterances of T frames (channel-first) from split operands,
- * when the workspace holds them (else the fp32 SGEMM path, return 1): X's
- * parts as [x2; x1; x0] per utterance at the padded pitch Tp (T rounded up
- * to 8, so every row starts 16-byte aligned) into the workspace, W's as
- * [w0 | w1 | w2] (model load), one strided-batched bf16 GEMM per band
- * (smallest first, the later ones added through beta = 1; band 0 in K chunks
- * of 512, because the tensor cores' accumulation rounds less exactly than an
- * fp32 add) into a padded fp32 product behind them, then the pad columns
- * dropped into C. */
-static int pw_split(pkcu_encoder_model *m, cublasHandle_t h, int Mo, int T, int items, const void *wrows,
-                    const float *X, float *C, pkcu_stream_t stream, int *fallback)
-{
-    const int K = PK_D, Tp = (T + 7) & ~7;
-    const size_t xbytes = ((size_t)items * 3 * K * Tp * 2 + 255) & ~(size_t)255;
-    const size_t cbytes = (size_t)items * Mo * Tp * 4;
-    *fallback = 0;
-    if (xbytes + cbytes > m->split_cap) {
-        *fallback = 1;
-        return PKCU_OK;
-    }
-    const uint16_t *Xp = (const uint16_t *)m->split_ws;   /* bf16 elements */
-    float *Cp = (float *)((char *)m->split_ws + xbytes);
-    int st = pk_split_cols_bf16x3(X, m->split_ws, items, K, T, Tp, stream);
-    if (st) return st;
-    const uint16_t *Wp = (const uint16_t *)wrows;
-    static const float one = 1.0f, zero = 0.0f;
-    enum { SPLIT_CHUNK = 512 };
-    struct { int k; long long wcol, xrow; const float *beta; } part[2 + PK_D / SPLIT_CHUNK];
-    int np = 0;
-    part[np].k = 3 * K; part[np].wcol = 0; part[np].xrow = 0; part[np++].beta = &zero;
-    part[np].k = 2 * K; part[np].wcol = 0; part[np].xrow = K; part[np++].beta = &one;
-    for (int k0 = 0; k0 < K; k0 += SPLIT_CHUNK) {
-        part[np].k = K - k0 < SPLIT_CHUNK ? K - k0 : SPLIT_CHUNK;
-        part[np].wcol = k0;
-        part[np].xrow = 2LL * K + k0;
-        part[np++].beta = &one;
-    }
-    for (int i = 0; i < np; i++) {
-        const cublasStatus_t cs = cublasGemmStridedBatchedEx(
-            h, CUBLAS_OP_N, CUBLAS_OP_N, Tp, Mo, part[i].k, &one, Xp + part[i].xrow * Tp, CUDA_R_16BF, Tp,
-            3LL * K * Tp, Wp + part[i].wcol, CUDA_R_16BF, 3 * K, 0, part[i].beta, Cp, CUDA_R_32F, Tp,
-            (long long)Mo * Tp, items, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-        if (cs != CUBLAS_STATUS_SUCCESS)
-            return pkcu_fail(PKCU_ERR_CUDA, "cuBLAS bf16 GEMM failed (%d)", (int)cs);
-    }
-    return pk_depad_rows(Cp, C, (long long)items * Mo, T, Tp, stream);
 }
 
 /* The block's row-major projection on the library's tcgen05 GEMM: the
@@ -383,6 +337,30 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
         switch (gemm) {
         case PKCU_GEMM_FF1_1: return proj_swish(f->m, b, W_FF1_1, (int)F, gi->ln_ff1, p->ff1_b1, gi->h1, stream);
         case PKCU_GEMM_FF2_1: return proj_swish(f->m, b, W_FF2_1, (int)F, gi->ln_ff2, p->ff2_b1, gi->h2, stream);
+        case PKCU_GEMM_PW1: {   /* gated [1024, T] = GLU(W_pw1 LN_conv + b) from time-first LN rows */
+            pk_tc_epi e;
+            memset(&e, 0, sizeof(e));
+            e.mode = PK_TC_GLU;
+            e.bias = p->pw1_b;
+            e.C = gi->gated;
+            e.seq = f->seq;
+            return proj_tc(f->m, b, W_PW1, (int)F, gi->cf, &e, stream);
+        }
+        case PKCU_GEMM_PW2: {   /* x[t, d] += (W_pw2 dw + b)[d, t], dw channel-first per item */
+            Fwd *ff = f;
+            if ((size_t)F * 3 * PK_D * 2 > ff->m->split_cap)
+                return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: split workspace too small");
+            int st = pk_split_cf_t(gi->dw, ff->m->split_ws, PK_D, ff->seq, stream);
+            if (st) return st;
+            pk_tc_epi e;
+            memset(&e, 0, sizeof(e));
+            e.mode = PK_TC_RESID;
+            e.alpha = 1.0f;
+            e.rscale = 1.0f;
+            e.bias = p->pw2_b;
+            e.C = ff->x;
+            return pk_tc_gemm(ff->m->split_ws, ff->m->stack[b][W_PW2], 3, (int)F, PK_D, PK_D, &e, stream);
+        }
         case PKCU_GEMM_QKV: {
             pk_tc_epi e;
             memset(&e, 0, sizeof(e));
@@ -452,26 +430,14 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
             st = rm_gemm(h, T, PK_DH, T, gi->S + so, T, (long long)T * T, gi->V + fo * PK_D, PK_DH,
                          (long long)T * PK_DH, 0, gemm_dst(go->attn_h) + fo * PK_D, PK_DH, (long long)T * PK_DH, Hb);
             break;
-        case PKCU_GEMM_PW1: { /* [2048, T] = W_pw1 [2048, 1024] x cf [1024, T] */
-            int fb = 1;
-            if (f->m->stack[b][W_PW1])
-                st = pw_split(f->m, h, 2 * PK_D, T, per, f->m->stack[b][W_PW1], gi->cf + fo * PK_D,
-                              gemm_dst(go->pw1) + fo * 2 * PK_D, stream, &fb);
-            if (!st && fb)
-                st = rm_gemm(h, 2 * PK_D, T, PK_D, W[W_PW1], PK_D, 0, gi->cf + fo * PK_D, T,
-                             (long long)PK_D * T, 0, gemm_dst(go->pw1) + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
+        case PKCU_GEMM_PW1:   /* [2048, T] = W_pw1 [2048, 1024] x cf [1024, T] (fp32 path) */
+            st = rm_gemm(h, 2 * PK_D, T, PK_D, W[W_PW1], PK_D, 0, gi->cf + fo * PK_D, T,
+                         (long long)PK_D * T, 0, gemm_dst(go->pw1) + fo * 2 * PK_D, T, 2LL * PK_D * T, per);
             break;
-        }
-        case PKCU_GEMM_PW2: { /* [1024, T] = W_pw2 x dw [1024, T] */
-            int fb = 1;
-            if (f->m->stack[b][W_PW2])
-                st = pw_split(f->m, h, PK_D, T, per, f->m->stack[b][W_PW2], gi->dw + fo * PK_D,
-                              gemm_dst(go->pw2) + fo * PK_D, stream, &fb);
-            if (!st && fb)
-                st = rm_gemm(h, PK_D, T, PK_D, W[W_PW2], PK_D, 0, gi->dw + fo * PK_D, T,
-                             (long long)PK_D * T, 0, gemm_dst(go->pw2) + fo * PK_D, T, (long long)PK_D * T, per);
+        case PKCU_GEMM_PW2:   /* [1024, T] = W_pw2 x dw [1024, T] (fp32 path) */
+            st = rm_gemm(h, PK_D, T, PK_D, W[W_PW2], PK_D, 0, gi->dw + fo * PK_D, T,
+                         (long long)PK_D * T, 0, gemm_dst(go->pw2) + fo * PK_D, T, (long long)PK_D * T, per);
             break;
-        }
         default:
             return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_forward: unknown GEMM %d", gemm);
         }
@@ -525,10 +491,12 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
     }
     /* with every projection on the tcgen05 GEMM, bias+Swish and the QKV split
      * run in its epilogues */
-    int all_tc = m->stacks != NULL;
+    int all_tc = m->stacks != NULL && gemm_in->gated != NULL;
     for (int b = 0; b < m->n_blocks && all_tc; b++)
-        all_tc = m->stack[b][W_FF1_1] && m->stack[b][W_FF2_1] && m->stack[b][W_QKV];
-    Fwd f = {m, gemm_out, gemm_in, seq, off, all_tc ? (PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV) : 0u};
+        all_tc = m->stack[b][W_FF1_1] && m->stack[b][W_FF2_1] && m->stack[b][W_QKV] && m->stack[b][W_PW1] &&
+                 m->stack[b][W_PW2];
+    Fwd f = {m, gemm_out, gemm_in, seq, off,
+             all_tc ? (PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV | PKCU_FUSED_CONV) : 0u, x};
     const int st = pkcu_encoder_nongemm_fused(x, m->params, m->n_blocks, gemm_out, gemm_in, seq, fwd_hook,
                                               &f, f.fused, stream);
     free(off);

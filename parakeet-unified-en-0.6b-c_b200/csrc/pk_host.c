@@ -426,7 +426,7 @@ int pkcu_encoder_nongemm_fused(float *x, const pkcu_block_params *blocks, int n_
 {
     if (!x || !blocks || n_blocks < 0 || !go || !gi || !seq)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: NULL argument");
-    if (fused & ~(unsigned)(PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV))
+    if (fused & ~(unsigned)(PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV | PKCU_FUSED_CONV))
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: unknown fusion flags 0x%x", fused);
     if (fused && !hook)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_encoder_nongemm: fusion flags without a GEMM hook");
@@ -462,15 +462,28 @@ int pkcu_encoder_nongemm_fused(float *x, const pkcu_block_params *blocks, int n_
         PK_HOOK(b, PKCU_GEMM_AV);
         PK_TRY(pkcu_head_concat(go->attn_h, gi->attn, seq, stream));
         PK_HOOK(b, PKCU_GEMM_OUT);
-        PK_TRY(pkcu_residual_layer_norm_transpose(x, go->att_out, p->out_b, 1.0f, p->norm_conv_w,
-                                                  p->norm_conv_b, gi->cf, seq, stream));
-        /* conv module (csrc/encoder.c:439-478) */
-        PK_HOOK(b, PKCU_GEMM_PW1);
-        PK_TRY(pkcu_glu_dwconv_bn_swish(go->pw1, p->pw1_b, p->dw_w, p->dw_b, NULL, 0.0f, 1, gi->dw,
-                                        PK_D, 9, seq, stream));
-        PK_HOOK(b, PKCU_GEMM_PW2);
-        PK_TRY(pkcu_transpose_add_layer_norm(x, go->pw2, p->pw2_b, p->norm_ff2_w, p->norm_ff2_b,
-                                             gi->ln_ff2, seq, stream));
+        if (fused & PKCU_FUSED_CONV) {
+            /* conv module with its GEMM epilogues in the hook: LN_conv time-first
+             * into cf, the PW1 hook writes the GLU output, the PW2 hook adds
+             * pw2 + bias to x */
+            PK_TRY(pkcu_residual_layer_norm(x, go->att_out, p->out_b, 1.0f, p->norm_conv_w,
+                                            p->norm_conv_b, gi->cf, F, stream));
+            PK_HOOK(b, PKCU_GEMM_PW1);
+            PK_TRY(pkcu_dwconv_bn_swish(gi->gated, p->dw_w, p->dw_b, NULL, 0.0f, 1, gi->dw, PK_D, 9,
+                                        seq, stream));
+            PK_HOOK(b, PKCU_GEMM_PW2);
+            PK_TRY(pkcu_layer_norm_rows(x, p->norm_ff2_w, p->norm_ff2_b, gi->ln_ff2, F, PK_D, stream));
+        } else {
+            PK_TRY(pkcu_residual_layer_norm_transpose(x, go->att_out, p->out_b, 1.0f, p->norm_conv_w,
+                                                      p->norm_conv_b, gi->cf, seq, stream));
+            /* conv module (csrc/encoder.c:439-478) */
+            PK_HOOK(b, PKCU_GEMM_PW1);
+            PK_TRY(pkcu_glu_dwconv_bn_swish(go->pw1, p->pw1_b, p->dw_w, p->dw_b, NULL, 0.0f, 1, gi->dw,
+                                            PK_D, 9, seq, stream));
+            PK_HOOK(b, PKCU_GEMM_PW2);
+            PK_TRY(pkcu_transpose_add_layer_norm(x, go->pw2, p->pw2_b, p->norm_ff2_w, p->norm_ff2_b,
+                                                 gi->ln_ff2, seq, stream));
+        }
         /* FF2 and the block's final LN (csrc/encoder.c:489-490) */
         PK_HOOK(b, PKCU_GEMM_FF2_1);
         if (!(fused & PKCU_FUSED_FF_SWISH))

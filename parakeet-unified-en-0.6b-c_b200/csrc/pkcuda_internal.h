@@ -61,6 +61,8 @@ int pk_tc_wait_timeouts(unsigned *count, int reset);   /* k_tcgemm.cu */
 #define PK_TC_SWISH 1   /* C = Swish(alpha A W + bias)                  */
 #define PK_TC_RESID 2   /* C += rscale (alpha A W + bias), one FMA      */
 #define PK_TC_QKV   3   /* the QKV head split with pos_bias_u / v       */
+#define PK_TC_CF    4   /* rows = frames of seq: C per item [N, T] (+ bias[n]) */
+#define PK_TC_GLU   5   /* as CF, columns interleaved value / gate by 32: GLU -> [N/2, T] */
 typedef struct {
     int mode;
     float alpha, beta, rscale;
@@ -77,6 +79,11 @@ int pk_tc_prepare(const void *data, int bits, float scale, int K, int N, void *p
                   pkcu_stream_t stream);
 int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                const pk_tc_epi *ep, pkcu_stream_t stream);
+/* A pointwise weight W [N, K] (already K-major) -> three-part planes [N, 3K];
+ * glu: rows interleaved value / gate in groups of 32 for PK_TC_GLU. */
+int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *planes, pkcu_stream_t stream);
+/* Channel-first items X [C, T_b] -> time-first three-part rows [frames, 3C]. */
+int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream);
 
 /* For synchronous entry points, after their final synchronisation: reads and
  * resets both counters and returns PKCU_ERR_CUDA (with a message naming what)
@@ -92,18 +99,9 @@ int pk_check_wait_timeouts(const char *what);
 int pk_gemm_f32_rm(const float *A, const float *B, float *C, int M, int N, int K,
                    pkcu_stream_t stream);
 
-/* fp32 operands as three bf16 parts (k_split.cu): rows of A [M, K] to
- * out [M, 3K] = [a0 | a1 | a2]; W [K, N] to the stack S [3K, N] =
- * [w2; w1; w0] (K resp. N a multiple of 4, 16-byte aligned). */
+/* fp32 activations as three bf16 parts (k_split.cu): rows of A [M, K] to
+ * out [M, 3K] = [a0 | a1 | a2] (K a multiple of 4, 16-byte aligned). */
 int pk_split_rows_bf16x3(const float *A, void *out, long long M, int K, pkcu_stream_t stream);
-int pk_split_stack_bf16x3(const float *W, void *S, int K, int N, pkcu_stream_t stream);
-/* items x [K, T] (any T) to items x [3K, Tp] = [x2; x1; x0], rows at pitch
- * Tp >= T; pk_depad_rows copies rows x [Tp] to rows x [T]. */
-int pk_split_cols_bf16x3(const float *X, void *out, long long items, int K, int T, int Tp,
-                         pkcu_stream_t stream);
-int pk_depad_rows(const float *src, float *dst, long long rows, int T, int Tp, pkcu_stream_t stream);
-/* int8 -> bf16, exact (an int8 weight's single part). */
-int pk_i8_to_bf16(const int8_t *q, void *out, long long n, pkcu_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -63,7 +63,8 @@ EXPORTED = (
     "pkcu_chunk_stitch", "pkcu_asr_encode", "pkcu_asr_set_chunk_mode",
     "pkcu_weight_create", "pkcu_weight_destroy", "pkcu_wmatmul_work_bytes", "pkcu_wmatmul",
     "pkcu_wmatmul_bias_swish", "pkcu_wmatmul_bias_residual", "pkcu_wmatmul_qkv",
-    "pkcu_encoder_nongemm_fused",
+    "pkcu_encoder_nongemm_fused", "pkcu_conv_weight_create", "pkcu_pointwise_conv1d",
+    "pkcu_pointwise_conv1d_glu",
 )
 
 
@@ -196,6 +197,9 @@ _SIGS = {
     "pkcu_wmatmul_bias_swish": (I, [VP, VP, VP, VP, I, VP, VP]),
     "pkcu_wmatmul_bias_residual": (I, [VP, VP, VP, VP, F, I, VP, VP]),
     "pkcu_wmatmul_qkv": (I, [VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, VP]),
+    "pkcu_conv_weight_create": (I, [VP, I, I, I, VP, C.POINTER(VP)]),
+    "pkcu_pointwise_conv1d": (I, [VP, VP, VP, VP, I, VP, VP]),
+    "pkcu_pointwise_conv1d_glu": (I, [VP, VP, VP, VP, I, VP, VP]),
 }
 
 _lib = None
@@ -342,6 +346,17 @@ class Weight:
             self.close()
         except Exception:
             pass
+
+
+class ConvWeight(Weight):
+    """pkcu_weight of a pointwise convolution: fp32 W [Cout, Cin] as stored,
+    glu=True for pkcu_pointwise_conv1d_glu."""
+
+    def __init__(self, data, Cout, Cin, glu=False, stream=None):
+        h = VP()
+        call("pkcu_conv_weight_create", data if isinstance(data, int) else ptr(data), int(Cout), int(Cin),
+             int(bool(glu)), stream_handle(stream), C.byref(h))
+        self.handle, self.K, self.N = h, Cin, Cout
 
 
 class ChunkPlan:

@@ -1,9 +1,9 @@
-"""The split-operand kernels (csrc/k_split.cu) behind the encoder model's
-fp32-accurate bf16 GEMMs, bit-exact against the numpy restatement of the
-three-part split (oracle/pyoracle.py: split3_bf16), through their C entry
-points: activation rows to [a0 | a1 | a2], weights to the stack [w2; w1; w0],
-channel-first inputs to [x2; x1; x0] at a padded pitch, and the copy that
-drops the pad columns of a product."""
+"""The operand preparation of the library's tcgen05 GEMM, bit-exact against
+the numpy restatement of the three-part split (oracle/pyoracle.py:
+split3_bf16) through the C entry points: activation rows to [a0 | a1 | a2]
+(k_split.cu); a [K, N] weight transposed to K-major planes [N, 3K], an int8
+weight's q to [N, K] bf16 (k_tcgemm.cu); a pointwise weight's rows to
+[N, 3K] with the GLU interleave; channel-first items to time-first parts."""
 from __future__ import annotations
 
 import ctypes as C
@@ -17,15 +17,15 @@ from gpuhelp import dev
 
 pytestmark = pytest.mark.gpu
 
-VP, I, LL = C.c_void_p, C.c_int, C.c_longlong
+VP, I, LL, F = C.c_void_p, C.c_int, C.c_longlong, C.c_float
 
 
 def _lib(cuda):
     L = cuda.lib()
     L.pk_split_rows_bf16x3.argtypes = [VP, VP, LL, I, VP]
-    L.pk_split_stack_bf16x3.argtypes = [VP, VP, I, I, VP]
-    L.pk_split_cols_bf16x3.argtypes = [VP, VP, LL, I, I, I, VP]
-    L.pk_depad_rows.argtypes = [VP, VP, LL, I, I, VP]
+    L.pk_tc_prepare.argtypes = [VP, I, F, I, I, VP, C.POINTER(F), VP]
+    L.pk_tc_prepare_rows.argtypes = [VP, I, I, I, VP, VP]
+    L.pk_split_cf_t.argtypes = [VP, VP, I, VP, VP]
     return L
 
 
@@ -35,61 +35,91 @@ def _values(rng, shape):
     return (rng.standard_normal(n) * np.exp(rng.uniform(-12, 12, n))).astype(np.float32).reshape(shape)
 
 
-def _parts_u16(t, shape):
+def _u16(t, shape):
     import torch
     torch.cuda.synchronize()
     return t.cpu().numpy().view(np.uint16).reshape(shape)
 
 
-def test_split_rows_bitexact(cuda):
+def _empty16(n):
     import torch
+    from gpuhelp import ALIVE
+    t = torch.empty(n, dtype=torch.int16, device="cuda")
+    ALIVE.append(t)
+    return t
+
+
+def _rows_parts(a):
+    """[R, K] fp32 -> [R, 3K] bf16 bits, row = [a0 | a1 | a2]."""
+    p0, p1, p2 = po.split3_bf16(a)
+    return np.concatenate([p0, p1, p2], axis=-1)
+
+
+def test_split_rows_bitexact(cuda):
     L = _lib(cuda)
     M, K = 37, 1024
-    a = _values(np.random.default_rng(51), (M, K))
-    out = torch.empty(M * 3 * K, dtype=torch.int16, device="cuda")
+    a = _values(np.random.default_rng(1), (M, K))
+    out = _empty16(M * 3 * K)
     assert L.pk_split_rows_bf16x3(dev(a).data_ptr(), out.data_ptr(), M, K, None) == 0
-    got = _parts_u16(out, (M, 3, K))
-    for i, p in enumerate(po.split3_bf16(a)):
-        assert_bitexact(got[:, i, :], p, f"part {i}")
+    assert_bitexact(_u16(out, (M, 3 * K)), _rows_parts(a), "rows [a0 | a1 | a2]")
 
 
-def test_split_stack_bitexact(cuda):
-    import torch
+@pytest.mark.parametrize("K,N", [(1024, 4096), (4096, 1024), (64, 96)])
+def test_prepare_fp32_weight_bitexact(cuda, K, N):
     L = _lib(cuda)
-    K, N = 64, 96
-    w = _values(np.random.default_rng(52), (K, N))
-    out = torch.empty(3 * K * N, dtype=torch.int16, device="cuda")
-    assert L.pk_split_stack_bf16x3(dev(w).data_ptr(), out.data_ptr(), K, N, None) == 0
-    got = _parts_u16(out, (3, K, N))
-    p0, p1, p2 = po.split3_bf16(w)
-    for i, p in enumerate((p2, p1, p0)):   # the stack [w2; w1; w0]
-        assert_bitexact(got[i], p, f"stack part {i}")
+    w = _values(np.random.default_rng(K + N), (K, N))
+    out = _empty16(N * 3 * K)
+    alpha = F(0)
+    assert L.pk_tc_prepare(dev(w).data_ptr(), 32, 0.0, K, N, out.data_ptr(), C.byref(alpha), None) == 0
+    assert alpha.value == 1.0
+    assert_bitexact(_u16(out, (N, 3 * K)), _rows_parts(np.ascontiguousarray(w.T)), "planes [N, 3K]")
 
 
-def test_split_cols_and_depad_bitexact(cuda):
-    import torch
+def test_prepare_int8_weight_exact(cuda):
     L = _lib(cuda)
-    items, K, T = 3, 40, 13
-    Tp = (T + 7) & ~7
-    x = _values(np.random.default_rng(53), (items, K, T))
-    out = torch.empty(items * 3 * K * Tp, dtype=torch.int16, device="cuda")
-    assert L.pk_split_cols_bf16x3(dev(x).data_ptr(), out.data_ptr(), items, K, T, Tp,
-                                  None) == 0
-    got = _parts_u16(out, (items, 3, K, Tp))[..., :T]   # pad columns are unspecified
-    p0, p1, p2 = po.split3_bf16(x)
-    for i, p in enumerate((p2, p1, p0)):   # [x2; x1; x0] per item
-        assert_bitexact(got[:, i], p, f"column part {i}")
-    padded = _values(np.random.default_rng(54), (7, Tp))
-    dst = torch.empty(7 * T, dtype=torch.float32, device="cuda")
-    assert L.pk_depad_rows(dev(padded).data_ptr(), dst.data_ptr(), 7, T, Tp, None) == 0
-    torch.cuda.synchronize()
-    assert_bitexact(dst.cpu().numpy().reshape(7, T), padded[:, :T], "depad")
+    K, N = 1024, 3072
+    q = np.random.default_rng(2).integers(-127, 128, (K, N)).astype(np.int8)
+    out = _empty16(N * K)
+    alpha = F(0)
+    assert L.pk_tc_prepare(dev(q).data_ptr(), 8, 0.004, K, N, out.data_ptr(), C.byref(alpha), None) == 0
+    assert alpha.value == np.float32(0.004)
+    want = po.split3_bf16(np.ascontiguousarray(q.T).astype(np.float32))
+    assert_bitexact(_u16(out, (N, K)), want[0], "q as bf16 [N, K]")
+    assert not want[1].any()   # q is exact in one bf16 part
+
+
+@pytest.mark.parametrize("glu", [0, 1])
+def test_prepare_pointwise_rows(cuda, glu):
+    L = _lib(cuda)
+    N, K = 2048, 1024
+    w = _values(np.random.default_rng(3 + glu), (N, K))
+    out = _empty16(N * 3 * K)
+    assert L.pk_tc_prepare_rows(dev(w).data_ptr(), N, K, glu, out.data_ptr(), None) == 0
+    src = np.arange(N)
+    if glu:   # rows 64k .. 64k + 31: value channels 32k ..; the next 32: their gates
+        n = np.arange(N)
+        blk, r = n // 64, n % 64
+        src = np.where(r < 32, blk * 32 + r, N // 2 + blk * 32 + r - 32)
+    assert_bitexact(_u16(out, (N, 3 * K)), _rows_parts(w[src]), "pointwise planes")
+
+
+def test_split_channel_first_items_to_time_first(cuda):
+    L = _lib(cuda)
+    Cc = 1024
+    lengths = [375, 7, 416]
+    rng = np.random.default_rng(4)
+    xs = [_values(rng, (Cc, T)) for T in lengths]
+    out = _empty16(sum(lengths) * 3 * Cc)
+    with cuda.Seq(lengths) as seq:
+        assert L.pk_split_cf_t(dev(np.concatenate([x.reshape(-1) for x in xs])).data_ptr(), out.data_ptr(),
+                               Cc, seq.handle, None) == 0
+        got = _u16(out, (sum(lengths), 3 * Cc))
+    want = np.concatenate([_rows_parts(np.ascontiguousarray(x.T)) for x in xs])
+    assert_bitexact(got, want, "time-first parts")
 
 
 def test_split_entry_points_reject_bad_arguments(cuda):
     L = _lib(cuda)
     ERR_ARG = 1
     assert L.pk_split_rows_bf16x3(None, None, 4, 1024, None) == ERR_ARG
-    assert L.pk_split_stack_bf16x3(None, None, 4, 8, None) == ERR_ARG
-    assert L.pk_split_cols_bf16x3(None, None, 1, 4, 5, 4, None) == ERR_ARG   # Tp < T as well
-    assert L.pk_depad_rows(None, None, 1, 5, 8, None) == ERR_ARG
+    assert L.pk_split_cf_t(None, None, 1024, None, None) == ERR_ARG

@@ -171,3 +171,47 @@ def test_bad_arguments(cuda):
     assert L.pkcu_weight_create(x.data_ptr(), 16, 0.0, None, 32, 1, 32, 64, None, C.byref(h)) == 1   # bits
     assert L.pkcu_weight_create(x.data_ptr(), 8, 0.0, None, 32, 1, 32, 64, None, C.byref(h)) == 1    # scale
     assert L.pkcu_wmatmul(None, None, None, 1, 1.0, 0.0, None, None) == 1
+
+
+def conv_bound(w, x):
+    return 1e-5 * (np.abs(w).astype(np.float64) @ np.abs(x).astype(np.float64)) + 2e-6
+
+
+@pytest.mark.parametrize("Cout,T", [(1024, 375), (2048, 33), (1024, 1)])
+def test_pointwise_conv1d(cuda, reference, Cout, T):
+    """pkcu_pointwise_conv1d against the reference's pk_pointwise_conv1d
+    (csrc/tensor_ops.c:579-590): out = W x + b, channel-first."""
+    Cin = 1024
+    rng = np.random.default_rng(Cout + T)
+    x = rng.standard_normal((Cin, T)).astype(np.float32)
+    w = (rng.standard_normal((Cout, Cin)) / np.sqrt(Cin)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(Cout)).astype(np.float32)
+    want = reference.pointwise_conv1d(x, w, b)
+    out = empty(Cout * T)
+    with cuda.ConvWeight(dev(w), Cout, Cin, glu=False) as W:
+        cuda.call("pkcu_pointwise_conv1d", dev(x).data_ptr(), W.handle, dev(b).data_ptr(), out.data_ptr(), T,
+                  work(cuda, T, Cin).data_ptr(), None)
+        got = host(out).reshape(Cout, T)
+    check(got, want, conv_bound(w, x), "W x + b")
+
+
+@pytest.mark.parametrize("T", [375, 129])
+def test_pointwise_conv1d_glu(cuda, reference, oracle, T):
+    """The first pointwise convolution with the GLU in its epilogue against
+    pk_pointwise_conv1d then the GLU restatement (csrc/encoder.c:457-465);
+    the GLU is 1-Lipschitz in a and 0.25 |a| in g, so the bound carries over."""
+    C2, Cin = 2048, 1024
+    rng = np.random.default_rng(T)
+    x = rng.standard_normal((Cin, T)).astype(np.float32)
+    w = (rng.standard_normal((C2, Cin)) / np.sqrt(Cin)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(C2)).astype(np.float32)
+    pw1 = reference.pointwise_conv1d(x, w, b)
+    want = oracle.glu_channel_first(pw1)
+    out = empty(C2 // 2 * T)
+    with cuda.ConvWeight(dev(w), C2, Cin, glu=True) as W:
+        cuda.call("pkcu_pointwise_conv1d_glu", dev(x).data_ptr(), W.handle, dev(b).data_ptr(), out.data_ptr(),
+                  T, work(cuda, T, Cin).data_ptr(), None)
+        got = host(out).reshape(C2 // 2, T)
+    tb = conv_bound(w, x)
+    tol = tb[:C2 // 2] + 0.25 * np.abs(pw1[:C2 // 2]) * tb[C2 // 2:] + 1e-5 * np.abs(want) + 2e-6
+    check(got, want, tol, "GLU(W x + b)")
