@@ -64,7 +64,7 @@ def parse_args():
     ap.add_argument("--pre-only", action="store_true",
                     help="with --aux-only: time only the pre-encode stage")
     ap.add_argument("--gemm-only", action="store_true",
-                    help="with --aux-only: time only the GEMMs with fused epilogues")
+                    help="with --aux-only: time only the weight products (tcgen05 GEMMs with fused epilogues)")
     ap.add_argument("--gemm-rows", type=int, default=24000,
                     help="rows M of the fused-GEMM timing")
     ap.add_argument("--forward-only", action="store_true",
@@ -692,6 +692,98 @@ def time_fused_gemms(stream, reps, M=GEMM_ROWS):
     return res
 
 
+def time_tc_gemms(stream, reps, M=GEMM_ROWS):
+    """The weight products on the library's tcgen05 GEMM (pkcu_wmatmul*) at
+    the block's shapes, M = 24000 rows (64 utterances x 375 frames): FF
+    linear1 + bias + Swish and linear2 + bias + 0.5 residual, the fused QKV
+    with its head split, and the first pointwise convolution with its GLU, for
+    the reference's weight storages (int8 per-tensor as its checkpoints store
+    the projections, fp32, GPTQ int4 with G = 32 along N). Each call includes
+    the activation's three-part split. Reported: ms (CUDA events), fp32
+    TFLOP/s (2 M N K / t) and the bf16 tensor rate it runs at (three MMAs per
+    product for an int8 weight, six for fp32 / int4) as a fraction of the
+    measured sustained bf16 peak (the GEMMs run inside long steps)."""
+    import torch
+    import pkcuda
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(13)
+    f32 = dict(device=dev, dtype=torch.float32)
+    sh = stream.cuda_stream
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+    except (OSError, KeyError, ValueError):
+        peak = 1400.0
+    L = pkcuda.lib()
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(max(reps, 1)):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / max(reps, 1)
+
+    def weight(bits, K, N):
+        if bits == 8:
+            q = torch.randint(-127, 128, (K * N,), generator=g, device=dev, dtype=torch.int8)
+            return pkcuda.Weight(q, 8, K, N, scale=0.004, stream=stream), [q]
+        if bits == 4:
+            pk = torch.randint(0, 256, (K * N // 2,), generator=g, device=dev, dtype=torch.uint8)
+            sc = 1e-3 + 1.9e-2 * torch.rand(K * N // 32, generator=g, **f32)
+            return pkcuda.Weight(pk, 4, K, N, scales=sc, stream=stream), [pk, sc]
+        W = torch.randn(K * N, generator=g, **f32) / K ** 0.5
+        return pkcuda.Weight(W, 32, K, N, stream=stream), [W]
+
+    res = {}
+    cases = (("ff1_bias_swish_int8", 8, 4096, 1024), ("ff2_bias_residual_int8", 8, 1024, 4096),
+             ("qkv_head_split_int8", 8, 3072, 1024), ("ff1_bias_swish_fp32", 32, 4096, 1024),
+             ("ff1_bias_swish_int4_g32", 4, 4096, 1024), ("pw1_glu_fp32", 32, 2048, 1024))
+    for name, bits, N, K in cases:
+        A = torch.randn(M * K, generator=g, **f32)
+        b = 0.1 * torch.randn(N, generator=g, **f32)
+        work = torch.empty(int(L.pkcu_wmatmul_work_bytes(M, K)) // 4 + 64, **f32)
+        if name.startswith("pw1"):
+            Wc = torch.randn(N * K, generator=g, **f32) / K ** 0.5
+            w, keep = pkcuda.ConvWeight(Wc, N, K, glu=True, stream=stream), [Wc]
+            X = torch.randn(K * M, generator=g, **f32)   # one item of M frames, channel-first
+            out = torch.empty(N // 2 * M, **f32)
+            fn = lambda: pkcuda.call("pkcu_pointwise_conv1d_glu", X.data_ptr(), w.handle, b.data_ptr(),
+                                     out.data_ptr(), M, work.data_ptr(), sh)
+        else:
+            w, keep = weight(bits, K, N)
+            out = torch.randn(M * N, generator=g, **f32)
+            if "swish" in name:
+                fn = lambda: pkcuda.call("pkcu_wmatmul_bias_swish", A.data_ptr(), w.handle, b.data_ptr(),
+                                         out.data_ptr(), M, work.data_ptr(), sh)
+            elif "residual" in name:
+                fn = lambda: pkcuda.call("pkcu_wmatmul_bias_residual", A.data_ptr(), w.handle, b.data_ptr(),
+                                         out.data_ptr(), C.c_float(0.5), M, work.data_ptr(), sh)
+            else:
+                seq = pkcuda.Seq([375] * (M // 375))
+                u = 0.1 * torch.randn(D, generator=g, **f32)
+                v = 0.1 * torch.randn(D, generator=g, **f32)
+                heads = [torch.empty(M * D, **f32) for _ in range(4)]
+                fn = lambda: pkcuda.call("pkcu_wmatmul_qkv", A.data_ptr(), w.handle, b.data_ptr(), u.data_ptr(),
+                                         v.data_ptr(), *[t.data_ptr() for t in heads], seq.handle,
+                                         work.data_ptr(), sh)
+        ms = timed(fn)
+        flop = 2.0 * M * N * K
+        prods = 3 if bits == 8 else 6
+        res[name] = {"M": M, "N": N, "K": K, "ms": round(ms, 4), "tflops_fp32": round(flop / ms / 1e9, 1),
+                     "tensor_bf16_tflops": round(prods * flop / ms / 1e9, 1),
+                     "tensor_frac_sustained": round(prods * flop / ms / 1e9 / peak, 3)}
+        w.close()
+        del A, b, work, out, keep
+    torch.cuda.synchronize()
+    res["peak_bf16_tflops_sustained"] = peak
+    return res
+
+
 FWD_UTTS = 32
 
 
@@ -1174,7 +1266,8 @@ def aux_only(args, local_rank):
             print(json.dumps({"encoder_forward": fwd}), flush=True)
             return
         if args.gemm_only:
-            print(json.dumps({"fused_gemms": time_fused_gemms(stream, args.aux_reps, args.gemm_rows)}),
+            print(json.dumps({"tc_gemms": time_tc_gemms(stream, args.aux_reps, args.gemm_rows),
+                              "fused_gemms_fastfp32": time_fused_gemms(stream, args.aux_reps, args.gemm_rows)}),
                   flush=True)
             return
         if args.decode_only:
@@ -1317,7 +1410,8 @@ def run_extras(args, stream, world):
     mel-to-tokens and the decode alone, each beside the reference's own code
     on the host where one exists."""
     cpu = world == 1 and not args.no_cpu_baseline
-    ex = {"decode": time_decode(stream, 3), "fused_gemms": time_fused_gemms(stream, 3),
+    ex = {"decode": time_decode(stream, 3), "tc_gemms": time_tc_gemms(stream, 3),
+          "fused_gemms_fastfp32": time_fused_gemms(stream, 3),
           "encoder_forward": time_encoder_forward(stream, 2)}
     asr = time_asr(stream, 1)
     asr["every_frame_blank"] = {k: v for k, v in time_asr(stream, 1, blank_bias=6.0).items()

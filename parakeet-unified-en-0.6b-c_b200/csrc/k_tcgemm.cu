@@ -23,7 +23,8 @@
 // summed with ordinary fp32 adds. Two accumulators alternate, so the MMAs of
 // the next run overlap the drain of the last.
 //
-// Kernel. One CTA per 128 x 256 output tile, 320 threads: warp 0 issues the
+// Kernel. Persistent, one CTA per SM taking 128 x 256 output tiles in turn,
+// 320 threads: warp 0 issues the
 // TMA loads (cp.async.bulk.tensor, no multicast) of each 32-wide K block --
 // the three A parts (128 x 32 each) and the weight planes (256 x 32 each),
 // 64-byte swizzled -- into a ring of stages, completion on the stage's
@@ -32,7 +33,9 @@
 // of each stage, then tcgen05.commit frees the stage; warps 2..9 drain the
 // accumulators (tcgen05.ld, one TMEM lane quadrant and 128 columns per warp)
 // and run the epilogue from registers: alpha, bias, then store / Swish /
-// scaled residual / the QKV head split with pos_bias_u/v. Every wait is
+// scaled residual / the QKV head split with pos_bias_u/v / channel-first
+// store with or without the GLU. A tile's epilogue math and stores run while
+// the MMAs of the CTA's next tile fill the freed accumulators. Every wait is
 // bounded by the global timer; a wait that runs out records an error and the
 // CTA skips the rest of its work.
 #include <cuda.h>
@@ -295,9 +298,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int nkb = K / BK;
   const int n_runs = (nkb + C::DRAIN_KB - 1) / C::DRAIN_KB;
+  // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; n-blocks
+  // vary fastest, so the CTAs of a wave share the rows of A they read
+  const int tiles_n = (N + BN - 1) / BN;
+  const int n_tiles = tiles_n * ((M + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -327,130 +333,144 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 0) {
     // ── producer: TMA loads of each K block into the stage ring ──
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nkb; kb++) {
-        const int s = kb % C::STAGES;
-        if (kb >= C::STAGES && !mbar_wait(empty + s, ((kb / C::STAGES) - 1) & 1)) {
-          atomicAdd(&g_wait_timeouts, 1u);
-          s_abort = 1;
-          break;
+      int it = 0;   // K blocks issued by this CTA, over all its tiles
+      bool stop = false;
+      for (int tile = blockIdx.x; tile < n_tiles && !stop; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+        for (int kb = 0; kb < nkb; kb++) {
+          const int s = it % C::STAGES;
+          if (it >= C::STAGES && !mbar_wait(empty + s, ((it / C::STAGES) - 1) & 1)) {
+            atomicAdd(&g_wait_timeouts, 1u);
+            s_abort = 1;
+          }
+          if (*(volatile int *)&s_abort) {
+            stop = true;
+            break;
+          }
+          unsigned char *st = smem + s * C::STAGE;
+          mbar_arrive_tx(full + s, C::STAGE);
+          for (int p = 0; p < 3; p++) tma_load_2d(st + p * A_TILE, &map_a, p * K + kb * BK, m0, full + s);
+          for (int p = 0; p < NPB; p++)
+            tma_load_2d(st + 3 * A_TILE + p * B_TILE, &map_b, p * K + kb * BK, n0, full + s);
+          it++;
         }
-        if (*(volatile int *)&s_abort) break;
-        unsigned char *st = smem + s * C::STAGE;
-        mbar_arrive_tx(full + s, C::STAGE);
-        for (int p = 0; p < 3; p++) tma_load_2d(st + p * A_TILE, &map_a, p * K + kb * BK, m0, full + s);
-        for (int p = 0; p < NPB; p++)
-          tma_load_2d(st + 3 * A_TILE + p * B_TILE, &map_b, p * K + kb * BK, n0, full + s);
-        issued = kb + 1;
       }
       if (*(volatile int *)&s_abort) {
         // a wait ran out somewhere: let this CTA's copies still in flight land
         // (bounded) before its shared memory is released
-        for (int kb = issued > C::STAGES ? issued - C::STAGES : 0; kb < issued; kb++)
-          mbar_wait(full + kb % C::STAGES, (kb / C::STAGES) & 1);
+        for (int j = it > C::STAGES ? it - C::STAGES : 0; j < it; j++)
+          mbar_wait(full + j % C::STAGES, (j / C::STAGES) & 1);
       }
     }
   } else if (warp == 1) {
     // ── MMA issue: one thread ──
     if (lane == 0) {
       constexpr unsigned IDESC = idesc_bf16(BM, BN);
-      int kb = 0;
-      for (int run = 0; run < n_runs && !*(volatile int *)&s_abort; run++) {
-        const int buf = run & 1;
-        if (run >= 2 && !mbar_wait(acc_empty + buf, ((run >> 1) - 1) & 1)) {
-          atomicAdd(&g_wait_timeouts, 1u);
-          s_abort = 1;
-          break;
-        }
-        tc_fence_after();
-        const unsigned d = tmem + buf * BN;
-        const int kb_end = kb + C::DRAIN_KB < nkb ? kb + C::DRAIN_KB : nkb;
-        bool first = true;
-        for (; kb < kb_end; kb++) {
-          const int s = kb % C::STAGES;
-          if (!mbar_wait(full + s, (kb / C::STAGES) & 1)) {
+      int it = 0, gr = 0;   // K blocks consumed and accumulator runs, over all tiles
+      for (int tile = blockIdx.x; tile < n_tiles && !*(volatile int *)&s_abort; tile += gridDim.x) {
+        int kb = 0;
+        for (int run = 0; run < n_runs && !*(volatile int *)&s_abort; run++, gr++) {
+          const int buf = gr & 1;
+          if (gr >= 2 && !mbar_wait(acc_empty + buf, ((gr >> 1) - 1) & 1)) {
             atomicAdd(&g_wait_timeouts, 1u);
             s_abort = 1;
             break;
           }
           tc_fence_after();
-          const unsigned st = smem_u32(smem + s * C::STAGE);
-#pragma unroll
-          for (int k = 0; k < BK / 16; k++) {
-#pragma unroll
-            for (int p = 0; p < C::PRODUCTS; p++) {
-              int ia, ib;
-              product_parts(NPB, p, ia, ib);
-              const unsigned long long da = sdesc_k64(st + ia * A_TILE + k * 32);
-              const unsigned long long db = sdesc_k64(st + 3 * A_TILE + ib * B_TILE + k * 32);
-              umma(d, da, db, IDESC, first ? 0u : 1u);
-              first = false;
+          const unsigned d = tmem + buf * BN;
+          const int kb_end = kb + C::DRAIN_KB < nkb ? kb + C::DRAIN_KB : nkb;
+          bool first = true;
+          for (; kb < kb_end; kb++, it++) {
+            const int s = it % C::STAGES;
+            if (!mbar_wait(full + s, (it / C::STAGES) & 1)) {
+              atomicAdd(&g_wait_timeouts, 1u);
+              s_abort = 1;
+              break;
             }
+            tc_fence_after();
+            const unsigned st = smem_u32(smem + s * C::STAGE);
+#pragma unroll
+            for (int k = 0; k < BK / 16; k++) {
+#pragma unroll
+              for (int p = 0; p < C::PRODUCTS; p++) {
+                int ia, ib;
+                product_parts(NPB, p, ia, ib);
+                const unsigned long long da = sdesc_k64(st + ia * A_TILE + k * 32);
+                const unsigned long long db = sdesc_k64(st + 3 * A_TILE + ib * B_TILE + k * 32);
+                umma(d, da, db, IDESC, first ? 0u : 1u);
+                first = false;
+              }
+            }
+            umma_commit(empty + s);   // the stage is free once these MMAs are done
           }
-          umma_commit(empty + s);   // the stage is free once these MMAs are done
+          if (*(volatile int *)&s_abort) break;
+          umma_commit(acc_full + buf);   // this run's sum is ready to drain
         }
-        if (*(volatile int *)&s_abort) break;
-        umma_commit(acc_full + buf);   // this run's sum is ready to drain
       }
       // every MMA issued here has finished before the TMEM is released
       umma_commit(done);
       mbar_wait(done, 0);
     }
   } else {
-    // ── drain and epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 ──
+    // ── drain and epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31; the
+    // MMAs of the next tile run into the free accumulators meanwhile ──
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const unsigned lane_addr = ((unsigned)(q * 32) << 16) + half * 128;
-    float sum[128];
-#pragma unroll
-    for (int j = 0; j < 128; j++) sum[j] = 0.0f;
+    int gr = 0;
     bool ok = true;
-    for (int run = 0; run < n_runs; run++) {
-      const int buf = run & 1;
-      // the outcome is made warp-uniform: tcgen05.ld needs every lane
-      if (!__all_sync(PK_FULL_MASK, mbar_wait(acc_full + buf, (run >> 1) & 1))) {
-        if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
-        s_abort = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      float sum[128];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        float v[32];
-        tmem_ld32(tmem + lane_addr + buf * BN + c * 32, v);
-#pragma unroll
-        for (int j = 0; j < 32; j++) sum[c * 32 + j] += v[j];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty + buf);
-    }
-    const long long r = (long long)m0 + row;
-    if (ok && r < M && epi.mode == PK_TC_GLU) {
-      // columns 64k .. 64k + 31 hold value channels 32k .., the next 32 their gates
-#pragma unroll
-      for (int c = 0; c < 4; c += 2) {
-        const int n = n0 + half * 128 + c * 32;
-        if (n < N) {
-          float a[32], g[32];
-#pragma unroll
-          for (int j = 0; j < 32; j++) {
-            a[j] = sum[c * 32 + j] * epi.alpha;
-            g[j] = sum[(c + 1) * 32 + j] * epi.alpha;
-          }
-          epi_glu32(epi, r, n / 2, epi.channels, a, g);
+      for (int j = 0; j < 128; j++) sum[j] = 0.0f;
+      for (int run = 0; run < n_runs; run++, gr++) {
+        const int buf = gr & 1;
+        // the outcome is made warp-uniform: tcgen05.ld needs every lane
+        if (!__all_sync(PK_FULL_MASK, mbar_wait(acc_full + buf, (gr >> 1) & 1))) {
+          if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+          s_abort = 1;
+          ok = false;
+          break;
         }
-      }
-    } else if (ok && r < M) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int n = n0 + half * 128 + c * 32;
-        if (n < N) {
+        for (int c = 0; c < 4; c++) {
           float v[32];
+          tmem_ld32(tmem + lane_addr + buf * BN + c * 32, v);
 #pragma unroll
-          for (int j = 0; j < 32; j++) v[j] = sum[c * 32 + j] * epi.alpha;
-          epi_store32(epi, r, n, v);
+          for (int j = 0; j < 32; j++) sum[c * 32 + j] += v[j];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + buf);
+      }
+      const long long r = (long long)m0 + row;
+      if (ok && r < M && epi.mode == PK_TC_GLU) {
+        // columns 64k .. 64k + 31 hold value channels 32k .., the next 32 their gates
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+          const int n = n0 + half * 128 + c * 32;
+          if (n < N) {
+            float a[32], g[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              a[j] = sum[c * 32 + j] * epi.alpha;
+              g[j] = sum[(c + 1) * 32 + j] * epi.alpha;
+            }
+            epi_glu32(epi, r, n / 2, epi.channels, a, g);
+          }
+        }
+      } else if (ok && r < M) {
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int n = n0 + half * 128 + c * 32;
+          if (n < N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = sum[c * 32 + j] * epi.alpha;
+            epi_store32(epi, r, n, v);
+          }
         }
       }
     }
@@ -628,7 +648,9 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K, co
   using C = tc::Cfg<NPB>;
   static int flags[64];
   smem_optin(tc::tc_gemm_kernel<NPB>, C::SMEM, flags);
-  const dim3 grid((unsigned)((N + tc::BN - 1) / tc::BN), (unsigned)((M + tc::BM - 1) / tc::BM));
+  // persistent: one CTA per SM (the stage ring fills most of its shared memory)
+  const long long tiles = (long long)((N + tc::BN - 1) / tc::BN) * ((M + tc::BM - 1) / tc::BM);
+  const unsigned grid = (unsigned)(tiles < pkcu_sm_count() ? tiles : pkcu_sm_count());
   tc::tc_gemm_kernel<NPB><<<grid, tc::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, e);
   return pkcu_launch_status("tcgen05 GEMM");
 }
