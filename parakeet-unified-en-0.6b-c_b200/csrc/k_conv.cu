@@ -5,8 +5,9 @@
 // bias (csrc/tensor_ops.c:585-589), then out[c,t] = a * 1/(1 + expf(-g)) with
 // a = pw1[c,t], g = pw1[C+c,t]. Per item the [C, T] halves are contiguous, so
 // the kernel streams both halves as flat float4 arrays (12 bytes per output).
-// The gate uses CUDA's expf; the reference's -ffast-math build uses glibc's
-// vectorised expf, so GLU is compared within tolerance.
+// The gate's exp is the library's own (glu_gate, pk_common.cuh); the
+// reference's -ffast-math build uses glibc's vectorised expf, so GLU is
+// compared within tolerance.
 //
 // Depthwise conv (csrc/tensor_ops.c:477-575): out[c,t] = b[c] + sum_k
 // x[c, t-pad+k] * w[c,k], pad = (K-1)/2, taps outside [0, T) skipped, the sum
@@ -29,7 +30,7 @@ constexpr int DW_CHUNK = 128;
 constexpr int DW_MAX_K = PK_DW_MAX_K;
 constexpr int DW_SMEM_PER_WARP = DW_CHUNK + DW_MAX_K - 1;
 
-__device__ __forceinline__ float glu1(float a, float g) { return a * sigmoid_libm(g); }
+__device__ __forceinline__ float glu1(float a, float g) { return glu_gate(a, g); }
 
 // Channel-first GLU over each item's [2C, T] block.
 __global__ void __launch_bounds__(GLU_THREADS)
@@ -359,8 +360,7 @@ constexpr int DWA_ROW = 656;
 
 __host__ __device__ constexpr int dwa_row_need(int T) { return 4 * ((T + 6) / 4) + 8; }
 
-// GLU of 4 values: a * sigmoid(g), the pair reciprocal when both denominators
-// are below 2^126 (bit-identical to glu1 on each value).
+// GLU of 4 values as two packed pairs (bit-identical to glu1 on each value).
 __device__ __forceinline__ float4 glu4(float4 a, float4 g, float ba, float bg, bool bias) {
   if (bias) {
     const float2 a01 = add2(make_float2(a.x, a.y), splat2(ba));
@@ -370,18 +370,8 @@ __device__ __forceinline__ float4 glu4(float4 a, float4 g, float ba, float bg, b
     a = make_float4(a01.x, a01.y, a23.x, a23.y);
     g = make_float4(g01.x, g01.y, g23.x, g23.y);
   }
-  const float2 d01 = add2(splat2(1.0f), make_float2(expf(-g.x), expf(-g.y)));
-  const float2 d23 = add2(splat2(1.0f), make_float2(expf(-g.z), expf(-g.w)));
-  float2 r01, r23;
-  if (fmaxf(fmaxf(d01.x, d01.y), fmaxf(d23.x, d23.y)) < 0x1p126f) {
-    r01 = rcp2_1_2e126(d01);
-    r23 = rcp2_1_2e126(d23);
-  } else {
-    r01 = make_float2(sigmoid_libm(g.x), sigmoid_libm(g.y));
-    r23 = make_float2(sigmoid_libm(g.z), sigmoid_libm(g.w));
-  }
-  const float2 o01 = mul2(make_float2(a.x, a.y), r01);
-  const float2 o23 = mul2(make_float2(a.z, a.w), r23);
+  const float2 o01 = glu_gate2(make_float2(a.x, a.y), make_float2(g.x, g.y));
+  const float2 o23 = glu_gate2(make_float2(a.z, a.w), make_float2(g.z, g.w));
   return make_float4(o01.x, o01.y, o23.x, o23.y);
 }
 

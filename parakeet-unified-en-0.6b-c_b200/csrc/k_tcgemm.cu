@@ -196,14 +196,15 @@ __device__ __forceinline__ void store_cf32(const Epi &e, long long r, int c0, in
 // channel pairs: a = the 32 "value" channels d0 .. d0 + 31, g = their gates
 // d0 + C .. (the weight's rows are interleaved in groups of 32 at
 // preparation, so both halves of a pair sit in one thread's columns);
-// bias as pk_pointwise_conv1d adds it, then a * 1/(1 + expf(-g)).
+// bias as pk_pointwise_conv1d adds it, then a * 1/(1 + exp(-g)) as the GLU
+// kernels compute it (glu_gate).
 __device__ __forceinline__ void epi_glu32(const Epi &e, long long r, int d0, int C, float (&a)[32],
                                           const float (&g)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; j++) {
     const float va = e.bias ? a[j] + __ldg(e.bias + d0 + j) : a[j];
     const float vb = e.bias ? g[j] + __ldg(e.bias + C + d0 + j) : g[j];
-    a[j] = va * sigmoid_libm(vb);
+    a[j] = glu_gate(va, vb);
   }
   store_cf32(e, r, d0, C, a);
 }

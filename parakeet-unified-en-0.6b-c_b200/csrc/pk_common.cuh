@@ -209,6 +209,57 @@ __device__ __forceinline__ float sigmoid_libm(float b) {
   return d < 0x1p126f ? rcp_1_2e126(d) : __frcp_rn(d);
 }
 
+// ── the GLU gate (csrc/encoder.c:460-463: a * 1/(1 + expf(-b))) ───────────────
+// The reference's build evaluates expf with glibc's vector exp; the gate here
+// computes e^x from the hardware base-2 exponential instead, for |x| <= 86:
+// k = round(x log2 e) with the 1.5 * 2^23 shifter (one FMA: the rounding to an
+// integer happens in the add), f = x log2 e - k with log2 e split into its
+// float value and the float of the remainder (two FMAs; |f| <= 0.5 + 2^-20),
+// 2^f by ex2.approx.ftz on f in [-0.5, 0.5], and 2^k added to the exponent
+// field (the shifted value's low bits are k, so bits(t) << 23 is k << 23 mod
+// 2^32). Then 1 + e and its hardware reciprocal (rcp.approx, 1 ulp: the
+// denominator lies in [1, 2.2e37], so the result is a normal float). The gate
+// argument is clamped to [-86, 86] first: past it the sigmoid is 1 or below
+// 4.5e-38, where the reference gives 1 or below that (0 once expf overflows);
+// a NaN gate gives NaN as in the reference. Error against the correctly
+// rounded sigmoid: a few units in the last place (checked on the device
+// against glibc by a dense sweep), inside the GLU's tolerance.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+constexpr float GATE_L2E_HI = 1.44269502162933349609375f;   // float(log2 e)
+constexpr float GATE_L2E_LO = 1.925963033500011e-08f;       // float(log2 e - GATE_L2E_HI)
+constexpr float GATE_SHIFT = 12582912.0f;                   // 1.5 * 2^23
+
+__device__ __forceinline__ float2 glu_gate2(float2 a, float2 g) {
+  float2 m = sub2(splat2(0.0f), g);
+  m.x = fminf(fmaxf(m.x, -86.0f), 86.0f);
+  m.y = fminf(fmaxf(m.y, -86.0f), 86.0f);
+  const float2 t = fma2(m, splat2(GATE_L2E_HI), splat2(GATE_SHIFT));
+  float2 f = fma2(m, splat2(GATE_L2E_HI), sub2(splat2(GATE_SHIFT), t));
+  f = fma2(m, splat2(GATE_L2E_LO), f);
+  const float ex = __uint_as_float(__float_as_uint(ex2_approx(f.x)) + (__float_as_uint(t.x) << 23));
+  const float ey = __uint_as_float(__float_as_uint(ex2_approx(f.y)) + (__float_as_uint(t.y) << 23));
+  const float2 d = add2(splat2(1.0f), make_float2(ex, ey));
+  float2 o = mul2(a, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+  if (g.x != g.x) o.x = g.x;
+  if (g.y != g.y) o.y = g.y;
+  return o;
+}
+// The same operations on one value (bit-identical to either half of glu_gate2).
+__device__ __forceinline__ float glu_gate(float a, float g) {
+  float m = __fsub_rn(0.0f, g);
+  m = fminf(fmaxf(m, -86.0f), 86.0f);
+  const float t = fmaf(m, GATE_L2E_HI, GATE_SHIFT);
+  float f = fmaf(m, GATE_L2E_HI, __fsub_rn(GATE_SHIFT, t));
+  f = fmaf(m, GATE_L2E_LO, f);
+  const float e = __uint_as_float(__float_as_uint(ex2_approx(f)) + (__float_as_uint(t) << 23));
+  const float o = __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
+  return g != g ? g : o;
+}
+
 // ── exact division by a run-time divisor ─────────────────────────────────────
 // n / d for n < 2^32 and 1 <= d < 2^32 as a 64-bit multiply-high with
 // m = floor(2^64 / d) + 1: n*m/2^64 = n/d + err with 0 < err < 2^-32 <= 1/d,

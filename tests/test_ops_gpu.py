@@ -52,6 +52,42 @@ def test_swish_dense_sweep(cuda, oracle):
     assert_bitexact(host(xd), oracle.swish(x), "swish sweep")
 
 
+def test_glu_gate_dense_sweep(cuda, oracle):
+    """The GLU gate's own exp (ex2-based, pk_common.cuh glu_gate) on a dense
+    sweep of gate values in [-100, 100] (every 509th float) plus the clamp
+    edges and NaN: a * 1/(1 + exp(-g)) with a = 1 against the restatement
+    (glibc expf, as the reference computes it) within the GLU tolerance, and
+    against the float64 sigmoid within 4 units in the last place inside the
+    clamp (|g| <= 86) where the result is a normal float."""
+    u = np.arange(0, 0x42C80000, 509, dtype=np.uint32)     # [+0, 100)
+    pos = u.view(np.float32)
+    g = np.concatenate([pos, -pos, np.float32([86.0, -86.0, 85.99, -86.01, 88.7, -88.8, 1e30, -1e30])])
+    g = g.astype(np.float32)
+    n = (g.size + D - 1) // D * D
+    g = np.concatenate([g, np.zeros(n - g.size, np.float32)])
+    rows = n // D
+    tf = np.empty((rows, 2 * D), np.float32)
+    tf[:, :D] = 1.0
+    tf[:, D:] = g.reshape(rows, D)
+    out = empty((rows, D))
+    with cuda.Seq([rows]) as seq:
+        cuda.call("pkcu_glu", dev(tf).data_ptr(), None, out.data_ptr(), D, cuda.PKCU_TIME_FIRST,
+                  seq.handle, cuda.stream_handle())
+        got = host(out).reshape(-1)
+    assert_close(got, oracle.glu_time_first(tf).reshape(-1), "gate vs glibc expf")
+    exact = 1.0 / (1.0 + np.exp(-g.astype(np.float64)))
+    normal = (exact >= np.finfo(np.float32).tiny) & (np.abs(g) <= 86.0)   # inside the clamp
+    ulp = np.spacing(exact[normal].astype(np.float32)).astype(np.float64)
+    err_ulp = np.abs(got[normal].astype(np.float64) - exact[normal]) / ulp
+    assert err_ulp.max() <= 4.0, err_ulp.max()
+    # a NaN gate gives NaN (1/(1 + expf(NaN)) in the reference)
+    tf[0, D] = np.nan
+    with cuda.Seq([rows]) as seq:
+        cuda.call("pkcu_glu", dev(tf).data_ptr(), None, out.data_ptr(), D, cuda.PKCU_TIME_FIRST,
+                  seq.handle, cuda.stream_handle())
+        assert np.isnan(host(out)[0, 0])
+
+
 # ── LayerNorm family ──────────────────────────────────────────────────────────
 
 @pytest.mark.parametrize("R,Dd,offset", [(1, 1024, 0), (7, 1024, 0), (375, 1024, 0),
