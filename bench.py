@@ -879,19 +879,27 @@ def time_asr_decode(stream, reps, n_utts=256, T=375, cpu=True):
         d, bp, jp = _synthetic_checkpoint(blank_bias=bb)
         try:
             enc = np.random.default_rng(21).standard_normal((n_utts * T, D)).astype(np.float32)
+            modes = {}
             with pkcuda.Weights(bp, jp) as w:
                 w.upload(stream)
                 with pkcuda.ASR(w, stream) as asr:
                     x = torch.from_numpy(enc).cuda()
-                    toks = asr.decode(x, [T] * n_utts, stream)
-                    torch.cuda.synchronize()
-                    t0 = time.perf_counter()
-                    for _ in range(max(reps, 1)):
+                    for mname, mode in (("fused_cuda_cores", asr.DECODE_FUSED), ("tcgen05", asr.DECODE_TC)):
+                        asr.set_decode_mode(mode)
                         toks = asr.decode(x, [T] * n_utts, stream)
-                    dt = (time.perf_counter() - t0) / max(reps, 1)
+                        torch.cuda.synchronize()
+                        t0 = time.perf_counter()
+                        for _ in range(max(reps, 1)):
+                            toks = asr.decode(x, [T] * n_utts, stream)
+                        modes[mname] = ((time.perf_counter() - t0) / max(reps, 1), toks)
+            dt, toks = min(modes.values(), key=lambda v: v[0])
+            same = all(len(a) == len(b) and (a == b).all() for a, b in zip(modes["fused_cuda_cores"][1],
+                                                                          modes["tcgen05"][1]))
             ntok = int(sum(len(t) for t in toks))
             r = {"utterances": n_utts, "frames": T, "blank_bias": bb, "seconds_per_call": round(dt, 4),
-                 "frames_per_s": round(n_utts * T / dt), "tokens_per_frame": round(ntok / (n_utts * T), 3)}
+                 "frames_per_s": round(n_utts * T / dt), "tokens_per_frame": round(ntok / (n_utts * T), 3),
+                 "seconds_per_call_by_mode": {k: round(v[0], 4) for k, v in modes.items()},
+                 "modes_agree": bool(same)}
             if cpu:
                 r["cpu_baseline"] = _cpu_ref_decode(bp, jp, enc[:T], T)
             out[name] = r

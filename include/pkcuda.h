@@ -593,12 +593,15 @@ int  pkcu_asr_set_chunk_mode(pkcu_asr *m, int mode);   /* PKCU_CHUNK_AUTO / _OFF
 int  pkcu_asr_decode(pkcu_asr *m, const float *enc, const int *enc_frames, int n_utts,
                      int *tokens, int *n_tokens, pkcu_stream_t stream);
 /* How pkcu_asr_transcribe and pkcu_asr_decode decode: FUSED (the default) -- the decoder's own
- * product kernels (pkcu_greedy_decode_fused); GRAPH -- cuBLAS products at the
- * decoder's GEMM hooks inside its CUDA graph (pkcu_greedy_decode_graph);
- * EAGER -- the same products launched one at a time (pkcu_greedy_decode). */
+ * CUDA-core product kernels (pkcu_greedy_decode_fused); TC -- the products on
+ * the library's tcgen05 GEMM at the decoder's hooks inside its CUDA graph;
+ * GRAPH -- cuBLAS products at those hooks (pkcu_greedy_decode_graph);
+ * EAGER -- the cuBLAS products launched one at a time (pkcu_greedy_decode).
+ * The encoder projection (joint.enc) runs on the tcgen05 GEMM in every mode. */
 #define PKCU_ASR_DECODE_FUSED 0
 #define PKCU_ASR_DECODE_GRAPH 1
 #define PKCU_ASR_DECODE_EAGER 2
+#define PKCU_ASR_DECODE_TC    3
 int  pkcu_asr_set_decode_mode(pkcu_asr *m, int mode);
 
 /* ── batched greedy RNN-T decode (csrc/decoder.c:80-132) ──────────────────

@@ -49,20 +49,24 @@
 namespace pk {
 namespace tc {
 
-constexpr int BM = 128, BN = 256, BK = 32;
+constexpr int BM = 128, BK = 32;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr int A_TILE = BM * BK * 2;   // one A part of a stage: 8 KB
-constexpr int B_TILE = BN * BK * 2;   // one weight plane of a stage: 16 KB
-constexpr int TMEM_COLS = 2 * BN;     // two accumulators
 
-template <int NPB>
+// Tile width BN: 256 for large products, 64 when 256-wide tiles would leave
+// most SMs idle (the decoder's products over a batch of a few hundred rows).
+template <int NPB, int BN_>
 struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int B_TILE = BN * BK * 2;      // one weight plane of a stage
   static constexpr int STAGE = 3 * A_TILE + NPB * B_TILE;
-  static constexpr int STAGES = NPB == 1 ? 5 : 3;
+  static constexpr int STAGES = (220 * 1024) / STAGE < 6 ? (220 * 1024) / STAGE : 6;
   static constexpr int PRODUCTS = NPB == 1 ? 3 : 6;
   static constexpr int DRAIN_KB = NPB == 1 ? 4 : 2;   // K blocks per accumulator run (24 MMAs)
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr int TMEM_COLS = 2 * BN;            // two accumulators
+  static constexpr int CW = BN / 2;                   // columns per epilogue warp
 };
 
 // Part pairs (A part, weight plane) with i + j <= 2, in issue order.
@@ -164,6 +168,7 @@ struct Epi {
   float *Qu, *Qv, *Kh, *Vh;
   SeqDev seq;
   int channels;          // CF / GLU: output channels per frame (GLU: C, half of N)
+  int vec;               // row-major output rows 16-byte aligned (ldc % 4 == 0)
 };
 
 // Item of frame r: a division for a uniform batch, else a binary search of
@@ -282,11 +287,29 @@ __device__ __forceinline__ void epi_store32(const Epi &e, long long r, int n0, f
   for (int j = 0; j < 32; j += 4) st4(c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
 }
 
-template <int NPB>
+// Row-major STORE / SWISH / RESID of the columns n .. n + ncols - 1 (ncols <=
+// 32) one at a time: a ragged last column group (N not a multiple of 32) or
+// rows that are not 16-byte aligned (ldc not a multiple of 4).
+__device__ __forceinline__ void epi_store_tail(const Epi &e, long long r, int n, int ncols, const float (&v)[32]) {
+  float *c = e.C + r * e.ldc + n;
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    if (j < ncols) {
+      float o = e.bias ? v[j] + __ldg(e.bias + n + j) : v[j];
+      if (e.mode == PK_TC_SWISH) o = swish_poly(o);
+      else if (e.mode == PK_TC_RESID) o = fmaf(o, e.rscale, c[j]);
+      else if (e.beta != 0.0f) o = fmaf(e.beta, c[j], o);
+      c[j] = o;
+    }
+  }
+}
+
+template <int NPB, int BN_>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                int M, int N, int K, Epi epi) {
-  using C = Cfg<NPB>;
+  using C = Cfg<NPB, BN_>;
+  constexpr int BN = C::BN, B_TILE = C::B_TILE, TMEM_COLS = C::TMEM_COLS, CW = C::CW;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -417,14 +440,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // MMAs of the next tile run into the free accumulators meanwhile ──
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const unsigned lane_addr = ((unsigned)(q * 32) << 16) + half * 128;
+    const unsigned lane_addr = ((unsigned)(q * 32) << 16) + half * CW;
     int gr = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-      float sum[128];
+      float sum[CW];
 #pragma unroll
-      for (int j = 0; j < 128; j++) sum[j] = 0.0f;
+      for (int j = 0; j < CW; j++) sum[j] = 0.0f;
       for (int run = 0; run < n_runs; run++, gr++) {
         const int buf = gr & 1;
         // the outcome is made warp-uniform: tcgen05.ld needs every lane
@@ -436,7 +459,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < CW / 32; c++) {
           float v[32];
           tmem_ld32(tmem + lane_addr + buf * BN + c * 32, v);
 #pragma unroll
@@ -447,11 +470,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (lane == 0) mbar_arrive(acc_empty + buf);
       }
       const long long r = (long long)m0 + row;
-      if (ok && r < M && epi.mode == PK_TC_GLU) {
+      if (CW >= 64 && ok && r < M && epi.mode == PK_TC_GLU) {
         // columns 64k .. 64k + 31 hold value channels 32k .., the next 32 their gates
 #pragma unroll
-        for (int c = 0; c < 4; c += 2) {
-          const int n = n0 + half * 128 + c * 32;
+        for (int c = 0; c + 1 < CW / 32; c += 2) {
+          const int n = n0 + half * CW + c * 32;
           if (n < N) {
             float a[32], g[32];
 #pragma unroll
@@ -464,13 +487,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
       } else if (ok && r < M) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-          const int n = n0 + half * 128 + c * 32;
+        for (int c = 0; c < CW / 32; c++) {
+          const int n = n0 + half * CW + c * 32;
           if (n < N) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; j++) v[j] = sum[c * 32 + j] * epi.alpha;
-            epi_store32(epi, r, n, v);
+            if (n + 32 <= N && epi.vec) epi_store32(epi, r, n, v);
+            else epi_store_tail(epi, r, n, N - n < 32 ? N - n : 32, v);
           }
         }
       }
@@ -643,20 +667,40 @@ int tmap_bf16(CUtensorMap *map, const void *base, long long rows, long long cols
   return PKCU_OK;
 }
 
-template <int NPB>
+template <int NPB, int BN>
+int *optin_flags() {
+  static int flags[64];
+  return flags;
+}
+
+template <int NPB, int BN>
 int launch(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K, const tc::Epi &e,
            cudaStream_t s) {
-  using C = tc::Cfg<NPB>;
-  static int flags[64];
-  smem_optin(tc::tc_gemm_kernel<NPB>, C::SMEM, flags);
+  using C = tc::Cfg<NPB, BN>;
+  smem_optin(tc::tc_gemm_kernel<NPB, BN>, C::SMEM, optin_flags<NPB, BN>());
   // persistent: one CTA per SM (the stage ring fills most of its shared memory)
-  const long long tiles = (long long)((N + tc::BN - 1) / tc::BN) * ((M + tc::BM - 1) / tc::BM);
+  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + tc::BM - 1) / tc::BM);
   const unsigned grid = (unsigned)(tiles < pkcu_sm_count() ? tiles : pkcu_sm_count());
-  tc::tc_gemm_kernel<NPB><<<grid, tc::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, e);
+  tc::tc_gemm_kernel<NPB, BN><<<grid, tc::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, e);
   return pkcu_launch_status("tcgen05 GEMM");
 }
 
+// 256-wide tiles unless they would occupy fewer than half the SMs (the GLU
+// epilogue needs them: a value group and its gates in one warp's columns).
+int narrow_tiles(int M, int N, int mode) {
+  if (mode == PK_TC_GLU) return 0;
+  const long long wide = (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM);
+  return wide * 2 < pkcu_sm_count();
+}
+
 }  // namespace
+
+extern "C" void pk_tc_warm(void) {
+  smem_optin(tc::tc_gemm_kernel<1, 256>, tc::Cfg<1, 256>::SMEM, optin_flags<1, 256>());
+  smem_optin(tc::tc_gemm_kernel<3, 256>, tc::Cfg<3, 256>::SMEM, optin_flags<3, 256>());
+  smem_optin(tc::tc_gemm_kernel<1, 64>, tc::Cfg<1, 64>::SMEM, optin_flags<1, 64>());
+  smem_optin(tc::tc_gemm_kernel<3, 64>, tc::Cfg<3, 64>::SMEM, optin_flags<3, 64>());
+}
 
 extern "C" int pk_tc_wait_timeouts(unsigned *count, int reset) {
   return tc::pk_tc_wait_timeouts_acc(count, reset);
@@ -697,11 +741,14 @@ extern "C" int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq 
 extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                           const pk_tc_epi *ep, pkcu_stream_t stream) {
   if (!a_parts || !planes || !ep || (npb != 1 && npb != 3) || M <= 0 || N <= 0 || K <= 0 ||
-      K % tc::BK || N % 32 || !PK_ALIGNED16(a_parts) || !PK_ALIGNED16(planes))
+      K % tc::BK || (N % 32 && ep->mode != PK_TC_STORE && ep->mode != PK_TC_SWISH &&
+                     ep->mode != PK_TC_RESID) ||
+      !PK_ALIGNED16(a_parts) || !PK_ALIGNED16(planes))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: bad arguments (M %d, N %d, K %d)", M, N, K);
+  const int narrow = narrow_tiles(M, N, ep->mode);
   CUtensorMap ma, mb;
   int st = tmap_bf16(&ma, a_parts, M, 3LL * K, 3LL * K, tc::BM);
-  if (!st) st = tmap_bf16(&mb, planes, N, (long long)npb * K, (long long)npb * K, tc::BN);
+  if (!st) st = tmap_bf16(&mb, planes, N, (long long)npb * K, (long long)npb * K, narrow ? 64 : 256);
   if (st) return st;
   tc::Epi e;
   e.mode = ep->mode;
@@ -727,11 +774,13 @@ extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int 
       (!ep->seq || !e.bias || !e.u || !e.v || !e.Qu || !e.Qv || !e.Kh || !e.Vh || N != 3 * PK_D ||
        M != ep->seq->frames))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the QKV epilogue needs the batch and its outputs");
-  if ((e.mode == PK_TC_STORE || e.mode == PK_TC_SWISH || e.mode == PK_TC_RESID) &&
-      (!e.C || !PK_ALIGNED16(e.C) || e.ldc % 4))
-    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: output must be 16-byte aligned rows");
-  return npb == 1 ? launch<1>(ma, mb, M, N, K, e, (cudaStream_t)stream)
-                  : launch<3>(ma, mb, M, N, K, e, (cudaStream_t)stream);
+  if ((e.mode == PK_TC_STORE || e.mode == PK_TC_SWISH || e.mode == PK_TC_RESID) && (!e.C || e.ldc < N))
+    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: no output, or rows shorter than N");
+  e.vec = PK_ALIGNED16(e.C) && e.ldc % 4 == 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (narrow)
+    return npb == 1 ? launch<1, 64>(ma, mb, M, N, K, e, s) : launch<3, 64>(ma, mb, M, N, K, e, s);
+  return npb == 1 ? launch<1, 256>(ma, mb, M, N, K, e, s) : launch<3, 256>(ma, mb, M, N, K, e, s);
 }
 
 // ── public entry points: weight products (csrc/tensor_ops.c:50-61) ──────────

@@ -537,6 +537,10 @@ struct pkcu_asr {
     const float *j_enc, *j_pred, *j_out;   /* [1024, 640], [640, 640], [640, 1025] */
     pkcu_dec_params dec;
     int decode_mode;                   /* PKCU_ASR_DECODE_* */
+    void *tc_planes;                   /* the decoder's products as tcgen05 GEMM operands */
+    const void *tc_w[7];               /* per PKCU_GEMM_DEC_* - 32: K-major three-part planes */
+    void *dec_ws;                      /* the products' activation parts */
+    size_t dec_ws_cap;
     /* the last call's working buffers, kept while the same lengths come again */
     int t_n, *t_frames;                /* mel frames the transcribe buffers were made for */
     pkcu_pre_plan *t_plan;
@@ -600,7 +604,8 @@ static int *copy_lengths(const int *frames, int n)
 int pkcu_asr_set_decode_mode(pkcu_asr *m, int mode)
 {
     if (!m) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_decode_mode: NULL model");
-    if (mode != PKCU_ASR_DECODE_FUSED && mode != PKCU_ASR_DECODE_GRAPH && mode != PKCU_ASR_DECODE_EAGER)
+    if (mode != PKCU_ASR_DECODE_FUSED && mode != PKCU_ASR_DECODE_GRAPH && mode != PKCU_ASR_DECODE_EAGER &&
+        mode != PKCU_ASR_DECODE_TC)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_set_decode_mode: unknown mode %d", mode);
     m->decode_mode = mode;
     return PKCU_OK;
@@ -614,6 +619,8 @@ void pkcu_asr_destroy(pkcu_asr *m)
     pkcu_encoder_model_destroy(m->enc);
     if (m->blas) cublasDestroy(m->blas);
     if (m->owned) cudaFree(m->owned);
+    if (m->tc_planes) cudaFree(m->tc_planes);
+    if (m->dec_ws) cudaFree(m->dec_ws);
     free(m);
 }
 
@@ -689,9 +696,33 @@ int pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out)
     if (!st) {
         m->dec.embed = dp[0]; m->dec.lstm0_b = dp[1]; m->dec.lstm1_b = dp[2];
         m->dec.joint_enc_b = dp[3]; m->dec.joint_pred_b = dp[4]; m->dec.joint_out_b = dp[5];
-        if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
-            st = pkcu_launch_status("pkcu_asr_create");
     }
+    /* the decoder's products as tcgen05 GEMM operands (three bf16 parts,
+     * K-major): joint.enc [1024, 640], the LSTM W_i / W_r [2560, 640] (already
+     * [N, K]), joint.pred [640, 640], joint.out [640, 1025]; without the memory
+     * the cuBLAS / CUDA-core paths remain */
+    if (!st) {
+        static const long long tk[7] = {PK_D, 640, 640, 640, 640, 640, 640};
+        static const long long tn[7] = {640, 2560, 2560, 2560, 2560, 640, 1025};
+        long long off[8] = {0};
+        for (int i = 0; i < 7; i++) off[i + 1] = off[i] + ((3 * tk[i] * tn[i] + 127) & ~127LL);
+        if (cudaMalloc(&m->tc_planes, sizeof(uint16_t) * (size_t)off[7]) != cudaSuccess) {
+            cudaGetLastError();
+            m->tc_planes = NULL;
+        } else {
+            const float *src[7] = {m->j_enc, m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
+            for (int i = 0; i < 7 && !st; i++) {
+                void *dstp = (uint16_t *)m->tc_planes + off[i];
+                float alpha;
+                st = (i >= 1 && i <= 4) ? pk_tc_prepare_rows(src[i], (int)tn[i], (int)tk[i], 0, dstp, stream)
+                                        : pk_tc_prepare(src[i], 32, 0.0f, (int)tk[i], (int)tn[i], dstp, &alpha, stream);
+                m->tc_w[i] = dstp;
+            }
+            if (!st) pk_tc_warm();
+        }
+    }
+    if (!st && cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+        st = pkcu_launch_status("pkcu_asr_create");
     if (st) {
         pkcu_asr_destroy(m);
         return st;
@@ -737,6 +768,42 @@ static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr_transcribe: unknown decoder GEMM %d", gemm);
 }
 
+/* The decoder's products on the library's tcgen05 GEMM: the activation rows'
+ * three bf16 parts into the decode workspace, then the product with the
+ * weight's planes (prepared at pkcu_asr_create). Capture-safe: no allocation,
+ * no synchronisation (the workspace is sized before the decode starts). */
+static int dec_tc(DecCtx *c, int which, int M, int N, int K, const float *A, float *C, pkcu_stream_t stream)
+{
+    pkcu_asr *m = c->m;
+    if ((size_t)M * 3 * K * 2 > m->dec_ws_cap)
+        return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: decode workspace too small");
+    int st = pk_split_rows_bf16x3(A, m->dec_ws, M, K, stream);
+    if (st) return st;
+    pk_tc_epi e;
+    memset(&e, 0, sizeof(e));
+    e.mode = PK_TC_STORE;
+    e.alpha = 1.0f;
+    e.C = C;
+    return pk_tc_gemm(m->dec_ws, m->tc_w[which], 3, M, N, K, &e, stream);
+}
+
+static int dec_hook_tc(void *user, int block, int gemm, pkcu_stream_t stream)
+{
+    (void)block;
+    DecCtx *c = (DecCtx *)user;
+    const int B = c->B, Hd = 640;
+    switch (gemm) {
+    case PKCU_GEMM_DEC_ENC:   return dec_tc(c, 0, (int)c->F, Hd, PK_D, c->x, c->go.enc, stream);
+    case PKCU_GEMM_DEC_L0_WI: return dec_tc(c, 1, B, 4 * Hd, Hd, c->gi.x0, c->go.g0i, stream);
+    case PKCU_GEMM_DEC_L0_WR: return dec_tc(c, 2, B, 4 * Hd, Hd, c->gi.h0, c->go.g0r, stream);
+    case PKCU_GEMM_DEC_L1_WI: return dec_tc(c, 3, B, 4 * Hd, Hd, c->gi.h0, c->go.g1i, stream);
+    case PKCU_GEMM_DEC_L1_WR: return dec_tc(c, 4, B, 4 * Hd, Hd, c->gi.h1, c->go.g1r, stream);
+    case PKCU_GEMM_DEC_PRED:  return dec_tc(c, 5, B, Hd, Hd, c->gi.h1, c->go.pred, stream);
+    case PKCU_GEMM_DEC_OUT:   return dec_tc(c, 6, B, 1025, Hd, c->gi.hidden, c->go.out, stream);
+    }
+    return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: unknown decoder GEMM %d", gemm);
+}
+
 /* Greedy decode of encoder outputs x [sum enc_frames, 1024] with the model's
  * decoder, in the model's decode mode; host results. The decoder (with its
  * captured graph) is kept for the next call with the same lengths. */
@@ -764,14 +831,32 @@ static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_
     dc->F = F;
     dc->B = n_utts;
     pkcu_decoder *dec = m->d_dec;
+    /* the tcgen05 products' activation parts: the encoder projection's F rows
+     * of 1024, the per-iteration products' B rows of 640 */
+    const size_t need = (size_t)(F * 3 * PK_D * 2 > (long long)n_utts * 3 * 640 * 2 ? F * 3 * PK_D * 2
+                                                                                   : (long long)n_utts * 3 * 640 * 2);
+    if (m->tc_planes && need > m->dec_ws_cap) {
+        if (m->dec_ws) cudaFree(m->dec_ws);
+        m->dec_ws_cap = 0;
+        if (cudaMalloc(&m->dec_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            m->dec_ws = NULL;
+            return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_asr: %zu bytes of decode workspace", need);
+        }
+        m->dec_ws_cap = need;
+    }
+    pkcu_gemm_hook enc_hook = m->tc_planes ? dec_hook_tc : dec_hook;
     if (m->decode_mode == PKCU_ASR_DECODE_FUSED) {
         if (!m->d_weights) {
             const pkcu_dec_weights dw = {m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
             st = pkcu_decoder_set_weights(dec, &dw, stream);
             m->d_weights = !st;
         }
-        if (!st) st = dec_hook(dc, -1, PKCU_GEMM_DEC_ENC, stream);
+        if (!st) st = enc_hook(dc, -1, PKCU_GEMM_DEC_ENC, stream);
         if (!st) st = pkcu_greedy_decode_fused(dec, &m->dec, stream);
+    } else if (m->decode_mode == PKCU_ASR_DECODE_TC) {
+        if (!m->tc_planes) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: the tensor-core decode needs its operands");
+        st = pkcu_greedy_decode_graph(dec, &m->dec, dec_hook_tc, dc, stream);
     } else {
         st = m->decode_mode == PKCU_ASR_DECODE_EAGER
                  ? pkcu_greedy_decode(dec, &m->dec, dec_hook, dc, stream)

@@ -79,6 +79,9 @@ int pk_tc_prepare(const void *data, int bits, float scale, int K, int N, void *p
                   pkcu_stream_t stream);
 int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                const pk_tc_epi *ep, pkcu_stream_t stream);
+/* Raises the GEMM kernels' shared-memory limit now, so that a first launch
+ * inside a stream capture makes no attribute call. */
+void pk_tc_warm(void);
 /* A pointwise weight W [N, K] (already K-major) -> three-part planes [N, 3K];
  * glu: rows interleaved value / gate in groups of 32 for PK_TC_GLU. */
 int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *planes, pkcu_stream_t stream);

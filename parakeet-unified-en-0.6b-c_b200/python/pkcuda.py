@@ -784,7 +784,7 @@ class ASR:
         check(lib().pkcu_asr_create(weights.h, stream_handle(stream), C.byref(h)), "pkcu_asr_create")
         self.handle = h
 
-    DECODE_FUSED, DECODE_GRAPH, DECODE_EAGER = 0, 1, 2
+    DECODE_FUSED, DECODE_GRAPH, DECODE_EAGER, DECODE_TC = 0, 1, 2, 3
 
     def set_decode_mode(self, mode: int) -> None:
         call("pkcu_asr_set_decode_mode", self.handle, int(mode))

@@ -318,7 +318,7 @@ def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):
             frames = [mel.shape[1], mel2.shape[1]]
             got = []
             ref_enc = dev(np.concatenate([e.reshape(-1) for e in enc]))
-            for mode in (asr.DECODE_FUSED, asr.DECODE_GRAPH, asr.DECODE_EAGER):
+            for mode in (asr.DECODE_FUSED, asr.DECODE_TC, asr.DECODE_GRAPH, asr.DECODE_EAGER):
                 asr.set_decode_mode(mode)
                 got.append(asr.transcribe(mels, frames))
                 # the decode alone, on the reference's own encoder outputs
