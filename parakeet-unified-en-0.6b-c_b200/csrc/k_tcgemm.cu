@@ -169,6 +169,10 @@ struct Epi {
   SeqDev seq;
   int channels;          // CF / GLU: output channels per frame (GLU: C, half of N)
   int vec;               // row-major output rows 16-byte aligned (ldc % 4 == 0)
+  // Z products of the same shape in one launch (the per-head products): entry
+  // z reads A rows from z * a_z and B rows from z * b_z, and writes from C + z * c_z
+  int Z;
+  long long a_z, b_z, c_z;
 };
 
 // Item of frame r: a division for a uniform batch, else a binary search of
@@ -287,6 +291,16 @@ __device__ __forceinline__ void epi_store32(const Epi &e, long long r, int n0, f
   for (int j = 0; j < 32; j += 4) st4(c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
 }
 
+// STORE_T: C[n, m] = alpha (A W)[m, n] -- the product written transposed, so
+// the lanes of a warp (consecutive m) store consecutive addresses.
+__device__ __forceinline__ void epi_store_t(float *cz, long long ldc, long long r, int n, int ncols,
+                                            const float (&v)[32]) {
+  float *o = cz + (long long)n * ldc + r;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j < ncols) o[(long long)j * ldc] = v[j];
+}
+
 // Row-major STORE / SWISH / RESID of the columns n .. n + ncols - 1 (ncols <=
 // 32) one at a time: a ragged last column group (N not a multiple of 32) or
 // rows that are not 16-byte aligned (ldc not a multiple of 4).
@@ -327,7 +341,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; n-blocks
   // vary fastest, so the CTAs of a wave share the rows of A they read
   const int tiles_n = (N + BN - 1) / BN;
-  const int n_tiles = tiles_n * ((M + BM - 1) / BM);
+  const int per_z = tiles_n * ((M + BM - 1) / BM);
+  const int n_tiles = per_z * epi.Z;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -360,7 +375,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       int it = 0;   // K blocks issued by this CTA, over all its tiles
       bool stop = false;
       for (int tile = blockIdx.x; tile < n_tiles && !stop; tile += gridDim.x) {
-        const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+        const int z = tile / per_z, t = tile - z * per_z;
+        const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+        const int ya = (int)(z * epi.a_z) + m0, yb = (int)(z * epi.b_z) + n0;
         for (int kb = 0; kb < nkb; kb++) {
           const int s = it % C::STAGES;
           if (it >= C::STAGES && !mbar_wait(empty + s, ((it / C::STAGES) - 1) & 1)) {
@@ -373,9 +390,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
           unsigned char *st = smem + s * C::STAGE;
           mbar_arrive_tx(full + s, C::STAGE);
-          for (int p = 0; p < 3; p++) tma_load_2d(st + p * A_TILE, &map_a, p * K + kb * BK, m0, full + s);
+          for (int p = 0; p < 3; p++) tma_load_2d(st + p * A_TILE, &map_a, p * K + kb * BK, ya, full + s);
           for (int p = 0; p < NPB; p++)
-            tma_load_2d(st + 3 * A_TILE + p * B_TILE, &map_b, p * K + kb * BK, n0, full + s);
+            tma_load_2d(st + 3 * A_TILE + p * B_TILE, &map_b, p * K + kb * BK, yb, full + s);
           it++;
         }
       }
@@ -444,7 +461,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     int gr = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      const int z = tile / per_z, t = tile - z * per_z;
+      const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
       float sum[CW];
 #pragma unroll
       for (int j = 0; j < CW; j++) sum[j] = 0.0f;
@@ -485,7 +503,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             epi_glu32(epi, r, n / 2, epi.channels, a, g);
           }
         }
-      } else if (ok && r < M) {
+      } else if (ok && r < M && epi.mode == PK_TC_STORE_T) {
 #pragma unroll
         for (int c = 0; c < CW / 32; c++) {
           const int n = n0 + half * CW + c * 32;
@@ -493,8 +511,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; j++) v[j] = sum[c * 32 + j] * epi.alpha;
-            if (n + 32 <= N && epi.vec) epi_store32(epi, r, n, v);
-            else epi_store_tail(epi, r, n, N - n < 32 ? N - n : 32, v);
+            epi_store_t(epi.C + z * epi.c_z, epi.ldc, r, n, N - n < 32 ? N - n : 32, v);
+          }
+        }
+      } else if (ok && r < M) {
+        Epi ez = epi;
+        ez.C = epi.C + z * epi.c_z;
+#pragma unroll
+        for (int c = 0; c < CW / 32; c++) {
+          const int n = n0 + half * CW + c * 32;
+          if (n < N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = sum[c * 32 + j] * epi.alpha;
+            if (n + 32 <= N && ez.vec) epi_store32(ez, r, n, v);
+            else epi_store_tail(ez, r, n, N - n < 32 ? N - n : 32, v);
           }
         }
       }
@@ -617,6 +648,59 @@ __global__ void split_cf_t_kernel(const float *__restrict__ X, __nv_bfloat16 *__
   }
 }
 
+// Rows A [M, K] (any K) -> parts [M, 3 Kp], row m = [a0 | a1 | a2] each Kp wide
+// with zeros from column K on: a K-major operand whose K is padded to the
+// GEMM's 32-wide K blocks (the score rows S of the context product, K = T).
+__global__ void split_rows_pad_kernel(const float *__restrict__ A, __nv_bfloat16 *__restrict__ out, long long M,
+                                      int K, int Kp) {
+  const long long total = M * Kp;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long m = e / Kp;
+    const int k = (int)(e - m * Kp);
+    const float x = k < K ? __ldg(A + m * K + k) : 0.0f;
+    const __nv_bfloat16 p0 = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(p0);
+    const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+    __nv_bfloat16 *o = out + m * 3 * Kp + k;
+    o[0] = p0;
+    o[Kp] = p1;
+    o[2 * Kp] = p2;
+  }
+}
+
+// Z matrices X [R, Cc] (one after another) -> their transposes as parts: out
+// rows z Cc + c = [x0 | x1 | x2] of column c, each Kp wide, zeros from R on
+// (the value heads V [T, 128] as the context product's K-major operand).
+__global__ void split_t_pad_kernel(const float *__restrict__ X, __nv_bfloat16 *__restrict__ out, int R, int Cc,
+                                   int Kp) {
+  __shared__ float tile[32][33];
+  const int z = blockIdx.z;
+  const int r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float *x = X + (long long)z * R * Cc;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < R && c < Cc) ? __ldg(x + (long long)r * Cc + c) : 0.0f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
+    if (c < Cc && r < Kp) {
+      const float v = tile[tx][i];   // 0 past R
+      const __nv_bfloat16 p0 = __float2bfloat16_rn(v);
+      const float r1 = v - __bfloat162float(p0);
+      const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+      __nv_bfloat16 *o = out + ((long long)z * Cc + c) * 3 * Kp + r;
+      o[0] = p0;
+      o[Kp] = p1;
+      o[2 * Kp] = p2;
+    }
+  }
+}
+
 PK_WAIT_TIMEOUTS_ACCESSOR(pk_tc_wait_timeouts_acc)
 
 }  // namespace tc
@@ -679,7 +763,7 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K, co
   using C = tc::Cfg<NPB, BN>;
   smem_optin(tc::tc_gemm_kernel<NPB, BN>, C::SMEM, optin_flags<NPB, BN>());
   // persistent: one CTA per SM (the stage ring fills most of its shared memory)
-  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + tc::BM - 1) / tc::BM);
+  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + tc::BM - 1) / tc::BM) * e.Z;
   const unsigned grid = (unsigned)(tiles < pkcu_sm_count() ? tiles : pkcu_sm_count());
   tc::tc_gemm_kernel<NPB, BN><<<grid, tc::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, e);
   return pkcu_launch_status("tcgen05 GEMM");
@@ -689,6 +773,7 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K, co
 // epilogue needs them: a value group and its gates in one warp's columns).
 int narrow_tiles(int M, int N, int mode) {
   if (mode == PK_TC_GLU) return 0;
+  if (N <= 128) return 1;   // a 256-wide tile would be half padding
   const long long wide = (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM);
   return wide * 2 < pkcu_sm_count();
 }
@@ -730,6 +815,24 @@ extern "C" int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *p
   return pkcu_launch_status("tcgen05 GEMM pointwise weight preparation");
 }
 
+extern "C" int pk_split_rows_pad(const float *A, void *parts, long long M, int K, int Kp, pkcu_stream_t stream) {
+  if (!A || !parts || M <= 0 || K <= 0 || Kp < K) return pkcu_fail(PKCU_ERR_ARG, "pk_split_rows_pad: bad argument");
+  long long blocks = (M * Kp + 255) / 256;
+  if (blocks > 16LL * pkcu_sm_count()) blocks = 16LL * pkcu_sm_count();
+  tc::split_rows_pad_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      A, static_cast<__nv_bfloat16 *>(parts), M, K, Kp);
+  return pkcu_launch_status("pk_split_rows_pad");
+}
+
+extern "C" int pk_split_t_pad(const float *X, void *parts, int Z, int R, int Cc, int Kp, pkcu_stream_t stream) {
+  if (!X || !parts || Z <= 0 || Z > 65535 || R <= 0 || Cc <= 0 || Kp < R)
+    return pkcu_fail(PKCU_ERR_ARG, "pk_split_t_pad: bad argument");
+  const dim3 grid((unsigned)((Kp + 31) / 32), (unsigned)((Cc + 31) / 32), (unsigned)Z);
+  tc::split_t_pad_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(X, static_cast<__nv_bfloat16 *>(parts), R, Cc,
+                                                                  Kp);
+  return pkcu_launch_status("pk_split_t_pad");
+}
+
 extern "C" int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream) {
   if (!X || !parts || !seq || C <= 0) return pkcu_fail(PKCU_ERR_ARG, "pk_split_cf_t: bad argument");
   const dim3 grid((unsigned)((seq->dev.max_T + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)seq->dev.n_items);
@@ -738,17 +841,42 @@ extern "C" int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq 
   return pkcu_launch_status("pk_split_cf_t");
 }
 
+namespace {
+int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long long b_rows, int npb, int M,
+                int N, int K, const pk_tc_epi *ep, int Z, long long a_z, long long b_z, long long c_z,
+                pkcu_stream_t stream);
+}
+
 extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                           const pk_tc_epi *ep, pkcu_stream_t stream) {
+  return tc_gemm_run(a_parts, M, planes, N, npb, M, N, K, ep, 1, 0, 0, 0, stream);
+}
+
+extern "C" int pk_tc_gemm_batched(const void *a_parts, long long a_rows, const void *b_parts, long long b_rows,
+                                  int M, int N, int K, const pk_tc_epi *ep, int Z, long long a_z,
+                                  long long b_z, long long c_z, pkcu_stream_t stream) {
+  // TMA row coordinates are 32-bit; rows past a_rows / b_rows read as zeros
+  if (Z <= 0 || a_z < 0 || b_z < 0 || (long long)(Z - 1) * a_z + M > 0x7fffff00LL ||
+      (long long)(Z - 1) * b_z + N > 0x7fffff00LL)
+    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: bad batch (%d entries)", Z);
+  return tc_gemm_run(a_parts, a_rows, b_parts, b_rows, 3, M, N, K, ep, Z, a_z, b_z, c_z, stream);
+}
+
+namespace {
+int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long long b_rows, int npb, int M,
+                int N, int K, const pk_tc_epi *ep, int Z, long long a_z, long long b_z, long long c_z,
+                pkcu_stream_t stream) {
   if (!a_parts || !planes || !ep || (npb != 1 && npb != 3) || M <= 0 || N <= 0 || K <= 0 ||
       K % tc::BK || (N % 32 && ep->mode != PK_TC_STORE && ep->mode != PK_TC_SWISH &&
-                     ep->mode != PK_TC_RESID) ||
+                     ep->mode != PK_TC_RESID && ep->mode != PK_TC_STORE_T) ||
       !PK_ALIGNED16(a_parts) || !PK_ALIGNED16(planes))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: bad arguments (M %d, N %d, K %d)", M, N, K);
-  const int narrow = narrow_tiles(M, N, ep->mode);
+  const int narrow = ep->mode != PK_TC_GLU &&
+                     (N <= 128 || Z * (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM) * 2 <
+                                      pkcu_sm_count());
   CUtensorMap ma, mb;
-  int st = tmap_bf16(&ma, a_parts, M, 3LL * K, 3LL * K, tc::BM);
-  if (!st) st = tmap_bf16(&mb, planes, N, (long long)npb * K, (long long)npb * K, narrow ? 64 : 256);
+  int st = tmap_bf16(&ma, a_parts, a_rows, 3LL * K, 3LL * K, tc::BM);
+  if (!st) st = tmap_bf16(&mb, planes, b_rows, (long long)npb * K, (long long)npb * K, narrow ? 64 : 256);
   if (st) return st;
   tc::Epi e;
   e.mode = ep->mode;
@@ -776,12 +904,19 @@ extern "C" int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int 
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the QKV epilogue needs the batch and its outputs");
   if ((e.mode == PK_TC_STORE || e.mode == PK_TC_SWISH || e.mode == PK_TC_RESID) && (!e.C || e.ldc < N))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: no output, or rows shorter than N");
-  e.vec = PK_ALIGNED16(e.C) && e.ldc % 4 == 0;
+  e.vec = PK_ALIGNED16(e.C) && e.ldc % 4 == 0 && (c_z % 4) == 0;
+  e.Z = Z;
+  e.a_z = a_z;
+  e.b_z = b_z;
+  e.c_z = c_z;
+  if (e.mode == PK_TC_STORE_T && (!e.C || !ep->ldc || ep->ldc < M))
+    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the transposed store needs rows of at least M");
   cudaStream_t s = (cudaStream_t)stream;
   if (narrow)
     return npb == 1 ? launch<1, 64>(ma, mb, M, N, K, e, s) : launch<3, 64>(ma, mb, M, N, K, e, s);
   return npb == 1 ? launch<1, 256>(ma, mb, M, N, K, e, s) : launch<3, 256>(ma, mb, M, N, K, e, s);
 }
+}  // namespace
 
 // ── public entry points: weight products (csrc/tensor_ops.c:50-61) ──────────
 

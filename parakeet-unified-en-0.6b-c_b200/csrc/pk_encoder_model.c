@@ -11,11 +11,12 @@
  * distinct utterance length) run on the library's tcgen05 GEMM (k_tcgemm.cu)
  * with fp32 accuracy: an int8 weight used as stored (q exact in bf16, its
  * scale applied to the sum), any other as the three bf16 parts of its fp32
- * values, the activation as three bf16 parts. The pointwise convolutions run
- * on split operands through cuBLAS bf16 GEMMs band by band, and the per-head
- * score, positional-score and context products as cuBLAS single-precision
- * GEMMs (no TF32), strided batches over heads (and over utterances when the
- * batch is uniform). */
+ * values, the activation as three bf16 parts; the pointwise convolutions on it
+ * too (the first one's GLU and the second one's residual in its epilogues),
+ * and the per-head score, positional-score and context products as batched
+ * launches over heads (and over utterances when the batch is uniform) with
+ * both operands split. cuBLAS single-precision GEMMs remain only for a model
+ * that could not hold the GEMM's operands. */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -321,6 +322,59 @@ static int proj_swish(pkcu_encoder_model *m, int b, int k, int M, const float *A
     return proj_tc(m, b, k, M, A, &e, stream);
 }
 
+/* Workspace bytes of the per-head products of `per` items of T frames on the
+ * tcgen05 GEMM: the larger of the score products' two operands (K / P heads
+ * and Q heads, 128 wide) and the context product's (the score rows padded to
+ * Kp = T rounded up to 32, and the value heads transposed). */
+static size_t heads_need(int T, int per)
+{
+    const long long Z = (long long)PK_H * per, L = 2LL * T - 1, Kp = (T + 31) & ~31;
+    const long long sc = (Z * L + Z * T) * 3 * PK_DH * 2;
+    const long long av = (Z * T + Z * PK_DH) * 3 * Kp * 2;
+    return (size_t)(sc > av ? sc : av);
+}
+
+/* The per-head products of `per` consecutive items of T frames (Z = 8 per
+ * entries of one shape, one launch) on the tcgen05 GEMM, both operands split
+ * into the model's workspace:
+ *   ac[z][i][j] = K[z][j] . Qu[z][i]  (A = K heads, B = Q+u heads, stored transposed)
+ *   bd[z][i][j] = P[z][j] . Qv[z][i]  (A = P heads, B = Q+v heads, stored transposed)
+ *   attn[z] = S[z] V[z]                (A = score rows padded, B = V heads transposed)
+ * The transposed stores put the lanes of a warp on consecutive j. */
+static int heads_tc(pkcu_encoder_model *m, int gemm, int T, int per, const pkcu_gemm_inputs *gi,
+                    const pkcu_gemm_outputs *go, long long fo, long long po, long long so, long long bo,
+                    pkcu_stream_t stream)
+{
+    const int Z = PK_H * per, L = 2 * T - 1, Kp = (T + 31) & ~31;
+    uint16_t *ws = (uint16_t *)m->split_ws;
+    pk_tc_epi e;
+    memset(&e, 0, sizeof(e));
+    e.alpha = 1.0f;
+    int st;
+    if (gemm == PKCU_GEMM_AC || gemm == PKCU_GEMM_BD) {
+        const int ac = gemm == PKCU_GEMM_AC;
+        const long long arows = (long long)Z * (ac ? T : L), brows = (long long)Z * T;
+        uint16_t *pa = ws, *pb = ws + arows * 3 * PK_DH;
+        st = pk_split_rows_bf16x3(ac ? gi->K + fo * PK_D : gi->P_h + po * PK_D, pa, arows, PK_DH, stream);
+        if (!st) st = pk_split_rows_bf16x3(ac ? gi->Qu + fo * PK_D : gi->Qv + fo * PK_D, pb, brows, PK_DH, stream);
+        if (st) return st;
+        e.mode = PK_TC_STORE_T;
+        e.C = ac ? gemm_dst(go->ac) + so : gemm_dst(go->bd) + bo;
+        e.ldc = ac ? T : L;
+        return pk_tc_gemm_batched(pa, arows, pb, brows, ac ? T : L, T, PK_DH, &e, Z, ac ? T : L, T,
+                                  (long long)T * (ac ? T : L), stream);
+    }
+    const long long arows = (long long)Z * T, brows = (long long)Z * PK_DH;
+    uint16_t *pa = ws, *pb = ws + arows * 3 * Kp;
+    st = pk_split_rows_pad(gi->S + so, pa, arows, T, Kp, stream);
+    if (!st) st = pk_split_t_pad(gi->V + fo * PK_D, pb, Z, T, PK_DH, Kp, stream);
+    if (st) return st;
+    e.mode = PK_TC_STORE;
+    e.C = gemm_dst(go->attn_h) + fo * PK_D;
+    e.ldc = PK_DH;
+    return pk_tc_gemm_batched(pa, arows, pb, brows, T, PK_DH, Kp, &e, Z, T, PK_DH, (long long)T * PK_DH, stream);
+}
+
 static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
 {
     Fwd *f = (Fwd *)user;
@@ -415,6 +469,12 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
         const long long fo = f->off[4 * i], po = f->off[4 * i + 1], so = f->off[4 * i + 2],
                         bo = f->off[4 * i + 3];
         int st = PKCU_OK;
+        if ((gemm == PKCU_GEMM_AC || gemm == PKCU_GEMM_BD || gemm == PKCU_GEMM_AV) && f->m->stacks &&
+            heads_need(T, per) <= f->m->split_cap) {
+            st = heads_tc(f->m, gemm, T, per, gi, go, fo, po, so, bo, stream);
+            if (st) return st;
+            continue;
+        }
         switch (gemm) {
         case PKCU_GEMM_AC:    /* ac[h] = (Q + u)[h] K[h]^T */
             st = rm_gemm(h, T, T, PK_DH, gi->Qu + fo * PK_D, PK_DH, (long long)T * PK_DH,
@@ -477,6 +537,12 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
     }
     size_t need = (size_t)rows_ff * 3 * PK_FF * 2;
     if ((size_t)rows_pos * 3 * PK_D * 2 > need) need = (size_t)rows_pos * 3 * PK_D * 2;
+    /* the per-head products: all items at once when the lengths agree, else one item at a time */
+    const int uni = seq->dev.uniform_T;
+    for (int i = 0; i < (uni ? 1 : n); i++) {
+        const size_t hn = heads_need(uni ? uni : seq->lengths[i], uni ? n : 1);
+        if (hn > need) need = hn;
+    }
     if (m->stacks && need > m->split_cap) {
         if (m->split_ws) cudaFree(m->split_ws);
         m->split_ws = NULL;

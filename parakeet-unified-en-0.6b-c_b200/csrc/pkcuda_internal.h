@@ -63,6 +63,7 @@ int pk_tc_wait_timeouts(unsigned *count, int reset);   /* k_tcgemm.cu */
 #define PK_TC_QKV   3   /* the QKV head split with pos_bias_u / v       */
 #define PK_TC_CF    4   /* rows = frames of seq: C per item [N, T] (+ bias[n]) */
 #define PK_TC_GLU   5   /* as CF, columns interleaved value / gate by 32: GLU -> [N/2, T] */
+#define PK_TC_STORE_T 6 /* C[n * ldc + m] = alpha (A W)[m, n]: the product written transposed */
 typedef struct {
     int mode;
     float alpha, beta, rscale;
@@ -79,12 +80,23 @@ int pk_tc_prepare(const void *data, int bits, float scale, int K, int N, void *p
                   pkcu_stream_t stream);
 int pk_tc_gemm(const void *a_parts, const void *planes, int npb, int M, int N, int K,
                const pk_tc_epi *ep, pkcu_stream_t stream);
+/* Z products of one shape in one launch, both operands three-part planes:
+ * A [a_rows, 3K] with entry z's M rows from row z * a_z, B [b_rows, 3K] with
+ * its N rows from z * b_z (rows past an entry's own belong to the next one and
+ * only produce discarded outputs), output from ep->C + z * c_z. */
+int pk_tc_gemm_batched(const void *a_parts, long long a_rows, const void *b_parts, long long b_rows,
+                       int M, int N, int K, const pk_tc_epi *ep, int Z, long long a_z, long long b_z,
+                       long long c_z, pkcu_stream_t stream);
 /* Raises the GEMM kernels' shared-memory limit now, so that a first launch
  * inside a stream capture makes no attribute call. */
 void pk_tc_warm(void);
 /* A pointwise weight W [N, K] (already K-major) -> three-part planes [N, 3K];
  * glu: rows interleaved value / gate in groups of 32 for PK_TC_GLU. */
 int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *planes, pkcu_stream_t stream);
+/* Rows A [M, K] -> parts [M, 3 Kp] zero-padded from K; Z matrices X [R, Cc]
+ * -> the parts of their transposes, rows z Cc + c of 3 Kp, zero from R. */
+int pk_split_rows_pad(const float *A, void *parts, long long M, int K, int Kp, pkcu_stream_t stream);
+int pk_split_t_pad(const float *X, void *parts, int Z, int R, int Cc, int Kp, pkcu_stream_t stream);
 /* Channel-first items X [C, T_b] -> time-first three-part rows [frames, 3C]. */
 int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream);
 

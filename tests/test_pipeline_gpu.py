@@ -333,3 +333,32 @@ def test_asr_transcribe_matches_reference_engine(cuda, model, tmp_path):
         for g in got:
             assert len(g[b]) == len(want[b]) and (g[b] == want[b]).all(), \
                 (b, len(g[b]), len(want[b]))
+
+
+@pytest.mark.parametrize("frames", [[3000, 3000], [3000, 1999]], ids=["uniform", "ragged"])
+def test_asr_encode_at_bench_length(cuda, model, tmp_path, frames):
+    """pkcu_asr_encode at the bench's utterance length (3000 mel frames = 375
+    encoder frames; all 24 blocks, every product on the library's tcgen05
+    GEMM: the per-head products as one batched launch for a uniform batch, one
+    per utterance for a ragged one) against the reference engine's pk_encoder
+    on the first spectrogram."""
+    if not po.ref_full_available():
+        pytest.skip("oracle/_ref/libpkref_full.so not built (reference tree absent)")
+    tensors, bp, jp, _ = model
+    rng = np.random.default_rng(33)
+    mels = [rng.standard_normal((128, f)).astype(np.float32) for f in frames]
+    if frames[0] == frames[1]:
+        mels[1] = mels[0]
+    enc_ref, _ = reference_run(bp, jp, mels[0], tmp_path)
+    ef = [cuda.lib().pkcu_asr_encoder_frames(f) for f in frames]
+    with cuda.Weights(bp, jp) as w:
+        w.upload(cuda.stream_handle())
+        with cuda.ASR(w) as asr:
+            out = empty(sum(ef) * D)
+            asr.encode(dev(np.concatenate([m.reshape(-1) for m in mels])), frames, out)
+            enc = host(out).reshape(-1, D)
+    err = np.abs(enc[:ef[0]].astype(np.float64) - enc_ref).max()
+    print(f"{frames}: max |gpu - reference| = {err:.3e} over {ef[0]} frames")
+    assert err <= 5e-5, err
+    if frames[0] == frames[1]:
+        assert np.array_equal(enc[:ef[0]], enc[ef[0]:])

@@ -215,3 +215,4 @@ def test_pointwise_conv1d_glu(cuda, reference, oracle, T):
     tb = conv_bound(w, x)
     tol = tb[:C2 // 2] + 0.25 * np.abs(pw1[:C2 // 2]) * tb[C2 // 2:] + 1e-5 * np.abs(want) + 2e-6
     check(got, want, tol, "GLU(W x + b)")
+
