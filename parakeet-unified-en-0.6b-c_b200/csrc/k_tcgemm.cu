@@ -613,6 +613,29 @@ __global__ void prep_split_rows_kernel(const float *__restrict__ W, __nv_bfloat1
   }
 }
 
+// Two row sets side by side as one K-major operand: row m of the output is the
+// parts of [X1[m] (K1) | X2[m] (K2)], each part K1 + K2 wide (the decoder's
+// [x | h] against [W_i | W_r]: one product per LSTM layer instead of two).
+__global__ void split_rows_cat_kernel(const float *__restrict__ X1, const float *__restrict__ X2,
+                                      __nv_bfloat16 *__restrict__ out, long long M, int K1, int K2) {
+  const int K = K1 + K2;
+  const long long total = M * K;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long m = e / K;
+    const int k = (int)(e - m * K);
+    const float x = k < K1 ? __ldg(X1 + m * K1 + k) : __ldg(X2 + m * K2 + (k - K1));
+    const __nv_bfloat16 p0 = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(p0);
+    const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+    __nv_bfloat16 *o = out + m * 3 * K + k;
+    o[0] = p0;
+    o[K] = p1;
+    o[2 * K] = p2;
+  }
+}
+
 // Channel-first items X [C, T_b] (item after item) -> time-first parts
 // [frames, 3C], row f0_b + t = [x0 | x1 | x2] of column t: the operand of a
 // pointwise convolution as a K-major matrix. 32 x 32 tiles through shared
@@ -831,6 +854,17 @@ extern "C" int pk_split_t_pad(const float *X, void *parts, int Z, int R, int Cc,
   tc::split_t_pad_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(X, static_cast<__nv_bfloat16 *>(parts), R, Cc,
                                                                   Kp);
   return pkcu_launch_status("pk_split_t_pad");
+}
+
+extern "C" int pk_split_rows_cat(const float *X1, const float *X2, void *parts, long long M, int K1, int K2,
+                                 pkcu_stream_t stream) {
+  if (!X1 || !X2 || !parts || M <= 0 || K1 <= 0 || K2 <= 0)
+    return pkcu_fail(PKCU_ERR_ARG, "pk_split_rows_cat: bad argument");
+  long long blocks = (M * (K1 + K2) + 255) / 256;
+  if (blocks > 16LL * pkcu_sm_count()) blocks = 16LL * pkcu_sm_count();
+  tc::split_rows_cat_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      X1, X2, static_cast<__nv_bfloat16 *>(parts), M, K1, K2);
+  return pkcu_launch_status("pk_split_rows_cat");
 }
 
 extern "C" int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream) {

@@ -604,7 +604,8 @@ struct pkcu_asr {
     pkcu_dec_params dec;
     int decode_mode;                   /* PKCU_ASR_DECODE_* */
     void *tc_planes;                   /* the decoder's products as tcgen05 GEMM operands */
-    const void *tc_w[7];               /* per PKCU_GEMM_DEC_* - 32: K-major three-part planes */
+    const void *tc_w[5];               /* joint.enc, [W_i | W_r] of both layers, joint.pred, joint.out:
+                                          K-major three-part planes */
     void *dec_ws;                      /* the products' activation parts */
     size_t dec_ws_cap;
     /* the last call's working buffers, kept while the same lengths come again */
@@ -768,22 +769,23 @@ int pkcu_asr_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu_asr **out)
      * [N, K]), joint.pred [640, 640], joint.out [640, 1025]; without the memory
      * the cuBLAS / CUDA-core paths remain */
     if (!st) {
-        static const long long tk[7] = {PK_D, 640, 640, 640, 640, 640, 640};
-        static const long long tn[7] = {640, 2560, 2560, 2560, 2560, 640, 1025};
-        long long off[8] = {0};
-        for (int i = 0; i < 7; i++) off[i + 1] = off[i] + ((3 * tk[i] * tn[i] + 127) & ~127LL);
-        if (cudaMalloc(&m->tc_planes, sizeof(uint16_t) * (size_t)off[7]) != cudaSuccess) {
+        /* 0 joint.enc [K 1024, N 640]; 1, 2 the layers' [W_i | W_r] as rows [2560, 1280]
+         * (one product of [x | h] per layer); 3 joint.pred [640, 640]; 4 joint.out [640, 1025] */
+        static const long long tk[5] = {PK_D, 1280, 1280, 640, 640};
+        static const long long tn[5] = {640, 2560, 2560, 640, 1025};
+        long long off[6] = {0};
+        for (int i = 0; i < 5; i++) off[i + 1] = off[i] + ((3 * tk[i] * tn[i] + 127) & ~127LL);
+        if (cudaMalloc(&m->tc_planes, sizeof(uint16_t) * (size_t)off[5]) != cudaSuccess) {
             cudaGetLastError();
             m->tc_planes = NULL;
         } else {
-            const float *src[7] = {m->j_enc, m->wi[0], m->wr[0], m->wi[1], m->wr[1], m->j_pred, m->j_out};
-            for (int i = 0; i < 7 && !st; i++) {
-                void *dstp = (uint16_t *)m->tc_planes + off[i];
-                float alpha;
-                st = (i >= 1 && i <= 4) ? pk_tc_prepare_rows(src[i], (int)tn[i], (int)tk[i], 0, dstp, stream)
-                                        : pk_tc_prepare(src[i], 32, 0.0f, (int)tk[i], (int)tn[i], dstp, &alpha, stream);
-                m->tc_w[i] = dstp;
-            }
+            float alpha;
+            for (int i = 0; i < 5; i++) m->tc_w[i] = (uint16_t *)m->tc_planes + off[i];
+            st = pk_tc_prepare(m->j_enc, 32, 0.0f, PK_D, 640, (void *)m->tc_w[0], &alpha, stream);
+            for (int l = 0; l < 2 && !st; l++)
+                st = pk_split_rows_cat(m->wi[l], m->wr[l], (void *)m->tc_w[1 + l], 2560, 640, 640, stream);
+            if (!st) st = pk_tc_prepare(m->j_pred, 32, 0.0f, 640, 640, (void *)m->tc_w[3], &alpha, stream);
+            if (!st) st = pk_tc_prepare(m->j_out, 32, 0.0f, 640, 1025, (void *)m->tc_w[4], &alpha, stream);
             if (!st) pk_tc_warm();
         }
     }
@@ -838,12 +840,14 @@ static int dec_hook(void *user, int block, int gemm, pkcu_stream_t stream)
  * three bf16 parts into the decode workspace, then the product with the
  * weight's planes (prepared at pkcu_asr_create). Capture-safe: no allocation,
  * no synchronisation (the workspace is sized before the decode starts). */
-static int dec_tc(DecCtx *c, int which, int M, int N, int K, const float *A, float *C, pkcu_stream_t stream)
+static int dec_tc(DecCtx *c, int which, int M, int N, int K, const float *A, const float *A2, float *C,
+                  pkcu_stream_t stream)
 {
     pkcu_asr *m = c->m;
     if ((size_t)M * 3 * K * 2 > m->dec_ws_cap)
         return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: decode workspace too small");
-    int st = pk_split_rows_bf16x3(A, m->dec_ws, M, K, stream);
+    int st = A2 ? pk_split_rows_cat(A, A2, m->dec_ws, M, K / 2, K / 2, stream)
+                : pk_split_rows_bf16x3(A, m->dec_ws, M, K, stream);
     if (st) return st;
     pk_tc_epi e;
     memset(&e, 0, sizeof(e));
@@ -858,14 +862,17 @@ static int dec_hook_tc(void *user, int block, int gemm, pkcu_stream_t stream)
     (void)block;
     DecCtx *c = (DecCtx *)user;
     const int B = c->B, Hd = 640;
+    /* each layer's two gate products as one, [x | h] [W_i | W_r]^T, into g*i; the
+     * W_r outputs g*r stay zero (cleared before the decode), so the cell's
+     * g_r + g_i is that one product exactly */
     switch (gemm) {
-    case PKCU_GEMM_DEC_ENC:   return dec_tc(c, 0, (int)c->F, Hd, PK_D, c->x, c->go.enc, stream);
-    case PKCU_GEMM_DEC_L0_WI: return dec_tc(c, 1, B, 4 * Hd, Hd, c->gi.x0, c->go.g0i, stream);
-    case PKCU_GEMM_DEC_L0_WR: return dec_tc(c, 2, B, 4 * Hd, Hd, c->gi.h0, c->go.g0r, stream);
-    case PKCU_GEMM_DEC_L1_WI: return dec_tc(c, 3, B, 4 * Hd, Hd, c->gi.h0, c->go.g1i, stream);
-    case PKCU_GEMM_DEC_L1_WR: return dec_tc(c, 4, B, 4 * Hd, Hd, c->gi.h1, c->go.g1r, stream);
-    case PKCU_GEMM_DEC_PRED:  return dec_tc(c, 5, B, Hd, Hd, c->gi.h1, c->go.pred, stream);
-    case PKCU_GEMM_DEC_OUT:   return dec_tc(c, 6, B, 1025, Hd, c->gi.hidden, c->go.out, stream);
+    case PKCU_GEMM_DEC_ENC:   return dec_tc(c, 0, (int)c->F, Hd, PK_D, c->x, NULL, c->go.enc, stream);
+    case PKCU_GEMM_DEC_L0_WI: return dec_tc(c, 1, B, 4 * Hd, 2 * Hd, c->gi.x0, c->gi.h0, c->go.g0i, stream);
+    case PKCU_GEMM_DEC_L0_WR: return PKCU_OK;
+    case PKCU_GEMM_DEC_L1_WI: return dec_tc(c, 2, B, 4 * Hd, 2 * Hd, c->gi.h0, c->gi.h1, c->go.g1i, stream);
+    case PKCU_GEMM_DEC_L1_WR: return PKCU_OK;
+    case PKCU_GEMM_DEC_PRED:  return dec_tc(c, 3, B, Hd, Hd, c->gi.h1, NULL, c->go.pred, stream);
+    case PKCU_GEMM_DEC_OUT:   return dec_tc(c, 4, B, 1025, Hd, c->gi.hidden, NULL, c->go.out, stream);
     }
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: unknown decoder GEMM %d", gemm);
 }
@@ -899,8 +906,8 @@ static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_
     pkcu_decoder *dec = m->d_dec;
     /* the tcgen05 products' activation parts: the encoder projection's F rows
      * of 1024, the per-iteration products' B rows of 640 */
-    const size_t need = (size_t)(F * 3 * PK_D * 2 > (long long)n_utts * 3 * 640 * 2 ? F * 3 * PK_D * 2
-                                                                                   : (long long)n_utts * 3 * 640 * 2);
+    const size_t need = (size_t)(F * 3 * PK_D * 2 > (long long)n_utts * 3 * 1280 * 2 ? F * 3 * PK_D * 2
+                                                                                    : (long long)n_utts * 3 * 1280 * 2);
     if (m->tc_planes && need > m->dec_ws_cap) {
         if (m->dec_ws) cudaFree(m->dec_ws);
         m->dec_ws_cap = 0;
@@ -922,6 +929,10 @@ static int asr_decode(pkcu_asr *m, const float *x, const int *enc_frames, int n_
         if (!st) st = pkcu_greedy_decode_fused(dec, &m->dec, stream);
     } else if (m->decode_mode == PKCU_ASR_DECODE_TC) {
         if (!m->tc_planes) return pkcu_fail(PKCU_ERR_ARG, "pkcu_asr: the tensor-core decode needs its operands");
+        const size_t gb = sizeof(float) * (size_t)n_utts * 2560;
+        if (cudaMemsetAsync(dc->go.g0r, 0, gb, (cudaStream_t)stream) != cudaSuccess ||
+            cudaMemsetAsync(dc->go.g1r, 0, gb, (cudaStream_t)stream) != cudaSuccess)
+            return pkcu_fail(PKCU_ERR_CUDA, "pkcu_asr: clearing the W_r products");
         st = pkcu_greedy_decode_graph(dec, &m->dec, dec_hook_tc, dc, stream);
     } else {
         st = m->decode_mode == PKCU_ASR_DECODE_EAGER

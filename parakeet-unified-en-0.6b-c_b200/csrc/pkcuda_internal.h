@@ -97,6 +97,9 @@ int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *planes, pkcu
  * -> the parts of their transposes, rows z Cc + c of 3 Kp, zero from R. */
 int pk_split_rows_pad(const float *A, void *parts, long long M, int K, int Kp, pkcu_stream_t stream);
 int pk_split_t_pad(const float *X, void *parts, int Z, int R, int Cc, int Kp, pkcu_stream_t stream);
+/* Rows [X1[m] | X2[m]] (K1 + K2 wide) -> parts [M, 3 (K1 + K2)]. */
+int pk_split_rows_cat(const float *X1, const float *X2, void *parts, long long M, int K1, int K2,
+                      pkcu_stream_t stream);
 /* Channel-first items X [C, T_b] -> time-first three-part rows [frames, 3C]. */
 int pk_split_cf_t(const float *X, void *parts, int C, const pkcu_seq *seq, pkcu_stream_t stream);
 
