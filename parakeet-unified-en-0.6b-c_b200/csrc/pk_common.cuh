@@ -107,41 +107,16 @@ __device__ __forceinline__ float exp_poly_nonpos(float x) {
 }
 
 // ── packed fp32 pairs (sm_100 f32x2 arithmetic) ──────────────────────────────
-// add/sub/mul/fma.rn.f32x2 apply one IEEE fp32 operation, round to nearest,
-// to each half of a register pair: the results are those of the scalar
-// instructions, at half the issue slots. Used where the kernels are bound by
-// instruction issue (polynomial exp, Swish, depthwise taps, score combine).
-
-__device__ __forceinline__ unsigned long long pk2(float2 v) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
-  return r;
-}
-__device__ __forceinline__ float2 unpk2(unsigned long long r) {
-  float2 v;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
-  return v;
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
-  return unpk2(r);
-}
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
-  return unpk2(r);
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)));
-  return unpk2(r);
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
-  return unpk2(r);
-}
+// The f32x2 add / mul / fma (CUDA's __fadd2_rn / __fmul2_rn / __ffma2_rn for
+// sm_100) apply one IEEE fp32 operation, round to nearest, to each half of a
+// register pair: the results are those of the scalar instructions, at half the
+// issue slots. Used where the kernels are bound by instruction issue
+// (polynomial exp, Swish, depthwise taps, score combine). a - b is formed as
+// a + (-b), which is the same IEEE result.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
 
 // exp_poly_clamped on a pair (inputs already in [-87, 87]); per element the
