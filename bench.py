@@ -474,9 +474,10 @@ def tensor_at(addr, n):
     return torch.as_tensor(h, device="cuda")
 
 
-def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
-    """Average device time of each kernel of the sequence, launched alone on
-    the bench stream over the full batch (CUDA events on that stream)."""
+def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=10):
+    """Device time of each kernel of the sequence, launched alone on the bench
+    stream over the full batch (CUDA events on that stream): the median of
+    three runs of `reps` back-to-back launches, averaged per launch."""
     import torch
     import pkcuda
     F, T, n = seq.frames, args.T, args.utts
@@ -510,14 +511,18 @@ def time_kernels(args, seq, x_addr, gout, gin, blocks, stream, reps=5):
     for name, nbytes, per_block in kernel_table(F, T, n):
         fn = calls[name]
         fn()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(reps):
-            fn()
-        e1.record(stream)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        # median of three runs of `reps` back-to-back launches
+        runs = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            runs.append(e0.elapsed_time(e1) / reps)
+        ms = sorted(runs)[1]
         table[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
                        "launches_per_step": per_block * args.blocks}
     return table

@@ -394,12 +394,13 @@ __global__ void __launch_bounds__(32 * DWA_WARPS)
 dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
                  const float *__restrict__ b, const float *__restrict__ bn, float bn_eps,
                  float *__restrict__ out, int C, SeqDev seq, const float *__restrict__ glu_bias,
-                 long long x_total) {
+                 long long x_total, int rs) {
   static_assert(SW == DW_SWISH_NONE || SW == DW_SWISH_POLY, "no scalar Swish tail here");
   constexpr int K = 9;
   constexpr int LPR = DWA_LPR;
-  __shared__ __align__(16) float stage[DWA_CH][DWA_ROW];
-  __shared__ __align__(16) float stage_g[GLU ? DWA_CH : 1][GLU ? DWA_ROW : 4];
+  // DWA_CH staging rows of rs floats (then DWA_CH more for the GLU gate half)
+  extern __shared__ float4 dwa_smem4[];
+  float *stage = reinterpret_cast<float *>(dwa_smem4);
   __shared__ unsigned long long bars[DWA_WARPS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane / LPR, li = lane % LPR;
@@ -410,8 +411,8 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
   const int T = seq_T(seq, item);
   const long long f0 = seq_frame_off(seq, item);
   const long long row = (GLU ? 2 * f0 * C : f0 * C) + (long long)c * T;
-  float *s = stage[slot];
-  float *sg = stage_g[GLU ? slot : 0];
+  float *s = stage + slot * rs;
+  float *sg = stage + (GLU ? DWA_CH + slot : slot) * rs;
   unsigned long long *bar = bars + warp;
   if (lane == 0) {
     mbar_init(bar, DWA_RPW);   // one arrival per row
@@ -531,9 +532,13 @@ static int launch_dwconv(const float *x, const float *w, const float *b, const f
       dwa_row_need(sd.max_T) <= DWA_ROW) {
     const dim3 grid_al((unsigned)(C / DWA_CH), (unsigned)sd.n_items);
     const long long x_total = (glu ? 2 : 1) * frames * C;
+    // staging sized for the batch's longest item (at most 42 KB), so shorter
+    // batches keep more CTAs resident per SM
+    const int rs = dwa_row_need(sd.max_T);
+    const size_t smem = sizeof(float) * (size_t)(glu ? 2 : 1) * DWA_CH * rs;
 #define PK_DW_AL(SWV, BNV, GLUV)                                                         \
-  dwconv_al_kernel<SWV, BNV, GLUV><<<grid_al, 32 * DWA_WARPS, 0, s>>>(x, w, b, bn, bn_eps, out, C, \
-                                                                 sd, glu_bias, x_total)
+  dwconv_al_kernel<SWV, BNV, GLUV><<<grid_al, 32 * DWA_WARPS, smem, s>>>(                \
+      x, w, b, bn, bn_eps, out, C, sd, glu_bias, x_total, rs)
 #define PK_DW_AL_SW(BNV, GLUV)                                  \
   do {                                                          \
     if (apply_swish) PK_DW_AL(DW_SWISH_POLY, BNV, GLUV);        \

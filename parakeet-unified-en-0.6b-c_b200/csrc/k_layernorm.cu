@@ -26,7 +26,7 @@ namespace pk {
 
 constexpr int LN_VEC = PK_D / 128;      // float4 per lane for a 1024-wide row
 constexpr int LN_ROWS_PER_CTA = 8;      // one warp per row, 256 threads
-constexpr int LT_TT = 16;               // frames per CTA in the transposing kernels
+constexpr int LT_TT = 32;               // frames per CTA in the transposing kernels
 constexpr int LT_STRIDE = PK_D + 4;     // smem row stride (keeps float4 alignment)
 constexpr int LT_THREADS = 32 * LT_TT;  // one warp per frame
 constexpr size_t LT_SMEM = sizeof(float) * LT_TT * LT_STRIDE;
@@ -149,9 +149,14 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // LayerNorm of frames [t0, t0 + LT_TT) of one item, optionally after the attention
 // residual, written channel-first: cf[d, t] per item [D, T_b]
 // (csrc/encoder.c:447-452). The normalised rows are staged in shared memory
-// and leave as 64-byte runs of 16 consecutive frames per channel.
+// and leave as 128-byte runs of 32 consecutive frames per channel: one warp
+// store per channel. (Channel-first runs of 16 frames moved measurably less:
+// 3.9 against 5.1 TB/s for the bare transposed write of 256 x 375 frames.
+// Persistent forms of both transposing kernels, one CTA per SM with the next
+// tile's rows prefetched into L2, measured slower still: 0.64 / 0.60 of the
+// copy bandwidth against 0.85 / 0.84.)
 template <bool RESID>
-__global__ void __launch_bounds__(LT_THREADS, 2)
+__global__ void __launch_bounds__(LT_THREADS, 1)
 ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                     float alpha, const float *__restrict__ g, const float *__restrict__ b,
                     float *__restrict__ cf, SeqDev seq) {
@@ -192,7 +197,7 @@ ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restri
 // y per item [D, T_b] with the pointwise bias of csrc/tensor_ops.c:585-589),
 // optionally followed by the FF2 LayerNorm of the updated rows.
 template <bool WITH_LN>
-__global__ void __launch_bounds__(LT_THREADS, 2)
+__global__ void __launch_bounds__(LT_THREADS, 1)
 transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                      const float *__restrict__ g, const float *__restrict__ b,
                      float *__restrict__ ln, SeqDev seq) {
