@@ -87,22 +87,29 @@ enum { ROW_BIAS = 0, ROW_BIAS_SWISH = 1, ROW_RESID = 2 };
 // ROW_RESID     : x[r,c] = fma(y[r,c] + b[c], alpha, x[r,c])
 // Vector path: len % 4 == 0 and 16-byte aligned pointers. TAIL: the flat
 // length is not a multiple of 8, so the last elements take Swish's scalar form.
+// One warp per segment of a row: the row's float4s [seg * seg4, (seg + 1) * seg4),
+// segs segments per row (1 for large batches; short batches split rows so that
+// more warps share the latency).
 template <int OP, bool TAIL>
 __global__ void __launch_bounds__(32 * ROWS_PER_CTA)
 row_vec_kernel(const float *in, const float *__restrict__ b, const float *__restrict__ y,
-               float alpha, float *out, long long n_rows, int len, long long n8) {
+               float alpha, float *out, long long n_rows, int len, long long n8, int segs) {
   const int lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const long long wid = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const long long row = wid / segs;
   if (row >= n_rows) return;
   const long long base = row * len;
   const int len4 = len >> 2;
+  const int seg4 = (len4 + segs - 1) / segs;
+  const int seg0 = (int)(wid - row * segs) * seg4;
+  const int seg_end = min(len4, seg0 + seg4);
   constexpr int U = 8;
-  for (int c0 = lane; c0 < len4; c0 += 32 * U) {
+  for (int c0 = seg0 + lane; c0 < seg_end; c0 += 32 * U) {
     float4 v[U], t[U];
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int c = c0 + 32 * u;
-      if (c < len4) {
+      if (c < seg_end) {
         v[u] = ld4(in + base + 4 * c);
         if (OP == ROW_RESID) t[u] = ldg4_stream(y + base + 4 * c);
       }
@@ -110,7 +117,7 @@ row_vec_kernel(const float *in, const float *__restrict__ b, const float *__rest
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int c = c0 + 32 * u;
-      if (c >= len4) continue;
+      if (c >= seg_end) continue;
       float4 bb = b ? __ldg(reinterpret_cast<const float4 *>(b) + c) : make_float4(0, 0, 0, 0);
       float4 r;
       if (OP == ROW_BIAS) {
@@ -210,11 +217,16 @@ static int launch_rows(const float *in, const float *b, const float *y, float al
   const bool vec = (len % 4 == 0) && PK_ALIGNED16(in) && PK_ALIGNED16(out) &&
                    (!b || PK_ALIGNED16(b)) && (!y || PK_ALIGNED16(y));
   if (vec) {
-    const unsigned grid = (unsigned)((n_rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA);
+    // rows of 256+ float4s split into segments of at least 256 when fewer
+    // than 48 row-warps per SM would run
+    int segs = 1;
+    if (n_rows < (long long)pkcu_sm_count() * 48) segs = (len / 4 + 255) / 256;
+    if (segs < 1) segs = 1;
+    const unsigned grid = (unsigned)((n_rows * segs + ROWS_PER_CTA - 1) / ROWS_PER_CTA);
     if (n8 == n)
-      row_vec_kernel<OP, false><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8);
+      row_vec_kernel<OP, false><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8, segs);
     else
-      row_vec_kernel<OP, true><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8);
+      row_vec_kernel<OP, true><<<grid, 32 * ROWS_PER_CTA, 0, s>>>(in, b, y, alpha, out, n_rows, len, n8, segs);
   } else {
     row_scalar_kernel<OP><<<flat_grid(n, EW_THREADS * 4), EW_THREADS, 0, s>>>(
         in, b, y, alpha, out, n, len, n8);

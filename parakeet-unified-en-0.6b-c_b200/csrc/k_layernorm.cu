@@ -26,10 +26,12 @@ namespace pk {
 
 constexpr int LN_VEC = PK_D / 128;      // float4 per lane for a 1024-wide row
 constexpr int LN_ROWS_PER_CTA = 8;      // one warp per row, 256 threads
-constexpr int LT_TT = 32;               // frames per CTA in the transposing kernels
 constexpr int LT_STRIDE = PK_D + 4;     // smem row stride (keeps float4 alignment)
-constexpr int LT_THREADS = 32 * LT_TT;  // one warp per frame
-constexpr size_t LT_SMEM = sizeof(float) * LT_TT * LT_STRIDE;
+// The transposing kernels take TT frames per CTA, one warp per frame: 32
+// (128 KB tile, one CTA per SM) when the batch gives every SM a tile, else 16
+// (64 KB, two per SM), so that short batches still spread over the SMs.
+template <int TT>
+constexpr size_t lt_smem() { return sizeof(float) * TT * LT_STRIDE; }
 
 // Normalises one 1024-wide row held in a warp's registers.
 __device__ __forceinline__ void ln_regs(float4 (&v)[LN_VEC], const float *__restrict__ g,
@@ -146,7 +148,7 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
   }
 }
 
-// LayerNorm of frames [t0, t0 + LT_TT) of one item, optionally after the attention
+// LayerNorm of frames [t0, t0 + TT) of one item, optionally after the attention
 // residual, written channel-first: cf[d, t] per item [D, T_b]
 // (csrc/encoder.c:447-452). The normalised rows are staged in shared memory
 // and leave as 128-byte runs of 32 consecutive frames per channel: one warp
@@ -155,8 +157,8 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // Persistent forms of both transposing kernels, one CTA per SM with the next
 // tile's rows prefetched into L2, measured slower still: 0.64 / 0.60 of the
 // copy bandwidth against 0.85 / 0.84.)
-template <bool RESID>
-__global__ void __launch_bounds__(LT_THREADS, 1)
+template <int TT, bool RESID>
+__global__ void __launch_bounds__(32 * TT, 32 / TT)
 ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                     float alpha, const float *__restrict__ g, const float *__restrict__ b,
                     float *__restrict__ cf, SeqDev seq) {
@@ -164,9 +166,9 @@ ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restri
   float *tile = reinterpret_cast<float *>(lt_smem4);
   const int item = blockIdx.y;
   const int T = seq_T(seq, item);
-  const int t0 = blockIdx.x * LT_TT;
+  const int t0 = blockIdx.x * TT;
   if (t0 >= T) return;
-  const int nrows = min(LT_TT, T - t0);
+  const int nrows = min(TT, T - t0);
   const long long f0 = seq_frame_off(seq, item);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < nrows) {
@@ -184,20 +186,20 @@ ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restri
       st4(tile + warp * LT_STRIDE + 4 * (lane + 32 * j), v[j]);
   }
   __syncthreads();
-  const int t = threadIdx.x & (LT_TT - 1), dsub = threadIdx.x / LT_TT;
+  const int t = threadIdx.x & (TT - 1), dsub = threadIdx.x / TT;
   if (t < nrows) {
     float *dst = cf + f0 * PK_D + t0 + t;
     const float *src = tile + t * LT_STRIDE;
 #pragma unroll 8
-    for (int d = dsub; d < PK_D; d += LT_THREADS / LT_TT) dst[(long long)d * T] = src[d];
+    for (int d = dsub; d < PK_D; d += 32) dst[(long long)d * T] = src[d];
   }
 }
 
 // Conv-module residual x[t,d] += y[d,t] + bias[d] (csrc/encoder.c:475-477,
 // y per item [D, T_b] with the pointwise bias of csrc/tensor_ops.c:585-589),
 // optionally followed by the FF2 LayerNorm of the updated rows.
-template <bool WITH_LN>
-__global__ void __launch_bounds__(LT_THREADS, 1)
+template <int TT, bool WITH_LN>
+__global__ void __launch_bounds__(32 * TT, 32 / TT)
 transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
                      const float *__restrict__ g, const float *__restrict__ b,
                      float *__restrict__ ln, SeqDev seq) {
@@ -205,18 +207,18 @@ transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restr
   float *tile = reinterpret_cast<float *>(lt_smem4);
   const int item = blockIdx.y;
   const int T = seq_T(seq, item);
-  const int t0 = blockIdx.x * LT_TT;
+  const int t0 = blockIdx.x * TT;
   if (t0 >= T) return;
-  const int nrows = min(LT_TT, T - t0);
+  const int nrows = min(TT, T - t0);
   const long long f0 = seq_frame_off(seq, item);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   {
-    const int t = threadIdx.x & (LT_TT - 1), dsub = threadIdx.x / LT_TT;
+    const int t = threadIdx.x & (TT - 1), dsub = threadIdx.x / TT;
     if (t < nrows) {
       const float *src = y + f0 * PK_D + t0 + t;
       float *dst = tile + t * LT_STRIDE;
 #pragma unroll 8
-      for (int d = dsub; d < PK_D; d += LT_THREADS / LT_TT) dst[d] = __ldcs(src + (long long)d * T);
+      for (int d = dsub; d < PK_D; d += 32) dst[d] = __ldcs(src + (long long)d * T);
     }
   }
   __syncthreads();
@@ -239,7 +241,7 @@ transpose_add_kernel(float *x, const float *__restrict__ y, const float *__restr
   }
 }
 
-static int g_lt_flags[4][64];
+static int g_lt_flags[8][64];
 
 static unsigned ln_grid(long long n_rows) {
   return (unsigned)((n_rows + LN_ROWS_PER_CTA - 1) / LN_ROWS_PER_CTA);
@@ -303,9 +305,28 @@ static int check_seq_tile(const pkcu_seq *seq, const char *what) {
   return PKCU_OK;
 }
 
-static dim3 lt_grid(const pkcu_seq *seq) {
-  return dim3((unsigned)((seq->dev.max_T + LT_TT - 1) / LT_TT), (unsigned)seq->dev.n_items);
+static bool lt_wide(const pkcu_seq *seq) {
+  return (long long)((seq->dev.max_T + 31) / 32) * seq->dev.n_items >= pkcu_sm_count();
 }
+
+template <int TT>
+static dim3 lt_grid(const pkcu_seq *seq) {
+  return dim3((unsigned)((seq->dev.max_T + TT - 1) / TT), (unsigned)seq->dev.n_items);
+}
+
+// Launches kernel<32, FLAG> or kernel<16, FLAG> (flags slot k or k + 4).
+#define PK_LT_LAUNCH(KERNEL, FLAG, k, stream, ...)                                             \
+  do {                                                                                         \
+    if (lt_wide(seq)) {                                                                        \
+      smem_optin(KERNEL<32, FLAG>, lt_smem<32>(), g_lt_flags[k]);                              \
+      KERNEL<32, FLAG><<<lt_grid<32>(seq), 32 * 32, lt_smem<32>(), (cudaStream_t)(stream)>>>(  \
+          __VA_ARGS__);                                                                        \
+    } else {                                                                                   \
+      smem_optin(KERNEL<16, FLAG>, lt_smem<16>(), g_lt_flags[(k) + 4]);                        \
+      KERNEL<16, FLAG><<<lt_grid<16>(seq), 32 * 16, lt_smem<16>(), (cudaStream_t)(stream)>>>(  \
+          __VA_ARGS__);                                                                        \
+    }                                                                                          \
+  } while (0)
 
 extern "C" int pkcu_layer_norm_transpose(const float *x, const float *gamma, const float *beta,
                                          float *cf, const pkcu_seq *seq,
@@ -316,9 +337,8 @@ extern "C" int pkcu_layer_norm_transpose(const float *x, const float *gamma, con
       !PK_ALIGNED16(beta))
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_layer_norm_transpose: bad or misaligned pointer");
   if (seq->frames == 0) return PKCU_OK;
-  smem_optin(ln_transpose_kernel<false>, LT_SMEM, g_lt_flags[0]);
-  ln_transpose_kernel<false><<<lt_grid(seq), LT_THREADS, LT_SMEM, (cudaStream_t)stream>>>(
-      const_cast<float *>(x), nullptr, nullptr, 0.0f, gamma, beta, cf, seq->dev);
+  PK_LT_LAUNCH(ln_transpose_kernel, false, 0, stream, const_cast<float *>(x), nullptr, nullptr,
+               0.0f, gamma, beta, cf, seq->dev);
   return pkcu_launch_status("pkcu_layer_norm_transpose");
 }
 
@@ -332,9 +352,8 @@ extern "C" int pkcu_residual_layer_norm_transpose(float *x, const float *y, cons
       !PK_ALIGNED16(gamma) || !PK_ALIGNED16(beta) || (bias && !PK_ALIGNED16(bias)))
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_residual_layer_norm_transpose: bad or misaligned pointer");
   if (seq->frames == 0) return PKCU_OK;
-  smem_optin(ln_transpose_kernel<true>, LT_SMEM, g_lt_flags[1]);
-  ln_transpose_kernel<true><<<lt_grid(seq), LT_THREADS, LT_SMEM, (cudaStream_t)stream>>>(
-      x, y, bias, alpha, gamma, beta, cf, seq->dev);
+  PK_LT_LAUNCH(ln_transpose_kernel, true, 1, stream, x, y, bias, alpha, gamma, beta, cf,
+               seq->dev);
   return pkcu_launch_status("pkcu_residual_layer_norm_transpose");
 }
 
@@ -345,9 +364,8 @@ extern "C" int pkcu_transpose_add(float *x, const float *y, const float *bias,
   if (!x || !y || !PK_ALIGNED16(x) || (bias && !PK_ALIGNED16(bias)))
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_transpose_add: bad or misaligned pointer");
   if (seq->frames == 0) return PKCU_OK;
-  smem_optin(transpose_add_kernel<false>, LT_SMEM, g_lt_flags[2]);
-  transpose_add_kernel<false><<<lt_grid(seq), LT_THREADS, LT_SMEM, (cudaStream_t)stream>>>(
-      x, y, bias, nullptr, nullptr, nullptr, seq->dev);
+  PK_LT_LAUNCH(transpose_add_kernel, false, 2, stream, x, y, bias, nullptr, nullptr, nullptr,
+               seq->dev);
   return pkcu_launch_status("pkcu_transpose_add");
 }
 
@@ -360,8 +378,6 @@ extern "C" int pkcu_transpose_add_layer_norm(float *x, const float *y, const flo
       !PK_ALIGNED16(beta) || !PK_ALIGNED16(ln) || (bias && !PK_ALIGNED16(bias)))
     return pkcu_fail(PKCU_ERR_ARG, "pkcu_transpose_add_layer_norm: bad or misaligned pointer");
   if (seq->frames == 0) return PKCU_OK;
-  smem_optin(transpose_add_kernel<true>, LT_SMEM, g_lt_flags[3]);
-  transpose_add_kernel<true><<<lt_grid(seq), LT_THREADS, LT_SMEM, (cudaStream_t)stream>>>(
-      x, y, bias, gamma, beta, ln, seq->dev);
+  PK_LT_LAUNCH(transpose_add_kernel, true, 3, stream, x, y, bias, gamma, beta, ln, seq->dev);
   return pkcu_launch_status("pkcu_transpose_add_layer_norm");
 }

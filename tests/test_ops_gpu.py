@@ -13,6 +13,9 @@ from gpuhelp import D, DH, FF, H, Layout, dev, empty, host
 pytestmark = pytest.mark.gpu
 
 RAGGED = [[1, 7, 3, 32], [408, 416, 416, 408], [9], [375, 375]]
+# enough 32-frame tiles for every SM: the transposing kernels' 32-frame path
+# (the cases above take the 16-frame one)
+WIDE = [[375] * 13 + [1, 37]]
 
 
 def rng(seed):
@@ -143,7 +146,7 @@ def test_residual_layer_norm(cuda, oracle):
     assert_close(host(xd), oracle.layer_norm_rows(oracle.residual(x, y, 1.0), g1, b1), "no next")
 
 
-@pytest.mark.parametrize("lengths", RAGGED)
+@pytest.mark.parametrize("lengths", RAGGED + WIDE)
 def test_layer_norm_transpose(cuda, oracle, lengths):
     r = rng(sum(lengths))
     L = Layout(lengths)
@@ -174,7 +177,7 @@ def test_layer_norm_transpose(cuda, oracle, lengths):
             assert_close(L.chunk(got, i, D, (D, T)), want, f"res item {i}")
 
 
-@pytest.mark.parametrize("lengths", RAGGED)
+@pytest.mark.parametrize("lengths", RAGGED + WIDE)
 def test_transpose_add_layer_norm(cuda, oracle, lengths):
     r = rng(7 + sum(lengths))
     L = Layout(lengths)
