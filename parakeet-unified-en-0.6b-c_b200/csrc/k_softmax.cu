@@ -352,8 +352,8 @@ template <int NCH, int ROWS, bool SOFTMAX>
 __device__ __forceinline__ void score_rows(const float *sa, const SlotRow &cur, float *S,
                                            float scale, int li);
 
-// Shared memory per warp: NBUF buffers x ROWS rows x (ac, bd) x stg floats.
-template <int NCH, int ROWS, bool SOFTMAX>
+// Shared memory per warp: NB (ring depth) buffers x ROWS rows x (ac, bd) x stg floats.
+template <int NCH, int ROWS, bool SOFTMAX, int NB>
 __global__ void __launch_bounds__(32 * PIPE_WARPS)
 relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *S, float scale,
                           SeqDev seq, unsigned total_rows, long long ac_total, long long bd_total,
@@ -361,15 +361,15 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
   constexpr int LPR = 32 / ROWS;
   constexpr int STG = 4 * LPR * NCH + 8;   // floats per staged ac row or bd band
   extern __shared__ float4 pipe_smem4[];
-  __shared__ unsigned long long bars[PIPE_WARPS][NBUF];
+  __shared__ unsigned long long bars[PIPE_WARPS][NB];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane / LPR, li = lane % LPR;
   // buffer b, row g: ac at wb + ((b * ROWS + g) * 2) * STG, bd STG floats later
-  float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * NBUF * ROWS * 2 * STG;
+  float *wb = reinterpret_cast<float *>(pipe_smem4) + (size_t)warp * NB * ROWS * 2 * STG;
   unsigned long long *bar = bars[warp];
   if (lane == 0) {
 #pragma unroll
-    for (int b = 0; b < NBUF; b++) mbar_init(bar + b, ROWS);
+    for (int b = 0; b < NB; b++) mbar_init(bar + b, ROWS);
     mbar_init_fence();
   }
   __syncwarp();
@@ -379,10 +379,10 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
   const unsigned r_end = (unsigned)min((unsigned long long)total_rows, first + rows_per_warp);
   const bool uniform = seq.uniform_T > 0;
   const int uT = uniform ? seq.uniform_T : 1;
-  // ring: slot n % NBUF holds group n; groups 0 .. NBUF-2 are issued up
-  // front, group n + NBUF - 1 while group n is computed. The loop is unrolled
+  // ring: slot n % NB holds group n; groups 0 .. NB-2 are issued up
+  // front, group n + NB - 1 while group n is computed. The loop is unrolled
   // over the slots so that each slot's row record stays in registers.
-  SlotRow slot[NBUF];
+  SlotRow slot[NB];
   unsigned irow = (unsigned)first + g;   // this group's row of the next group to issue
   int iu = uniform ? (int)(irow % (unsigned)uT) : 0;
   auto issue = [&](int b) -> SlotRow {
@@ -401,19 +401,19 @@ relpos_scores_pipe_kernel(const float *ac, const float *__restrict__ bd, float *
     return r;
   };
 #pragma unroll
-  for (int b = 0; b < NBUF - 1; b++) slot[b] = issue(b);
+  for (int b = 0; b < NB - 1; b++) slot[b] = issue(b);
   unsigned parity = 0;   // bit b: phase parity of buffer b's next completion
   unsigned base = (unsigned)first;
   while (true) {
 #pragma unroll
-    for (int b = 0; b < NBUF; b++) {   // compile-time slot b computes group n
+    for (int b = 0; b < NB; b++) {   // compile-time slot b computes group n
       if (base >= r_end) return;       // nothing in flight: later groups are past the range
-      slot[(b + NBUF - 1) % NBUF] = issue((b + NBUF - 1) % NBUF);   // the slot freed last
+      slot[(b + NB - 1) % NB] = issue((b + NB - 1) % NB);   // the slot freed last
       const bool ok = mbar_wait(bar + b, (parity >> b) & 1);
       if (__any_sync(PK_FULL_MASK, !ok)) {   // a copy never landed: give up this warp
         if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
 #pragma unroll
-        for (int o = 0; o < NBUF; o++)
+        for (int o = 0; o < NB; o++)
           if (o != b) mbar_wait(bar + o, (parity >> o) & 1);
         return;
       }
@@ -525,15 +525,15 @@ static void launch_scores_warp(const float *ac, const float *bd, float *S, float
                                                                               seq->dev);
 }
 
-template <int NCH, int ROWS, bool SOFTMAX>
+template <int NCH, int ROWS, bool SOFTMAX, int NB = NBUF>
 static void launch_scores_pipe(const float *ac, const float *bd, float *S, float scale,
                                const pkcu_seq *seq, cudaStream_t s) {
   constexpr int STG = 4 * (32 / ROWS) * NCH + 8;
-  const size_t smem = sizeof(float) * NBUF * ROWS * 2 * (size_t)STG * PIPE_WARPS;
+  const size_t smem = sizeof(float) * NB * ROWS * 2 * (size_t)STG * PIPE_WARPS;
   static int flags[64];
-  smem_optin(relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX>, smem, flags);
+  smem_optin(relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX, NB>, smem, flags);
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX>,
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX, NB>,
                                                 32 * PIPE_WARPS, smem);
   if (per_sm < 1) per_sm = 1;
   const long long rows = (long long)PK_H * seq->frames;
@@ -544,7 +544,7 @@ static void launch_scores_pipe(const float *ac, const float *bd, float *S, float
   const long long warps = grid * PIPE_WARPS;
   long long per_warp = (rows + warps - 1) / warps;
   per_warp = (per_warp + ROWS - 1) / ROWS * ROWS;
-  relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
+  relpos_scores_pipe_kernel<NCH, ROWS, SOFTMAX, NB><<<(unsigned)grid, 32 * PIPE_WARPS, smem, s>>>(
       ac, bd, S, scale, seq->dev, (unsigned)rows, seq->score_elems, seq->bd_elems,
       (unsigned)per_warp);
 }
@@ -563,12 +563,22 @@ static int launch_scores(const float *ac, const float *bd, float *S, float scale
   // chunks; two rows per warp (16 lanes each) up to 8 chunks per lane, one
   // row per warp above that
   const int nq = (T + 6) / 4;
-  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && PK_ALIGNED16(S) && nq <= 32 * 8 && pipe_rows_fit(seq)) {
+  // The pipelined kernel needs a few dozen rows per warp to cover its ring's
+  // ramp; below about 32 rows per warp of a full wave (12 warps per SM) the
+  // one-warp-per-row kernel is faster (8 chunks of 416 frames: 34.9 against
+  // 38.4 us).
+  const bool few_rows = (long long)PK_H * seq->frames < (long long)pkcu_sm_count() * 12 * 32;
+  if (PK_ALIGNED16(ac) && PK_ALIGNED16(bd) && PK_ALIGNED16(S) && nq <= 32 * 8 && pipe_rows_fit(seq) &&
+      !(few_rows && npl <= 32)) {
+    // measured at 256 x 375 / 256 x 416: two rows per warp up to 6 chunks per
+    // lane (<6, 2>: 0.59 ms); one row per warp above (<4, 1>: 0.72 ms at
+    // T = 416, against 0.97 ms for <8, 2>, whose 90 registers and 66 KB per
+    // CTA left six warps per SM)
     if (nq <= 16 * 1) launch_scores_pipe<1, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (nq <= 16 * 2) launch_scores_pipe<2, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (nq <= 16 * 4) launch_scores_pipe<4, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (nq <= 16 * 6) launch_scores_pipe<6, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
-    else if (nq <= 16 * 8) launch_scores_pipe<8, 2, SOFTMAX>(ac, bd, S, scale, seq, s);
+    else if (nq <= 32 * 4) launch_scores_pipe<4, 1, SOFTMAX>(ac, bd, S, scale, seq, s);
     else if (nq <= 32 * 6) launch_scores_pipe<6, 1, SOFTMAX>(ac, bd, S, scale, seq, s);
     else launch_scores_pipe<8, 1, SOFTMAX>(ac, bd, S, scale, seq, s);
     return PKCU_OK;

@@ -250,6 +250,35 @@ def test_relpos_scores(cuda, oracle, lengths):
         assert_bitexact(host(acd), got, "in place")
 
 
+# Batches with enough score rows for the pipelined kernel (the cases above
+# are short enough for the one-warp-per-row kernel): one case per chunk
+# configuration of the dispatch, ragged where it matters.
+@pytest.mark.parametrize("lengths", [[50] * 150, [120] * 60, [250] * 29, [375] * 19 + [1],
+                                     [416] * 17 + [408], [700] * 11, [1000] * 7 + [999]])
+def test_relpos_scores_pipelined(cuda, oracle, lengths):
+    r = rng(17 + sum(lengths))
+    L = Layout(lengths)
+    ac = r.standard_normal(L.score[-1]).astype(np.float32) * 4
+    bd = r.standard_normal(L.bd[-1]).astype(np.float32) * 4
+    scale = np.float32(1.0) / np.sqrt(np.float32(128.0))
+    with cuda.Seq(lengths) as seq:
+        acd, bdd = dev(ac), dev(bd)
+        out = empty(L.score[-1])
+        cuda.call("pkcu_relpos_combine", acd.data_ptr(), bdd.data_ptr(), out.data_ptr(),
+                  float(scale), seq.handle, cuda.stream_handle())
+        got = host(out)
+        comb = [oracle.relpos_combine(L.scores(ac, i), L.bds(bd, i), float(scale))
+                for i in range(len(lengths))]
+        for i in range(len(lengths)):
+            assert_bitexact(L.scores(got, i), comb[i], f"combine {i}")
+        cuda.call("pkcu_relpos_combine_softmax", acd.data_ptr(), bdd.data_ptr(), out.data_ptr(),
+                  float(scale), seq.handle, cuda.stream_handle())
+        got = host(out)
+        for i, T in enumerate(lengths):
+            want = oracle.softmax_rows(comb[i].reshape(H * T, T)).reshape(H, T, T)
+            assert_close(L.scores(got, i), want, f"softmax {i}")
+
+
 # ── head layouts ──────────────────────────────────────────────────────────────
 
 @pytest.mark.parametrize("lengths", RAGGED)
