@@ -791,16 +791,6 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K, co
   tc::tc_gemm_kernel<NPB, BN><<<grid, tc::THREADS, C::SMEM, s>>>(ma, mb, M, N, K, e);
   return pkcu_launch_status("tcgen05 GEMM");
 }
-
-// 256-wide tiles unless they would occupy fewer than half the SMs (the GLU
-// epilogue needs them: a value group and its gates in one warp's columns).
-int narrow_tiles(int M, int N, int mode) {
-  if (mode == PK_TC_GLU) return 0;
-  if (N <= 128) return 1;   // a 256-wide tile would be half padding
-  const long long wide = (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM);
-  return wide * 2 < pkcu_sm_count();
-}
-
 }  // namespace
 
 extern "C" void pk_tc_warm(void) {
@@ -905,6 +895,9 @@ int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long 
                      ep->mode != PK_TC_RESID && ep->mode != PK_TC_STORE_T) ||
       !PK_ALIGNED16(a_parts) || !PK_ALIGNED16(planes))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: bad arguments (M %d, N %d, K %d)", M, N, K);
+  // 256-wide tiles unless N <= 128 (half padding) or they would occupy fewer
+  // than half the SMs; the GLU epilogue always takes them (a value group and
+  // its gates in one warp's columns)
   const int narrow = ep->mode != PK_TC_GLU &&
                      (N <= 128 || Z * (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM) * 2 <
                                       pkcu_sm_count());

@@ -121,9 +121,16 @@ __device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
 
 // exp_poly_clamped on a pair (inputs already in [-87, 87]); per element the
 // same operations as the scalar form. -kf*ln2 + x == kf*(-ln2) + x exactly.
+// The product x * log2(e) is formed by two scalar __fmul_rn, which are never
+// contracted: a packed multiply followed by the packed shifter add was fused
+// into one multiply-add in the generated code (measured), and then k rounds
+// differently from the reference wherever the rounded product is a tie k + 1/2
+// (x = 1.03972077: the reference's k is 2, the fused form's 1).
 __device__ __forceinline__ float2 exp_poly2_clamped(float2 x) {
   constexpr float kShift = 12582912.0f;
-  const float2 shifted = add2(mul2(x, splat2(1.44269504088896341f)), splat2(kShift));
+  const float2 shifted = add2(make_float2(__fmul_rn(x.x, 1.44269504088896341f),
+                                          __fmul_rn(x.y, 1.44269504088896341f)),
+                              splat2(kShift));
   const float2 kf = sub2(shifted, splat2(kShift));
   const float2 r = fma2(kf, splat2(-0.69314718055994529f), x);
   float2 y = splat2(1.0f / 120.0f);

@@ -55,6 +55,38 @@ def test_swish_dense_sweep(cuda, oracle):
     assert_bitexact(host(xd), oracle.swish(x), "swish sweep")
 
 
+def exp_rounding_ties():
+    """Floats x in [-87, 87] whose float32 product x * log2(e) is exactly
+    k + 1/2: the inputs on which the reference's exp (pk_exp_avx2,
+    csrc/tensor_ops.c:97-121: the product rounded, then rounded to an integer,
+    ties to even) and an exp that fuses the product into the rounding add
+    choose different k."""
+    l2e = np.float32(1.44269504088896341)
+    found = []
+    for t in np.arange(126, dtype=np.float32) + np.float32(0.5):   # |k + 1/2|
+        b0 = int(np.array([t / l2e], np.float32).view(np.int32)[0])
+        xs = np.arange(b0 - 64, b0 + 65, dtype=np.int32).view(np.float32)
+        found.extend(xs[(xs * l2e) == t].tolist())
+    x = np.array(found, np.float32)
+    x = x[x <= np.float32(87.0)]
+    return np.concatenate([x, -x])
+
+
+def test_swish_exp_rounding_ties(cuda, oracle):
+    """Swish bit-exact against the restatement on every input whose exp
+    argument sits on a rounding tie of x * log2(e) (and its two float
+    neighbours): the packed f32x2 arithmetic must round the product and the
+    shifter add separately, as the reference does."""
+    ties = exp_rounding_ties()
+    assert ties.size > 200
+    near = np.concatenate([np.nextafter(ties, np.float32(np.inf)), np.nextafter(ties, np.float32(-np.inf))])
+    v = -np.concatenate([ties, near]).astype(np.float32)   # Swish takes exp(-v)
+    v = np.concatenate([v, np.zeros((-v.size) % 8, np.float32)])
+    vd = dev(v)
+    cuda.call("pkcu_swish", vd.data_ptr(), v.size, cuda.stream_handle())
+    assert_bitexact(host(vd), oracle.swish(v), "swish on exp rounding ties")
+
+
 def test_glu_gate_dense_sweep(cuda, oracle):
     """The GLU gate's own exp (ex2-based, pk_common.cuh glu_gate) on a dense
     sweep of gate values in [-100, 100] (every 509th float) plus the clamp
