@@ -156,7 +156,10 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // 3.9 against 5.1 TB/s for the bare transposed write of 256 x 375 frames.
 // Persistent forms of both transposing kernels, one CTA per SM with the next
 // tile's rows prefetched into L2, measured slower still: 0.64 / 0.60 of the
-// copy bandwidth against 0.85 / 0.84.)
+// copy bandwidth against 0.85 / 0.84. So did two cures for the 4-way bank
+// conflict of the column reads (row stride 1028): warp instructions over 4
+// channels x 8 frames (0.80 / 0.44: 32-byte pieces per instruction), and rows
+// held as scalars with an odd stride (0.80 / 0.86).)
 template <int TT, bool RESID>
 __global__ void __launch_bounds__(32 * TT, 32 / TT)
 ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
