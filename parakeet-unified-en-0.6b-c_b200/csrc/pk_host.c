@@ -406,7 +406,10 @@ void pk_depthwise_conv1d(const float *x, const float *w, const float *b, float *
 
 /* ── sequence driver ─────────────────────────────────────────────────────── */
 
-int pkcu_encoder_nongemm_launches(int n_blocks) { return n_blocks > 0 ? 1 + 12 * n_blocks : 0; }
+/* The first block's LN_ff1, then per block: bias+Swish (FF1), residual+LN,
+ * QKV split, positional split, scores, head concat, residual+LN+transpose,
+ * GLU+conv, transpose-add+LN, bias+Swish (FF2), residual+LN+LN. */
+int pkcu_encoder_nongemm_launches(int n_blocks) { return n_blocks > 0 ? 1 + 11 * n_blocks : 0; }
 
 #define PK_TRY(call) do { int st_ = (call); if (st_) return st_; } while (0)
 #define PK_HOOK(blk, g) do { if (hook) PK_TRY(hook(hook_user, (blk), (g), stream)); } while (0)

@@ -62,7 +62,7 @@ def test_status_strings(L):
     assert L.pkcu_status_string(1) == b"invalid argument"
     assert L.pkcu_status_string(2) == b"CUDA error"
     assert L.pkcu_version().decode().count(".") == 2
-    assert L.pkcu_encoder_nongemm_launches(24) == 1 + 12 * 24
+    assert L.pkcu_encoder_nongemm_launches(24) == 1 + 11 * 24
 
 
 def test_argument_validation_without_gpu(L):

@@ -165,3 +165,23 @@ def test_encoder_nongemm_24_blocks_stays_bounded(cuda, oracle):
         x, caps = oracle.conformer_block(x, p, si)
     assert_close(gx, x, "x after 24 blocks")
     assert np.isfinite(gx).all()
+
+
+def test_sequence_launch_count(cuda):
+    """pkcu_encoder_nongemm_launches (the bench's gpu_launches claim) equals
+    the number of kernels one call launches, counted by the CUDA profiler."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    lengths, n_blocks = [37, 5, 40], 2
+    blocks, items = make_batch(lengths, n_blocks, seed=77)
+    run_gpu(cuda, lengths, blocks, items)   # warm-up: first-call attribute setup
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        run_gpu(cuda, lengths, blocks, items)
+        torch.cuda.synchronize()
+    seq_kernels = ("ln1024_kernel", "row_vec_kernel", "qkv_split_kernel", "pos_split_kernel",
+                   "relpos_scores", "head_concat_kernel", "ln_transpose_kernel",
+                   "dwconv_al_kernel", "dwconv_row_kernel", "transpose_add_kernel")
+    n = sum(1 for e in prof.events()
+            if e.device_type == torch.autograd.DeviceType.CUDA and any(k in e.name for k in seq_kernels))
+    assert n == cuda.lib().pkcu_encoder_nongemm_launches(n_blocks), n
