@@ -361,17 +361,18 @@ constexpr int DWA_ROW = 656;
 __host__ __device__ constexpr int dwa_row_need(int T) { return 4 * ((T + 6) / 4) + 8; }
 
 // GLU of 4 values as two packed pairs (bit-identical to glu1 on each value).
+template <class F = F2Ptx>
 __device__ __forceinline__ float4 glu4(float4 a, float4 g, float ba, float bg, bool bias) {
   if (bias) {
-    const float2 a01 = add2(make_float2(a.x, a.y), splat2(ba));
-    const float2 a23 = add2(make_float2(a.z, a.w), splat2(ba));
-    const float2 g01 = add2(make_float2(g.x, g.y), splat2(bg));
-    const float2 g23 = add2(make_float2(g.z, g.w), splat2(bg));
+    const float2 a01 = F::add(make_float2(a.x, a.y), splat2(ba));
+    const float2 a23 = F::add(make_float2(a.z, a.w), splat2(ba));
+    const float2 g01 = F::add(make_float2(g.x, g.y), splat2(bg));
+    const float2 g23 = F::add(make_float2(g.z, g.w), splat2(bg));
     a = make_float4(a01.x, a01.y, a23.x, a23.y);
     g = make_float4(g01.x, g01.y, g23.x, g23.y);
   }
-  const float2 o01 = glu_gate2(make_float2(a.x, a.y), make_float2(g.x, g.y));
-  const float2 o23 = glu_gate2(make_float2(a.z, a.w), make_float2(g.z, g.w));
+  const float2 o01 = glu_gate2<F>(make_float2(a.x, a.y), make_float2(g.x, g.y));
+  const float2 o23 = glu_gate2<F>(make_float2(a.z, a.w), make_float2(g.z, g.w));
   return make_float4(o01.x, o01.y, o23.x, o23.y);
 }
 
@@ -384,7 +385,8 @@ __device__ __forceinline__ float dwa_finish(float val, float mean, float den, fl
 
 // Two channel rows per warp (lane group g = lane / 16 takes row 2w + g), so
 // the copy issue, the parameter loads and the one-output-per-lane edge steps
-// of both rows share their instructions; DWA_WARPS warps = 8 channels per CTA
+// of both rows share their instructions (packed arithmetic in the F2Cu form,
+// measured faster here); DWA_WARPS warps = 8 channels per CTA
 // (C % 8 == 0 on this path, so every row of a CTA exists). Staging sized to the
 // batch keeps nine such CTAs (36 warps) on an SM at T = 375; a persistent form
 // with a two-buffer copy pipeline per warp (16 warps per SM) measured 0.64-0.67
@@ -459,7 +461,7 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
     const int tail0 = g_hi > g_lo ? 4 * g_hi - off : n_head;
     const int n_left = n_head + (T - tail0);
     for (int q = g_lo + li; q < g_hi; q += LPR)
-      st4(s + 4 + 4 * q, glu4(ld4(s + 4 + 4 * q), ld4(sg + 4 + 4 * q), ba, bg, gbias));
+      st4(s + 4 + 4 * q, glu4<F2Cu>(ld4(s + 4 + 4 * q), ld4(sg + 4 + 4 * q), ba, bg, gbias));
     if (li < n_left) {
       const int t = li < n_head ? li : tail0 + (li - n_head);
       float aa = s[4 + off + t], gg = sg[4 + off + t];
@@ -486,16 +488,16 @@ dwconv_al_kernel(const float *__restrict__ x, const float *__restrict__ w,
     float2 v01 = splat2(bias), v23 = splat2(bias);
 #pragma unroll
     for (int k = 0; k < K; k++) {
-      v01 = fma2(make_float2(win[k], win[k + 1]), splat2(wk[k]), v01);
-      v23 = fma2(make_float2(win[k + 2], win[k + 3]), splat2(wk[k]), v23);
+      v01 = F2Cu::fma(make_float2(win[k], win[k + 1]), splat2(wk[k]), v01);
+      v23 = F2Cu::fma(make_float2(win[k + 2], win[k + 3]), splat2(wk[k]), v23);
     }
     if (BN) {
       v01 = make_float2(((v01.x - mean) / den) * gam + bet, ((v01.y - mean) / den) * gam + bet);
       v23 = make_float2(((v23.x - mean) / den) * gam + bet, ((v23.y - mean) / den) * gam + bet);
     }
     if (SW == DW_SWISH_POLY) {
-      v01 = swish_poly2(v01);
-      v23 = swish_poly2(v23);
+      v01 = swish_poly2<F2Cu>(v01);
+      v23 = swish_poly2<F2Cu>(v23);
     }
     st4(orow + t0, make_float4(v01.x, v01.y, v23.x, v23.y));
   }

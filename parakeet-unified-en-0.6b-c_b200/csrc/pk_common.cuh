@@ -107,16 +107,70 @@ __device__ __forceinline__ float exp_poly_nonpos(float x) {
 }
 
 // ── packed fp32 pairs (sm_100 f32x2 arithmetic) ──────────────────────────────
-// The f32x2 add / mul / fma (CUDA's __fadd2_rn / __fmul2_rn / __ffma2_rn for
-// sm_100) apply one IEEE fp32 operation, round to nearest, to each half of a
-// register pair: the results are those of the scalar instructions, at half the
-// issue slots. Used where the kernels are bound by instruction issue
-// (polynomial exp, Swish, depthwise taps, score combine). a - b is formed as
-// a + (-b), which is the same IEEE result.
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+// add/sub/mul/fma.rn.f32x2 apply one IEEE fp32 operation, round to nearest,
+// to each half of a register pair: the results are those of the scalar
+// instructions, at half the issue slots. Used where the kernels are bound by
+// instruction issue (polynomial exp, Swish, depthwise taps, score combine).
+//
+// Two forms of the same operations, chosen per kernel by measurement:
+//   F2Ptx  inline PTX (the default: add2 / sub2 / mul2 / fma2 below). Faster in
+//          the Swish and int4 dequant kernels (0.87 / 0.73 of the copy
+//          bandwidth against 0.80 / 0.64 with the other form).
+//   F2Cu   CUDA's __fadd2_rn / __fmul2_rn / __ffma2_rn, which the compiler can
+//          schedule and allocate as pairs: faster in the GLU + depthwise conv
+//          kernel (204 against 219 us at 256 x 375, same box).
+// Both give the same results. Either way a packed multiply feeding a packed add
+// may be fused into one multiply-add by the assembler: where the separately
+// rounded product matters (the exp's k), it is formed with scalar __fmul_rn.
+
+struct F2Ptx {
+  static __device__ __forceinline__ unsigned long long pk(float2 v) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+    return r;
+  }
+  static __device__ __forceinline__ float2 unpk(unsigned long long r) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+  }
+  static __device__ __forceinline__ float2 add(float2 a, float2 b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+    return unpk(r);
+  }
+  static __device__ __forceinline__ float2 sub(float2 a, float2 b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+    return unpk(r);
+  }
+  static __device__ __forceinline__ float2 mul(float2 a, float2 b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+    return unpk(r);
+  }
+  static __device__ __forceinline__ float2 fma(float2 a, float2 b, float2 c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)), "l"(pk(c)));
+    return unpk(r);
+  }
+};
+
+struct F2Cu {   // a - b as a + (-b): the same IEEE result
+  static __device__ __forceinline__ float2 add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+  static __device__ __forceinline__ float2 sub(float2 a, float2 b) {
+    return __fadd2_rn(a, make_float2(-b.x, -b.y));
+  }
+  static __device__ __forceinline__ float2 mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+  static __device__ __forceinline__ float2 fma(float2 a, float2 b, float2 c) {
+    return __ffma2_rn(a, b, c);
+  }
+};
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return F2Ptx::add(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return F2Ptx::sub(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return F2Ptx::mul(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return F2Ptx::fma(a, b, c); }
 __device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
 
 // exp_poly_clamped on a pair (inputs already in [-87, 87]); per element the
@@ -126,22 +180,23 @@ __device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
 // into one multiply-add in the generated code (measured), and then k rounds
 // differently from the reference wherever the rounded product is a tie k + 1/2
 // (x = 1.03972077: the reference's k is 2, the fused form's 1).
+template <class F = F2Ptx>
 __device__ __forceinline__ float2 exp_poly2_clamped(float2 x) {
   constexpr float kShift = 12582912.0f;
-  const float2 shifted = add2(make_float2(__fmul_rn(x.x, 1.44269504088896341f),
-                                          __fmul_rn(x.y, 1.44269504088896341f)),
-                              splat2(kShift));
-  const float2 kf = sub2(shifted, splat2(kShift));
-  const float2 r = fma2(kf, splat2(-0.69314718055994529f), x);
+  const float2 shifted = F::add(make_float2(__fmul_rn(x.x, 1.44269504088896341f),
+                                            __fmul_rn(x.y, 1.44269504088896341f)),
+                                splat2(kShift));
+  const float2 kf = F::sub(shifted, splat2(kShift));
+  const float2 r = F::fma(kf, splat2(-0.69314718055994529f), x);
   float2 y = splat2(1.0f / 120.0f);
-  y = fma2(y, r, splat2(1.0f / 24.0f));
-  y = fma2(y, r, splat2(1.0f / 6.0f));
-  y = fma2(y, r, splat2(0.5f));
-  y = fma2(y, r, splat2(1.0f));
-  y = fma2(y, r, splat2(1.0f));
+  y = F::fma(y, r, splat2(1.0f / 24.0f));
+  y = F::fma(y, r, splat2(1.0f / 6.0f));
+  y = F::fma(y, r, splat2(0.5f));
+  y = F::fma(y, r, splat2(1.0f));
+  y = F::fma(y, r, splat2(1.0f));
   const int px = (__float_as_int(shifted.x) - (0x4B400000 - 127)) << 23;
   const int py = (__float_as_int(shifted.y) - (0x4B400000 - 127)) << 23;
-  return mul2(y, make_float2(__int_as_float(px), __int_as_float(py)));
+  return F::mul(y, make_float2(__int_as_float(px), __int_as_float(py)));
 }
 
 // Correctly rounded 1/d for d in [1, 2^126): the hardware approximation
@@ -158,18 +213,20 @@ __device__ __forceinline__ float rcp_1_2e126(float d) {
   const float r0 = rcp_approx(d);
   return fmaf(fmaf(-d, r0, 1.0f), r0, r0);
 }
+template <class F = F2Ptx>
 __device__ __forceinline__ float2 rcp2_1_2e126(float2 d) {
   const float2 r0 = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-  const float2 e = fma2(make_float2(-d.x, -d.y), r0, splat2(1.0f));
-  return fma2(e, r0, r0);
+  const float2 e = F::fma(make_float2(-d.x, -d.y), r0, splat2(1.0f));
+  return F::fma(e, r0, r0);
 }
 
+template <class F = F2Ptx>
 __device__ __forceinline__ float2 swish_poly2(float2 v) {
-  float2 m = sub2(splat2(0.0f), v);
+  float2 m = F::sub(splat2(0.0f), v);
   m.x = fminf(fmaxf(m.x, -87.0f), 87.0f);
   m.y = fminf(fmaxf(m.y, -87.0f), 87.0f);
-  const float2 d = add2(splat2(1.0f), exp_poly2_clamped(m));
-  return mul2(v, rcp2_1_2e126(d));
+  const float2 d = F::add(splat2(1.0f), exp_poly2_clamped<F>(m));
+  return F::mul(v, rcp2_1_2e126<F>(d));
 }
 
 // Swish of the vector body of pk_swish (csrc/tensor_ops.c:383-388):
@@ -215,17 +272,18 @@ constexpr float GATE_L2E_HI = 1.44269502162933349609375f;   // float(log2 e)
 constexpr float GATE_L2E_LO = 1.925963033500011e-08f;       // float(log2 e - GATE_L2E_HI)
 constexpr float GATE_SHIFT = 12582912.0f;                   // 1.5 * 2^23
 
+template <class F = F2Ptx>
 __device__ __forceinline__ float2 glu_gate2(float2 a, float2 g) {
-  float2 m = sub2(splat2(0.0f), g);
+  float2 m = F::sub(splat2(0.0f), g);
   m.x = fminf(fmaxf(m.x, -86.0f), 86.0f);
   m.y = fminf(fmaxf(m.y, -86.0f), 86.0f);
-  const float2 t = fma2(m, splat2(GATE_L2E_HI), splat2(GATE_SHIFT));
-  float2 f = fma2(m, splat2(GATE_L2E_HI), sub2(splat2(GATE_SHIFT), t));
-  f = fma2(m, splat2(GATE_L2E_LO), f);
+  const float2 t = F::fma(m, splat2(GATE_L2E_HI), splat2(GATE_SHIFT));
+  float2 f = F::fma(m, splat2(GATE_L2E_HI), F::sub(splat2(GATE_SHIFT), t));
+  f = F::fma(m, splat2(GATE_L2E_LO), f);
   const float ex = __uint_as_float(__float_as_uint(ex2_approx(f.x)) + (__float_as_uint(t.x) << 23));
   const float ey = __uint_as_float(__float_as_uint(ex2_approx(f.y)) + (__float_as_uint(t.y) << 23));
-  const float2 d = add2(splat2(1.0f), make_float2(ex, ey));
-  float2 o = mul2(a, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+  const float2 d = F::add(splat2(1.0f), make_float2(ex, ey));
+  float2 o = F::mul(a, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
   if (g.x != g.x) o.x = g.x;
   if (g.y != g.y) o.y = g.y;
   return o;
