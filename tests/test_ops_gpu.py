@@ -126,8 +126,8 @@ def test_glu_gate_dense_sweep(cuda, oracle):
 # ── LayerNorm family ──────────────────────────────────────────────────────────
 
 @pytest.mark.parametrize("R,Dd,offset", [(1, 1024, 0), (7, 1024, 0), (375, 1024, 0),
-                                         (1000, 1024, 0), (5, 37, 0), (4, 1024, 1),
-                                         (3, 2048, 0), (2, 1, 0)])
+                                         (1000, 1024, 0), (8000, 1024, 0), (5, 37, 0),
+                                         (4, 1024, 1), (3, 2048, 0), (2, 1, 0)])
 def test_layer_norm_rows(cuda, oracle, R, Dd, offset):
     r = rng(R * Dd + offset)
     x = r.standard_normal((R, Dd)).astype(np.float32)
@@ -146,9 +146,9 @@ def test_layer_norm_rows(cuda, oracle, R, Dd, offset):
     assert_close(host(xd).reshape(R, Dd), want, "ln inplace")
 
 
-def test_residual_layer_norm(cuda, oracle):
-    r = rng(3)
-    R = 777
+@pytest.mark.parametrize("R", [777, 7501])
+def test_residual_layer_norm(cuda, oracle, R):
+    r = rng(3 + R)
     x = r.standard_normal((R, D)).astype(np.float32)
     y = r.standard_normal((R, D)).astype(np.float32)
     bias = (0.1 * r.standard_normal(D)).astype(np.float32)
