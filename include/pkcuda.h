@@ -510,7 +510,10 @@ int  pkcu_encoder_model_create(const pkcu_weights *w, pkcu_stream_t stream, pkcu
 void pkcu_encoder_model_destroy(pkcu_encoder_model *m);
 int  pkcu_encoder_model_blocks(const pkcu_encoder_model *m);
 /* All blocks on x [frames, 1024] in place; gemm_out / gemm_in: device buffers
- * for the batch (those of a 1-group pkcu_encoder_ws fit). */
+ * for the batch (those of a 1-group pkcu_encoder_ws fit), used as scratch.
+ * With every projection on the tensor-core GEMM the FF hidden layers stay in
+ * the model's own buffer as the second product's bf16 operand parts, so
+ * gemm_in->h1 / h2 are not written. */
 int  pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_outputs *gemm_out,
                           const pkcu_gemm_inputs *gemm_in, const pkcu_seq *seq,
                           pkcu_stream_t stream);

@@ -173,6 +173,7 @@ struct Epi {
   // z reads A rows from z * a_z and B rows from z * b_z, and writes from C + z * c_z
   int Z;
   long long a_z, b_z, c_z;
+  __nv_bfloat16 *Cb;     // SWISH_SPLIT: the parts [M, 3N]
 };
 
 // Item of frame r: a division for a uniform batch, else a binary search of
@@ -251,6 +252,38 @@ __device__ __forceinline__ void epi_store32(const Epi &e, long long r, int n0, f
       float *dst = part == 1 ? e.Kh : e.Vh;
 #pragma unroll
       for (int j = 0; j < 32; j += 4) st4(dst + o + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+    }
+    return;
+  }
+  if (e.mode == PK_TC_SWISH_SPLIT) {
+    // Swish, then the three bf16 parts of each value as the activation split
+    // makes them (x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1)):
+    // 64-byte runs into the [h0 | h1 | h2] row of the next product's operand
+    const long long N = e.channels;
+    __nv_bfloat16 *o = e.Cb + r * 3 * N + n0;
+#pragma unroll
+    for (int j0 = 0; j0 < 32; j0 += 8) {
+      __align__(16) __nv_bfloat16 p[3][8];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        float2 h = make_float2(v[j0 + j], v[j0 + j + 1]);
+        if (e.bias) {
+          h.x = h.x + __ldg(e.bias + n0 + j0 + j);
+          h.y = h.y + __ldg(e.bias + n0 + j0 + j + 1);
+        }
+        h = swish_poly2(h);
+        const float hv[2] = {h.x, h.y};
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          p[0][j + u] = __float2bfloat16_rn(hv[u]);
+          const float r1 = hv[u] - __bfloat162float(p[0][j + u]);
+          p[1][j + u] = __float2bfloat16_rn(r1);
+          p[2][j + u] = __float2bfloat16_rn(r1 - __bfloat162float(p[1][j + u]));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 3; k++)
+        *reinterpret_cast<uint4 *>(o + k * N + j0) = *reinterpret_cast<const uint4 *>(p[k]);
     }
     return;
   }
@@ -922,6 +955,9 @@ int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long 
   if (ep->seq) e.seq = ep->seq->dev;
   else memset(&e.seq, 0, sizeof(e.seq));
   e.channels = e.mode == PK_TC_GLU ? N / 2 : N;
+  e.Cb = static_cast<__nv_bfloat16 *>(ep->Cb);
+  if (e.mode == PK_TC_SWISH_SPLIT && (!e.Cb || !PK_ALIGNED16(e.Cb) || N % 32 || Z != 1))
+    return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the split Swish epilogue needs aligned parts and N %% 32 == 0");
   if ((e.mode == PK_TC_CF || e.mode == PK_TC_GLU) &&
       (!ep->seq || !e.C || M != ep->seq->frames || (e.mode == PK_TC_GLU && N % 64)))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: a channel-first epilogue needs the batch and its output");
@@ -931,7 +967,7 @@ int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long 
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the QKV epilogue needs the batch and its outputs");
   if ((e.mode == PK_TC_STORE || e.mode == PK_TC_SWISH || e.mode == PK_TC_RESID) && (!e.C || e.ldc < N))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: no output, or rows shorter than N");
-  e.vec = PK_ALIGNED16(e.C) && e.ldc % 4 == 0 && (c_z % 4) == 0;
+  e.vec = (PK_ALIGNED16(e.C) && e.ldc % 4 == 0 && (c_z % 4) == 0) || e.mode == PK_TC_SWISH_SPLIT;
   e.Z = Z;
   e.a_z = a_z;
   e.b_z = b_z;

@@ -65,6 +65,9 @@ struct pkcu_encoder_model {
     float qscale[64][W_N];             /* > 0: the int8 weight's scale, w = q x this */
     void *split_ws;                    /* activation parts [rows, 3K] bf16, grown per forward */
     size_t split_cap;                  /* its bytes */
+    void *hsplit_ws;                   /* the FF hidden layer's parts [rows, 3 x 4096], written by
+                                          the first FF product's epilogue (fused forward) */
+    size_t hsplit_cap;
 };
 
 void pkcu_encoder_model_destroy(pkcu_encoder_model *m)
@@ -74,6 +77,7 @@ void pkcu_encoder_model_destroy(pkcu_encoder_model *m)
     if (m->arena) cudaFree(m->arena);
     if (m->stacks) cudaFree(m->stacks);
     if (m->split_ws) cudaFree(m->split_ws);
+    if (m->hsplit_ws) cudaFree(m->hsplit_ws);
     free(m);
 }
 
@@ -252,6 +256,7 @@ typedef struct {
     long long *off;   /* per item: frame, pos row, score, bd element offsets (4 x n_items) */
     unsigned fused;   /* PKCU_FUSED_* epilogues the hook's GEMMs apply */
     float *x;         /* the residual stream (the fused PW2 epilogue adds to it) */
+    void *hsplit;     /* fused: the FF hidden layer as bf16 parts (gemm_in h1 / h2 not written) */
 } Fwd;
 
 static const float ONE = 1.0f, ZERO = 0.0f;
@@ -310,15 +315,17 @@ static int proj_w(pkcu_encoder_model *m, cublasHandle_t h, int b, int k, int M, 
     return proj_tc(m, b, k, M, A, &e, stream);
 }
 
-/* FF linear1 with its bias and Swish in the GEMM's epilogue: h = Swish(A W + b1). */
-static int proj_swish(pkcu_encoder_model *m, int b, int k, int M, const float *A, const float *b1, float *h,
+/* FF linear1 with its bias and Swish in the GEMM's epilogue, h = Swish(A W + b1),
+ * written only as the three bf16 parts that FF linear2 reads (hparts [M, 3 x 4096]):
+ * the hidden layer never exists in fp32 and needs no split pass. */
+static int proj_swish(pkcu_encoder_model *m, int b, int k, int M, const float *A, const float *b1, void *hparts,
                       pkcu_stream_t stream)
 {
     pk_tc_epi e;
     memset(&e, 0, sizeof(e));
-    e.mode = PK_TC_SWISH;
+    e.mode = PK_TC_SWISH_SPLIT;
     e.bias = b1;
-    e.C = h;
+    e.Cb = hparts;
     return proj_tc(m, b, k, M, A, &e, stream);
 }
 
@@ -389,8 +396,19 @@ static int fwd_hook(void *user, int b, int gemm, pkcu_stream_t stream)
     const pkcu_block_params *p = &f->m->params[b];
     if (f->fused) {   /* the projections whose epilogues the sequence leaves to the GEMM */
         switch (gemm) {
-        case PKCU_GEMM_FF1_1: return proj_swish(f->m, b, W_FF1_1, (int)F, gi->ln_ff1, p->ff1_b1, gi->h1, stream);
-        case PKCU_GEMM_FF2_1: return proj_swish(f->m, b, W_FF2_1, (int)F, gi->ln_ff2, p->ff2_b1, gi->h2, stream);
+        case PKCU_GEMM_FF1_1: return proj_swish(f->m, b, W_FF1_1, (int)F, gi->ln_ff1, p->ff1_b1, f->hsplit, stream);
+        case PKCU_GEMM_FF2_1: return proj_swish(f->m, b, W_FF2_1, (int)F, gi->ln_ff2, p->ff2_b1, f->hsplit, stream);
+        case PKCU_GEMM_FF1_2:   /* the hidden layer's parts are already in hsplit */
+        case PKCU_GEMM_FF2_2: {
+            const int k = gemm == PKCU_GEMM_FF1_2 ? W_FF1_2 : W_FF2_2;
+            pk_tc_epi e;
+            memset(&e, 0, sizeof(e));
+            e.mode = PK_TC_STORE;
+            e.C = gemm_dst(gemm == PKCU_GEMM_FF1_2 ? go->ff1_out : go->ff2_out);
+            e.alpha = f->m->qscale[b][k] > 0.f ? f->m->qscale[b][k] : 1.0f;
+            return pk_tc_gemm(f->hsplit, f->m->stack[b][k], f->m->qscale[b][k] > 0.f ? 1 : 3, (int)F,
+                              W_COLS[k], W_K[k], &e, stream);
+        }
         case PKCU_GEMM_PW1: {   /* gated [1024, T] = GLU(W_pw1 LN_conv + b) from time-first LN rows */
             pk_tc_epi e;
             memset(&e, 0, sizeof(e));
@@ -559,10 +577,26 @@ int pkcu_encoder_forward(pkcu_encoder_model *m, float *x, const pkcu_gemm_output
      * run in its epilogues */
     int all_tc = m->stacks != NULL && gemm_in->gated != NULL;
     for (int b = 0; b < m->n_blocks && all_tc; b++)
-        all_tc = m->stack[b][W_FF1_1] && m->stack[b][W_FF2_1] && m->stack[b][W_QKV] && m->stack[b][W_PW1] &&
-                 m->stack[b][W_PW2];
+        all_tc = m->stack[b][W_FF1_1] && m->stack[b][W_FF1_2] && m->stack[b][W_FF2_1] &&
+                 m->stack[b][W_FF2_2] && m->stack[b][W_QKV] && m->stack[b][W_PW1] && m->stack[b][W_PW2];
+    if (all_tc) {   /* the FF hidden layer's parts */
+        const size_t hneed = (size_t)rows_ff * 3 * PK_FF * 2;
+        if (hneed > m->hsplit_cap) {
+            if (m->hsplit_ws) cudaFree(m->hsplit_ws);
+            m->hsplit_ws = NULL;
+            m->hsplit_cap = 0;
+            if (cudaMalloc(&m->hsplit_ws, hneed) != cudaSuccess) {
+                cudaGetLastError();
+                m->hsplit_ws = NULL;
+                free(off);
+                return pkcu_fail(PKCU_ERR_NOMEM, "pkcu_encoder_forward: %zu bytes of hidden-layer parts", hneed);
+            }
+            m->hsplit_cap = hneed;
+        }
+    }
     Fwd f = {m, gemm_out, gemm_in, seq, off,
-             all_tc ? (PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV | PKCU_FUSED_CONV) : 0u, x};
+             all_tc ? (PKCU_FUSED_FF_SWISH | PKCU_FUSED_QKV | PKCU_FUSED_CONV) : 0u, x,
+             all_tc ? m->hsplit_ws : NULL};
     const int st = pkcu_encoder_nongemm_fused(x, m->params, m->n_blocks, gemm_out, gemm_in, seq, fwd_hook,
                                               &f, f.fused, stream);
     free(off);

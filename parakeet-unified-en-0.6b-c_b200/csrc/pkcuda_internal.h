@@ -64,6 +64,8 @@ int pk_tc_wait_timeouts(unsigned *count, int reset);   /* k_tcgemm.cu */
 #define PK_TC_CF    4   /* rows = frames of seq: C per item [N, T] (+ bias[n]) */
 #define PK_TC_GLU   5   /* as CF, columns interleaved value / gate by 32: GLU -> [N/2, T] */
 #define PK_TC_STORE_T 6 /* C[n * ldc + m] = alpha (A W)[m, n]: the product written transposed */
+#define PK_TC_SWISH_SPLIT 7 /* Swish(alpha A W + bias) written only as its three bf16 parts,
+                               Cb [M, 3N] = [h0 | h1 | h2]: the next product's operand */
 typedef struct {
     int mode;
     float alpha, beta, rscale;
@@ -73,6 +75,7 @@ typedef struct {
     const float *u, *v;                  /* QKV: pos_bias_u / v [8, 128] */
     float *Qu, *Qv, *K, *V;              /* QKV: per-item [8, T, 128] outputs */
     const pkcu_seq *seq;                 /* QKV: the batch (M = its frames) */
+    void *Cb;                            /* SWISH_SPLIT: bf16 parts [M, 3N], 16-byte aligned */
 } pk_tc_epi;
 /* W [K, N] (bits 32: fp32, 8: int8 with per-tensor scale) -> planes: one
  * [N, K] plane of q for int8 (alpha = scale), else three [N, 3K] parts. */
