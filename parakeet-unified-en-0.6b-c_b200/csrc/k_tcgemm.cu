@@ -709,20 +709,28 @@ __global__ void split_cf_t_kernel(const float *__restrict__ X, __nv_bfloat16 *__
 // GEMM's 32-wide K blocks (the score rows S of the context product, K = T).
 __global__ void split_rows_pad_kernel(const float *__restrict__ A, __nv_bfloat16 *__restrict__ out, long long M,
                                       int K, int Kp) {
-  const long long total = M * Kp;
+  // a thread takes 8 consecutive columns of a row (Kp % 8 == 0): 8 coalesced
+  // scalar loads (rows of odd K are not 16-byte aligned) and one 16-byte
+  // store per part
+  const int K8 = Kp / 8;
+  const long long total = M * K8;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (long long)gridDim.x * blockDim.x) {
-    const long long m = e / Kp;
-    const int k = (int)(e - m * Kp);
-    const float x = k < K ? __ldg(A + m * K + k) : 0.0f;
-    const __nv_bfloat16 p0 = __float2bfloat16_rn(x);
-    const float r1 = x - __bfloat162float(p0);
-    const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
-    const __nv_bfloat16 p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
-    __nv_bfloat16 *o = out + m * 3 * Kp + k;
-    o[0] = p0;
-    o[Kp] = p1;
-    o[2 * Kp] = p2;
+    const long long m = e / K8;
+    const int k0 = (int)(e - m * K8) * 8;
+    const float *a = A + m * K;
+    __align__(16) __nv_bfloat16 p[3][8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float x = k0 + j < K ? __ldg(a + k0 + j) : 0.0f;
+      p[0][j] = __float2bfloat16_rn(x);
+      const float r1 = x - __bfloat162float(p[0][j]);
+      p[1][j] = __float2bfloat16_rn(r1);
+      p[2][j] = __float2bfloat16_rn(r1 - __bfloat162float(p[1][j]));
+    }
+    __nv_bfloat16 *o = out + m * 3 * Kp + k0;
+#pragma unroll
+    for (int q = 0; q < 3; q++) *reinterpret_cast<uint4 *>(o + (long long)q * Kp) = *reinterpret_cast<const uint4 *>(p[q]);
   }
 }
 
@@ -862,8 +870,9 @@ extern "C" int pk_tc_prepare_rows(const float *W, int N, int K, int glu, void *p
 }
 
 extern "C" int pk_split_rows_pad(const float *A, void *parts, long long M, int K, int Kp, pkcu_stream_t stream) {
-  if (!A || !parts || M <= 0 || K <= 0 || Kp < K) return pkcu_fail(PKCU_ERR_ARG, "pk_split_rows_pad: bad argument");
-  long long blocks = (M * Kp + 255) / 256;
+  if (!A || !parts || M <= 0 || K <= 0 || Kp < K || Kp % 8 || !PK_ALIGNED16(parts))
+    return pkcu_fail(PKCU_ERR_ARG, "pk_split_rows_pad: bad argument (Kp %% 8 == 0, parts 16-byte aligned)");
+  long long blocks = (M * (Kp / 8) + 255) / 256;
   if (blocks > 16LL * pkcu_sm_count()) blocks = 16LL * pkcu_sm_count();
   tc::split_rows_pad_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
       A, static_cast<__nv_bfloat16 *>(parts), M, K, Kp);
