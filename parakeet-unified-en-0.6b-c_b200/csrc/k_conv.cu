@@ -366,13 +366,12 @@ __device__ __forceinline__ float4 glu4(float4 a, float4 g, float ba, float bg, b
   if (bias) {
     const float2 a01 = F::add(make_float2(a.x, a.y), splat2(ba));
     const float2 a23 = F::add(make_float2(a.z, a.w), splat2(ba));
-    const float2 g01 = F::add(make_float2(g.x, g.y), splat2(bg));
-    const float2 g23 = F::add(make_float2(g.z, g.w), splat2(bg));
     a = make_float4(a01.x, a01.y, a23.x, a23.y);
-    g = make_float4(g01.x, g01.y, g23.x, g23.y);
   }
-  const float2 o01 = glu_gate2<F>(make_float2(a.x, a.y), make_float2(g.x, g.y));
-  const float2 o23 = glu_gate2<F>(make_float2(a.z, a.w), make_float2(g.z, g.w));
+  // the gate's bias enters the gate's own first FMA, -(g + bg) = g * -1 - bg
+  const float2 nbg = splat2(bias ? -bg : -0.0f);
+  const float2 o01 = glu_gate2<F>(make_float2(a.x, a.y), make_float2(g.x, g.y), nbg);
+  const float2 o23 = glu_gate2<F>(make_float2(a.z, a.w), make_float2(g.z, g.w), nbg);
   return make_float4(o01.x, o01.y, o23.x, o23.y);
 }
 

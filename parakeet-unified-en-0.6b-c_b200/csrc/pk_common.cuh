@@ -254,50 +254,58 @@ __device__ __forceinline__ float sigmoid_libm(float b) {
 // k = round(x log2 e) with the 1.5 * 2^23 shifter (one FMA: the rounding to an
 // integer happens in the add), f = x log2 e - k with log2 e split into its
 // float value and the float of the remainder (two FMAs; |f| <= 0.5 + 2^-20),
-// 2^f by ex2.approx.ftz on f in [-0.5, 0.5], and 2^k added to the exponent
+// 2^f by ex2.approx.ftz on f in [-0.5, 0.5], times 2^k built in the exponent
 // field (the shifted value's low bits are k, so bits(t) << 23 is k << 23 mod
-// 2^32). Then 1 + e and its hardware reciprocal (rcp.approx, 1 ulp: the
-// denominator lies in [1, 2.2e37], so the result is a normal float). The gate
-// argument is clamped to [-86, 86] first: past it the sigmoid is 1 or below
-// 4.5e-38, where the reference gives 1 or below that (0 once expf overflows);
-// a NaN gate gives NaN as in the reference. Error against the correctly
-// rounded sigmoid: a few units in the last place (checked on the device
-// against glibc by a dense sweep), inside the GLU's tolerance.
+// 2^32; the product is exact). Then 1 + e and its hardware reciprocal
+// (rcp.approx, 1 ulp: the denominator lies in [1, 2.2e37], so the result is a
+// normal float). The argument x = -(b + bias) is one FMA, b * -1 - bias, and is
+// clamped to [-86, 86] first: past it the sigmoid is 1 or below 4.5e-38, where
+// the reference gives 1 or below that (0 once expf overflows). The clamp keeps
+// a NaN (max.NaN / min.NaN), which then runs through ex2 and the products: a
+// NaN gate gives NaN as in the reference, with no select. Error against the
+// correctly rounded sigmoid: a few units in the last place (checked on the
+// device against glibc by a dense sweep), inside the GLU's tolerance.
 __device__ __forceinline__ float ex2_approx(float x) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
+__device__ __forceinline__ float clamp86_nan(float x) {
+  float r;
+  asm("{\n .reg .f32 t;\n max.NaN.f32 t, %1, 0fC2AC0000;\n min.NaN.f32 %0, t, 0f42AC0000;\n}"
+      : "=f"(r) : "f"(x));
+  return r;
+}
+// 2^k for the shifter value t = 1.5 * 2^23 + k
+__device__ __forceinline__ float gate_pow2k(float t) {
+  return __uint_as_float((__float_as_uint(t) << 23) + 0x3F800000u);
+}
 constexpr float GATE_L2E_HI = 1.44269502162933349609375f;   // float(log2 e)
 constexpr float GATE_L2E_LO = 1.925963033500011e-08f;       // float(log2 e - GATE_L2E_HI)
 constexpr float GATE_SHIFT = 12582912.0f;                   // 1.5 * 2^23
 
+// a * sigmoid(g + bias) on a pair, nbg = -bias (-0 without one)
 template <class F = F2Ptx>
-__device__ __forceinline__ float2 glu_gate2(float2 a, float2 g) {
-  float2 m = F::sub(splat2(0.0f), g);
-  m.x = fminf(fmaxf(m.x, -86.0f), 86.0f);
-  m.y = fminf(fmaxf(m.y, -86.0f), 86.0f);
+__device__ __forceinline__ float2 glu_gate2(float2 a, float2 g, float2 nbg) {
+  float2 m = F::fma(g, splat2(-1.0f), nbg);
+  m.x = clamp86_nan(m.x);
+  m.y = clamp86_nan(m.y);
   const float2 t = F::fma(m, splat2(GATE_L2E_HI), splat2(GATE_SHIFT));
   float2 f = F::fma(m, splat2(GATE_L2E_HI), F::sub(splat2(GATE_SHIFT), t));
   f = F::fma(m, splat2(GATE_L2E_LO), f);
-  const float ex = __uint_as_float(__float_as_uint(ex2_approx(f.x)) + (__float_as_uint(t.x) << 23));
-  const float ey = __uint_as_float(__float_as_uint(ex2_approx(f.y)) + (__float_as_uint(t.y) << 23));
-  const float2 d = F::add(splat2(1.0f), make_float2(ex, ey));
-  float2 o = F::mul(a, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
-  if (g.x != g.x) o.x = g.x;
-  if (g.y != g.y) o.y = g.y;
-  return o;
+  const float2 e = F::mul(make_float2(ex2_approx(f.x), ex2_approx(f.y)),
+                          make_float2(gate_pow2k(t.x), gate_pow2k(t.y)));
+  const float2 d = F::add(splat2(1.0f), e);
+  return F::mul(a, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
 }
 // The same operations on one value (bit-identical to either half of glu_gate2).
-__device__ __forceinline__ float glu_gate(float a, float g) {
-  float m = __fsub_rn(0.0f, g);
-  m = fminf(fmaxf(m, -86.0f), 86.0f);
+__device__ __forceinline__ float glu_gate(float a, float g, float nbg = -0.0f) {
+  const float m = clamp86_nan(fmaf(g, -1.0f, nbg));
   const float t = fmaf(m, GATE_L2E_HI, GATE_SHIFT);
   float f = fmaf(m, GATE_L2E_HI, __fsub_rn(GATE_SHIFT, t));
   f = fmaf(m, GATE_L2E_LO, f);
-  const float e = __uint_as_float(__float_as_uint(ex2_approx(f)) + (__float_as_uint(t) << 23));
-  const float o = __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
-  return g != g ? g : o;
+  const float e = __fmul_rn(ex2_approx(f), gate_pow2k(t));
+  return __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
 }
 
 // ── exact division by a run-time divisor ─────────────────────────────────────
