@@ -98,7 +98,7 @@ enum { LN_PLAIN = 0, LN_RESID = 1, LN_RESID2 = 2 };
 // MODE LN_RESID2: x = LN(x + alpha*(y+bias); g1,b1); out = LN(x; g2,b2) if g2
 // (LN_RESID2 held to 64 registers, four CTAs = 32 warps per SM: 0.98 of the copy
 // bandwidth against 0.92-0.93 at 75 registers and three CTAs, despite a few
-// spilled bytes; the other modes measured best unbounded.)
+// spilled bytes; residual + LN already runs at the copy bandwidth unbounded.)
 template <int MODE>
 __global__ void __launch_bounds__(32 * LN_ROWS_PER_CTA, MODE == LN_RESID2 ? 4 : 1)
 ln1024_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias, float alpha,
