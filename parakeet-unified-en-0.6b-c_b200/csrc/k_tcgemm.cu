@@ -839,6 +839,8 @@ extern "C" void pk_tc_warm(void) {
   smem_optin(tc::tc_gemm_kernel<3, 256>, tc::Cfg<3, 256>::SMEM, optin_flags<3, 256>());
   smem_optin(tc::tc_gemm_kernel<1, 64>, tc::Cfg<1, 64>::SMEM, optin_flags<1, 64>());
   smem_optin(tc::tc_gemm_kernel<3, 64>, tc::Cfg<3, 64>::SMEM, optin_flags<3, 64>());
+  smem_optin(tc::tc_gemm_kernel<1, 128>, tc::Cfg<1, 128>::SMEM, optin_flags<1, 128>());
+  smem_optin(tc::tc_gemm_kernel<3, 128>, tc::Cfg<3, 128>::SMEM, optin_flags<3, 128>());
 }
 
 extern "C" int pk_tc_wait_timeouts(unsigned *count, int reset) {
@@ -943,9 +945,13 @@ int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long 
   const int narrow = ep->mode != PK_TC_GLU &&
                      (N <= 128 || Z * (long long)((N + 255) / 256) * ((M + tc::BM - 1) / tc::BM) * 2 <
                                       pkcu_sm_count());
+  // otherwise 128-wide tiles where they pad N less than 256-wide ones (the
+  // per-head products, N = T = 375: 384 against 512 columns of MMA work)
+  const int bn = narrow ? 64
+                        : (ep->mode != PK_TC_GLU && (N + 127) / 128 * 128 < (N + 255) / 256 * 256 ? 128 : 256);
   CUtensorMap ma, mb;
   int st = tmap_bf16(&ma, a_parts, a_rows, 3LL * K, 3LL * K, tc::BM);
-  if (!st) st = tmap_bf16(&mb, planes, b_rows, (long long)npb * K, (long long)npb * K, narrow ? 64 : 256);
+  if (!st) st = tmap_bf16(&mb, planes, b_rows, (long long)npb * K, (long long)npb * K, bn);
   if (st) return st;
   tc::Epi e;
   e.mode = ep->mode;
@@ -984,8 +990,10 @@ int tc_gemm_run(const void *a_parts, long long a_rows, const void *planes, long 
   if (e.mode == PK_TC_STORE_T && (!e.C || !ep->ldc || ep->ldc < M))
     return pkcu_fail(PKCU_ERR_ARG, "tcgen05 GEMM: the transposed store needs rows of at least M");
   cudaStream_t s = (cudaStream_t)stream;
-  if (narrow)
+  if (bn == 64)
     return npb == 1 ? launch<1, 64>(ma, mb, M, N, K, e, s) : launch<3, 64>(ma, mb, M, N, K, e, s);
+  if (bn == 128)
+    return npb == 1 ? launch<1, 128>(ma, mb, M, N, K, e, s) : launch<3, 128>(ma, mb, M, N, K, e, s);
   return npb == 1 ? launch<1, 256>(ma, mb, M, N, K, e, s) : launch<3, 256>(ma, mb, M, N, K, e, s);
 }
 }  // namespace

@@ -63,8 +63,9 @@ def make_weight(cuda, args, K, N):
     return cuda.Weight(args.pop("data"), args.pop("bits"), K, N, **args)
 
 
+# (8000, 640, 1024) takes the 128-wide tiles (640 columns pad to 768 in 256-wide ones)
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 1024, 1024), (300, 4096, 1024),
-                                   (37, 1024, 4096), (1000, 3072, 1024)])
+                                   (37, 1024, 4096), (1000, 3072, 1024), (8000, 640, 1024)])
 @pytest.mark.parametrize("kind", ["f32", "i8", "i4_g32_n", "i4_g128_k"])
 def test_wmatmul_matches_reference(cuda, reference, oracle, kind, M, N, K):
     if kind == "i4_g128_k" and K % 128:
