@@ -293,8 +293,9 @@ argmax_rows_kernel(const float *__restrict__ logits, int32_t *__restrict__ out, 
   float bv = -INFINITY;
   int bi = INT_MAX;
   // each lane scans its entries in increasing order, so a strict '>' keeps the
-  // first maximum, and a NaN never compares greater
-#pragma unroll 4
+  // first maximum, and a NaN never compares greater; 16 loads per lane in
+  // flight (a 1025-logit row is 33 per lane)
+#pragma unroll 16
   for (int j = lane; j < V; j += 32) {
     const float v = __ldcs(l + j);
     if (v > bv) { bv = v; bi = j; }
