@@ -156,7 +156,7 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
 // ── epilogue ────────────────────────────────────────────────────────────────
 
 struct Epi {
-  int mode;              // PK_TC_STORE / _SWISH / _RESID / _QKV
+  int mode;              // PK_TC_* (STORE, SWISH, RESID, QKV, CF, GLU, STORE_T, SWISH_SPLIT)
   float alpha;           // applied to the product first (an int8 weight's scale)
   float beta;            // STORE: C = alpha AW + beta C (the reference's pk_wmatmul)
   float rscale;          // RESID: X += rscale (alpha AW + bias)
