@@ -162,8 +162,12 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // copy bandwidth against 0.85 / 0.84. So did two cures for the 4-way bank
 // conflict of the column reads (row stride 1028): warp instructions over 4
 // channels x 8 frames (0.80 / 0.44: 32-byte pieces per instruction), and rows
-// held as scalars with an odd stride (0.80 / 0.86). Requesting transpose-add's
-// x row before its channel-first reads measured 0.71 against 0.86.)
+// held as scalars with an odd stride (0.80 / 0.86). A tile without any bank
+// conflict (16-byte chunks at chunk index q ^ (row & 7), each lane moving a
+// float4 of four channels of one frame, still 128-byte runs per warp store)
+// gained nothing either: 0.87 / 0.82 against 0.87 / 0.84 on the same box.
+// Requesting transpose-add's x row before its channel-first reads measured
+// 0.71 against 0.86.)
 template <int TT, bool RESID>
 __global__ void __launch_bounds__(32 * TT, 32 / TT)
 ln_transpose_kernel(float *x, const float *__restrict__ y, const float *__restrict__ bias,
