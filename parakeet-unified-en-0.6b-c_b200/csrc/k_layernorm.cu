@@ -165,7 +165,11 @@ ln_generic_kernel(const float *x, const float *__restrict__ g, const float *__re
 // held as scalars with an odd stride (0.80 / 0.86). A tile without any bank
 // conflict (16-byte chunks at chunk index q ^ (row & 7), each lane moving a
 // float4 of four channels of one frame, still 128-byte runs per warp store)
-// gained nothing either: 0.87 / 0.82 against 0.87 / 0.84 on the same box.
+// gained nothing either: 0.87 / 0.82 against 0.87 / 0.84 on the same box. Nor
+// did two 512-thread CTAs per tile as a thread-block cluster (16 frames in each
+// CTA's 64 KB, two CTAs per SM, each CTA moving half the channels of all 32
+// frames through distributed shared memory): 0.35 / 0.44, the 4-byte accesses
+// to the peer's shared memory costing far more than the overlap gained.
 // Requesting transpose-add's x row before its channel-first reads measured
 // 0.71 against 0.86.)
 template <int TT, bool RESID>

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 RAGGED = [[1, 7, 3, 32], [408, 416, 416, 408], [9], [375, 375]]
 # enough 32-frame tiles for every SM: the transposing kernels' 32-frame path
 # (the cases above take the 16-frame one)
-WIDE = [[375] * 13 + [1, 37]]
+WIDE = [[375] * 13 + [1, 37, 16, 17]]
 
 
 def rng(seed):
