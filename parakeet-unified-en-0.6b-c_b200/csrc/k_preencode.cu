@@ -255,21 +255,38 @@ pre_dw5_kernel(const float *__restrict__ y2, const float *__restrict__ b3,
   for (int k = 0; k < 9; k++) w[k] = __ldg(w5 + c * 9 + k);
   const float bias = __ldg(b5 + c);
   __syncthreads();
-  float *dst = s3d + (long long)c * P3 + (seq_frame_off(seq3, item) + o0) * 16;
-  for (int o = threadIdx.x; o < nout * 16; o += 256) {
-    const int ol = o >> 4, ow = o & 15, oh = o0 + ol;
-    float val = bias;
+  // Thread = output row ol (tid / 4) x output columns ow = 4q..4q+3 (q = tid % 4):
+  // per input row one float4 of even columns (2 ow), one of odd columns
+  // (2 ow + 1) and the odd column 8q - 1 left of them; each output's taps in
+  // the reference's order (kh, then kw), column -1 being the zero padding.
+  const int ol = threadIdx.x >> 2, q = threadIdx.x & 3, oh = o0 + ol;
+  if (ol >= nout) return;
+  float acc0 = bias, acc1 = bias, acc2 = bias, acc3 = bias;
 #pragma unroll
-    for (int kh = 0; kh < 3; kh++) {
-      const int r = 2 * oh - 1 + kh;
-      if (r < 0 || r >= H2) continue;
-      const float *row = tile + (2 * ol + kh) * P5_LD;
-      if (ow > 0) val = fmaf(row[16 + ow - 1], w[kh * 3 + 0], val);   // column 2 ow - 1
-      val = fmaf(row[ow], w[kh * 3 + 1], val);                        // column 2 ow
-      val = fmaf(row[16 + ow], w[kh * 3 + 2], val);                   // column 2 ow + 1
-    }
-    dst[o] = val;
+  for (int kh = 0; kh < 3; kh++) {
+    const int r = 2 * oh - 1 + kh;
+    if (r < 0 || r >= H2) continue;
+    const float *row = tile + (2 * ol + kh) * P5_LD;
+    const float4 ev = ld4(row + 4 * q), od = ld4(row + 16 + 4 * q);
+    const float w0 = w[kh * 3 + 0], w1 = w[kh * 3 + 1], w2 = w[kh * 3 + 2];
+    if (q > 0) acc0 = fmaf(row[16 + 4 * q - 1], w0, acc0);
+    acc0 = fmaf(ev.x, w1, acc0);
+    acc0 = fmaf(od.x, w2, acc0);
+    acc1 = fmaf(od.x, w0, acc1);
+    acc1 = fmaf(ev.y, w1, acc1);
+    acc1 = fmaf(od.y, w2, acc1);
+    acc2 = fmaf(od.y, w0, acc2);
+    acc2 = fmaf(ev.z, w1, acc2);
+    acc2 = fmaf(od.z, w2, acc2);
+    acc3 = fmaf(od.z, w0, acc3);
+    acc3 = fmaf(ev.w, w1, acc3);
+    acc3 = fmaf(od.w, w2, acc3);
   }
+  float *o = s3d + (long long)c * P3 + (seq_frame_off(seq3, item) + oh) * 16 + 4 * q;
+  o[0] = acc0;
+  o[1] = acc1;
+  o[2] = acc2;
+  o[3] = acc3;
 }
 
 // flat[g, 16c + w] = relu(y3[c, 16g + w] + b6[c]), four floats per thread.
