@@ -215,14 +215,18 @@ pre_front_kernel(const float *__restrict__ mel, const float *__restrict__ w0g,
 
 constexpr int P5_R3 = 64;                  // dw5 output rows per CTA
 constexpr int P5_IN = 2 * P5_R3 + 1;       // input rows they read
-constexpr int P5_LD = 40;                  // floats per staged row: even columns, odd columns, pad
+constexpr int P5_LD = 32;                  // floats per staged row
 
 // s3d[c, item, oh, ow] = b5[c] + taps of relu(y2 + b3[c]) (dw5 applied to the
 // pw1 product): one CTA per (64 output rows, channel, item). The input rows
-// are contiguous in y2's channel row, so they are staged with coalesced
-// 16-byte loads (bias + ReLU applied once per element), split into even and
-// odd columns; with a row pitch of 40 floats the two output rows a warp
-// computes read disjoint bank halves.
+// are contiguous in y2's channel row: they arrive as 16-byte asynchronous
+// copies (the whole slab in flight at once), 16-byte chunk k of staged row R
+// at chunk k ^ ((R >> 1) & 1), so that the two output rows of a quarter-warp
+// read disjoint banks. Thread = output row ol (tid / 4) x output columns
+// ow = 4q..4q+3 (q = tid % 4): per input row the two float4 of columns
+// 8q..8q+7 and the column 8q - 1, bias + ReLU applied as they are read; each
+// output's taps in the reference's order (kh, then kw), column -1 being the
+// zero padding.
 __global__ void __launch_bounds__(256)
 pre_dw5_kernel(const float *__restrict__ y2, const float *__restrict__ b3,
                const float *__restrict__ w5, const float *__restrict__ b5, float *__restrict__ s3d,
@@ -236,29 +240,18 @@ pre_dw5_kernel(const float *__restrict__ y2, const float *__restrict__ b3,
   const int r0 = 2 * o0 - 1;                                 // input row of staged row 0
   const int rlo = max(r0, 0), rhi = min(2 * (o0 + nout) - 1, H2 - 1);
   const float *src = y2 + (long long)c * P2 + seq_frame_off(seq2, item) * 32;
-  const float bc = __ldg(b3 + c);
-  // 8 lanes per 128-byte row; a warp stages rows R, R+2, R+1, R+3 (lane groups
-  // 0..3) so that each half-warp's 8-byte stores cover all 32 banks.
-  const int n4 = ((rhi - rlo + 4) >> 2) * 32;
-  for (int e = threadIdx.x; e < n4; e += 256) {
-    const int sub = (e >> 3) & 3, k = e & 7;
-    const int r = rlo + 4 * (e >> 5) + ((sub & 1) << 1) + (sub >> 1);
-    if (r > rhi) continue;
-    float4 v = ldg4_stream(src + (long long)r * 32 + 4 * k);
-    v = make_float4(relu1(v.x + bc), relu1(v.y + bc), relu1(v.z + bc), relu1(v.w + bc));
-    float *row = tile + (r - r0) * P5_LD;
-    *reinterpret_cast<float2 *>(row + 2 * k) = make_float2(v.x, v.z);        // columns 4k, 4k+2
-    *reinterpret_cast<float2 *>(row + 16 + 2 * k) = make_float2(v.y, v.w);   // columns 4k+1, 4k+3
+  for (int e = threadIdx.x; e < (rhi - rlo + 1) * 8; e += 256) {
+    const int r = rlo + (e >> 3), k = e & 7, R = r - r0;
+    cp_async16(tile + R * P5_LD + 4 * (k ^ ((R >> 1) & 1)), src + (long long)r * 32 + 4 * k);
   }
+  cp_async_commit();
+  const float bc = __ldg(b3 + c);
   float w[9];
 #pragma unroll
   for (int k = 0; k < 9; k++) w[k] = __ldg(w5 + c * 9 + k);
   const float bias = __ldg(b5 + c);
+  cp_async_wait<0>();
   __syncthreads();
-  // Thread = output row ol (tid / 4) x output columns ow = 4q..4q+3 (q = tid % 4):
-  // per input row one float4 of even columns (2 ow), one of odd columns
-  // (2 ow + 1) and the odd column 8q - 1 left of them; each output's taps in
-  // the reference's order (kh, then kw), column -1 being the zero padding.
   const int ol = threadIdx.x >> 2, q = threadIdx.x & 3, oh = o0 + ol;
   if (ol >= nout) return;
   float acc0 = bias, acc1 = bias, acc2 = bias, acc3 = bias;
@@ -266,21 +259,24 @@ pre_dw5_kernel(const float *__restrict__ y2, const float *__restrict__ b3,
   for (int kh = 0; kh < 3; kh++) {
     const int r = 2 * oh - 1 + kh;
     if (r < 0 || r >= H2) continue;
-    const float *row = tile + (2 * ol + kh) * P5_LD;
-    const float4 ev = ld4(row + 4 * q), od = ld4(row + 16 + 4 * q);
+    const int R = 2 * ol + kh, sw = (R >> 1) & 1;
+    const float *row = tile + R * P5_LD;
+    float4 a = ld4(row + 4 * ((2 * q) ^ sw)), b = ld4(row + 4 * ((2 * q + 1) ^ sw));
+    a = make_float4(relu1(a.x + bc), relu1(a.y + bc), relu1(a.z + bc), relu1(a.w + bc));
+    b = make_float4(relu1(b.x + bc), relu1(b.y + bc), relu1(b.z + bc), relu1(b.w + bc));
     const float w0 = w[kh * 3 + 0], w1 = w[kh * 3 + 1], w2 = w[kh * 3 + 2];
-    if (q > 0) acc0 = fmaf(row[16 + 4 * q - 1], w0, acc0);
-    acc0 = fmaf(ev.x, w1, acc0);
-    acc0 = fmaf(od.x, w2, acc0);
-    acc1 = fmaf(od.x, w0, acc1);
-    acc1 = fmaf(ev.y, w1, acc1);
-    acc1 = fmaf(od.y, w2, acc1);
-    acc2 = fmaf(od.y, w0, acc2);
-    acc2 = fmaf(ev.z, w1, acc2);
-    acc2 = fmaf(od.z, w2, acc2);
-    acc3 = fmaf(od.z, w0, acc3);
-    acc3 = fmaf(ev.w, w1, acc3);
-    acc3 = fmaf(od.w, w2, acc3);
+    if (q > 0) acc0 = fmaf(relu1(row[4 * ((2 * q - 1) ^ sw) + 3] + bc), w0, acc0);
+    acc0 = fmaf(a.x, w1, acc0);
+    acc0 = fmaf(a.y, w2, acc0);
+    acc1 = fmaf(a.y, w0, acc1);
+    acc1 = fmaf(a.z, w1, acc1);
+    acc1 = fmaf(a.w, w2, acc1);
+    acc2 = fmaf(a.w, w0, acc2);
+    acc2 = fmaf(b.x, w1, acc2);
+    acc2 = fmaf(b.y, w2, acc2);
+    acc3 = fmaf(b.y, w0, acc3);
+    acc3 = fmaf(b.z, w1, acc3);
+    acc3 = fmaf(b.w, w2, acc3);
   }
   float *o = s3d + (long long)c * P3 + (seq_frame_off(seq3, item) + oh) * 16 + 4 * q;
   o[0] = acc0;
