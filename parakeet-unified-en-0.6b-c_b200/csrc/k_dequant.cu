@@ -192,7 +192,7 @@ __device__ __forceinline__ const float *scale_row(const float *scales, unsigned 
 // block of one row (one division per chunk); otherwise chunks run over the
 // flat array and each float4 finds its row. Four chunks per warp per
 // iteration, their loads issued together.
-template <bool BLOCKS, bool PRE>
+template <bool BLOCKS, bool PRE, bool NPRE = false>
 __global__ void __launch_bounds__(DQ_THREADS)
 dequant_i4_vec_kernel(const uint8_t *__restrict__ packed, const float *__restrict__ scales,
                       float *__restrict__ out, int K, int N, int G, int axis, FastDiv div_wpr,
@@ -217,9 +217,26 @@ dequant_i4_vec_kernel(const uint8_t *__restrict__ packed, const float *__restric
     // PRE (block chunks, scales along K: a float4 of scales per float4 of
     // weights): every chunk's scales requested before the first store, so their
     // (L2) latencies overlap instead of one per chunk (0.73 -> 0.88 of the copy
-    // bandwidth at G = 128; along N one broadcast scale per float4 measured
-    // better the other way)
+    // bandwidth at G = 128; along N, a broadcast float4 per float4 of weights
+    // prefetched this way measured worse: see NPRE)
     float4 sv[PRE ? U : 1][2];
+    // NPRE (block chunks, scales along N with G dividing 256, G >= 8): a chunk's
+    // 256 / G scales are one load by lanes 0 .. 256 / G - 1, every chunk's
+    // requested before the first store; each float4 then takes its group's scale
+    // from the lane holding it (G = 32: 0.80 -> 0.82 of the copy bandwidth).
+    float sn[NPRE ? U : 1];
+    if (NPRE) {
+      const unsigned gpc = 256u / (unsigned)G;
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const unsigned cu = c + u * warps;
+        sn[u] = 0.0f;
+        if (cu < n_chunks && (unsigned)lane < gpc) {
+          const unsigned k = fast_div(cu, div_bpr);
+          sn[u] = __ldg(scales + (long long)k * ng + fast_div(256 * (cu - k * bpr), div_G) + lane);
+        }
+      }
+    }
     if (PRE) {
 #pragma unroll
       for (int u = 0; u < U; u++) {
@@ -242,12 +259,20 @@ dequant_i4_vec_kernel(const uint8_t *__restrict__ packed, const float *__restric
       if (BLOCKS) {
         k = fast_div(cu, div_bpr);
         col0 = 256 * (cu - k * bpr);
-        if (!PRE) srow = scale_row(scales, k, N, ng, axis, div_G);
+        if (!PRE && !NPRE) srow = scale_row(scales, k, N, ng, axis, div_G);
       }
 #pragma unroll
       for (int j = 0; j < 2; j++) {
         const uint32_t src = __shfl_sync(PK_FULL_MASK, w[u], 16 * j + (lane >> 1));
         int col;
+        if (NPRE) {
+          col = (int)col0 + 128 * j + 4 * lane;
+          const float t = __shfl_sync(PK_FULL_MASK, sn[NPRE ? u : 0],
+                                      (int)fast_div((unsigned)(128 * j + 4 * lane), div_G));
+          const uint32_t h = (lane & 1) ? src >> 16 : src & 0xffffu;
+          st4(out + (long long)k * N + col, nib4_scaled(h, make_float4(t, t, t, t)));
+          continue;
+        }
         if (PRE) {
           col = (int)col0 + 128 * j + 4 * lane;
           const uint32_t h = (lane & 1) ? src >> 16 : src & 0xffffu;
@@ -408,6 +433,12 @@ extern "C" int pkcu_dequant_i4(const uint8_t *packed, const float *scales, float
   if (vec && N % 256 == 0 && axis == PKCU_GROUP_ALONG_K)
     dequant_i4_vec_kernel<true, true><<<dq_grid(dequant_i4_vec_kernel<true, true>, (long long)K * N / 8),
                                         DQ_THREADS, 0, (cudaStream_t)stream>>>(
+        packed, scales, out, K, N, group, axis, make_fastdiv((unsigned)(N / 8)),
+        make_fastdiv((unsigned)(N / 256)), make_fastdiv((unsigned)group));
+  else if (vec && N % 256 == 0 && group >= 8 && 256 % group == 0)
+    dequant_i4_vec_kernel<true, false, true><<<dq_grid(dequant_i4_vec_kernel<true, false, true>,
+                                                       (long long)K * N / 8),
+                                               DQ_THREADS, 0, (cudaStream_t)stream>>>(
         packed, scales, out, K, N, group, axis, make_fastdiv((unsigned)(N / 8)),
         make_fastdiv((unsigned)(N / 256)), make_fastdiv((unsigned)group));
   else if (vec && N % 256 == 0)

@@ -537,7 +537,8 @@ def test_requant_qkv(cuda, oracle):
                                         (1024, 4096, 128, 0), (4096, 1024, 128, 0),
                                         (6, 18, 3, 1), (16, 10, 8, 0), (8, 24, 2, 1),
                                         (24, 40, 4, 0), (3, 8, 8, 1), (5, 16, 16, 1),
-                                        (128, 72, 8, 1)])
+                                        (128, 72, 8, 1), (16, 512, 8, 1), (12, 512, 16, 1),
+                                        (8, 768, 64, 1), (3, 256, 128, 1), (4, 256, 256, 1)])
 def test_dequant_i4(cuda, oracle, K, N, G, axis):
     r = rng(K + N + G)
     q = r.integers(-8, 8, size=(K, N)).astype(np.int8)
