@@ -87,25 +87,36 @@ __device__ __forceinline__ void softmax_regs(float (&v)[NPL], int len, int lane)
   }
 }
 
-// In-place softmax of rows of len <= 32*NPL (pk_softmax_rows).
-template <int NPL>
+// In-place softmax of rows of len <= 32*NPL (pk_softmax_rows): a warp takes
+// ROWS consecutive rows and requests all of them before computing the first,
+// so that more loads are in flight per warp.
+template <int NPL, int ROWS>
 __global__ void __launch_bounds__(32 * SM_ROWS_PER_CTA)
 softmax_rows_warp_kernel(float *x, long long n_rows, int len) {
   const int lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * SM_ROWS_PER_CTA + (threadIdx.x >> 5);
-  if (row >= n_rows) return;
-  float *r = x + row * len;
-  float v[NPL];
+  const long long row0 = ((long long)blockIdx.x * SM_ROWS_PER_CTA + (threadIdx.x >> 5)) * ROWS;
+  if (row0 >= n_rows) return;
+  float v[ROWS][NPL];
 #pragma unroll
-  for (int k = 0; k < NPL; k++) {
-    const int j = lane + 32 * k;
-    v[k] = (j < len) ? r[j] : 0.0f;
+  for (int q = 0; q < ROWS; q++) {
+    const bool ok = row0 + q < n_rows;
+    const float *r = x + (ok ? row0 + q : row0) * len;
+#pragma unroll
+    for (int k = 0; k < NPL; k++) {
+      const int j = lane + 32 * k;
+      v[q][k] = (ok && j < len) ? r[j] : 0.0f;
+    }
   }
-  softmax_regs<NPL>(v, len, lane);
 #pragma unroll
-  for (int k = 0; k < NPL; k++) {
-    const int j = lane + 32 * k;
-    if (j < len) r[j] = v[k];
+  for (int q = 0; q < ROWS; q++) {
+    if (row0 + q >= n_rows) break;   // warp-uniform
+    softmax_regs<NPL>(v[q], len, lane);
+    float *r = x + (row0 + q) * len;
+#pragma unroll
+    for (int k = 0; k < NPL; k++) {
+      const int j = lane + 32 * k;
+      if (j < len) r[j] = v[q][k];
+    }
   }
 }
 
@@ -605,8 +616,11 @@ static int launch_scores(const float *ac, const float *bd, float *S, float scale
 
 template <int NPL>
 static void launch_softmax_warp(float *x, long long n_rows, int len, cudaStream_t s) {
-  const unsigned grid = (unsigned)((n_rows + SM_ROWS_PER_CTA - 1) / SM_ROWS_PER_CTA);
-  softmax_rows_warp_kernel<NPL><<<grid, 32 * SM_ROWS_PER_CTA, 0, s>>>(x, n_rows, len);
+  // two rows per warp for rows of 129..512 entries
+  constexpr int ROWS = (NPL >= 8 && NPL <= 16) ? 2 : 1;
+  const long long per_cta = (long long)SM_ROWS_PER_CTA * ROWS;
+  const unsigned grid = (unsigned)((n_rows + per_cta - 1) / per_cta);
+  softmax_rows_warp_kernel<NPL, ROWS><<<grid, 32 * SM_ROWS_PER_CTA, 0, s>>>(x, n_rows, len);
 }
 
 static int check_scores(const float *ac, const float *bd, const float *S, const pkcu_seq *seq,

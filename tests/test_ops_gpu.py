@@ -239,7 +239,8 @@ def test_transpose_add_layer_norm(cuda, oracle, lengths):
 # ── softmax and the relative-position scores ─────────────────────────────────
 
 @pytest.mark.parametrize("R,n", [(3, 1), (5, 7), (9, 8), (4, 31), (4, 33), (3000, 375),
-                                 (64, 416), (8, 1000), (6, 1025), (3, 5000)])
+                                 (64, 416), (8, 1000), (6, 1025), (3, 5000), (7, 300),
+                                 (5, 200), (3, 500), (17, 129)])
 def test_softmax_rows(cuda, oracle, R, n):
     x = (3 * rng(R + n).standard_normal((R, n))).astype(np.float32)
     xd = dev(x)
